@@ -1,0 +1,450 @@
+#!/usr/bin/env python
+"""EXL3 packed-weight GEMV benchmark on B200.
+
+One step = one batch-1 decode pass over the linear layers of the synthetic
+2B-class hybrid decoder: 28 layers x {q 2048x2048, k 2048x512, v 2048x512,
+o 2048x2048, gate 2048x6144, up 2048x6144, down 6144x2048} at 4 bpw (196
+EXL3 mul_mats, distinct weights per layer: 660 MB of packed trellis, far
+above the 126 MB L2, so every step streams its weights from HBM).  Weights are
+seeded synthetic (uniform random trellis words, +-1 input signs, +-U(0.01,0.03)
+output scales), activations fp16 N(0,1).
+
+  value   algorithmic bytes of all steps / device time of the K timed steps
+          (weights resident in HBM; the 196 C-ABI calls of a step are captured
+          once in a CUDA graph and replayed)
+  e2e     the same metric through the host-buffer C-ABI entry
+          (exl3cu_mul_mat_host): every call copies its fp16 x from pinned host
+          memory and its f32 y back, inside the timed region
+  --impl reference   the reference's own CPU operator (ggml_exl3_mul_mat from
+          oracle/_ref, compiled from the reference's sources) on all host cores
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own replica of the
+sweep -- the path has no exchange step in decode -- so scaling is weak and the
+time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "xiaomi-hexagon-exl3_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "EXL3 4bpw GEMV HBM GB/s; 2B decode tok/s at 1 and 8 ragged reqs, 1-8 GPU"
+LAYERS = 28
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--bits", type=int, default=4)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--no-sweep", action="store_true", help="skip the 2/3/5/6-bit side measurements")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--e2e-steps", type=int, default=30)
+    return ap.parse_args(argv)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def shapes():
+    from exl3_b200.synthetic import LAYER_SHAPES
+
+    return list(LAYER_SHAPES.items())
+
+
+def algo_bytes(bits, rows=1):
+    from exl3_b200.synthetic import algorithmic_bytes
+
+    return sum(algorithmic_bytes(k, n, bits, rows) for _, (k, n) in shapes())
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks during the timed region
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *exc):
+        self.text = ""
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.text, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.text, _ = self.proc.communicate()
+        return False
+
+    def summary(self):
+        rows = [r for r in csv.reader(io.StringIO(getattr(self, "text", ""))) if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip().lower() == "active"})
+        loaded = sorted(sm)[len(sm) // 2:] if sm else []
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------------
+# workload
+
+def build_stack(torch, ops, bits, layers, device, seed):
+    """Seeded synthetic weights generated on the device, uploaded through the C ABI."""
+    g = torch.Generator(device=f"cuda:{device}")
+    g.manual_seed(seed)
+    dev = f"cuda:{device}"
+    entries = []
+    for layer in range(layers):
+        for name, (k, n) in shapes():
+            trellis = torch.randint(0, 65536, (k // 16, n // 16, 16 * bits), generator=g, device=dev,
+                                    dtype=torch.int32).to(torch.int16)
+            suh = (torch.randint(0, 2, (k,), generator=g, device=dev) * 2 - 1).to(torch.float16)
+            sign = (torch.randint(0, 2, (n,), generator=g, device=dev) * 2 - 1).float()
+            svh = (sign * (0.01 + 0.02 * torch.rand(n, generator=g, device=dev))).to(torch.float16)
+            w = ops.Exl3Weight.from_trellis(trellis, suh.view(torch.int16), svh.view(torch.int16), device=device)
+            x = torch.randn((1, k), generator=g, device=dev).to(torch.float16)
+            y = torch.empty((1, n), dtype=torch.float32, device=dev)
+            entries.append({"layer": layer, "name": name, "k": k, "n": n, "w": w, "x": x, "y": y,
+                            "trellis": trellis if layer == 0 else None, "suh": suh if layer == 0 else None,
+                            "svh": svh if layer == 0 else None})
+            del trellis
+    torch.cuda.synchronize(device)
+    return entries
+
+
+def time_graph(torch, dist, entries, steps, warmup, world):
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            for e in entries:
+                e["w"].mul_mat(e["x"], out=e["y"], stream=stream)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream, capture_error_mode="relaxed"):
+        for e in entries:
+            e["w"].mul_mat(e["x"], out=e["y"], stream=stream)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            graph.replay()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        end.record(stream)
+    end.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    del graph
+    return ms
+
+
+def time_e2e(torch, ops, entries, steps):
+    """Host-buffer C-ABI calls: pinned fp16 x in, f32 y out, copies inside the timed region."""
+    stream = torch.cuda.Stream()
+    hx = [e["x"].cpu().pin_memory() for e in entries]
+    hy = [torch.empty((1, e["n"]), dtype=torch.float32).pin_memory() for e in entries]
+    npx = [t.numpy() for t in hx]
+    npy = [t.numpy() for t in hy]
+
+    def step():
+        for e, x, y in zip(entries, npx, npy):
+            e["w"].mul_mat_host(x, out=y, synchronize=False, stream=stream)
+        stream.synchronize()
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    end.synchronize()
+    wall_ms = (time.perf_counter() - t0) * 1e3
+    h2d = sum(2 * e["k"] for e in entries)
+    d2h = sum(4 * e["n"] for e in entries)
+    return max(start.elapsed_time(end), wall_ms), h2d, d2h
+
+
+def kernel_durations(torch, entries, reps=20):
+    """Per-shape average kernel time (events around `reps` back-to-back calls of one shape on
+    one layer's weights after rotating through others -- a warm-ish, per-launch figure)."""
+    out = {}
+    stream = torch.cuda.Stream()
+    for name in dict(shapes()):
+        es = [e for e in entries if e["name"] == name]
+        with torch.cuda.stream(stream):
+            s, t = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            for e in es:
+                e["w"].mul_mat(e["x"], out=e["y"], stream=stream)
+            s.record(stream)
+            for _ in range(max(1, reps // len(es))):
+                for e in es:  # distinct layers: cold in L2 once the stack exceeds it
+                    e["w"].mul_mat(e["x"], out=e["y"], stream=stream)
+            t.record(stream)
+        t.synchronize()
+        out[name] = s.elapsed_time(t) / (max(1, reps // len(es)) * len(es))
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU legs
+
+def cpu_records(entries):
+    from exl3_b200.format import pack_records
+
+    recs = []
+    for e in entries:
+        if e["layer"] != 0:
+            continue
+        tr = e["trellis"].cpu().numpy().view("uint16")
+        su = e["suh"].cpu().numpy().view("uint16")
+        sv = e["svh"].cpu().numpy().view("uint16")
+        recs.append((e["k"], e["n"], pack_records(tr, su, sv, BITS_USED), e["x"].cpu().numpy()))
+    return recs
+
+
+BITS_USED = 4
+
+
+def cpu_layer_pass(ref, kind, recs, bits, nth):
+    for k, n, rec, x in recs:
+        if kind == "reference":
+            ref.mul_mat(rec, bits, k, n, x, nth=nth)
+        else:
+            ref.mul_mat(rec, bits, k, n, x, nth=nth)
+
+
+def cpu_checker():
+    from oracle.oracle import Oracle, Reference, have_reference, host_threads
+
+    if have_reference():
+        return Reference(), "reference", host_threads()
+    return Oracle(), "port", host_threads()
+
+
+def cpu_baseline(recs, bits, budget_s=8.0):
+    ref, kind, nth = cpu_checker()
+    layer_bytes = algo_bytes(bits)
+    cpu_layer_pass(ref, kind, recs, bits, nth)  # warm-up: builds the codebook tables
+    times = []
+    t_all = time.perf_counter()
+    while len(times) < 3 or (time.perf_counter() - t_all < budget_s and len(times) < 200):
+        t0 = time.perf_counter()
+        cpu_layer_pass(ref, kind, recs, bits, nth)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": layer_bytes / med / 1e9, "unit": "GB/s", "cores": nth, "kind": kind,
+            "sample": f"one decoder layer (7 matrices, 4 bpw, batch 1) of the same workload, "
+                      f"{len(times)} timed passes, median; ggml_exl3_mul_mat ith/nth split over {nth} threads"
+            if kind == "reference" else f"oracle port, one layer, {len(times)} passes, {nth} threads"}
+
+
+# ---------------------------------------------------------------------------------------------
+
+def run_reference_arm(args, rank, world):
+    import numpy as np
+
+    if world > 1 and rank != 0:
+        return
+    from exl3_b200 import synthetic
+    from exl3_b200.format import pack_records
+
+    ref, kind, nth = cpu_checker()
+    bits = args.bits
+    n_layers = 4  # distinct layers rotated per step (94 MB of records, beyond the host caches)
+    layers = []
+    for layer in range(n_layers):
+        recs = []
+        for i, (name, (k, n)) in enumerate(shapes()):
+            m = synthetic.matrix(k, n, bits, seed=10_000 * layer + i)
+            recs.append((k, n, pack_records(m.trellis, m.suh, m.svh, bits),
+                         synthetic.activations(1, k, seed=20_000 * layer + i)))
+        layers.append(recs)
+    for s in range(args.warmup):
+        cpu_layer_pass(ref, kind, layers[s % n_layers], bits, nth)
+    t0 = time.perf_counter()
+    for s in range(args.steps):
+        cpu_layer_pass(ref, kind, layers[s % n_layers], bits, nth)
+    dt = time.perf_counter() - t0
+    step_bytes = algo_bytes(bits)
+    value = step_bytes * args.steps / dt / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"configs[1] per-layer GEMV sweep at {bits} bpw, batch 1; one step = one decoder "
+                               f"layer (7 matrices) rotating over {n_layers} seeded layers",
+                   "bits": bits, "rows": 1, "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": nth, "kind": kind,
+                         "sample": "ggml_exl3_mul_mat (reference sources, oracle/_ref) with ith/nth over "
+                                   f"{nth} threads" if kind == "reference" else "oracle port"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    _ = np
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    from exl3_b200 import ops
+
+    global BITS_USED
+    BITS_USED = args.bits
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device(f"cuda:{local}"))
+    pk, pk_kind = peaks()
+    entries = build_stack(torch, ops, args.bits, args.layers, local, seed=1234 + 7919 * rank)
+    step_bytes = algo_bytes(args.bits) * args.layers
+    launches_per_step = len(entries)
+
+    with ClockSampler(local) as clk:
+        ms = time_graph(torch, dist, entries, args.steps, args.warmup, world)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = step_bytes * world / (ms_step * 1e-3) / 1e9
+
+    e2e_ms, h2d, d2h = time_e2e(torch, ops, entries, args.e2e_steps)
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = step_bytes * world / (e2e_ms / args.e2e_steps * 1e-3) / 1e9
+
+    per_shape_ms = kernel_durations(torch, entries)
+    sweep = {}
+    if not args.no_sweep:
+        other = [b for b in (2, 3, 5, 6) if b != args.bits]
+        for b in other:
+            es = build_stack(torch, ops, b, args.layers, local, seed=99 + b)
+            sms = time_graph(torch, dist, es, max(10, args.steps // 4), 5, world)
+            sweep[str(b)] = round(algo_bytes(b) * args.layers / (sms / max(10, args.steps // 4) * 1e-3) / 1e9, 1)
+            for e in es:
+                e["w"].free()
+            del es
+            torch.cuda.empty_cache()
+        sweep[str(args.bits)] = round(value / world, 1)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(cpu_records(entries), args.bits)
+
+    traffic = None
+    tf = ROOT / "profiles" / "gemv_traffic.json"
+    if tf.exists():
+        try:
+            traffic = json.loads(tf.read_text()).get("traffic_bytes_per_step_4bpw")
+        except (ValueError, AttributeError):
+            traffic = None
+
+    peak_hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    per_gpu = value / world
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp16",
+            "data": "synthetic",
+            "config": {
+                "workload": f"configs[1]: batch-1 decode GEMV sweep, {args.layers} layers x "
+                            "{q,k,v,o,gate,up,down} of the 2B decoder",
+                "bits": args.bits, "rows": 1, "layers": args.layers, "matrices_per_step": launches_per_step,
+                "weights_mb_per_step": round(step_bytes / 1e6, 1),
+                "l2": "no flush: each step streams %.0f MB of distinct weights, > 126 MB L2" % (step_bytes / 1e6),
+                "activations": "fp16 N(0,1)", "accumulate": "fp32", "parallelism": f"dp{world} replicas",
+                "timing": "CUDA graph of the step's C-ABI calls, replayed; CUDA events on the replay stream",
+            },
+            "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak_hbm, "unit": "GB/s",
+                         "frac": round(per_gpu / peak_hbm, 4), "traffic": traffic,
+                         "peak_source": f"{pk_kind} hbm_gbs", "kernel": "exl3cu::k_gemv<4, mul1>",
+                         "per_shape_kernel_us": {k: round(v * 1e3, 2) for k, v in per_shape_ms.items()}},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "api": "exl3cu_mul_mat_host (pinned host buffers)",
+                    "ms_per_step": round(e2e_ms / args.e2e_steps, 4)},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+            "sweep_gbs_by_bits": sweep,
+        }
+        print(json.dumps(line), flush=True)
+    for e in entries:
+        e["w"].free()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,130 @@
+/*
+ * exl3cu -- C ABI of the B200 (sm_100a) EXL3 packed-weight matmul library.
+ *
+ * Plain pointers and sizes only.  Every entry returns an int status
+ * (enum exl3cu_status) and never throws; exl3cu_last_error() gives the
+ * detail of the last failure on the calling thread.  Calls taking a
+ * `stream` are stream-ordered (a cudaStream_t, NULL = legacy default stream)
+ * and do not synchronise unless stated.  Pointers named d_* are device
+ * memory of the weight's device; h_* are host memory.
+ *
+ * Reference interfaces each entry replaces (jyohukuchan/xiaomi-hexagon-exl3):
+ *   codec      include/exl3_codec.h:10-29 (exl3::decode_codebook/decode_inner/
+ *              hadamard128/reconstruct) -- host-pointer C++ versions of these
+ *              are in include/exl3_codec.h of this library.
+ *   operator   ggml_exl3_mul_mat, include/exl3-block.h:46 / src/exl3-ggml.cpp:51-92,
+ *              and the device operator op_exl3_matmul, src/exl3-htp.c:159-232,
+ *              whose HTP_STATUS_* codes the statuses below mirror.
+ *   weights    the runtime group records of include/exl3-block.h:14,34-39
+ *              (tools/export_native_gguf.py:27-36) or the upstream trellis/suh/svh
+ *              tensors (src/exl3_model.cpp:79-157), loaded once into persistent
+ *              device buffers (the role the ggml backend buffer plays upstream).
+ */
+#ifndef EXL3CU_H
+#define EXL3CU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EXL3CU_ABI_VERSION 1
+
+/* Mirrors HTP_STATUS_{OK, INVAL_PARAMS, NO_SUPPORT, VTCM_TOO_SMALL, INTERNAL_ERR}
+ * of src/exl3-htp.c:159-232 (VTCM_TOO_SMALL's analogue is device memory). */
+enum exl3cu_status {
+    EXL3CU_OK = 0,
+    EXL3CU_INVALID_ARGUMENT = 1,
+    EXL3CU_NO_SUPPORT = 2,
+    EXL3CU_OUT_OF_MEMORY = 3,
+    EXL3CU_CUDA_ERROR = 4
+};
+
+/* Activation dtypes: the ggml type ids (GGML_TYPE_F32 = 0, GGML_TYPE_F16 = 1). */
+enum exl3cu_dtype { EXL3CU_F32 = 0, EXL3CU_F16 = 1 };
+
+/* exl3::Codebook (include/exl3_codec.h:8). */
+enum exl3cu_codebook { EXL3CU_CB_3INST = 0, EXL3CU_CB_MCG = 1, EXL3CU_CB_MUL1 = 2 };
+
+typedef struct exl3cu_weight exl3cu_weight;
+
+int exl3cu_abi_version(void);
+const char * exl3cu_status_string(int status);
+const char * exl3cu_last_error(void);
+
+/* ---- codec on device buffers ----------------------------------------------------- */
+
+/* d_out[i] = exl3::decode_codebook(d_states[i], codebook)   (src/exl3_codec.cpp:68-86) */
+int exl3cu_decode_codebook(const uint16_t * d_states, size_t count, unsigned codebook, uint16_t * d_out,
+                           void * stream);
+
+/* exl3::decode_inner_slice: upstream trellis [k/16][n/16][16*bits] -> row-major fp16
+ * [k][column_count], bit-exact (src/exl3_codec.cpp:123-145). */
+int exl3cu_decode_inner(const uint16_t * d_packed, size_t k, size_t n, size_t first_column, size_t column_count,
+                        unsigned bits, unsigned codebook, uint16_t * d_out, void * stream);
+
+/* exl3::hadamard128 in place on count (multiple of 128) fp32 values (src/exl3_codec.cpp:147-167). */
+int exl3cu_hadamard128(float * d_values, size_t count, void * stream);
+
+/* exl3::reconstruct_slice: original-basis fp16 [k][column_count] (src/exl3_codec.cpp:169-204). */
+int exl3cu_reconstruct(const uint16_t * d_packed, const uint16_t * d_suh, const uint16_t * d_svh, size_t k,
+                       size_t n, size_t first_column, size_t column_count, unsigned bits, unsigned codebook,
+                       uint16_t * d_out, void * stream);
+
+/* ---- persistent device weights ----------------------------------------------------- */
+
+/* Load column blocks [first_block, first_block + block_count) of a k x n matrix
+ * (block_count 0 = all) from runtime group records -- n/128 * k/128 records of
+ * 2048*bits + 512 bytes, record (nb,kb) at nb*(k/128)+kb (include/exl3-block.h:14).
+ * `records` may be host or device memory.  Synchronises the device. */
+int exl3cu_weight_from_records(const void * records, size_t record_bytes, size_t k, size_t n, unsigned bits,
+                               unsigned codebook, size_t first_block, size_t block_count, int device,
+                               exl3cu_weight ** out);
+
+/* Same from the upstream tensors: trellis [k/16][n/16][16*bits] uint16, suh [k], svh [n] fp16. */
+int exl3cu_weight_from_trellis(const uint16_t * trellis, const uint16_t * suh, const uint16_t * svh, size_t k,
+                               size_t n, unsigned bits, unsigned codebook, size_t first_block, size_t block_count,
+                               int device, exl3cu_weight ** out);
+
+int exl3cu_weight_free(exl3cu_weight * w);
+
+/* n_local = 128 * block_count columns held by this handle. */
+int exl3cu_weight_info(const exl3cu_weight * w, size_t * k, size_t * n_local, unsigned * bits, unsigned * codebook,
+                       size_t * device_bytes);
+
+/* Decode the handle's device-layout weights back to row-major inner fp16 [k][n_local]. */
+int exl3cu_weight_decode_inner(const exl3cu_weight * w, uint16_t * d_out, void * stream);
+
+/* ---- the operator ---------------------------------------------------------------- */
+
+/* y[r][0..n_local) = x[r] . W for r < rows (ggml_exl3_mul_mat semantics,
+ * src/exl3-ggml.cpp:51-92): x rows of k f32/f16 values (x_dtype), row stride
+ * x_row_stride elements; y rows of n_local f32, stride y_row_stride.  Uses the
+ * handle's own split-K workspace: calls on one handle must be ordered on one
+ * stream (or otherwise serialised) by the caller. */
+int exl3cu_mul_mat(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
+                   float * d_y, size_t y_row_stride, void * stream);
+
+/* Bytes of split-K workspace exl3cu_mul_mat_ws needs for this handle (any rows). */
+size_t exl3cu_mul_mat_workspace_bytes(const exl3cu_weight * w);
+
+/* As exl3cu_mul_mat with a caller-owned workspace of at least
+ * exl3cu_mul_mat_workspace_bytes(w) bytes, zero-filled once before its first use
+ * (the operator leaves it zeroed again).  Lets independent streams share one handle. */
+int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
+                      float * d_y, size_t y_row_stride, void * d_workspace, size_t workspace_bytes, void * stream);
+
+/* Host-buffer form: copies x to the device, runs the operator, copies y back.
+ * With synchronize != 0 it returns after y is in h_y (the ggml operator's
+ * contract); otherwise the copies are only stream-ordered and h_x/h_y should be
+ * pinned.  Staging buffers are owned by the handle. */
+int exl3cu_mul_mat_host(exl3cu_weight * w, const void * h_x, int x_dtype, size_t rows, size_t x_row_stride,
+                        float * h_y, size_t y_row_stride, int synchronize, void * stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXL3CU_H */

@@ -1,0 +1,126 @@
+"""GPU parity of the codec kernels against the oracle and the reference's golden
+vectors.  Integer work is bit-exact: codebooks over all 65536 states, inner
+decode for bits 1..8 x 3 codebooks, the device-layout conversion.  H128 and
+reconstruct follow the reference's fp32 operation order and are compared
+bit-for-bit as well, with the reference's own tolerances as the floor."""
+import hashlib
+
+import numpy as np
+import pytest
+
+import kat
+
+pytestmark = pytest.mark.gpu
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+@pytest.fixture(scope="module")
+def ops(cuda_lib):
+    from exl3_b200 import ops as _ops
+
+    return _ops
+
+
+@pytest.mark.parametrize("cb", range(3))
+def test_codebook_exhaustive(ops, oracle, golden, cb):
+    _, meta = golden
+    table = ops.decode_codebook(np.arange(65536, dtype=np.uint16), cb)
+    mismatches = np.nonzero(table != oracle.codebook_table(cb))[0]
+    assert mismatches.size == 0, f"{mismatches.size} states differ, first {mismatches[:8]}"
+    assert sha(table) == meta[f"cb_sha256_{cb}"]
+
+
+@pytest.mark.parametrize("bits", range(1, 9))
+def test_decode_inner_golden(ops, oracle, golden, bits):
+    data, meta = golden
+    packed = kat.kat_packed(bits)
+    for cb in range(3):
+        inner = ops.decode_inner(packed, kat.KAT_K, kat.KAT_N, bits, cb)
+        assert np.array_equal(inner[:2], data[f"inner_head_{bits}_{cb}"])
+        assert sha(inner) == meta[f"inner_sha256_{bits}_{cb}"], (bits, cb)
+
+
+@pytest.mark.parametrize("bits", range(1, 9))
+def test_device_layout_roundtrip(ops, oracle, bits):
+    """Upstream tensors and runtime records both land in the device layout; decoding it back
+    gives the reference's inner matrix bit for bit, for whole matrices and column-block slices."""
+    from exl3_b200 import format as fmt
+
+    rng = np.random.default_rng(100 + bits)
+    k, n = 384, 512
+    packed = rng.integers(0, 65536, (k // 16, n // 16, 16 * bits), dtype=np.uint16)
+    suh = rng.choice([-1.0, 1.0], k).astype(np.float16).view(np.uint16)
+    svh = (rng.choice([-1.0, 1.0], n) * rng.uniform(0.01, 0.03, n)).astype(np.float16).view(np.uint16)
+    for cb in range(3):
+        ref = oracle.decode_inner(packed, k, n, bits, cb)
+        w = ops.Exl3Weight.from_trellis(packed, suh, svh, codebook=cb)
+        assert np.array_equal(w.decode_inner(), ref), (bits, cb)
+        w.free()
+    rec = fmt.pack_records(packed, suh, svh, bits)
+    w = ops.Exl3Weight.from_records(rec, k, n, bits, codebook=2, first_block=1, block_count=2)
+    assert w.n == 256
+    assert np.array_equal(w.decode_inner(), oracle.decode_inner(packed, k, n, bits, 2)[:, 128:384])
+    w.free()
+
+
+def test_decode_inner_slices_and_random(ops, oracle):
+    rng = np.random.default_rng(5)
+    for bits in (2, 3, 5, 7):
+        k, n = 16 * int(rng.integers(1, 20)), 16 * int(rng.integers(2, 30))
+        packed = rng.integers(0, 65536, (k // 16, n // 16, 16 * bits), dtype=np.uint16)
+        first = 16 * int(rng.integers(0, n // 16))
+        count = 16 * int(rng.integers(1, (n - first) // 16 + 1))
+        got = ops.decode_inner(packed, k, n, bits, 2, first_column=first, column_count=count)
+        assert np.array_equal(got, oracle.decode_inner(packed, k, n, bits, 2, first, count))
+
+
+def test_zero_ring_decode(ops, oracle):
+    for bits in range(1, 9):
+        for cb in range(3):
+            tile = ops.decode_inner(np.zeros(16 * bits, np.uint16), 16, 16, bits, cb)
+            assert np.all(tile == oracle.decode_codebook(np.array([0]), cb)[0])
+
+
+def test_invalid_codec_arguments(ops):
+    from exl3_b200 import Exl3InvalidArgument
+
+    with pytest.raises(Exl3InvalidArgument):
+        ops.decode_inner(np.zeros(64, np.uint16), 16, 16, 0, 2)
+    with pytest.raises(Exl3InvalidArgument):
+        ops.decode_inner(np.zeros(64, np.uint16), 16, 16, 4, 3)
+    with pytest.raises(Exl3InvalidArgument):  # slice past the end (reference tests/test_codec.cpp:86)
+        ops.decode_inner(np.zeros(64, np.uint16), 16, 16, 4, 2, first_column=16, column_count=16)
+    with pytest.raises(Exl3InvalidArgument):
+        ops.hadamard128(np.zeros(100, np.float32))
+
+
+def test_hadamard128_bit_exact(ops, oracle, golden):
+    data, meta = golden
+    blocks = kat.kat_h128_blocks()
+    h = ops.hadamard128(blocks)
+    assert sha(h) == meta["h128_sha256"]
+    assert np.array_equal(h[5], data["h128_block5"])
+    v = np.array([(i % 19 - 9) / 17 for i in range(256)], np.float32)
+    assert np.max(np.abs(ops.hadamard128(ops.hadamard128(v)) - v)) < 1e-6
+
+
+@pytest.mark.parametrize("bits", range(1, 9))
+def test_reconstruct_golden(ops, oracle, golden, bits):
+    _, meta = golden
+    k, n = kat.KAT_K, kat.KAT_N
+    packed = kat.kat_packed(bits)
+    suh, svh = kat.kat_scales()
+    for cb in range(3):
+        got = ops.reconstruct(packed, suh, svh, k, n, bits, cb)
+        ref = oracle.reconstruct(packed, suh, svh, k, n, bits, cb)
+        g = got.view(np.float16).astype(np.float64)
+        r = ref.view(np.float16).astype(np.float64)
+        rel = np.max(np.abs(g - r)) / np.max(np.abs(r))
+        nmse = np.sum((g - r) ** 2) / np.sum(r ** 2)
+        assert rel <= 2e-3 and nmse <= 1e-6  # reference tools/exl3_verify.cpp:44-69 bars
+        assert sha(got) == meta[f"recon_sha256_{bits}_{cb}"], (bits, cb)
+    sl = ops.reconstruct(packed, suh, svh, k, n, bits, 2, first_column=128, column_count=256)
+    assert np.array_equal(sl, oracle.reconstruct(packed, suh, svh, k, n, bits, 2, 128, 256))

@@ -1,0 +1,227 @@
+"""GPU parity of the EXL3 operator (the GEMV hot path) against the oracle.
+
+Tolerance (north star): max|y - y_ref| / max|y_ref| <= 2e-3 with fp32
+accumulation, plus the reference graph test's NMSE < 1e-5
+(tests/test-exl3-graph.cpp:100).  The CUDA path rotates activations in fp32
+and feeds them to the tensor cores as fp16 (as the reference's HMX path does),
+which sets its error floor around 3e-4 max-abs-rel.
+"""
+import numpy as np
+import pytest
+import torch
+
+import kat
+
+pytestmark = pytest.mark.gpu
+
+TOL_MAX_ABS_REL = 2e-3
+TOL_NMSE = 1e-5
+
+
+def errs(y, ref):
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    rel = np.max(np.abs(y - ref)) / max(np.max(np.abs(ref)), 1e-30)
+    nmse = np.sum((y - ref) ** 2) / max(np.sum(ref ** 2), 1e-300)
+    return rel, nmse
+
+
+def assert_close(y, ref, what=""):
+    assert np.all(np.isfinite(y)), what
+    rel, nmse = errs(y, ref)
+    assert rel <= TOL_MAX_ABS_REL and nmse < TOL_NMSE, f"{what}: max_abs_rel={rel:.3e} nmse={nmse:.3e}"
+
+
+@pytest.fixture(scope="module")
+def ops(cuda_lib):
+    from exl3_b200 import ops as _ops
+
+    return _ops
+
+
+def _mm(ops, w, x):
+    xt = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    y = w.mul_mat(xt)
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+@pytest.mark.parametrize("bits", range(1, 9))
+def test_mul_mat_golden(ops, golden, bits):
+    """Against ggml_exl3_mul_mat's own output (4/6/8-bit) or the reference-codec loop."""
+    from exl3_b200 import format as fmt
+
+    data, _ = golden
+    k, n = kat.KAT_K, kat.KAT_N
+    suh, svh = kat.kat_scales()
+    rec = fmt.pack_records(kat.kat_packed(bits), suh, svh, bits)
+    w = ops.Exl3Weight.from_records(rec, k, n, bits)
+    for rows in ((1, 4, 8) if bits in (4, 6, 8) else (1, 4)):
+        x = kat.kat_input(rows)
+        assert_close(_mm(ops, w, x), data[f"mm_y_b{bits}_r{rows}"], f"bits={bits} rows={rows}")
+    x16 = kat.kat_input(1).astype(np.float16)
+    assert_close(_mm(ops, w, x16), data[f"mm_y16_b{bits}_r1"], f"bits={bits} f16")
+    w.free()
+
+
+def test_mul_mat_golden_codebooks(ops, golden):
+    from exl3_b200 import format as fmt
+
+    data, _ = golden
+    k, n = kat.KAT_K, kat.KAT_N
+    suh, svh = kat.kat_scales()
+    rec = fmt.pack_records(kat.kat_packed(4), suh, svh, 4)
+    for cb in (0, 1):
+        w = ops.Exl3Weight.from_records(rec, k, n, 4, codebook=cb)
+        assert_close(_mm(ops, w, kat.kat_input(1)), data[f"mm_cb{cb}_b4_r1"], f"cb={cb}")
+        w.free()
+
+
+def test_config0_single_layer(ops, oracle):
+    """2048 x 6144, 4 bpw, mul1, fp16 N(0,1) batch 1."""
+    from exl3_b200 import synthetic
+
+    m = synthetic.matrix(2048, 6144, 4, seed=0)
+    rec = m.records()
+    w = ops.Exl3Weight.from_records(rec, 2048, 6144, 4)
+    inner = w.decode_inner()
+    assert np.array_equal(inner, oracle.decode_inner(m.trellis, 2048, 6144, 4, 2))
+    x = synthetic.activations(1, 2048, seed=1)
+    ref = oracle.mul_mat(rec, 4, 2048, 6144, x, nth=8)
+    assert_close(_mm(ops, w, x), ref, "config0")
+    w.free()
+
+
+@pytest.mark.parametrize("bits", (2, 3, 4, 5, 6))
+def test_config1_layer_sweep(ops, oracle, bits):
+    """every per-layer shape of the 2B decoder at 2..6 bpw, batch 1."""
+    from exl3_b200 import synthetic
+
+    for i, (name, (k, n)) in enumerate(synthetic.LAYER_SHAPES.items()):
+        m = synthetic.matrix(k, n, bits, seed=1000 * bits + i)
+        rec = m.records()
+        w = ops.Exl3Weight.from_records(rec, k, n, bits)
+        x = synthetic.activations(1, k, seed=7 + i)
+        assert_close(_mm(ops, w, x), oracle.mul_mat(rec, bits, k, n, x, nth=8), f"{name} {k}x{n} @{bits}")
+        w.free()
+
+
+@pytest.mark.parametrize("rows", (2, 3, 7, 8, 9, 13, 37))
+def test_batches(ops, oracle, rows):
+    from exl3_b200 import synthetic
+
+    k, n, bits = 1024, 768, 4
+    m = synthetic.matrix(k, n, bits, seed=rows)
+    rec = m.records()
+    w = ops.Exl3Weight.from_records(rec, k, n, bits)
+    x = synthetic.activations(rows, k, seed=rows + 1)
+    assert_close(_mm(ops, w, x), oracle.mul_mat(rec, bits, k, n, x, nth=8), f"rows={rows}")
+    xf = x.astype(np.float32)
+    assert_close(_mm(ops, w, xf), oracle.mul_mat(rec, bits, k, n, xf, nth=8), f"rows={rows} f32")
+    w.free()
+
+
+def test_strided_rows_and_column_slices(ops, oracle):
+    from exl3_b200 import synthetic
+
+    k, n, bits = 768, 1024, 3
+    m = synthetic.matrix(k, n, bits, seed=11)
+    rec = m.records()
+    x = synthetic.activations(5, k, seed=12)
+    ref = oracle.mul_mat(rec, bits, k, n, x, nth=8)
+    w = ops.Exl3Weight.from_records(rec, k, n, bits)
+    xpad = torch.zeros((5, k + 64), dtype=torch.float16, device="cuda")
+    xpad[:, :k] = torch.from_numpy(x).cuda()
+    ypad = torch.full((5, n + 128), float("nan"), dtype=torch.float32, device="cuda")
+    w.mul_mat(xpad[:, :k], out=ypad[:, :n])
+    torch.cuda.synchronize()
+    yp = ypad.cpu().numpy()
+    assert_close(yp[:, :n], ref, "strided")
+    assert np.all(np.isnan(yp[:, n:])), "wrote outside y rows"
+    w.free()
+    # a handle holding column blocks [2, 5) computes exactly those columns
+    ws = ops.Exl3Weight.from_records(rec, k, n, bits, first_block=2, block_count=3)
+    assert_close(_mm(ops, ws, x), ref[:, 256:640], "column slice")
+    ws.free()
+
+
+def test_deterministic_and_workspace_reuse(ops):
+    from exl3_b200 import synthetic
+
+    k, n, bits = 4096, 1024, 4
+    m = synthetic.matrix(k, n, bits, seed=3)
+    w = ops.Exl3Weight.from_records(m.records(), k, n, bits)
+    assert w.workspace_bytes > 0  # this shape splits K
+    x = torch.from_numpy(synthetic.activations(1, k, seed=4)).cuda()
+    first = w.mul_mat(x).clone()
+    outs = [w.mul_mat(x) for _ in range(20)]
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o, first)
+    ws = torch.zeros(w.workspace_bytes // 4 + 4, dtype=torch.float32, device="cuda")
+    for _ in range(3):
+        assert torch.equal(w.mul_mat(x, workspace=ws), first)
+    w.free()
+
+
+def test_host_buffer_path(ops, oracle):
+    from exl3_b200 import synthetic
+
+    k, n, bits = 2048, 2048, 4
+    m = synthetic.matrix(k, n, bits, seed=21)
+    rec = m.records()
+    w = ops.Exl3Weight.from_records(rec, k, n, bits)
+    x = synthetic.activations(3, k, seed=22)
+    y_host = w.mul_mat_host(x)
+    assert np.array_equal(y_host, _mm(ops, w, x))
+    assert_close(y_host, oracle.mul_mat(rec, bits, k, n, x, nth=8), "host path")
+    w.free()
+
+
+def test_large_matrix_config4(ops, oracle):
+    """configs[4] shape: [4096, 14336] weight (k=14336, n=4096) at 4 bpw, batch 1 and 8."""
+    from exl3_b200 import synthetic
+
+    k, n, bits = 14336, 4096, 4
+    m = synthetic.matrix(k, n, bits, seed=44)
+    rec = m.records()
+    w = ops.Exl3Weight.from_records(rec, k, n, bits)
+    for rows in (1, 8):
+        x = synthetic.activations(rows, k, seed=45 + rows)
+        assert_close(_mm(ops, w, x), oracle.mul_mat(rec, bits, k, n, x, nth=16), f"config4 rows={rows}")
+    w.free()
+
+
+def test_linearity_full_size(ops):
+    """Size-independent property at a full BASELINE size: y(a x1 + b x2) = a y(x1) + b y(x2)."""
+    from exl3_b200 import synthetic
+
+    k, n, bits = 6144, 2048, 4
+    m = synthetic.matrix(k, n, bits, seed=9)
+    w = ops.Exl3Weight.from_records(m.records(), k, n, bits)
+    x1 = torch.from_numpy(synthetic.activations(1, k, seed=1).astype(np.float32)).cuda()
+    x2 = torch.from_numpy(synthetic.activations(1, k, seed=2).astype(np.float32)).cuda()
+    y = w.mul_mat(0.5 * x1 + 0.25 * x2)
+    y12 = 0.5 * w.mul_mat(x1) + 0.25 * w.mul_mat(x2)
+    torch.cuda.synchronize()
+    rel, _ = errs(y.cpu().numpy(), y12.cpu().numpy())
+    assert rel < 2e-3
+    w.free()
+
+
+def test_invalid_mul_mat_arguments(ops):
+    from exl3_b200 import Exl3InvalidArgument, synthetic
+
+    m = synthetic.matrix(256, 256, 4, seed=1)
+    w = ops.Exl3Weight.from_records(m.records(), 256, 256, 4)
+    with pytest.raises(Exl3InvalidArgument):
+        w.mul_mat(torch.zeros((1, 255), dtype=torch.float16, device="cuda"))
+    with pytest.raises(Exl3InvalidArgument):  # host memory handed to the device entry point
+        from exl3_b200 import _lib
+        import ctypes
+
+        x = np.zeros((1, 256), np.float16)
+        y = np.zeros((1, 256), np.float32)
+        _lib.check(_lib.lib().exl3cu_mul_mat(w.handle, ctypes.c_void_p(x.ctypes.data), 1, 1, 256,
+                                             ctypes.c_void_p(y.ctypes.data), 256, None))
+    w.free()

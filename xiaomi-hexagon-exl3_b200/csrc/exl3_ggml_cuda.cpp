@@ -1,0 +1,81 @@
+// ggml_exl3_mul_mat for ggml's CPU backend, executed on a B200 through the
+// exl3cu C ABI.  Drop-in for the reference's src/exl3-ggml.cpp:51-92: same
+// symbol, same tensor contract (src0 EXL3_4/6/8 [k, n] runtime records, src1
+// F32/F16 [k, r1, r2, r3] with byte strides nb[], dst F32 [n, r1, r2, r3]),
+// same GGML_ASSERT checks.
+//
+// ggml calls an op from nth threads with ith = 0..nth-1 and joins them on a
+// barrier before the next op.  Thread 0 alone drives the GPU -- it uploads the
+// weight on first sight (cached by data pointer, shape and type for the life
+// of the process, as ggml treats weights as immutable once loaded), stages
+// the activations, runs the operator and copies y back before returning (on
+// the legacy default stream, synchronised); the other threads return at once
+// and wait on ggml's barrier.
+//
+// Device: EXL3CU_DEVICE (default 0).  Built in a llama.cpp tree this file
+// compiles against upstream's ggml.h / ggml-cpu-impl.h; the standalone build
+// uses the stand-ins in csrc/ggml_stub.
+#include "exl3-block.h"
+#include "exl3cu.h"
+#include "ggml-cpu-impl.h"
+#include "ggml.h"
+
+#include <cstdio>
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+namespace {
+
+std::mutex g_mu;
+std::map<std::tuple<const void *, int, int64_t, int64_t>, exl3cu_weight *> g_weights;
+
+int target_device() {
+    const char * env = std::getenv("EXL3CU_DEVICE");
+    return env ? std::atoi(env) : 0;
+}
+
+[[noreturn]] void die(const char * what, int rc) {
+    std::fprintf(stderr, "exl3cu: %s failed (%s): %s\n", what, exl3cu_status_string(rc), exl3cu_last_error());
+    std::abort();
+}
+
+exl3cu_weight * weight_for(const ggml_tensor * w, unsigned bits, size_t k, size_t n) {
+    const auto key = std::make_tuple(static_cast<const void *>(w->data), int(w->type), int64_t(k), int64_t(n));
+    std::lock_guard<std::mutex> g(g_mu);
+    auto it = g_weights.find(key);
+    if (it != g_weights.end()) return it->second;
+    exl3cu_weight * h = nullptr;
+    const size_t bytes = (k / 128) * (n / 128) * exl3_group_bytes(bits);
+    int rc = exl3cu_weight_from_records(w->data, bytes, k, n, bits, EXL3CU_CB_MUL1, 0, 0, target_device(), &h);
+    if (rc) die("uploading EXL3 weight", rc);
+    g_weights[key] = h;
+    return h;
+}
+
+}  // namespace
+
+extern "C" void ggml_exl3_mul_mat(const ggml_compute_params * params, ggml_tensor * dst) {
+    const ggml_tensor * weight = dst->src[0];
+    const ggml_tensor * input = dst->src[1];
+    const size_t k = size_t(weight->ne[0]), n = size_t(weight->ne[1]);
+    const unsigned bits = exl3_type_bits(weight->type);
+    GGML_ASSERT(bits && k % 128 == 0 && n % 128 == 0 && weight->ne[2] == 1 && weight->ne[3] == 1);
+    GGML_ASSERT(input->type == GGML_TYPE_F32 || input->type == GGML_TYPE_F16);
+    if (params->ith != 0) return;
+    const size_t es = input->type == GGML_TYPE_F32 ? 4 : 2;
+    GGML_ASSERT(size_t(input->ne[0]) == k && input->nb[0] == es && dst->nb[0] == 4 && size_t(dst->ne[0]) == n);
+    GGML_ASSERT(input->nb[1] % es == 0 && dst->nb[1] % 4 == 0);
+    exl3cu_weight * h = weight_for(weight, bits, k, n);
+    const int dtype = input->type == GGML_TYPE_F32 ? EXL3CU_F32 : EXL3CU_F16;
+    for (int64_t i3 = 0; i3 < input->ne[3]; ++i3) {
+        for (int64_t i2 = 0; i2 < input->ne[2]; ++i2) {
+            const char * x = static_cast<const char *>(input->data) + i2 * input->nb[2] + i3 * input->nb[3];
+            char * y = static_cast<char *>(dst->data) + i2 * dst->nb[2] + i3 * dst->nb[3];
+            const int rc = exl3cu_mul_mat_host(h, x, dtype, size_t(input->ne[1]), input->nb[1] / es,
+                                               reinterpret_cast<float *>(y), dst->nb[1] / 4, 1, nullptr);
+            if (rc) die("ggml_exl3_mul_mat", rc);
+        }
+    }
+}

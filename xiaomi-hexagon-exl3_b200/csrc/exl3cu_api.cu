@@ -1,0 +1,467 @@
+// C ABI of libexl3cu (include/exl3cu.h): validation, persistent weight
+// handles, workspace management and launches.  Mirrors the argument checks of
+// the reference's device operator op_exl3_matmul (src/exl3-htp.c:160-190) and
+// codec (src/exl3_codec.cpp:12-19, 117-135), returning status codes instead of
+// asserting or throwing.
+#include "exl3cu.h"
+#include "exl3cu_internal.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+
+using namespace exl3cu;
+
+struct exl3cu_weight {
+    int device;
+    size_t k;
+    size_t n_total;
+    size_t first_block;
+    size_t nblocks;
+    unsigned bits;
+    unsigned codebook;
+    int sms;
+    uint32_t * lsc;
+    __half * su;
+    __half * sv;
+    void * ws;           // split-K workspace (partials + zeroed counters)
+    size_t ws_bytes;
+    GemvPlan plan;       // for rows = 8 (cps/splits do not depend on rows)
+    void * stage_x;      // host-form staging
+    size_t stage_x_bytes;
+    float * stage_y;
+    size_t stage_y_bytes;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char * fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char * what) {
+    (void)cudaGetLastError();  // clear a non-sticky error so the context stays usable
+    return fail(e == cudaErrorMemoryAllocation ? EXL3CU_OUT_OF_MEMORY : EXL3CU_CUDA_ERROR, "%s: %s", what,
+                cudaGetErrorString(e));
+}
+
+#define CU_TRY(expr, what)                                     \
+    do {                                                       \
+        cudaError_t _e = (expr);                               \
+        if (_e != cudaSuccess) return cuda_fail(_e, (what));   \
+    } while (0)
+
+bool valid_codec(unsigned bits, unsigned cb) { return bits >= 1 && bits <= 8 && cb <= 2; }
+
+bool valid_shape(size_t k, size_t n, size_t multiple) {
+    return k && n && k % multiple == 0 && n % multiple == 0 && k <= SIZE_MAX / n;
+}
+
+// A device pointer of `device` (or managed memory); rejects host pointers,
+// which a kernel could not dereference.
+int check_device_ptr(const void * p, int device, const char * name) {
+    if (!p) return fail(EXL3CU_INVALID_ARGUMENT, "%s is NULL", name);
+    cudaPointerAttributes attr;
+    cudaError_t e = cudaPointerGetAttributes(&attr, p);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        return fail(EXL3CU_INVALID_ARGUMENT, "%s is not a CUDA pointer", name);
+    }
+    if (attr.type == cudaMemoryTypeManaged) return EXL3CU_OK;
+    if (attr.type != cudaMemoryTypeDevice)
+        return fail(EXL3CU_INVALID_ARGUMENT, "%s must be device memory (got host/unregistered memory)", name);
+    if (device >= 0 && attr.device != device)
+        return fail(EXL3CU_INVALID_ARGUMENT, "%s lives on device %d, expected device %d", name, attr.device, device);
+    return EXL3CU_OK;
+}
+
+int current_device(int * dev) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    return EXL3CU_OK;
+}
+
+// Makes `device` current for the scope and restores the caller's device after.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&prev) != cudaSuccess) { ok = false; return; }
+        if (prev != device && cudaSetDevice(device) != cudaSuccess) ok = false;
+    }
+    ~DeviceGuard() {
+        int cur;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int device_sms(int device) {
+    static std::mutex mu;
+    static int cache[64] = {0};
+    std::lock_guard<std::mutex> g(mu);
+    if (device < 0 || device >= 64) return 148;
+    if (!cache[device]) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0) v = 148;
+        cache[device] = v;
+    }
+    return cache[device];
+}
+
+void release(exl3cu_weight * w) {
+    if (!w) return;
+    DeviceGuard g(w->device);
+    cudaFree(w->lsc);
+    cudaFree(w->su);
+    cudaFree(w->sv);
+    cudaFree(w->ws);
+    cudaFree(w->stage_x);
+    cudaFree(w->stage_y);
+    delete w;
+}
+
+// Common tail of the two loaders: allocate, plan, zero the workspace.
+int make_weight(size_t k, size_t n, unsigned bits, unsigned cb, size_t first_block, size_t block_count, int device,
+                exl3cu_weight ** out, exl3cu_weight ** made) {
+    if (!out) return fail(EXL3CU_INVALID_ARGUMENT, "out is NULL");
+    *out = nullptr;
+    if (!valid_codec(bits, cb)) return fail(EXL3CU_INVALID_ARGUMENT, "bits must be 1..8 and codebook 0..2");
+    if (!valid_shape(k, n, 128)) return fail(EXL3CU_INVALID_ARGUMENT, "k and n must be nonzero multiples of 128");
+    if (k > 65536 || n > 1048576)
+        return fail(EXL3CU_NO_SUPPORT, "k <= 65536 and n <= 1048576 (the reference operator's limits)");
+    const size_t nb_all = n / 128;
+    if (block_count == 0) block_count = nb_all - (first_block < nb_all ? first_block : nb_all);
+    if (first_block >= nb_all || block_count == 0 || block_count > nb_all - first_block)
+        return fail(EXL3CU_INVALID_ARGUMENT, "column block range [%zu, +%zu) outside %zu blocks", first_block,
+                    block_count, nb_all);
+    int ndev = 0;
+    CU_TRY(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+    if (device < 0 || device >= ndev) return fail(EXL3CU_INVALID_ARGUMENT, "device %d not present", device);
+    auto * w = new (std::nothrow) exl3cu_weight();
+    if (!w) return fail(EXL3CU_OUT_OF_MEMORY, "host allocation");
+    w->device = device;
+    w->k = k;
+    w->n_total = n;
+    w->first_block = first_block;
+    w->nblocks = block_count;
+    w->bits = bits;
+    w->codebook = cb;
+    w->sms = device_sms(device);
+    w->plan = plan_gemv(w->sms, k, block_count, 8);
+    w->ws_bytes = gemv_workspace_bytes(block_count, w->plan.splits);
+    const size_t lsc_bytes = block_count * (k / 16) * 256u * bits;
+    cudaError_t e = cudaMalloc(&w->lsc, lsc_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&w->su, k * sizeof(__half));
+    if (e == cudaSuccess) e = cudaMalloc(&w->sv, block_count * 128 * sizeof(__half));
+    if (e == cudaSuccess && w->ws_bytes) e = cudaMalloc(&w->ws, w->ws_bytes);
+    if (e == cudaSuccess && w->ws_bytes) e = cudaMemset(w->ws, 0, w->ws_bytes);
+    if (e != cudaSuccess) {
+        release(w);
+        return cuda_fail(e, "allocating device weights");
+    }
+    *made = w;
+    return EXL3CU_OK;
+}
+
+int validate_mm(const exl3cu_weight * w, const void * x, int x_dtype, size_t rows, size_t x_stride, const float * y,
+                size_t y_stride) {
+    if (!w) return fail(EXL3CU_INVALID_ARGUMENT, "weight handle is NULL");
+    if (x_dtype != EXL3CU_F32 && x_dtype != EXL3CU_F16)
+        return fail(EXL3CU_INVALID_ARGUMENT, "x dtype must be F32 (0) or F16 (1)");
+    if (!rows) return fail(EXL3CU_INVALID_ARGUMENT, "rows must be >= 1");
+    const size_t n_local = w->nblocks * 128;
+    if (x_stride < w->k || y_stride < n_local) return fail(EXL3CU_INVALID_ARGUMENT, "row stride shorter than a row");
+    if (x_stride % 4 || y_stride % 4) return fail(EXL3CU_INVALID_ARGUMENT, "row strides must be multiples of 4 elements");
+    const size_t xa = x_dtype == EXL3CU_F32 ? 16 : 8;
+    if (reinterpret_cast<uintptr_t>(x) % xa) return fail(EXL3CU_INVALID_ARGUMENT, "x must be %zu-byte aligned", xa);
+    if (reinterpret_cast<uintptr_t>(y) % 16) return fail(EXL3CU_INVALID_ARGUMENT, "y must be 16-byte aligned");
+    return EXL3CU_OK;
+}
+
+int run_mm(const exl3cu_weight * w, const void * x, int x_dtype, size_t rows, size_t x_stride, float * y,
+           size_t y_stride, void * ws, cudaStream_t st) {
+    GemvArgs a{};
+    a.lsc = w->lsc;
+    a.su = w->su;
+    a.sv = w->sv;
+    a.x_f16 = x_dtype == EXL3CU_F16;
+    a.x_stride = (long long)x_stride;
+    a.y_stride = (long long)y_stride;
+    a.nblocks = int(w->nblocks);
+    a.nchunks = int(w->k / 16);
+    a.cps = w->plan.cps;
+    a.splits = w->plan.splits;
+    if (a.splits > 1) {
+        a.ws_partial = static_cast<float *>(ws);
+        a.ws_count = reinterpret_cast<unsigned *>(static_cast<char *>(ws) + w->nblocks * size_t(a.splits) * 8 * 128 *
+                                                                               sizeof(float));
+    }
+    const size_t es = x_dtype == EXL3CU_F32 ? 4 : 2;
+    for (size_t r0 = 0; r0 < rows; r0 += 8) {
+        const int rb = int(rows - r0 < 8 ? rows - r0 : 8);
+        GemvPlan p = plan_gemv(w->sms, w->k, w->nblocks, rb);
+        p.cps = w->plan.cps;
+        p.splits = w->plan.splits;
+        a.rows = rb;
+        a.x = static_cast<const char *>(x) + r0 * x_stride * es;
+        a.y = y + r0 * y_stride;
+        cudaError_t e = launch_gemv(a, p, w->bits, w->codebook, st);
+        if (e != cudaSuccess) return cuda_fail(e, "launching the EXL3 GEMV");
+    }
+    return EXL3CU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int exl3cu_abi_version(void) { return EXL3CU_ABI_VERSION; }
+
+const char * exl3cu_status_string(int status) {
+    switch (status) {
+        case EXL3CU_OK: return "ok";
+        case EXL3CU_INVALID_ARGUMENT: return "invalid argument";
+        case EXL3CU_NO_SUPPORT: return "not supported";
+        case EXL3CU_OUT_OF_MEMORY: return "out of device memory";
+        case EXL3CU_CUDA_ERROR: return "CUDA error";
+        default: return "unknown status";
+    }
+}
+
+const char * exl3cu_last_error(void) { return g_last_error.c_str(); }
+
+int exl3cu_decode_codebook(const uint16_t * d_states, size_t count, unsigned codebook, uint16_t * d_out,
+                           void * stream) {
+    if (codebook > 2) return fail(EXL3CU_INVALID_ARGUMENT, "Unknown EXL3 codebook");
+    if (!count) return EXL3CU_OK;
+    int dev, rc;
+    if ((rc = current_device(&dev))) return rc;
+    if ((rc = check_device_ptr(d_states, dev, "states"))) return rc;
+    if ((rc = check_device_ptr(d_out, dev, "out"))) return rc;
+    CU_TRY(launch_codebook(d_states, count, codebook, d_out, static_cast<cudaStream_t>(stream)), "codebook kernel");
+    return EXL3CU_OK;
+}
+
+int exl3cu_decode_inner(const uint16_t * d_packed, size_t k, size_t n, size_t first_column, size_t column_count,
+                        unsigned bits, unsigned codebook, uint16_t * d_out, void * stream) {
+    if (!valid_codec(bits, codebook)) return fail(EXL3CU_INVALID_ARGUMENT, "EXL3 integer bitrate must be in [1,8]");
+    if (!valid_shape(k, n, 16)) return fail(EXL3CU_INVALID_ARGUMENT, "Invalid EXL3 matrix dimensions");
+    if (!column_count || first_column % 16 || column_count % 16 || first_column > n ||
+        column_count > n - first_column)
+        return fail(EXL3CU_INVALID_ARGUMENT, "Invalid EXL3 column slice");
+    int dev, rc;
+    if ((rc = current_device(&dev))) return rc;
+    if ((rc = check_device_ptr(d_packed, dev, "packed"))) return rc;
+    if ((rc = check_device_ptr(d_out, dev, "out"))) return rc;
+    if (reinterpret_cast<uintptr_t>(d_out) % 16) return fail(EXL3CU_INVALID_ARGUMENT, "out must be 16-byte aligned");
+    CU_TRY(launch_decode_inner(d_packed, k, n, first_column, column_count, bits, codebook, d_out,
+                               static_cast<cudaStream_t>(stream)),
+           "decode kernel");
+    return EXL3CU_OK;
+}
+
+int exl3cu_hadamard128(float * d_values, size_t count, void * stream) {
+    if (count % 128) return fail(EXL3CU_INVALID_ARGUMENT, "H128 length must be a multiple of 128");
+    if (!count) return EXL3CU_OK;
+    int dev, rc;
+    if ((rc = current_device(&dev))) return rc;
+    if ((rc = check_device_ptr(d_values, dev, "values"))) return rc;
+    if (reinterpret_cast<uintptr_t>(d_values) % 16) return fail(EXL3CU_INVALID_ARGUMENT, "values must be 16-byte aligned");
+    CU_TRY(launch_hadamard128(d_values, count, static_cast<cudaStream_t>(stream)), "hadamard kernel");
+    return EXL3CU_OK;
+}
+
+int exl3cu_reconstruct(const uint16_t * d_packed, const uint16_t * d_suh, const uint16_t * d_svh, size_t k,
+                       size_t n, size_t first_column, size_t column_count, unsigned bits, unsigned codebook,
+                       uint16_t * d_out, void * stream) {
+    if (!valid_shape(k, n, 128)) return fail(EXL3CU_INVALID_ARGUMENT, "Invalid EXL3 matrix dimensions");
+    if (first_column % 128 || column_count % 128)
+        return fail(EXL3CU_INVALID_ARGUMENT, "H128 slices must align to 128 columns");
+    int rc = exl3cu_decode_inner(d_packed, k, n, first_column, column_count, bits, codebook, d_out, stream);
+    if (rc) return rc;
+    int dev;
+    if ((rc = current_device(&dev))) return rc;
+    if ((rc = check_device_ptr(d_suh, dev, "suh"))) return rc;
+    if ((rc = check_device_ptr(d_svh, dev, "svh"))) return rc;
+    CU_TRY(launch_reconstruct_blocks(d_out, k, column_count, first_column, d_suh, d_svh,
+                                     static_cast<cudaStream_t>(stream)),
+           "reconstruct kernel");
+    return EXL3CU_OK;
+}
+
+int exl3cu_weight_from_records(const void * records, size_t record_bytes, size_t k, size_t n, unsigned bits,
+                               unsigned codebook, size_t first_block, size_t block_count, int device,
+                               exl3cu_weight ** out) {
+    if (!records) return fail(EXL3CU_INVALID_ARGUMENT, "records is NULL");
+    if (!valid_shape(k, n, 128) || bits < 1 || bits > 8)
+        return fail(EXL3CU_INVALID_ARGUMENT, "k, n must be multiples of 128 and bits 1..8");
+    const size_t group_bytes = 2048u * bits + 512u;
+    if ((k / 128) * (n / 128) * group_bytes > record_bytes)
+        return fail(EXL3CU_INVALID_ARGUMENT, "record buffer holds %zu bytes, need %zu", record_bytes,
+                    (k / 128) * (n / 128) * group_bytes);
+    DeviceGuard guard(device);
+    if (!guard.ok) return fail(EXL3CU_INVALID_ARGUMENT, "cannot select device %d", device);
+    exl3cu_weight * w = nullptr;
+    int rc = make_weight(k, n, bits, codebook, first_block, block_count, device, out, &w);
+    if (rc) return rc;
+    // stage only the records of the selected column blocks (contiguous: nb-major)
+    const size_t kb_count = k / 128;
+    const size_t span = w->nblocks * kb_count * group_bytes;
+    const uint8_t * src = static_cast<const uint8_t *>(records) + w->first_block * kb_count * group_bytes;
+    uint8_t * staged = nullptr;
+    cudaError_t e = cudaMalloc(&staged, span);
+    if (e == cudaSuccess) e = cudaMemcpy(staged, src, span, cudaMemcpyDefault);
+    if (e == cudaSuccess) e = launch_records_to_lsc(staged, k, bits, 0, w->nblocks, w->lsc, nullptr);
+    // su from records (0..kb) of the first staged block, sv from record (nb, 0) of each block
+    if (e == cudaSuccess)
+        e = cudaMemcpy2D(w->su, 256, staged + 2048u * bits, group_bytes, 256, kb_count, cudaMemcpyDeviceToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy2D(w->sv, 256, staged + 2048u * bits + 256u, kb_count * group_bytes, 256, w->nblocks,
+                         cudaMemcpyDeviceToDevice);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaFree(staged);
+    if (e != cudaSuccess) {
+        release(w);
+        return cuda_fail(e, "uploading EXL3 records");
+    }
+    *out = w;
+    return EXL3CU_OK;
+}
+
+int exl3cu_weight_from_trellis(const uint16_t * trellis, const uint16_t * suh, const uint16_t * svh, size_t k,
+                               size_t n, unsigned bits, unsigned codebook, size_t first_block, size_t block_count,
+                               int device, exl3cu_weight ** out) {
+    if (!trellis || !suh || !svh) return fail(EXL3CU_INVALID_ARGUMENT, "trellis, suh and svh are required");
+    DeviceGuard guard(device);
+    if (!guard.ok) return fail(EXL3CU_INVALID_ARGUMENT, "cannot select device %d", device);
+    exl3cu_weight * w = nullptr;
+    int rc = make_weight(k, n, bits, codebook, first_block, block_count, device, out, &w);
+    if (rc) return rc;
+    const size_t tbytes = k * n * bits / 8;
+    uint16_t * staged = nullptr;
+    cudaError_t e = cudaMalloc(&staged, tbytes);
+    if (e == cudaSuccess) e = cudaMemcpy(staged, trellis, tbytes, cudaMemcpyDefault);
+    if (e == cudaSuccess) e = launch_trellis_to_lsc(staged, k, n, bits, w->first_block, w->nblocks, w->lsc, nullptr);
+    if (e == cudaSuccess) e = cudaMemcpy(w->su, suh, k * 2, cudaMemcpyDefault);
+    if (e == cudaSuccess) e = cudaMemcpy(w->sv, svh + w->first_block * 128, w->nblocks * 256, cudaMemcpyDefault);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaFree(staged);
+    if (e != cudaSuccess) {
+        release(w);
+        return cuda_fail(e, "uploading EXL3 trellis");
+    }
+    *out = w;
+    return EXL3CU_OK;
+}
+
+int exl3cu_weight_free(exl3cu_weight * w) {
+    release(w);
+    return EXL3CU_OK;
+}
+
+int exl3cu_weight_info(const exl3cu_weight * w, size_t * k, size_t * n_local, unsigned * bits, unsigned * codebook,
+                       size_t * device_bytes) {
+    if (!w) return fail(EXL3CU_INVALID_ARGUMENT, "weight handle is NULL");
+    if (k) *k = w->k;
+    if (n_local) *n_local = w->nblocks * 128;
+    if (bits) *bits = w->bits;
+    if (codebook) *codebook = w->codebook;
+    if (device_bytes)
+        *device_bytes = w->nblocks * (w->k / 16) * 256u * w->bits + w->k * 2 + w->nblocks * 256 + w->ws_bytes;
+    return EXL3CU_OK;
+}
+
+int exl3cu_weight_decode_inner(const exl3cu_weight * w, uint16_t * d_out, void * stream) {
+    if (!w) return fail(EXL3CU_INVALID_ARGUMENT, "weight handle is NULL");
+    int rc = check_device_ptr(d_out, w->device, "out");
+    if (rc) return rc;
+    if (reinterpret_cast<uintptr_t>(d_out) % 16) return fail(EXL3CU_INVALID_ARGUMENT, "out must be 16-byte aligned");
+    DeviceGuard guard(w->device);
+    CU_TRY(launch_lsc_decode(w->lsc, w->k, w->nblocks, w->bits, w->codebook, d_out, static_cast<cudaStream_t>(stream)),
+           "device-layout decode kernel");
+    return EXL3CU_OK;
+}
+
+size_t exl3cu_mul_mat_workspace_bytes(const exl3cu_weight * w) { return w ? w->ws_bytes : 0; }
+
+int exl3cu_mul_mat(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
+                   float * d_y, size_t y_row_stride, void * stream) {
+    int rc = validate_mm(w, d_x, x_dtype, rows, x_row_stride, d_y, y_row_stride);
+    if (rc) return rc;
+    if ((rc = check_device_ptr(d_x, w->device, "x"))) return rc;
+    if ((rc = check_device_ptr(d_y, w->device, "y"))) return rc;
+    DeviceGuard guard(w->device);
+    return run_mm(w, d_x, x_dtype, rows, x_row_stride, d_y, y_row_stride, w->ws, static_cast<cudaStream_t>(stream));
+}
+
+int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
+                      float * d_y, size_t y_row_stride, void * d_workspace, size_t workspace_bytes, void * stream) {
+    int rc = validate_mm(w, d_x, x_dtype, rows, x_row_stride, d_y, y_row_stride);
+    if (rc) return rc;
+    if (workspace_bytes < w->ws_bytes)
+        return fail(EXL3CU_INVALID_ARGUMENT, "workspace of %zu bytes, need %zu", workspace_bytes, w->ws_bytes);
+    if (w->ws_bytes) {
+        if ((rc = check_device_ptr(d_workspace, w->device, "workspace"))) return rc;
+        if (reinterpret_cast<uintptr_t>(d_workspace) % 16)
+            return fail(EXL3CU_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+    }
+    if ((rc = check_device_ptr(d_x, w->device, "x"))) return rc;
+    if ((rc = check_device_ptr(d_y, w->device, "y"))) return rc;
+    DeviceGuard guard(w->device);
+    return run_mm(w, d_x, x_dtype, rows, x_row_stride, d_y, y_row_stride, d_workspace,
+                  static_cast<cudaStream_t>(stream));
+}
+
+int exl3cu_mul_mat_host(exl3cu_weight * w, const void * h_x, int x_dtype, size_t rows, size_t x_row_stride,
+                        float * h_y, size_t y_row_stride, int synchronize, void * stream) {
+    if (!h_x || !h_y) return fail(EXL3CU_INVALID_ARGUMENT, "x and y are required");
+    if (!w) return fail(EXL3CU_INVALID_ARGUMENT, "weight handle is NULL");
+    if (x_dtype != EXL3CU_F32 && x_dtype != EXL3CU_F16)
+        return fail(EXL3CU_INVALID_ARGUMENT, "x dtype must be F32 (0) or F16 (1)");
+    if (!rows) return fail(EXL3CU_INVALID_ARGUMENT, "rows must be >= 1");
+    const size_t n_local = w->nblocks * 128;
+    if (x_row_stride < w->k || y_row_stride < n_local)
+        return fail(EXL3CU_INVALID_ARGUMENT, "row stride shorter than a row");
+    DeviceGuard guard(w->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t es = x_dtype == EXL3CU_F32 ? 4 : 2;
+    const size_t xb = rows * w->k * es, yb = rows * n_local * sizeof(float);
+    if (w->stage_x_bytes < xb) {
+        CU_TRY(cudaStreamSynchronize(st), "synchronising before staging growth");
+        cudaFree(w->stage_x);
+        w->stage_x = nullptr;
+        w->stage_x_bytes = 0;
+        CU_TRY(cudaMalloc(&w->stage_x, xb), "allocating x staging");
+        w->stage_x_bytes = xb;
+    }
+    if (w->stage_y_bytes < yb) {
+        CU_TRY(cudaStreamSynchronize(st), "synchronising before staging growth");
+        cudaFree(w->stage_y);
+        w->stage_y = nullptr;
+        w->stage_y_bytes = 0;
+        CU_TRY(cudaMalloc(&w->stage_y, yb), "allocating y staging");
+        w->stage_y_bytes = yb;
+    }
+    CU_TRY(cudaMemcpy2DAsync(w->stage_x, w->k * es, h_x, x_row_stride * es, w->k * es, rows, cudaMemcpyHostToDevice, st),
+           "copying x to the device");
+    int rc = run_mm(w, w->stage_x, x_dtype, rows, w->k, w->stage_y, n_local, w->ws, st);
+    if (rc) return rc;
+    CU_TRY(cudaMemcpy2DAsync(h_y, y_row_stride * sizeof(float), w->stage_y, n_local * sizeof(float),
+                             n_local * sizeof(float), rows, cudaMemcpyDeviceToHost, st),
+           "copying y to the host");
+    if (synchronize) CU_TRY(cudaStreamSynchronize(st), "synchronising the stream");
+    return EXL3CU_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,20 @@
+"""B200-native EXL3 packed-weight matmul: Python face of the libexl3cu C ABI.
+
+The compute lives in hand-written sm_100a CUDA (``csrc/``) behind
+``include/exl3cu.h``; this package binds it for tests, benchmarks and
+torch-based callers.  Importing it does not touch the GPU; the first call
+loads ``libexl3cu.so`` and fails loudly if it is missing.
+"""
+from . import format, synthetic  # noqa: F401
+from ._lib import (CB_3INST, CB_MCG, CB_MUL1, F16, F32, Exl3Error,  # noqa: F401
+                   Exl3InvalidArgument, lib)
+
+__all__ = ["format", "synthetic", "lib", "Exl3Error", "Exl3InvalidArgument", "CB_3INST", "CB_MCG", "CB_MUL1",
+           "F16", "F32"]
+
+
+def __getattr__(name):
+    if name in ("ops", "Exl3Weight"):
+        from . import ops
+        return ops if name == "ops" else ops.Exl3Weight
+    raise AttributeError(name)

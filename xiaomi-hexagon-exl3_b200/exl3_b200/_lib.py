@@ -1,0 +1,92 @@
+"""ctypes binding of libexl3cu.so, the C ABI declared in include/exl3cu.h.
+
+The library is built in-tree (``xiaomi-hexagon-exl3_b200/build.py``); there is
+no fallback: if it is missing or fails to load, :func:`lib` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parents[1]
+LIB_PATH = PKG_DIR / "libexl3cu.so"
+GGML_LIB_PATH = PKG_DIR / "libexl3cu_ggml.so"
+
+OK, INVALID_ARGUMENT, NO_SUPPORT, OUT_OF_MEMORY, CUDA_ERROR = range(5)
+F32, F16 = 0, 1
+CB_3INST, CB_MCG, CB_MUL1 = 0, 1, 2
+
+# every symbol include/exl3cu.h declares
+EXPORTS = (
+    "exl3cu_abi_version", "exl3cu_status_string", "exl3cu_last_error",
+    "exl3cu_decode_codebook", "exl3cu_decode_inner", "exl3cu_hadamard128", "exl3cu_reconstruct",
+    "exl3cu_weight_from_records", "exl3cu_weight_from_trellis", "exl3cu_weight_free", "exl3cu_weight_info",
+    "exl3cu_weight_decode_inner", "exl3cu_mul_mat", "exl3cu_mul_mat_workspace_bytes", "exl3cu_mul_mat_ws",
+    "exl3cu_mul_mat_host",
+)
+
+
+class Exl3Error(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"exl3cu status {status}: {message}")
+        self.status = status
+
+
+class Exl3InvalidArgument(Exl3Error, ValueError):
+    pass
+
+
+_LIB = None
+
+_c = ctypes
+_vp = _c.c_void_p
+_sz = _c.c_size_t
+
+
+def _declare(L):
+    L.exl3cu_abi_version.restype = _c.c_int
+    L.exl3cu_status_string.restype = _c.c_char_p
+    L.exl3cu_status_string.argtypes = [_c.c_int]
+    L.exl3cu_last_error.restype = _c.c_char_p
+    L.exl3cu_decode_codebook.argtypes = [_vp, _sz, _c.c_uint, _vp, _vp]
+    L.exl3cu_decode_inner.argtypes = [_vp, _sz, _sz, _sz, _sz, _c.c_uint, _c.c_uint, _vp, _vp]
+    L.exl3cu_hadamard128.argtypes = [_vp, _sz, _vp]
+    L.exl3cu_reconstruct.argtypes = [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _c.c_uint, _c.c_uint, _vp, _vp]
+    L.exl3cu_weight_from_records.argtypes = [_vp, _sz, _sz, _sz, _c.c_uint, _c.c_uint, _sz, _sz, _c.c_int,
+                                             _c.POINTER(_vp)]
+    L.exl3cu_weight_from_trellis.argtypes = [_vp, _vp, _vp, _sz, _sz, _c.c_uint, _c.c_uint, _sz, _sz, _c.c_int,
+                                             _c.POINTER(_vp)]
+    L.exl3cu_weight_free.argtypes = [_vp]
+    L.exl3cu_weight_info.argtypes = [_vp, _c.POINTER(_sz), _c.POINTER(_sz), _c.POINTER(_c.c_uint),
+                                     _c.POINTER(_c.c_uint), _c.POINTER(_sz)]
+    L.exl3cu_weight_decode_inner.argtypes = [_vp, _vp, _vp]
+    L.exl3cu_mul_mat.argtypes = [_vp, _vp, _c.c_int, _sz, _sz, _vp, _sz, _vp]
+    L.exl3cu_mul_mat_workspace_bytes.restype = _sz
+    L.exl3cu_mul_mat_workspace_bytes.argtypes = [_vp]
+    L.exl3cu_mul_mat_ws.argtypes = [_vp, _vp, _c.c_int, _sz, _sz, _vp, _sz, _vp, _sz, _vp]
+    L.exl3cu_mul_mat_host.argtypes = [_vp, _vp, _c.c_int, _sz, _sz, _vp, _sz, _c.c_int, _vp]
+    non_status = ("exl3cu_status_string", "exl3cu_last_error", "exl3cu_mul_mat_workspace_bytes")
+    for name in EXPORTS:
+        if name not in non_status:
+            getattr(L, name).restype = _c.c_int
+
+
+def lib():
+    """Load (once) and return the C-ABI library; raises if it is not built."""
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is not built; run xiaomi-hexagon-exl3_b200/build.py")
+        L = _c.CDLL(str(LIB_PATH))
+        _declare(L)
+        _LIB = L
+    return _LIB
+
+
+def check(status: int) -> None:
+    if status == OK:
+        return
+    msg = lib().exl3cu_last_error().decode(errors="replace")
+    if status == INVALID_ARGUMENT:
+        raise Exl3InvalidArgument(status, msg)
+    raise Exl3Error(status, msg)

@@ -1,0 +1,195 @@
+"""Python face of the exl3cu C ABI: persistent EXL3 weights and the operator.
+
+Everything here calls into libexl3cu.so through ctypes; torch is used only for
+device memory and the current CUDA stream.  Mirrors the reference interface
+for this path: ``mul_mat`` is ``ggml_exl3_mul_mat`` (src/exl3-ggml.cpp:51-92,
+y = x . W with W = diag(su) H W_inner H diag(sv) per 128 block, f32 out), and
+the codec functions are those of include/exl3_codec.h:10-29.  Invalid
+arguments raise :class:`Exl3InvalidArgument` (a ValueError), as the reference
+raises std::invalid_argument.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import CB_MUL1, F16, F32, check, lib
+
+_vp = ctypes.c_void_p
+
+
+def _stream_handle(stream) -> _vp:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return _vp(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+
+
+def _ptr(t) -> _vp:
+    if isinstance(t, torch.Tensor):
+        return _vp(t.data_ptr())
+    if isinstance(t, np.ndarray):
+        return _vp(t.ctypes.data)
+    raise TypeError(f"unsupported buffer type {type(t)!r}")
+
+
+def _as_u16_tensor(a, device) -> torch.Tensor:
+    if isinstance(a, torch.Tensor):
+        t = a
+    else:
+        t = torch.from_numpy(np.ascontiguousarray(a).view(np.int16))
+    if t.dtype != torch.int16:
+        t = t.view(torch.int16) if t.element_size() == 2 else t
+    return t.to(device).contiguous()
+
+
+class Exl3Weight:
+    """An EXL3 matrix resident in device memory (column blocks [first_block, +block_count))."""
+
+    def __init__(self, handle: _vp, device: int):
+        self._h = handle
+        self.device = device
+        k, n_local, dev_bytes = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
+        bits, cb = ctypes.c_uint(), ctypes.c_uint()
+        check(lib().exl3cu_weight_info(self._h, ctypes.byref(k), ctypes.byref(n_local), ctypes.byref(bits),
+                                       ctypes.byref(cb), ctypes.byref(dev_bytes)))
+        self.k, self.n, self.bits, self.codebook = k.value, n_local.value, bits.value, cb.value
+        self.device_bytes = dev_bytes.value
+
+    # -- construction ------------------------------------------------------------------------
+    @classmethod
+    def from_records(cls, records, k: int, n: int, bits: int, codebook: int = CB_MUL1, device: int = 0,
+                     first_block: int = 0, block_count: int = 0) -> "Exl3Weight":
+        if isinstance(records, (bytes, bytearray)):
+            records = np.frombuffer(records, np.uint8)
+        if isinstance(records, np.ndarray):
+            records = np.ascontiguousarray(records)
+            nbytes = records.nbytes
+        else:
+            records = records.contiguous()
+            nbytes = records.numel() * records.element_size()
+        h = _vp()
+        check(lib().exl3cu_weight_from_records(_ptr(records), nbytes, k, n, bits, codebook, first_block,
+                                               block_count, device, ctypes.byref(h)))
+        return cls(h, device)
+
+    @classmethod
+    def from_trellis(cls, trellis, suh, svh, codebook: int = CB_MUL1, device: int = 0, first_block: int = 0,
+                     block_count: int = 0) -> "Exl3Weight":
+        if isinstance(trellis, torch.Tensor):  # host or device tensors; the ABI copies either
+            trellis, suh, svh = (t.contiguous() for t in (trellis, suh, svh))
+            if trellis.element_size() != 2 or suh.element_size() != 2 or svh.element_size() != 2:
+                raise TypeError("trellis, suh and svh must be 16-bit tensors")
+        else:
+            trellis = np.ascontiguousarray(np.asarray(trellis).view(np.uint16))
+            suh = np.ascontiguousarray(np.asarray(suh).view(np.uint16))
+            svh = np.ascontiguousarray(np.asarray(svh).view(np.uint16))
+        kt, nt, tw = trellis.shape
+        h = _vp()
+        check(lib().exl3cu_weight_from_trellis(_ptr(trellis), _ptr(suh), _ptr(svh), kt * 16, nt * 16, tw // 16,
+                                               codebook, first_block, block_count, device, ctypes.byref(h)))
+        return cls(h, device)
+
+    def free(self) -> None:
+        if getattr(self, "_h", None):
+            lib().exl3cu_weight_free(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    @property
+    def handle(self) -> _vp:
+        return self._h
+
+    @property
+    def workspace_bytes(self) -> int:
+        return lib().exl3cu_mul_mat_workspace_bytes(self._h)
+
+    # -- operator ------------------------------------------------------------------------------
+    def mul_mat(self, x: torch.Tensor, out: torch.Tensor | None = None, stream=None,
+                workspace: torch.Tensor | None = None) -> torch.Tensor:
+        """y = x . W for device tensors x [rows, k] (f32 or f16) -> y [rows, n] f32."""
+        if x.dtype not in (torch.float32, torch.float16):
+            raise TypeError("x must be float32 or float16")
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.stride(-1) != 1:
+            x2 = x2.contiguous()
+        rows = x2.shape[0]
+        if out is None:
+            out = torch.empty((rows, self.n), dtype=torch.float32, device=x.device)
+        dt = F32 if x.dtype == torch.float32 else F16
+        st = _stream_handle(stream)
+        if workspace is None:
+            check(lib().exl3cu_mul_mat(self._h, _ptr(x2), dt, rows, x2.stride(0), _ptr(out), out.stride(0), st))
+        else:
+            check(lib().exl3cu_mul_mat_ws(self._h, _ptr(x2), dt, rows, x2.stride(0), _ptr(out), out.stride(0),
+                                          _ptr(workspace), workspace.numel() * workspace.element_size(), st))
+        return out
+
+    def mul_mat_host(self, x: np.ndarray, out: np.ndarray | None = None, synchronize: bool = True,
+                     stream=None) -> np.ndarray:
+        """Host-buffer form (copies inside the call), the ggml CPU-backend contract."""
+        x = np.ascontiguousarray(x)
+        if x.dtype not in (np.float32, np.float16):
+            raise TypeError("x must be float32 or float16")
+        x2 = x.reshape(-1, x.shape[-1])
+        rows = x2.shape[0]
+        if out is None:
+            out = np.empty((rows, self.n), np.float32)
+        dt = F32 if x.dtype == np.float32 else F16
+        check(lib().exl3cu_mul_mat_host(self._h, _ptr(x2), dt, rows, x2.shape[1], _ptr(out), out.shape[1],
+                                        int(synchronize), _stream_handle(stream)))
+        return out
+
+    def decode_inner(self, stream=None) -> np.ndarray:
+        """The handle's device-layout weights decoded back to row-major inner fp16 bits [k, n]."""
+        out = torch.empty((self.k, self.n), dtype=torch.int16, device=f"cuda:{self.device}")
+        check(lib().exl3cu_weight_decode_inner(self._h, _ptr(out), _stream_handle(stream)))
+        torch.cuda.synchronize(self.device)
+        return out.cpu().numpy().view(np.uint16)
+
+
+# -- codec on device tensors (include/exl3_codec.h:10-29) ------------------------------------------
+
+def decode_codebook(states, codebook: int = CB_MUL1, device: int = 0) -> np.ndarray:
+    dev = f"cuda:{device}"
+    s = _as_u16_tensor(states, dev).reshape(-1)
+    out = torch.empty_like(s)
+    check(lib().exl3cu_decode_codebook(_ptr(s), s.numel(), codebook, _ptr(out), _stream_handle(None)))
+    return out.cpu().numpy().view(np.uint16)
+
+
+def decode_inner(packed, k: int, n: int, bits: int, codebook: int = CB_MUL1, first_column: int = 0,
+                 column_count: int | None = None, device: int = 0) -> np.ndarray:
+    dev = f"cuda:{device}"
+    p = _as_u16_tensor(packed, dev)
+    cc = n - first_column if column_count is None else column_count
+    out = torch.empty((k, max(cc, 0)), dtype=torch.int16, device=dev)
+    check(lib().exl3cu_decode_inner(_ptr(p), k, n, first_column, cc, bits, codebook, _ptr(out), _stream_handle(None)))
+    return out.cpu().numpy().view(np.uint16)
+
+
+def hadamard128(values, device: int = 0) -> np.ndarray:
+    t = torch.as_tensor(np.ascontiguousarray(values, np.float32)).to(f"cuda:{device}")
+    check(lib().exl3cu_hadamard128(_ptr(t), t.numel(), _stream_handle(None)))
+    return t.cpu().numpy()
+
+
+def reconstruct(packed, suh, svh, k: int, n: int, bits: int, codebook: int = CB_MUL1, first_column: int = 0,
+                column_count: int | None = None, device: int = 0) -> np.ndarray:
+    dev = f"cuda:{device}"
+    p, su, sv = (_as_u16_tensor(a, dev) for a in (packed, suh, svh))
+    cc = n - first_column if column_count is None else column_count
+    out = torch.empty((k, max(cc, 0)), dtype=torch.int16, device=dev)
+    check(lib().exl3cu_reconstruct(_ptr(p), _ptr(su), _ptr(sv), k, n, first_column, cc, bits, codebook, _ptr(out),
+                                   _stream_handle(None)))
+    return out.cpu().numpy().view(np.uint16)
+
+
+__all__ = ["Exl3Weight", "decode_codebook", "decode_inner", "hadamard128", "reconstruct", "_lib"]
