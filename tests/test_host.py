@@ -94,3 +94,10 @@ def test_synthetic_is_seeded():
     assert np.all((np.abs(sv) >= 0.0099) & (np.abs(sv) <= 0.0301))
     assert set(np.unique(a.suh.view(np.float16).astype(np.float32))) == {-1.0, 1.0}
     assert synthetic.algorithmic_bytes(2048, 6144, 4) == 6336512  # configs[0]
+
+
+def test_package_imports_without_gpu():
+    import exl3_b200
+    from exl3_b200 import ops
+
+    assert exl3_b200.ops is ops and exl3_b200.Exl3Weight is ops.Exl3Weight

@@ -14,7 +14,10 @@ __all__ = ["format", "synthetic", "lib", "Exl3Error", "Exl3InvalidArgument", "CB
 
 
 def __getattr__(name):
+    # ops imports torch; load it on first use only
     if name in ("ops", "Exl3Weight"):
-        from . import ops
-        return ops if name == "ops" else ops.Exl3Weight
+        import importlib
+
+        mod = importlib.import_module(".ops", __name__)
+        return mod if name == "ops" else mod.Exl3Weight
     raise AttributeError(name)
