@@ -123,6 +123,17 @@ int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, si
 int exl3cu_mul_mat_host(exl3cu_weight * w, const void * h_x, int x_dtype, size_t rows, size_t x_row_stride,
                         float * h_y, size_t y_row_stride, int synchronize, void * stream);
 
+/* No counterpart in the reference.  exl3cu_mul_mat for callers that may not
+ * allocate device memory: the split-K scratch is a fixed 4 MiB array inside the
+ * library (per GPU, for the life of the process) instead of a workspace.  The
+ * first call on a device resolves that array's address (make it before any
+ * stream capture); every call clears the part it needs first; calls that
+ * overlap on the GPU share the array and race, so order them on one stream.
+ * Returns EXL3CU_NO_SUPPORT when the weight's split-K plan needs more than the
+ * array holds. */
+int exl3cu_mul_mat_noalloc(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
+                           float * d_y, size_t y_row_stride, void * stream);
+
 #ifdef __cplusplus
 }
 #endif

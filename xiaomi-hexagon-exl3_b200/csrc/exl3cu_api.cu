@@ -465,3 +465,79 @@ int exl3cu_mul_mat_host(exl3cu_weight * w, const void * h_x, int x_dtype, size_t
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free operator entry.
+//
+// Some callers may not call cudaMalloc/cudaFree at all: a host framework that
+// owns and budgets every byte of device memory and plans its buffers before it
+// runs (ggml's backend scheduler works this way), or a latency-critical loop
+// that cannot afford the device-wide synchronisation cudaFree implies.  For
+// them, exl3cu_mul_mat_noalloc runs the split-K GEMV with its partial sums and
+// arrival tickets in the file-scope array below instead of a handle- or
+// caller-owned workspace.
+//
+// * Size: kStaticScratchBytes (4 MiB), held by every GPU that loads this
+//   library until the process exits.  A handle whose split-K plan needs more is
+//   rejected with EXL3CU_NO_SUPPORT and a message naming both sizes.
+// * Host code sees only a host-side stand-in for the array, so its device
+//   address is fetched with cudaGetSymbolAddress, once per device, with that
+//   device current -- done by the first call on each device, which should
+//   therefore come before any stream capture.
+// * Every call shares the array and it keeps the previous call's contents: each
+//   call clears the ticket counters it uses (cudaMemsetAsync on the caller's
+//   stream) before launching.  Calls whose executions overlap on the GPU -- on
+//   different streams, or from different threads without ordering -- race on
+//   the array and give wrong results; order them on one stream.
+// * Nothing here allocates: no cudaMalloc, cudaFree or allocating library call.
+// ---------------------------------------------------------------------------
+
+namespace {
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;
+}
+
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+namespace {
+
+std::mutex g_static_scratch_mu;
+void * g_static_scratch_dev[64] = {};
+
+// Device address of g_static_scratch on `device` (current on entry).
+int static_scratch_address(int device, void ** out) {
+    if (device < 0 || device >= 64) return fail(EXL3CU_NO_SUPPORT, "device index %d beyond 63", device);
+    std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+    if (!g_static_scratch_dev[device]) {
+        void * p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+        g_static_scratch_dev[device] = p;
+    }
+    *out = g_static_scratch_dev[device];
+    return EXL3CU_OK;
+}
+
+}  // namespace
+
+extern "C" int exl3cu_mul_mat_noalloc(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows,
+                                      size_t x_row_stride, float * d_y, size_t y_row_stride, void * stream) {
+    int rc = validate_mm(w, d_x, x_dtype, rows, x_row_stride, d_y, y_row_stride);
+    if (rc) return rc;
+    if ((rc = check_device_ptr(d_x, w->device, "x"))) return rc;
+    if ((rc = check_device_ptr(d_y, w->device, "y"))) return rc;
+    if (w->ws_bytes > kStaticScratchBytes)
+        return fail(EXL3CU_NO_SUPPORT, "this weight's split-K plan needs %zu bytes of scratch; the static scratch holds %zu",
+                    w->ws_bytes, kStaticScratchBytes);
+    DeviceGuard guard(w->device);
+    if (!guard.ok) return fail(EXL3CU_CUDA_ERROR, "cannot select device %d", w->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    void * scratch = nullptr;
+    if (w->ws_bytes) {
+        if ((rc = static_scratch_address(w->device, &scratch))) return rc;
+        // tickets follow the partials (run_mm's workspace layout) and must start at zero
+        const size_t partial_bytes = w->nblocks * size_t(w->plan.splits) * 8 * 128 * sizeof(float);
+        CU_TRY(cudaMemsetAsync(static_cast<char *>(scratch) + partial_bytes, 0, w->nblocks * sizeof(unsigned), st),
+               "clearing the static scratch tickets");
+    }
+    return run_mm(w, d_x, x_dtype, rows, x_row_stride, d_y, y_row_stride, scratch, st);
+}
