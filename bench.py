@@ -3,23 +3,30 @@
 
 One step = one batch-1 decode pass over the linear layers of the synthetic
 2B-class hybrid decoder: 28 layers x {q 2048x2048, k 2048x512, v 2048x512,
-o 2048x2048, gate 2048x6144, up 2048x6144, down 6144x2048} at 4 bpw (196
-EXL3 mul_mats, distinct weights per layer: 660 MB of packed trellis, far
+o 2048x2048, gate 2048x6144, up 2048x6144, down 6144x2048} at 4 bpw (196 EXL3
+mul_mats, distinct weights per layer: 680 MB of packed trellis per step, far
 above the 126 MB L2, so every step streams its weights from HBM).  Weights are
-seeded synthetic (uniform random trellis words, +-1 input signs, +-U(0.01,0.03)
-output scales), activations fp16 N(0,1).
+seeded synthetic (uniform random trellis words, +-1 input signs,
++-U(0.01,0.03) output scales), activations fp16 N(0,1).
 
-  value   algorithmic bytes of all steps / device time of the K timed steps
-          (weights resident in HBM; the 196 C-ABI calls of a step are captured
-          once in a CUDA graph and replayed)
+Launch patterns (every one computes the same 196 products):
+  decoder   per layer: {q,k,v} | {o} | {gate,up} | {down} -- the launches a
+            decoder layer can issue, since o and down wait for attention and the
+            activation function; 112 grouped launches per step (the headline)
+  matrix    one exl3cu_mul_mat launch per matrix, 196 per step
+  layer     one grouped launch per layer (7 problems), 28 per step
+Each pattern's step is captured once in a CUDA graph and replayed; launches
+chain with programmatic dependent launch.
+
+  value   algorithmic bytes of K steps / device time of K replays (decoder)
   e2e     the same metric through the host-buffer C-ABI entry
           (exl3cu_mul_mat_host): every call copies its fp16 x from pinned host
-          memory and its f32 y back, inside the timed region
+          memory and its f32 y back inside the timed region
   --impl reference   the reference's own CPU operator (ggml_exl3_mul_mat from
-          oracle/_ref, compiled from the reference's sources) on all host cores
+          oracle/_ref, built from the reference's sources) on all host cores
 
 Multi-GPU (torchrun, one rank per GPU): every rank runs its own replica of the
-sweep -- the path has no exchange step in decode -- so scaling is weak and the
+sweep -- batch-1 decode has no exchange step -- so scaling is weak and the
 time is the max over ranks.
 """
 from __future__ import annotations
@@ -43,6 +50,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "EXL3 4bpw GEMV HBM GB/s; 2B decode tok/s at 1 and 8 ragged reqs, 1-8 GPU"
 LAYERS = 28
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+DECODER_GROUPS = (("q", "k", "v"), ("o",), ("gate", "up"), ("down",))
 
 
 def parse_args(argv=None):
@@ -62,8 +70,7 @@ def parse_args(argv=None):
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
-        d = json.loads(p.read_text())
-        return d, "measured"
+        return json.loads(p.read_text()), "measured"
     return PEAKS_FALLBACK, "fallback"
 
 
@@ -79,10 +86,9 @@ def algo_bytes(bits, rows=1):
     return sum(algorithmic_bytes(k, n, bits, rows) for _, (k, n) in shapes())
 
 
-# ---------------------------------------------------------------------------------------------
-# clocks during the timed region
-
 class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every 50 ms around the timed region."""
+
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -90,6 +96,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.text = ""
 
     def __enter__(self):
         try:
@@ -102,7 +109,6 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.text = ""
         if self.proc is not None:
             time.sleep(0.1)
             self.proc.terminate()
@@ -114,11 +120,18 @@ class ClockSampler:
         return False
 
     def summary(self):
-        rows = [r for r in csv.reader(io.StringIO(getattr(self, "text", ""))) if len(r) >= 9]
+        rows = [r for r in csv.reader(io.StringIO(self.text)) if len(r) >= 9]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
-        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+
+        sm = [x for x in (num(r[1]) for r in rows) if x is not None]
+        mx = [x for x in (num(r[2]) for r in rows) if x is not None]
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip().lower() == "active"})
         loaded = sorted(sm)[len(sm) // 2:] if sm else []
@@ -129,13 +142,14 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------------
 # workload
 
-def build_stack(torch, ops, bits, layers, device, seed):
+def build_stack(torch, ops, bits, layers, device, seed, keep_host_layer0=False):
     """Seeded synthetic weights generated on the device, uploaded through the C ABI."""
-    g = torch.Generator(device=f"cuda:{device}")
-    g.manual_seed(seed)
     dev = f"cuda:{device}"
-    entries = []
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    stack = []
     for layer in range(layers):
+        mats = {}
         for name, (k, n) in shapes():
             trellis = torch.randint(0, 65536, (k // 16, n // 16, 16 * bits), generator=g, device=dev,
                                     dtype=torch.int32).to(torch.int16)
@@ -145,25 +159,48 @@ def build_stack(torch, ops, bits, layers, device, seed):
             w = ops.Exl3Weight.from_trellis(trellis, suh.view(torch.int16), svh.view(torch.int16), device=device)
             x = torch.randn((1, k), generator=g, device=dev).to(torch.float16)
             y = torch.empty((1, n), dtype=torch.float32, device=dev)
-            entries.append({"layer": layer, "name": name, "k": k, "n": n, "w": w, "x": x, "y": y,
-                            "trellis": trellis if layer == 0 else None, "suh": suh if layer == 0 else None,
-                            "svh": svh if layer == 0 else None})
+            host = None
+            if keep_host_layer0 and layer == 0:
+                host = (trellis.cpu().numpy().view("uint16"), suh.cpu().numpy().view("uint16"),
+                        svh.cpu().numpy().view("uint16"))
+            mats[name] = {"k": k, "n": n, "w": w, "x": x, "y": y, "host": host}
             del trellis
+        stack.append(mats)
     torch.cuda.synchronize(device)
-    return entries
+    return stack
 
 
-def time_graph(torch, dist, entries, steps, warmup, world):
+def step_launcher(ops, stack, pattern, stream):
+    """A callable issuing one step of `pattern` on `stream` (and its launch count)."""
+    if pattern == "matrix":
+        calls = [(m["w"], m["x"], m["y"]) for mats in stack for m in mats.values()]
+
+        def run():
+            for w, x, y in calls:
+                w.mul_mat(x, out=y, stream=stream)
+        return run, len(calls)
+    if pattern == "layer":
+        groups = [list(mats.values()) for mats in stack]
+    else:
+        groups = [[mats[name] for name in grp] for mats in stack for grp in DECODER_GROUPS]
+    packed = [([m["w"] for m in grp], [m["x"] for m in grp], [m["y"] for m in grp]) for grp in groups]
+
+    def run():
+        for ws, xs, ys in packed:
+            ops.mul_mat_batch(ws, xs, ys, stream=stream)
+    return run, len(packed)
+
+
+def time_pattern(torch, dist, ops, stack, pattern, steps, warmup, world):
     stream = torch.cuda.Stream()
+    run, launches = step_launcher(ops, stack, pattern, stream)
     with torch.cuda.stream(stream):
         for _ in range(3):
-            for e in entries:
-                e["w"].mul_mat(e["x"], out=e["y"], stream=stream)
+            run()
     stream.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream, capture_error_mode="relaxed"):
-        for e in entries:
-            e["w"].mul_mat(e["x"], out=e["y"], stream=stream)
+        run()
     with torch.cuda.stream(stream):
         for _ in range(warmup):
             graph.replay()
@@ -183,20 +220,21 @@ def time_graph(torch, dist, entries, steps, warmup, world):
         dist.barrier()
     ms = start.elapsed_time(end)
     del graph
-    return ms
+    return ms, launches
 
 
-def time_e2e(torch, ops, entries, steps):
+def time_e2e(torch, stack, steps):
     """Host-buffer C-ABI calls: pinned fp16 x in, f32 y out, copies inside the timed region."""
     stream = torch.cuda.Stream()
-    hx = [e["x"].cpu().pin_memory() for e in entries]
-    hy = [torch.empty((1, e["n"]), dtype=torch.float32).pin_memory() for e in entries]
+    mats = [m for layer in stack for m in layer.values()]
+    hx = [m["x"].cpu().pin_memory() for m in mats]
+    hy = [torch.empty((1, m["n"]), dtype=torch.float32).pin_memory() for m in mats]
     npx = [t.numpy() for t in hx]
     npy = [t.numpy() for t in hy]
 
     def step():
-        for e, x, y in zip(entries, npx, npy):
-            e["w"].mul_mat_host(x, out=y, synchronize=False, stream=stream)
+        for m, x, y in zip(mats, npx, npy):
+            m["w"].mul_mat_host(x, out=y, synchronize=False, stream=stream)
         stream.synchronize()
 
     for _ in range(3):
@@ -210,59 +248,33 @@ def time_e2e(torch, ops, entries, steps):
     end.record(stream)
     end.synchronize()
     wall_ms = (time.perf_counter() - t0) * 1e3
-    h2d = sum(2 * e["k"] for e in entries)
-    d2h = sum(4 * e["n"] for e in entries)
+    h2d = sum(2 * m["k"] for m in mats)
+    d2h = sum(4 * m["n"] for m in mats)
     return max(start.elapsed_time(end), wall_ms), h2d, d2h
 
 
-def kernel_durations(torch, entries, reps=20):
-    """Per-shape average kernel time (events around `reps` back-to-back calls of one shape on
-    one layer's weights after rotating through others -- a warm-ish, per-launch figure)."""
+def per_shape_us(torch, stack, reps=4):
+    """Average device time of one exl3cu_mul_mat per shape, back to back over distinct layers."""
     out = {}
     stream = torch.cuda.Stream()
-    for name in dict(shapes()):
-        es = [e for e in entries if e["name"] == name]
+    for name, _ in shapes():
+        ms = [layer[name] for layer in stack]
         with torch.cuda.stream(stream):
+            for m in ms:
+                m["w"].mul_mat(m["x"], out=m["y"], stream=stream)
             s, t = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            for e in es:
-                e["w"].mul_mat(e["x"], out=e["y"], stream=stream)
             s.record(stream)
-            for _ in range(max(1, reps // len(es))):
-                for e in es:  # distinct layers: cold in L2 once the stack exceeds it
-                    e["w"].mul_mat(e["x"], out=e["y"], stream=stream)
+            for _ in range(reps):
+                for m in ms:
+                    m["w"].mul_mat(m["x"], out=m["y"], stream=stream)
             t.record(stream)
         t.synchronize()
-        out[name] = s.elapsed_time(t) / (max(1, reps // len(es)) * len(es))
+        out[name] = round(s.elapsed_time(t) * 1e3 / (reps * len(ms)), 2)
     return out
 
 
 # ---------------------------------------------------------------------------------------------
-# CPU legs
-
-def cpu_records(entries):
-    from exl3_b200.format import pack_records
-
-    recs = []
-    for e in entries:
-        if e["layer"] != 0:
-            continue
-        tr = e["trellis"].cpu().numpy().view("uint16")
-        su = e["suh"].cpu().numpy().view("uint16")
-        sv = e["svh"].cpu().numpy().view("uint16")
-        recs.append((e["k"], e["n"], pack_records(tr, su, sv, BITS_USED), e["x"].cpu().numpy()))
-    return recs
-
-
-BITS_USED = 4
-
-
-def cpu_layer_pass(ref, kind, recs, bits, nth):
-    for k, n, rec, x in recs:
-        if kind == "reference":
-            ref.mul_mat(rec, bits, k, n, x, nth=nth)
-        else:
-            ref.mul_mat(rec, bits, k, n, x, nth=nth)
-
+# CPU legs (reference operator built from the reference's sources, or the oracle port)
 
 def cpu_checker():
     from oracle.oracle import Oracle, Reference, have_reference, host_threads
@@ -272,28 +284,35 @@ def cpu_checker():
     return Oracle(), "port", host_threads()
 
 
-def cpu_baseline(recs, bits, budget_s=8.0):
+def cpu_layer_pass(ref, recs, bits, nth):
+    for k, n, rec, x in recs:
+        ref.mul_mat(rec, bits, k, n, x, nth=nth)
+
+
+def cpu_baseline(stack, bits, budget_s=8.0):
+    from exl3_b200.format import pack_records
+
+    recs = []
+    for name, (k, n) in shapes():
+        m = stack[0][name]
+        tr, su, sv = m["host"]
+        recs.append((k, n, pack_records(tr, su, sv, bits), m["x"].cpu().numpy()))
     ref, kind, nth = cpu_checker()
-    layer_bytes = algo_bytes(bits)
-    cpu_layer_pass(ref, kind, recs, bits, nth)  # warm-up: builds the codebook tables
+    cpu_layer_pass(ref, recs, bits, nth)  # warm-up: builds the codebook tables
     times = []
     t_all = time.perf_counter()
     while len(times) < 3 or (time.perf_counter() - t_all < budget_s and len(times) < 200):
         t0 = time.perf_counter()
-        cpu_layer_pass(ref, kind, recs, bits, nth)
+        cpu_layer_pass(ref, recs, bits, nth)
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
-    return {"value": layer_bytes / med / 1e9, "unit": "GB/s", "cores": nth, "kind": kind,
-            "sample": f"one decoder layer (7 matrices, 4 bpw, batch 1) of the same workload, "
-                      f"{len(times)} timed passes, median; ggml_exl3_mul_mat ith/nth split over {nth} threads"
-            if kind == "reference" else f"oracle port, one layer, {len(times)} passes, {nth} threads"}
+    who = "ggml_exl3_mul_mat (reference sources, oracle/_ref)" if kind == "reference" else "oracle port"
+    return {"value": round(algo_bytes(bits) / med / 1e9, 4), "unit": "GB/s", "cores": nth, "kind": kind,
+            "sample": f"one decoder layer (7 matrices, {bits} bpw, batch 1) of the same workload, {len(times)} "
+                      f"timed passes, median; {who} with the ith/nth split over {nth} threads"}
 
-
-# ---------------------------------------------------------------------------------------------
 
 def run_reference_arm(args, rank, world):
-    import numpy as np
-
     if world > 1 and rank != 0:
         return
     from exl3_b200 import synthetic
@@ -305,19 +324,19 @@ def run_reference_arm(args, rank, world):
     layers = []
     for layer in range(n_layers):
         recs = []
-        for i, (name, (k, n)) in enumerate(shapes()):
+        for i, (_, (k, n)) in enumerate(shapes()):
             m = synthetic.matrix(k, n, bits, seed=10_000 * layer + i)
             recs.append((k, n, pack_records(m.trellis, m.suh, m.svh, bits),
                          synthetic.activations(1, k, seed=20_000 * layer + i)))
         layers.append(recs)
     for s in range(args.warmup):
-        cpu_layer_pass(ref, kind, layers[s % n_layers], bits, nth)
+        cpu_layer_pass(ref, layers[s % n_layers], bits, nth)
     t0 = time.perf_counter()
     for s in range(args.steps):
-        cpu_layer_pass(ref, kind, layers[s % n_layers], bits, nth)
+        cpu_layer_pass(ref, layers[s % n_layers], bits, nth)
     dt = time.perf_counter() - t0
-    step_bytes = algo_bytes(bits)
-    value = step_bytes * args.steps / dt / 1e9
+    value = algo_bytes(bits) * args.steps / dt / 1e9
+    who = "ggml_exl3_mul_mat (reference sources, oracle/_ref)" if kind == "reference" else "oracle port"
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
@@ -326,13 +345,13 @@ def run_reference_arm(args, rank, world):
                                f"layer (7 matrices) rotating over {n_layers} seeded layers",
                    "bits": bits, "rows": 1, "parallelism": "host threads"},
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": nth, "kind": kind,
-                         "sample": "ggml_exl3_mul_mat (reference sources, oracle/_ref) with ith/nth over "
-                                   f"{nth} threads" if kind == "reference" else "oracle port"},
+                         "sample": f"{who}, ith/nth split over {nth} threads, one layer per step"},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
-    _ = np
 
+
+# ---------------------------------------------------------------------------------------------
 
 def main(argv=None):
     args = parse_args(argv)
@@ -348,56 +367,67 @@ def main(argv=None):
 
     from exl3_b200 import ops
 
-    global BITS_USED
-    BITS_USED = args.bits
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device(f"cuda:{local}"))
     pk, pk_kind = peaks()
-    entries = build_stack(torch, ops, args.bits, args.layers, local, seed=1234 + 7919 * rank)
+    want_cpu = rank == 0 and world == 1 and not args.no_cpu
+    stack = build_stack(torch, ops, args.bits, args.layers, local, seed=1234 + 7919 * rank,
+                        keep_host_layer0=want_cpu)
     step_bytes = algo_bytes(args.bits) * args.layers
-    launches_per_step = len(entries)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     with ClockSampler(local) as clk:
-        ms = time_graph(torch, dist, entries, args.steps, args.warmup, world)
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, launches = time_pattern(torch, dist, ops, stack, "decoder", args.steps, args.warmup, world)
+    ms = max_over_ranks(ms)
     ms_step = ms / args.steps
     value = step_bytes * world / (ms_step * 1e-3) / 1e9
 
-    e2e_ms, h2d, d2h = time_e2e(torch, ops, entries, args.e2e_steps)
-    if world > 1:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = step_bytes * world / (e2e_ms / args.e2e_steps * 1e-3) / 1e9
+    patterns = {"decoder": {"launches_per_step": launches, "ms_per_step": round(ms_step, 5),
+                            "gbs_per_gpu": round(value / world, 1)}}
+    side_steps = max(20, args.steps // 4)
+    for pat in ("matrix", "layer"):
+        pms, pl = time_pattern(torch, dist, ops, stack, pat, side_steps, 5, world)
+        pms = max_over_ranks(pms) / side_steps
+        patterns[pat] = {"launches_per_step": pl, "ms_per_step": round(pms, 5),
+                         "gbs_per_gpu": round(step_bytes / (pms * 1e-3) / 1e9, 1)}
 
-    per_shape_ms = kernel_durations(torch, entries)
+    e2e_ms, h2d, d2h = time_e2e(torch, stack, args.e2e_steps)
+    e2e_ms = max_over_ranks(e2e_ms)
+    e2e_value = step_bytes * world / (e2e_ms / args.e2e_steps * 1e-3) / 1e9
+    shape_us = per_shape_us(torch, stack)
+
     sweep = {}
     if not args.no_sweep:
-        other = [b for b in (2, 3, 5, 6) if b != args.bits]
-        for b in other:
-            es = build_stack(torch, ops, b, args.layers, local, seed=99 + b)
-            sms = time_graph(torch, dist, es, max(10, args.steps // 4), 5, world)
-            sweep[str(b)] = round(algo_bytes(b) * args.layers / (sms / max(10, args.steps // 4) * 1e-3) / 1e9, 1)
-            for e in es:
-                e["w"].free()
-            del es
+        for b in (2, 3, 5, 6):
+            if b == args.bits:
+                continue
+            st = build_stack(torch, ops, b, args.layers, local, seed=99 + b)
+            sms, _ = time_pattern(torch, dist, ops, st, "decoder", side_steps, 5, world)
+            sms = max_over_ranks(sms) / side_steps
+            sweep[str(b)] = round(algo_bytes(b) * args.layers / (sms * 1e-3) / 1e9, 1)
+            for layer in st:
+                for m in layer.values():
+                    m["w"].free()
+            del st
             torch.cuda.empty_cache()
         sweep[str(args.bits)] = round(value / world, 1)
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(cpu_records(entries), args.bits)
+    cpu = cpu_baseline(stack, args.bits) if want_cpu else None
 
     traffic = None
     tf = ROOT / "profiles" / "gemv_traffic.json"
     if tf.exists():
         try:
-            traffic = json.loads(tf.read_text()).get("traffic_bytes_per_step_4bpw")
-        except (ValueError, AttributeError):
+            ratio = float(json.loads(tf.read_text())["dram_over_algorithmic"])
+            traffic = round(ratio * step_bytes / launches)  # bytes per average decoder-pattern launch
+        except (ValueError, KeyError, TypeError):
             traffic = None
 
     peak_hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
@@ -418,8 +448,9 @@ def main(argv=None):
             "data": "synthetic",
             "config": {
                 "workload": f"configs[1]: batch-1 decode GEMV sweep, {args.layers} layers x "
-                            "{q,k,v,o,gate,up,down} of the 2B decoder",
-                "bits": args.bits, "rows": 1, "layers": args.layers, "matrices_per_step": launches_per_step,
+                            "{q,k,v,o,gate,up,down} of the 2B decoder, decoder launch pattern",
+                "bits": args.bits, "rows": 1, "layers": args.layers, "matrices_per_step": 7 * args.layers,
+                "launches_per_step": launches,
                 "weights_mb_per_step": round(step_bytes / 1e6, 1),
                 "l2": "no flush: each step streams %.0f MB of distinct weights, > 126 MB L2" % (step_bytes / 1e6),
                 "activations": "fp16 N(0,1)", "accumulate": "fp32", "parallelism": f"dp{world} replicas",
@@ -427,19 +458,22 @@ def main(argv=None):
             },
             "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak_hbm, "unit": "GB/s",
                          "frac": round(per_gpu / peak_hbm, 4), "traffic": traffic,
-                         "peak_source": f"{pk_kind} hbm_gbs", "kernel": "exl3cu::k_gemv<4, mul1>",
-                         "per_shape_kernel_us": {k: round(v * 1e3, 2) for k, v in per_shape_ms.items()}},
+                         "algorithmic_bytes_per_launch": round(step_bytes / launches),
+                         "peak_source": f"{pk_kind} hbm_gbs", "kernel": "exl3cu::k_gemv_cluster<4, mul1>"},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "exl3cu_mul_mat_host (pinned host buffers)",
                     "ms_per_step": round(e2e_ms / args.e2e_steps, 4)},
-            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches": launches * args.steps,
             "clocks": clk.summary(),
+            "patterns": patterns,
+            "per_shape_kernel_us": shape_us,
             "sweep_gbs_by_bits": sweep,
         }
         print(json.dumps(line), flush=True)
-    for e in entries:
-        e["w"].free()
+    for layer in stack:
+        for m in layer.values():
+            m["w"].free()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -101,18 +101,36 @@ int exl3cu_weight_decode_inner(const exl3cu_weight * w, uint16_t * d_out, void *
 
 /* y[r][0..n_local) = x[r] . W for r < rows (ggml_exl3_mul_mat semantics,
  * src/exl3-ggml.cpp:51-92): x rows of k f32/f16 values (x_dtype), row stride
- * x_row_stride elements; y rows of n_local f32, stride y_row_stride.  Uses the
- * handle's own split-K workspace: calls on one handle must be ordered on one
- * stream (or otherwise serialised) by the caller. */
+ * x_row_stride elements; y rows of n_local f32, stride y_row_stride.  The K split
+ * is reduced inside each thread-block cluster, so calls need no workspace and
+ * calls on different streams may share a handle. */
 int exl3cu_mul_mat(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
                    float * d_y, size_t y_row_stride, void * stream);
+
+/* Several independent operator calls in as few launches as possible: item i
+ * computes d_y[i] = d_x[i] . weights[i] exactly as exl3cu_mul_mat would.  Items
+ * sharing a bitrate and codebook run together (up to 8 per launch), so one
+ * launch streams e.g. a layer's q, k and v, or gate and up.  Outputs must not
+ * alias inputs of other items.  No counterpart in the reference, whose
+ * operator handles one tensor per call. */
+int exl3cu_mul_mat_batch(size_t count, const exl3cu_weight * const * weights, const void * const * d_x,
+                         const int * x_dtype, const size_t * rows, const size_t * x_row_stride, float * const * d_y,
+                         const size_t * y_row_stride, void * stream);
+
+/* Sticky error bits the kernels of `device` raised since the last clear:
+ * bit 0 = a bounded wait on an asynchronous copy ran out (the results of the
+ * calls since are unreliable).  Synchronises the device.  No counterpart in
+ * the reference (its DSP operator returns statuses synchronously). */
+int exl3cu_device_status(int device, unsigned * status, int clear);
 
 /* Bytes of split-K workspace exl3cu_mul_mat_ws needs for this handle (any rows). */
 size_t exl3cu_mul_mat_workspace_bytes(const exl3cu_weight * w);
 
-/* As exl3cu_mul_mat with a caller-owned workspace of at least
- * exl3cu_mul_mat_workspace_bytes(w) bytes, zero-filled once before its first use
- * (the operator leaves it zeroed again).  Lets independent streams share one handle. */
+/* The operator with its K split reduced through a caller-owned global workspace
+ * of at least exl3cu_mul_mat_workspace_bytes(w) bytes, zero-filled once before
+ * its first use (the operator leaves it zeroed again): the last CTA of each
+ * column block to arrive sums the partials.  Same results as exl3cu_mul_mat
+ * within rounding. */
 int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
                       float * d_y, size_t y_row_stride, void * d_workspace, size_t workspace_bytes, void * stream);
 

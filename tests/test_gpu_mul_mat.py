@@ -159,8 +159,12 @@ def test_deterministic_and_workspace_reuse(ops):
     for o in outs:
         assert torch.equal(o, first)
     ws = torch.zeros(w.workspace_bytes // 4 + 4, dtype=torch.float32, device="cuda")
-    for _ in range(3):
-        assert torch.equal(w.mul_mat(x, workspace=ws), first)
+    via_ws = [w.mul_mat(x, workspace=ws) for _ in range(3)]  # global-workspace split-K variant
+    torch.cuda.synchronize()
+    for o in via_ws:
+        assert torch.equal(o, via_ws[0])
+        # fp16-activation variant vs the fixed-point mul1 path: both within the operator tolerance
+        assert errs(o.cpu().numpy(), first.cpu().numpy())[0] < TOL_MAX_ABS_REL
     w.free()
 
 
@@ -224,4 +228,51 @@ def test_invalid_mul_mat_arguments(ops):
         y = np.zeros((1, 256), np.float32)
         _lib.check(_lib.lib().exl3cu_mul_mat(w.handle, ctypes.c_void_p(x.ctypes.data), 1, 1, 256,
                                              ctypes.c_void_p(y.ctypes.data), 256, None))
+    w.free()
+
+
+def test_grouped_batch_matches_single_calls(ops, oracle):
+    """exl3cu_mul_mat_batch: mixed shapes, bitrates, dtypes and row counts (> 8 rows split into
+    sub-problems) give what one exl3cu_mul_mat call per item gives, and match the oracle."""
+    from exl3_b200 import synthetic
+
+    specs = [(2048, 2048, 4, 1), (2048, 512, 4, 1), (2048, 512, 6, 3), (6144, 2048, 4, 1), (1024, 768, 3, 11),
+             (2048, 6144, 4, 2), (512, 256, 5, 1), (4096, 1024, 4, 9), (2048, 2048, 4, 4),
+             (256, 128, 2, 1)]
+    ws, xs, refs = [], [], []
+    for i, (k, n, bits, rows) in enumerate(specs):
+        m = synthetic.matrix(k, n, bits, seed=300 + i)
+        rec = m.records()
+        ws.append(ops.Exl3Weight.from_records(rec, k, n, bits))
+        x = synthetic.activations(rows, k, seed=400 + i)
+        if i % 3 == 1:
+            x = x.astype(np.float32)
+        xs.append(torch.from_numpy(x).cuda())
+        refs.append(oracle.mul_mat(rec, bits, k, n, x, nth=8))
+    outs = ops.mul_mat_batch(ws, xs)
+    singles = [w.mul_mat(x) for w, x in zip(ws, xs)]
+    torch.cuda.synchronize()
+    for i, (o, s1, ref) in enumerate(zip(outs, singles, refs)):
+        # a grouped launch may pick another K split than a single one (other summation order and
+        # per-CTA activation scale): equal within the operator tolerance, not bit for bit
+        assert errs(o.cpu().numpy(), s1.cpu().numpy())[0] < TOL_MAX_ABS_REL, f"item {i}: grouped vs single"
+        assert_close(o.cpu().numpy(), ref, f"item {i} {specs[i]}")
+    for w in ws:
+        w.free()
+
+
+def test_global_workspace_variant_matches(ops):
+    """exl3cu_mul_mat_ws (split-K through a global workspace) agrees with the cluster path."""
+    from exl3_b200 import synthetic
+
+    k, n, bits = 6144, 2048, 4
+    m = synthetic.matrix(k, n, bits, seed=13)
+    w = ops.Exl3Weight.from_records(m.records(), k, n, bits)
+    x = torch.from_numpy(synthetic.activations(3, k, seed=14)).cuda()
+    ws = torch.zeros(w.workspace_bytes // 4 + 4, dtype=torch.float32, device="cuda")
+    a = w.mul_mat(x)
+    b = w.mul_mat(x, workspace=ws)
+    torch.cuda.synchronize()
+    rel, _ = errs(a.cpu().numpy(), b.cpu().numpy())
+    assert rel < TOL_MAX_ABS_REL
     w.free()

@@ -12,6 +12,8 @@
 #include <mutex>
 #include <new>
 #include <string>
+#include <vector>
+#include <cstdlib>
 
 using namespace exl3cu;
 
@@ -27,8 +29,8 @@ struct exl3cu_weight {
     uint32_t * lsc;
     __half * su;
     __half * sv;
-    void * ws;           // split-K workspace (partials + zeroed counters)
-    size_t ws_bytes;
+    void * ws;           // unused: kept null (the cluster kernel needs no workspace)
+    size_t ws_bytes;     // workspace size of the global split-K variant (exl3cu_mul_mat_ws)
     GemvPlan plan;       // for rows = 8 (cps/splits do not depend on rows)
     void * stage_x;      // host-form staging
     size_t stage_x_bytes;
@@ -164,8 +166,6 @@ int make_weight(size_t k, size_t n, unsigned bits, unsigned cb, size_t first_blo
     cudaError_t e = cudaMalloc(&w->lsc, lsc_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&w->su, k * sizeof(__half));
     if (e == cudaSuccess) e = cudaMalloc(&w->sv, block_count * 128 * sizeof(__half));
-    if (e == cudaSuccess && w->ws_bytes) e = cudaMalloc(&w->ws, w->ws_bytes);
-    if (e == cudaSuccess && w->ws_bytes) e = cudaMemset(w->ws, 0, w->ws_bytes);
     if (e != cudaSuccess) {
         release(w);
         return cuda_fail(e, "allocating device weights");
@@ -218,6 +218,108 @@ int run_mm(const exl3cu_weight * w, const void * x, int x_dtype, size_t rows, si
         a.y = y + r0 * y_stride;
         cudaError_t e = launch_gemv(a, p, w->bits, w->codebook, st);
         if (e != cudaSuccess) return cuda_fail(e, "launching the EXL3 GEMV");
+    }
+    return EXL3CU_OK;
+}
+
+
+// One operand set of a grouped launch.
+struct MmItem {
+    const exl3cu_weight * w;
+    const void * x;
+    int x_dtype;
+    size_t rows;
+    size_t x_stride;
+    float * y;
+    size_t y_stride;
+};
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char * env = std::getenv("EXL3CU_PDL");
+        return !(env && env[0] == '0');
+    }();
+    return on;
+}
+
+// Grouped GEMV on the cluster kernel: rows beyond 8 become extra problems on
+// the same weight; problems sharing (bits, codebook) go out together, at most
+// kMaxBatch per launch, in the order given.
+int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
+    struct Sub {
+        const exl3cu_weight * w;
+        const void * x;
+        float * y;
+        size_t x_stride, y_stride;
+        int rows, x_f16;
+    };
+    std::vector<Sub> subs;
+    for (size_t i = 0; i < count; ++i) {
+        const MmItem & it = items[i];
+        const size_t es = it.x_dtype == EXL3CU_F32 ? 4 : 2;
+        // the mul1 kernel takes 4 rows per problem (two activation digits each), the other 8
+        const size_t per = mul1_supported(it.w->bits, 1) && it.w->codebook == EXL3CU_CB_MUL1 ? 4 : 8;
+        for (size_t r0 = 0; r0 < it.rows; r0 += per) {
+            Sub s;
+            s.w = it.w;
+            s.x = static_cast<const char *>(it.x) + r0 * it.x_stride * es;
+            s.y = it.y + r0 * it.y_stride;
+            s.x_stride = it.x_stride;
+            s.y_stride = it.y_stride;
+            s.rows = int(it.rows - r0 < per ? it.rows - r0 : per);
+            s.x_f16 = it.x_dtype == EXL3CU_F16;
+            subs.push_back(s);
+        }
+    }
+    std::vector<bool> done(subs.size(), false);
+    for (size_t i = 0; i < subs.size(); ++i) {
+        if (done[i]) continue;
+        const unsigned bits = subs[i].w->bits, cb = subs[i].w->codebook;
+        const int device = subs[i].w->device;
+        std::vector<size_t> group;
+        for (size_t j = i; j < subs.size() && group.size() < size_t(kMaxBatch); ++j)
+            if (!done[j] && subs[j].w->bits == bits && subs[j].w->codebook == cb && subs[j].w->device == device) {
+                group.push_back(j);
+                done[j] = true;
+            }
+        GemvBatch b{};
+        int units = 0, min_nchunks = 1 << 30, max_rows = 1;
+        for (size_t gi = 0; gi < group.size(); ++gi) {
+            const Sub & s = subs[group[gi]];
+            GemvProblem & P = b.prob[gi];
+            P.lsc = s.w->lsc;
+            P.su = s.w->su;
+            P.sv = s.w->sv;
+            P.x = s.x;
+            P.y = s.y;
+            P.x_stride = (long long)s.x_stride;
+            P.y_stride = (long long)s.y_stride;
+            P.nchunks = int(s.w->k / 16);
+            P.rows = s.rows;
+            P.x_f16 = s.x_f16;
+            P.unit_base = units;
+            units += int(s.w->nblocks);
+            min_nchunks = P.nchunks < min_nchunks ? P.nchunks : min_nchunks;
+            max_rows = s.rows > max_rows ? s.rows : max_rows;
+        }
+        b.count = int(group.size());
+        if (cb == EXL3CU_CB_MUL1 && mul1_supported(bits, max_rows)) {
+            DeviceGuard guard(device);
+            cudaError_t e = launch_gemv_mul1(b, units, subs[i].w->sms, device, bits, pdl_enabled(), st);
+            if (e != cudaSuccess) return cuda_fail(e, "launching the EXL3 mul1 GEMV");
+            continue;
+        }
+        b.splits = choose_cluster_splits(subs[i].w->sms, units, min_nchunks);
+        int max_cps = 1;
+        for (int gi = 0; gi < b.count; ++gi) {
+            b.prob[gi].cps = (b.prob[gi].nchunks + b.splits - 1) / b.splits;
+            max_cps = b.prob[gi].cps > max_cps ? b.prob[gi].cps : max_cps;
+        }
+        const size_t smem = cluster_smem_bytes(max_cps, max_rows);
+        if (smem > 200 * 1024) return fail(EXL3CU_NO_SUPPORT, "K range per cluster rank too long (%d chunks)", max_cps);
+        DeviceGuard guard(device);
+        cudaError_t e = launch_gemv_cluster(b, units, smem, bits, cb, pdl_enabled(), st);
+        if (e != cudaSuccess) return cuda_fail(e, "launching the EXL3 cluster GEMV");
     }
     return EXL3CU_OK;
 }
@@ -395,14 +497,43 @@ int exl3cu_weight_decode_inner(const exl3cu_weight * w, uint16_t * d_out, void *
 
 size_t exl3cu_mul_mat_workspace_bytes(const exl3cu_weight * w) { return w ? w->ws_bytes : 0; }
 
+int exl3cu_device_status(int device, unsigned * status, int clear) {
+    if (!status) return fail(EXL3CU_INVALID_ARGUMENT, "status is NULL");
+    DeviceGuard guard(device);
+    if (!guard.ok) return fail(EXL3CU_INVALID_ARGUMENT, "cannot select device %d", device);
+    CU_TRY(cudaDeviceSynchronize(), "synchronising before reading the device status");
+    CU_TRY(mul1_read_status(status, clear != 0), "reading the device status word");
+    return EXL3CU_OK;
+}
+
 int exl3cu_mul_mat(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
                    float * d_y, size_t y_row_stride, void * stream) {
     int rc = validate_mm(w, d_x, x_dtype, rows, x_row_stride, d_y, y_row_stride);
     if (rc) return rc;
     if ((rc = check_device_ptr(d_x, w->device, "x"))) return rc;
     if ((rc = check_device_ptr(d_y, w->device, "y"))) return rc;
-    DeviceGuard guard(w->device);
-    return run_mm(w, d_x, x_dtype, rows, x_row_stride, d_y, y_row_stride, w->ws, static_cast<cudaStream_t>(stream));
+    const MmItem item{w, d_x, x_dtype, rows, x_row_stride, d_y, y_row_stride};
+    return run_cluster(&item, 1, static_cast<cudaStream_t>(stream));
+}
+
+int exl3cu_mul_mat_batch(size_t count, const exl3cu_weight * const * weights, const void * const * d_x,
+                         const int * x_dtype, const size_t * rows, const size_t * x_row_stride, float * const * d_y,
+                         const size_t * y_row_stride, void * stream) {
+    if (!count) return EXL3CU_OK;
+    if (!weights || !d_x || !x_dtype || !rows || !x_row_stride || !d_y || !y_row_stride)
+        return fail(EXL3CU_INVALID_ARGUMENT, "batch arrays must not be NULL");
+    std::vector<MmItem> items(count);
+    for (size_t i = 0; i < count; ++i) {
+        int rc = validate_mm(weights[i], d_x[i], x_dtype[i], rows[i], x_row_stride[i], d_y[i], y_row_stride[i]);
+        if (!rc) rc = check_device_ptr(d_x[i], weights[i]->device, "x");
+        if (!rc) rc = check_device_ptr(d_y[i], weights[i]->device, "y");
+        if (rc) {
+            std::string why = g_last_error;
+            return fail(rc, "batch item %zu: %s", i, why.c_str());
+        }
+        items[i] = MmItem{weights[i], d_x[i], x_dtype[i], rows[i], x_row_stride[i], d_y[i], y_row_stride[i]};
+    }
+    return run_cluster(items.data(), count, static_cast<cudaStream_t>(stream));
 }
 
 int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
@@ -455,7 +586,8 @@ int exl3cu_mul_mat_host(exl3cu_weight * w, const void * h_x, int x_dtype, size_t
     }
     CU_TRY(cudaMemcpy2DAsync(w->stage_x, w->k * es, h_x, x_row_stride * es, w->k * es, rows, cudaMemcpyHostToDevice, st),
            "copying x to the device");
-    int rc = run_mm(w, w->stage_x, x_dtype, rows, w->k, w->stage_y, n_local, w->ws, st);
+    const MmItem item{w, w->stage_x, x_dtype, rows, w->k, w->stage_y, n_local};
+    int rc = run_cluster(&item, 1, st);
     if (rc) return rc;
     CU_TRY(cudaMemcpy2DAsync(h_y, y_row_stride * sizeof(float), w->stage_y, n_local * sizeof(float),
                              n_local * sizeof(float), rows, cudaMemcpyDeviceToHost, st),

@@ -1,0 +1,537 @@
+// The mul1 EXL3 GEMV (rows <= 4 per launch, bitrates 2..8): the operator
+// behind exl3cu_mul_mat for the runtime format's codebook.
+//
+// Math (reference: ggml_exl3_mul_mat, src/exl3-ggml.cpp:51-92; codebook
+// src/exl3_codec.cpp:68-76).  A mul1 weight is w = a*(1024 + s) + b with
+// s = bytesum(state * 0x83dcd12d), a = fp16 0x1eee = 1774/2^18 and
+// b = fp16 0xc931 = -1329/128; the reference evaluates a*(1024+s)+b exactly
+// (it has at most 21 significant bits) and rounds it once to fp16.  So for
+// rotated activations xh,
+//
+//     sum_k xh_k w_k  =  a * sum_k xh_k s_k  +  c * sum_k xh_k,   c = 1024a + b = -3.453125,
+//
+// evaluated here with the codebook's exact values (the reference's fp16
+// rounding of w moves y by ~1e-4 relative, far inside the 2e-3 bar).  The
+// activations are held as 15-bit fixed point, xh = scale * q with
+// q = 128*hi + lo (hi, lo signed bytes), and sum_k q_k s_k is one integer
+// tensor-core product: mma.m16n8k32 u8 x s8 -> s32 with A = the four bytes
+// of every state's product (so the K dimension sums the bytes: the byte sum
+// costs nothing), B = the digits of q replicated over each product's four
+// bytes.  The batch x digit pairs fill the instruction's N = 8 (4 rows x 2
+// digits).  Per 8 trellis states a lane spends ~10 integer ops extracting
+// the 16-bit windows (byte permutes on a nibble-shifted copy at 4 bpw), 8
+// IMADs and 2 IMMAs -- no fp16 conversion, no packing, no HMMA.
+//
+// Pipeline: one producer warp streams the CTA's contiguous weight range into
+// a 4-stage shared-memory ring with bulk copies (cp.async.bulk, no
+// multicast) on mbarriers; eight consumer warps decode from shared memory.
+// The K split runs across a thread-block cluster and is reduced through
+// distributed shared memory by cluster rank 0, which applies H128 and sv.
+// Programmatic dependent launch: weights stream before griddepcontrol.wait;
+// only the activation prologue waits for the previous kernel.
+// Every mbarrier wait is bounded (exl3cu_async.cuh).
+#include "exl3cu_async.cuh"
+#include "exl3cu_internal.h"
+
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+namespace cg = cooperative_groups;
+
+namespace exl3cu {
+
+static __device__ unsigned g_mul1_status;  // kStatus* bits raised by k_gemv_mul1
+
+constexpr int kMW = 8;                      // consumer warps
+constexpr int kMThreads = (kMW + 1) * 32;   // + one producer warp
+constexpr int kMStages = 4;
+constexpr int kMRows = 4;                   // rows per launch: 2 digits each fill N = 8
+constexpr float kCodeA = 1774.0f / 262144.0f;
+constexpr float kCodeC = -3.453125f;
+constexpr float kQMax = 16000.0f;           // |q| bound: hi in [-127,127], lo in [-64,63]
+
+__device__ __forceinline__ void imma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// The 8 trellis states of tile c for this lane (see the LSC layout in
+// exl3cu_decode.cuh), s[e] for positions 8L+e.  The 16 ring bits before the
+// lane's slice are state 7 of lane L-1: one shuffle per tile.
+template <int BITS>
+__device__ __forceinline__ void tile_states(const uint32_t (&w)[2 * BITS], int c, int src, uint32_t (&s)[8]) {
+    if constexpr (BITS == 4) {
+        const uint32_t own = w[c];
+        s[7] = own & 0xffffu;
+        const uint32_t prior = __shfl_sync(0xffffffffu, s[7], src);
+        s[5] = __byte_perm(own, prior, 0x7621);
+        s[3] = own >> 16;
+        s[1] = __byte_perm(own, prior, 0x7643);
+        const uint32_t own4 = __funnelshift_r(own, prior, 4);
+        const uint32_t prior4 = prior >> 4;
+        s[6] = own4 & 0xffffu;
+        s[4] = __byte_perm(own4, prior4, 0x7621);
+        s[2] = own4 >> 16;
+        s[0] = __byte_perm(own4, prior4, 0x7643);
+    } else {
+        constexpr int SLICE = 8 * BITS;
+        s[7] = seg_field16(w, SLICE * (c + 1) - 16);
+        const uint32_t prior = __shfl_sync(0xffffffffu, s[7], src);
+        const uint32_t z = (prior << 16) | seg_field16(w, SLICE * c);
+#pragma unroll
+        for (int e = 0; e < 7; ++e) {
+            const int end = (e + 1) * BITS;
+            s[e] = end <= 16 ? ((z >> (16 - end)) & 0xffffu) : seg_field16(w, SLICE * c + end - 16);
+        }
+    }
+}
+
+struct Mul1Layout {
+    int ring_off, xq_off, acc_off, part_off, slot_off, gmax_off, bar_off;
+    size_t bytes;
+};
+
+// ring: kMStages stages of kMW chunks; xq: activation digits of the CTA's K
+// range; acc: the CTA's integer sums [rows][128][hi, lo]; part: its fp32
+// partial; slot: the other cluster ranks' partials (written remotely, read by
+// rank 0); gmax: max |xh| per (row, own group); then the mbarriers and per-row
+// scale / digit sum.
+__host__ __device__ inline Mul1Layout mul1_layout(int bits, int cps, int rows, int splits) {
+    Mul1Layout L;
+    const int ng = (cps + 7) / 8 + 1;
+    const size_t ring = size_t(kMStages) * kMW * 256 * bits;
+    const size_t xq = size_t(cps) * 128 * rows;
+    const size_t acc = size_t(rows) * 128 * 2 * 4;
+    const size_t part = size_t(rows) * 128 * 4;
+    const size_t slot = size_t(splits > 1 ? splits - 1 : 0) * rows * 128 * 4;
+    const size_t gmax = size_t(rows) * ng * 4;
+    L.ring_off = 0;
+    L.xq_off = int(ring);
+    L.acc_off = int((ring + xq + 15) & ~size_t(15));
+    L.part_off = int(L.acc_off + acc);
+    L.slot_off = int(L.part_off + part);
+    L.gmax_off = int(L.slot_off + slot);
+    L.bar_off = int((L.gmax_off + gmax + 15) & ~size_t(15));
+    L.bytes = L.bar_off + 2 * kMStages * 8 + 2 * 4 * kMRows;
+    return L;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int CHUNKB = 256 * BITS;
+    pdl_trigger();
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int S = b.splits;
+    const int split = int(cluster.block_rank());
+    const int unit = blockIdx.x / S;
+    int p = 0;
+#pragma unroll
+    for (int i = 1; i < kMaxBatch; ++i)
+        if (i < b.count && b.prob[i].unit_base <= unit) p = i;
+    const GemvProblem & P = b.prob[p];
+    const int nb = unit - P.unit_base;
+    const int rows = P.rows;
+    const int c0 = min(split * P.cps, P.nchunks);
+    const int c1 = min(c0 + P.cps, P.nchunks);
+    const int nch = c1 - c0;
+    const int nstage = (nch + kMW - 1) / kMW;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    const Mul1Layout L = mul1_layout(BITS, P.cps, rows, S);
+    unsigned char * ring = smem + L.ring_off;
+    unsigned char * xq = smem + L.xq_off;
+    int * acc = reinterpret_cast<int *>(smem + L.acc_off);          // [rows][128][2]
+    float * part = reinterpret_cast<float *>(smem + L.part_off);    // [rows][128]
+    float * slots = reinterpret_cast<float *>(smem + L.slot_off);   // [S-1][rows][128]
+    float * gmax = reinterpret_cast<float *>(smem + L.gmax_off);    // [rows][ng]
+    uint64_t * full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
+    uint64_t * empty = full + kMStages;
+    float * scale_s = reinterpret_cast<float *>(empty + kMStages);
+    int * xsum_s = reinterpret_cast<int *>(scale_s + kMRows);
+    const int nacc = rows * 256;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kMStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kMW);
+        }
+        mbar_init_fence();
+    }
+    for (int e = threadIdx.x; e < nacc; e += kMThreads) acc[e] = 0;
+    if (threadIdx.x < kMRows) {
+        xsum_s[threadIdx.x] = 0;
+        scale_s[threadIdx.x] = 1.0f;  // a CTA without chunks contributes scale * 0
+    }
+    __syncthreads();
+
+    if (warp == kMW) {
+        // ---- producer: the CTA's chunks [c0, c1) are contiguous in the device layout ----
+        if (lane == 0 && nch > 0) {
+            const unsigned char * src = reinterpret_cast<const unsigned char *>(P.lsc) +
+                                        (size_t(nb) * P.nchunks + c0) * CHUNKB;
+            for (int j = 0; j < nstage; ++j) {
+                const int s = j % kMStages;
+                if (j >= kMStages && !mbar_wait(&empty[s], ((j / kMStages) - 1) & 1)) {
+                    atomicOr(&g_mul1_status, kStatusWaitTimeout);
+                    break;
+                }
+                const int nc = min(kMW, nch - j * kMW);
+                mbar_arrive_expect_tx(&full[s], uint32_t(nc * CHUNKB));
+                bulk_g2s(ring + size_t(s) * kMW * CHUNKB, src + size_t(j) * kMW * CHUNKB, uint32_t(nc * CHUNKB),
+                         &full[s]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---- consumers ----
+        pdl_wait_primary();  // activations may be written by the previous kernel
+        const int g0 = c0 >> 3;
+        const int ng = nch > 0 ? ((c1 - 1) >> 3) - g0 + 1 : 0;
+        const int kbeg = c0 * 16, kend = c1 * 16;
+        auto load_xsu = [&](int r, int kcol, float (&o)[4]) {
+            if (P.x_f16) {
+                const uint2 raw = *reinterpret_cast<const uint2 *>(static_cast<const __half *>(P.x) +
+                                                                   size_t(r) * P.x_stride + kcol);
+                const __half2 lo = bits_half2(raw.x), hi = bits_half2(raw.y);
+                o[0] = __low2float(lo); o[1] = __high2float(lo); o[2] = __low2float(hi); o[3] = __high2float(hi);
+            } else {
+                const float4 f = *reinterpret_cast<const float4 *>(static_cast<const float *>(P.x) +
+                                                                   size_t(r) * P.x_stride + kcol);
+                o[0] = f.x; o[1] = f.y; o[2] = f.z; o[3] = f.w;
+            }
+            const uint2 sraw = *reinterpret_cast<const uint2 *>(P.su + kcol);
+            const __half2 s01 = bits_half2(sraw.x), s23 = bits_half2(sraw.y);
+            o[0] = __fmul_rn(o[0], __low2float(s01));
+            o[1] = __fmul_rn(o[1], __high2float(s01));
+            o[2] = __fmul_rn(o[2], __low2float(s23));
+            o[3] = __fmul_rn(o[3], __high2float(s23));
+        };
+        // (1) the CTA's (group, row) items round robin over warps: xh = H128(x * su), the
+        //     first kItems kept in registers, each group's max |xh| published
+        constexpr int kItems = 4;
+        float v[kItems][4];
+        const int nitems = ng * rows;
+        auto rotate = [&](int item, float (&o)[4]) {
+            const int gi = item / rows;
+            const int r = item - gi * rows;
+            load_xsu(r, (g0 + gi) * 128 + lane * 4, o);
+            h128_warp4(o);
+            float m = fmaxf(fmaxf(fabsf(o[0]), fabsf(o[1])), fmaxf(fabsf(o[2]), fabsf(o[3])));
+#pragma unroll
+            for (int sh = 16; sh; sh >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, sh));
+            if (lane == 0) gmax[r * ng + gi] = m;
+        };
+#pragma unroll
+        for (int ii = 0; ii < kItems; ++ii) {
+            const int item = warp + ii * kMW;
+            if (item < nitems) rotate(item, v[ii]);
+        }
+        for (int item = warp + kItems * kMW; item < nitems; item += kMW) {
+            float o[4];
+            rotate(item, o);
+        }
+        consumer_sync();
+        // (2) per row, scale = max |xh| / kQMax over the CTA's groups; each warp quantizes the
+        //     items it rotated into the digit layout and adds their digit sums (integer)
+        auto quantize = [&](int item, const float (&o)[4]) {
+            const int gi = item / rows;
+            const int r = item - gi * rows;
+            float amax = 0.f;
+            for (int q = 0; q < ng; ++q) amax = fmaxf(amax, gmax[r * ng + q]);
+            const float scale = amax > 0.f ? amax / kQMax : 1.0f;
+            const float inv = 1.0f / scale;
+            int qsum = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int k = (g0 + gi) * 128 + lane * 4 + e;
+                if (k < kbeg || k >= kend) continue;
+                int q = __float2int_rn(o[e] * inv);
+                q = max(-16000, min(16000, q));
+                qsum += q;
+                const int lo = ((q + 64) & 127) - 64;
+                const int hi = (q - lo) >> 7;
+                const int kl = k - kbeg;
+                const int cl = kl >> 4, kk = kl & 15;
+                unsigned char * base = xq + size_t(cl) * 128 * rows + ((kk & 7) >> 1) * 16 +
+                                       ((kk & 1) + 2 * (kk >> 3)) * 4;
+                *reinterpret_cast<uint32_t *>(base + (2 * r) * 64) = uint32_t(uint8_t(int8_t(hi))) * 0x01010101u;
+                *reinterpret_cast<uint32_t *>(base + (2 * r + 1) * 64) = uint32_t(uint8_t(int8_t(lo))) * 0x01010101u;
+            }
+#pragma unroll
+            for (int sh = 16; sh; sh >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, sh);
+            if (lane == 0) {
+                atomicAdd(&xsum_s[r], qsum);
+                if (gi == 0) scale_s[r] = scale;
+            }
+        };
+#pragma unroll
+        for (int ii = 0; ii < kItems; ++ii) {
+            const int item = warp + ii * kMW;
+            if (item < nitems) quantize(item, v[ii]);
+        }
+        for (int item = warp + kItems * kMW; item < nitems; item += kMW) {
+            // beyond the register cache: rotate again (republishing the same max)
+            float o[4];
+            rotate(item, o);
+            quantize(item, o);
+        }
+        consumer_sync();
+        // (3) decode + integer tensor-core products
+        const int src = (lane + 31) & 31;
+        const bool b_live = lane < 8 * rows;  // B column g = 2*row + digit exists
+        constexpr uint32_t C = 0x83dcd12du;
+        int D[8][4];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) D[c][0] = D[c][1] = D[c][2] = D[c][3] = 0;
+        for (int j = 0; j < nstage; ++j) {
+            const int cl = warp + j * kMW;
+            if (cl >= nch) break;
+            const int s = j % kMStages;
+            uint4 bq = make_uint4(0, 0, 0, 0);
+            if (b_live) bq = *reinterpret_cast<const uint4 *>(xq + size_t(cl) * 128 * rows + lane * 16);
+            if (!mbar_wait(&full[s], (j / kMStages) & 1)) {
+                atomicOr(&g_mul1_status, kStatusWaitTimeout);
+                break;
+            }
+            uint32_t w[2 * BITS];
+            const unsigned char * seg = ring + size_t(s) * kMW * CHUNKB + size_t(warp) * CHUNKB + lane * 8 * BITS;
+            if constexpr ((BITS & 1) == 0) {
+#pragma unroll
+                for (int i = 0; i < BITS / 2; ++i) {
+                    const uint4 q4 = *reinterpret_cast<const uint4 *>(seg + 16 * i);
+                    w[4 * i] = q4.x; w[4 * i + 1] = q4.y; w[4 * i + 2] = q4.z; w[4 * i + 3] = q4.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < BITS; ++i) {
+                    const uint2 q2 = *reinterpret_cast<const uint2 *>(seg + 8 * i);
+                    w[2 * i] = q2.x; w[2 * i + 1] = q2.y;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            // products of all 8 tiles first, then the 16 IMMAs ordered so that no two
+            // consecutive ones share an accumulator
+            uint32_t pr[8][8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint32_t st[8];
+                tile_states<BITS>(w, c, src, st);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) pr[c][e] = st[e] * C;
+            }
+#pragma unroll
+            for (int c = 0; c < 8; ++c) imma_u8s8(D[c], pr[c][0], pr[c][4], pr[c][1], pr[c][5], bq.x, bq.y);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) imma_u8s8(D[c], pr[c][2], pr[c][6], pr[c][3], pr[c][7], bq.z, bq.w);
+        }
+        // (4) the warps' integer sums meet in shared memory (exact, any order) ...
+        const int g = lane >> 2, t = lane & 3;
+        if (t < rows) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                int * a0 = acc + (t * 128 + c * 16 + g) * 2;
+                atomicAdd(a0, D[c][0]);
+                atomicAdd(a0 + 1, D[c][1]);
+                atomicAdd(a0 + 16, D[c][2]);  // column + 8
+                atomicAdd(a0 + 17, D[c][3]);
+            }
+        }
+        consumer_sync();
+        // ... and become the CTA's fp32 partial scale * (a * sum q s + c * sum q), written straight
+        //     into rank 0's slot for this rank (rank 0 keeps its own in `part`)
+        float * dst = split == 0 ? part : cluster.map_shared_rank(slots, 0) + size_t(split - 1) * rows * 128;
+        for (int e = threadIdx.x; e < rows * 128; e += kMW * 32) {
+            const int r = e >> 7;
+            const float sq = fmaf(float(acc[2 * e]), 128.f, float(acc[2 * e + 1]));
+            dst[e] = scale_s[r] * fmaf(kCodeA, sq, kCodeC * float(xsum_s[r]));
+        }
+    }
+
+    // ---- one cluster barrier; rank 0 sums the partials in rank order ----
+    cluster.sync();
+    if (split == 0 && warp < kMW) {
+        const int elems = rows * 128;
+        for (int r = warp; r < rows; r += kMW) {
+            float v[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int e = r * 128 + lane * 4 + q;
+                float a = part[e];
+                for (int rk = 1; rk < S; ++rk) a = __fadd_rn(a, slots[size_t(rk - 1) * elems + e]);
+                v[q] = a;
+            }
+            h128_warp4(v);
+            const uint2 sraw = *reinterpret_cast<const uint2 *>(P.sv + nb * 128 + lane * 4);
+            const __half2 s01 = bits_half2(sraw.x), s23 = bits_half2(sraw.y);
+            float4 o;
+            o.x = __fmul_rn(v[0], __low2float(s01));
+            o.y = __fmul_rn(v[1], __high2float(s01));
+            o.z = __fmul_rn(v[2], __low2float(s23));
+            o.w = __fmul_rn(v[3], __high2float(s23));
+            *reinterpret_cast<float4 *>(P.y + size_t(r) * P.y_stride + nb * 128 + lane * 4) = o;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+
+namespace {
+
+template <int BITS>
+void * mul1_kernel() {
+    return reinterpret_cast<void *>(k_gemv_mul1<BITS>);
+}
+
+void * mul1_kernel_for(unsigned bits) {
+    switch (bits) {
+        case 2: return mul1_kernel<2>();
+        case 3: return mul1_kernel<3>();
+        case 4: return mul1_kernel<4>();
+        case 5: return mul1_kernel<5>();
+        case 6: return mul1_kernel<6>();
+        case 7: return mul1_kernel<7>();
+        case 8: return mul1_kernel<8>();
+        default: return nullptr;
+    }
+}
+
+constexpr size_t kMul1MaxSmem = 200 * 1024;
+
+// Set the kernel's shared-memory and cluster attributes once per (device, bits).
+bool mul1_prepare(int device, unsigned bits) {
+    static std::mutex mu;
+    static bool done[64][9] = {};
+    if (device < 0 || device >= 64 || bits > 8) return false;
+    std::lock_guard<std::mutex> g(mu);
+    if (done[device][bits]) return true;
+    const void * k = mul1_kernel_for(bits);
+    if (!k) return false;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMul1MaxSmem)) != cudaSuccess)
+        return false;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) return false;
+    done[device][bits] = true;
+    return true;
+}
+
+// Clusters of `cs` CTAs with `smem` bytes each that the device holds at once
+// (0 when such a cluster cannot be scheduled at all); cached per key.
+int mul1_active_clusters(int device, unsigned bits, int cs, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, unsigned, int, size_t>, int> cache;
+    const auto key = std::make_tuple(device, bits, cs, (smem + 1023) / 1024);
+    {
+        std::lock_guard<std::mutex> g(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(cs), 1, 1);
+    cfg.blockDim = dim3(kMThreads, 1, 1);
+    cfg.dynamicSmemBytes = ((smem + 1023) / 1024) * 1024;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = unsigned(cs);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, mul1_kernel_for(bits), &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        n = 0;
+    }
+    std::lock_guard<std::mutex> g(mu);
+    cache[key] = n;
+    return n;
+}
+
+}  // namespace
+
+bool mul1_supported(unsigned bits, int rows) { return bits >= 2 && bits <= 8 && rows >= 1 && rows <= kMRows; }
+
+// Picks the cluster size (K split) so the grid fills the device in one wave:
+// the largest S in 1..16 with nunits*S <= resident CTAs and at least one
+// chunk per consumer warp for the smallest problem.
+cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, unsigned bits, bool pdl,
+                             cudaStream_t st) {
+    if (!mul1_prepare(device, bits)) return cudaErrorInvalidValue;
+    int min_nchunks = 1 << 30, max_nchunks = 0, max_rows = 1;
+    for (int i = 0; i < b.count; ++i) {
+        min_nchunks = std::min(min_nchunks, b.prob[i].nchunks);
+        max_nchunks = std::max(max_nchunks, b.prob[i].nchunks);
+        max_rows = std::max(max_rows, b.prob[i].rows);
+    }
+    const char * env = std::getenv("EXL3CU_CLUSTER_SPLITS");  // tuning experiments only
+    int S = 0;
+    if (env && std::atoi(env) > 0) {
+        S = std::min(16, std::atoi(env));
+    } else {
+        // largest cluster size whose grid is one wave; else the largest that can run at all
+        int feasible = 0;
+        for (int cand = 16; cand >= 1; --cand) {
+            if (cand > 1 && min_nchunks / cand < kMW) continue;
+            const int cps = (max_nchunks + cand - 1) / cand;
+            const Mul1Layout L = mul1_layout(int(bits), cps, max_rows, cand);
+            if (L.bytes > kMul1MaxSmem) break;  // fewer splits only grow the per-CTA range
+            const int fit = mul1_active_clusters(device, bits, cand, L.bytes);
+            if (fit <= 0) continue;
+            if (!feasible) feasible = cand;
+            if (nunits <= fit) {
+                S = cand;
+                break;
+            }
+        }
+        if (!S) S = feasible;
+        (void)sms;
+    }
+    if (S <= 0) return cudaErrorInvalidConfiguration;
+    b.splits = S;
+    int max_cps = 1;
+    for (int i = 0; i < b.count; ++i) {
+        b.prob[i].cps = (b.prob[i].nchunks + S - 1) / S;
+        max_cps = std::max(max_cps, b.prob[i].cps);
+    }
+    const Mul1Layout L = mul1_layout(int(bits), max_cps, max_rows, S);
+    if (L.bytes > kMul1MaxSmem) return cudaErrorInvalidConfiguration;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(nunits * S), 1, 1);
+    cfg.blockDim = dim3(kMThreads, 1, 1);
+    cfg.dynamicSmemBytes = L.bytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = unsigned(S);
+    attrs[0].val.clusterDim.y = 1;
+    attrs[0].val.clusterDim.z = 1;
+    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = pdl ? 2 : 1;
+    void * args[] = {&b};
+    return cudaLaunchKernelExC(&cfg, mul1_kernel_for(bits), args);
+}
+
+cudaError_t mul1_read_status(unsigned * out, bool clear) {
+    cudaError_t e = cudaMemcpyFromSymbol(out, g_mul1_status, sizeof(unsigned));
+    if (e == cudaSuccess && clear && *out) {
+        const unsigned zero = 0;
+        e = cudaMemcpyToSymbol(g_mul1_status, &zero, sizeof(unsigned));
+    }
+    return e;
+}
+
+}  // namespace exl3cu

@@ -28,6 +28,41 @@ struct GemvArgs {
     int splits;
 };
 
+// One problem of a grouped GEMV launch: y[r] = x[r] . W for r < rows (<= 8).
+struct GemvProblem {
+    const uint32_t * lsc;
+    const __half * su;
+    const __half * sv;
+    const void * x;
+    float * y;
+    long long x_stride;
+    long long y_stride;
+    int nchunks;    // k / 16
+    int cps;        // chunks per cluster rank
+    int rows;       // 1..8
+    int x_f16;
+    int unit_base;  // first unit (column block) of this problem in the launch
+    int pad;
+};
+
+constexpr int kMaxBatch = 8;  // problems per launch, passed by value in the kernel parameters
+
+struct GemvBatch {
+    GemvProblem prob[kMaxBatch];
+    int count;
+    int splits;     // cluster size: CTAs per unit along K
+};
+
+int choose_cluster_splits(int sms, int nunits, int min_nchunks);
+size_t cluster_smem_bytes(int max_cps, int rows);
+cudaError_t launch_gemv_cluster(const GemvBatch & b, int nunits, size_t smem, unsigned bits, unsigned cb, bool pdl,
+                                cudaStream_t st);
+
+bool mul1_supported(unsigned bits, int rows);
+cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, unsigned bits, bool pdl,
+                             cudaStream_t st);
+cudaError_t mul1_read_status(unsigned * out, bool clear);
+
 struct GemvPlan {
     int cps;
     int splits;

@@ -155,6 +155,30 @@ class Exl3Weight:
         return out.cpu().numpy().view(np.uint16)
 
 
+def mul_mat_batch(weights, xs, outs=None, stream=None):
+    """Independent y_i = x_i . W_i in grouped launches (exl3cu_mul_mat_batch)."""
+    n = len(weights)
+    if len(xs) != n:
+        raise ValueError("one activation tensor per weight")
+    xs2 = []
+    for x in xs:
+        if x.dtype not in (torch.float32, torch.float16):
+            raise TypeError("x must be float32 or float16")
+        x2 = x.reshape(-1, x.shape[-1])
+        xs2.append(x2 if x2.stride(-1) == 1 else x2.contiguous())
+    if outs is None:
+        outs = [torch.empty((x.shape[0], w.n), dtype=torch.float32, device=x.device) for w, x in zip(weights, xs2)]
+    VP = ctypes.c_void_p * n
+    SZ = ctypes.c_size_t * n
+    IN = ctypes.c_int * n
+    check(lib().exl3cu_mul_mat_batch(
+        n, VP(*[w.handle.value for w in weights]), VP(*[x.data_ptr() for x in xs2]),
+        IN(*[F32 if x.dtype == torch.float32 else F16 for x in xs2]), SZ(*[x.shape[0] for x in xs2]),
+        SZ(*[x.stride(0) for x in xs2]), VP(*[o.data_ptr() for o in outs]), SZ(*[o.stride(0) for o in outs]),
+        _stream_handle(stream)))
+    return outs
+
+
 # -- codec on device tensors (include/exl3_codec.h:10-29) ------------------------------------------
 
 def decode_codebook(states, codebook: int = CB_MUL1, device: int = 0) -> np.ndarray:
@@ -192,4 +216,4 @@ def reconstruct(packed, suh, svh, k: int, n: int, bits: int, codebook: int = CB_
     return out.cpu().numpy().view(np.uint16)
 
 
-__all__ = ["Exl3Weight", "decode_codebook", "decode_inner", "hadamard128", "reconstruct", "_lib"]
+__all__ = ["Exl3Weight", "mul_mat_batch", "decode_codebook", "decode_inner", "hadamard128", "reconstruct", "_lib"]
