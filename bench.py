@@ -459,7 +459,7 @@ def main(argv=None):
             "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak_hbm, "unit": "GB/s",
                          "frac": round(per_gpu / peak_hbm, 4), "traffic": traffic,
                          "algorithmic_bytes_per_launch": round(step_bytes / launches),
-                         "peak_source": f"{pk_kind} hbm_gbs", "kernel": "exl3cu::k_gemv_cluster<4, mul1>"},
+                         "peak_source": f"{pk_kind} hbm_gbs", "kernel": "exl3cu::k_gemv_mul1<4>"},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "exl3cu_mul_mat_host (pinned host buffers)",
