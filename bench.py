@@ -64,6 +64,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-sweep", action="store_true", help="skip the 2/3/5/6-bit side measurements")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--e2e-steps", type=int, default=30)
+    ap.add_argument("--config", choices=("sweep", "large"), default="sweep",
+                    help="sweep: configs[1] decode GEMV sweep (default); large: configs[4] column-split matrix")
     return ap.parse_args(argv)
 
 
@@ -353,6 +355,80 @@ def run_reference_arm(args, rank, world):
 
 # ---------------------------------------------------------------------------------------------
 
+def run_large(args, torch, dist, ops, rank, world, local):
+    """W [k=14336, n=4096] at 4 bpw, x [rows, 14336] fp16, column-split over the
+    ranks with one NCCL all-gather of the fp16 outputs.  Reports per-GPU GB/s of the local
+    EXL3 slice and the whole-operator time including the gather (max over ranks)."""
+    from exl3_b200.parallel import ColumnSplit, gather_columns
+
+    k, n, bits = 14336, 4096, args.bits
+    split = ColumnSplit(n, world)
+    first, count = split.range(rank)
+    dev = f"cuda:{local}"
+    g = torch.Generator(device=dev)
+    g.manual_seed(4242)  # identical full matrix on every rank; each keeps its blocks
+    trellis = torch.randint(0, 65536, (k // 16, n // 16, 16 * bits), generator=g, device=dev,
+                            dtype=torch.int32).to(torch.int16)
+    suh = (torch.randint(0, 2, (k,), generator=g, device=dev) * 2 - 1).to(torch.float16)
+    svh = ((torch.randint(0, 2, (n,), generator=g, device=dev) * 2 - 1).float() *
+           (0.01 + 0.02 * torch.rand(n, generator=g, device=dev))).to(torch.float16)
+    w = ops.Exl3Weight.from_trellis(trellis, suh.view(torch.int16), svh.view(torch.int16), device=local,
+                                    first_block=first, block_count=count)
+    del trellis
+    results = {}
+    stream = torch.cuda.Stream()
+    for rows in (1, 8):
+        x = torch.randn((rows, k), generator=g, device=dev).to(torch.float16)
+        y_local = torch.empty((rows, count * 128), dtype=torch.float32, device=dev)
+        local_bytes = k * count * 128 * bits // 8 + 2 * (k + count * 128) + 2 * k * rows + 4 * count * 128 * rows
+        timings = {}
+        for what in ("local", "operator"):
+            with torch.cuda.stream(stream):
+                for _ in range(max(3, args.warmup)):
+                    w.mul_mat(x, out=y_local, stream=stream)
+                    if what == "operator":
+                        gather_columns(y_local, split)
+            stream.synchronize()
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                s.record(stream)
+                for _ in range(args.steps):
+                    w.mul_mat(x, out=y_local, stream=stream)
+                    if what == "operator":
+                        gather_columns(y_local, split)
+                e.record(stream)
+            e.synchronize()
+            ms = s.elapsed_time(e) / args.steps
+            if world > 1:
+                t = torch.tensor([ms], dtype=torch.float64, device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            timings[what] = ms
+        results[str(rows)] = {"local_us": round(timings["local"] * 1e3, 2),
+                              "operator_us": round(timings["operator"] * 1e3, 2),
+                              "local_gbs_per_gpu": round(local_bytes / (timings["local"] * 1e-3) / 1e9, 1),
+                              "gather_bytes_per_rank": 2 * rows * 128 * split.max_blocks * world}
+    w.free()
+    if rank == 0:
+        pk, pk_kind = peaks()
+        peak = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+        b1 = results["1"]
+        print(json.dumps({
+            "metric": "EXL3 4bpw large-matrix GEMV, column split + NCCL all-gather (configs[4])",
+            "value": b1["local_gbs_per_gpu"], "unit": "GB/s per GPU", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "dtype": "fp16",
+            "data": "synthetic", "vs_baseline": None,
+            "config": {"workload": "W [4096,14336] (k=14336, n=4096) 4 bpw, x fp16 N(0,1); batch 1 and 8",
+                       "parallelism": f"column split tp{world}", "bits": bits},
+            "roofline": {"bound": "hbm", "achieved": b1["local_gbs_per_gpu"], "peak": peak, "unit": "GB/s",
+                         "frac": round(b1["local_gbs_per_gpu"] / peak, 4), "peak_source": f"{pk_kind} hbm_gbs"},
+            "by_batch": results}), flush=True)
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -370,6 +446,12 @@ def main(argv=None):
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device(f"cuda:{local}"))
+    if args.config == "large":
+        rc = run_large(args, torch, dist, ops, rank, world, local)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return rc
     pk, pk_kind = peaks()
     want_cpu = rank == 0 and world == 1 and not args.no_cpu
     stack = build_stack(torch, ops, args.bits, args.layers, local, seed=1234 + 7919 * rank,
