@@ -242,10 +242,103 @@ bool pdl_enabled() {
     return on;
 }
 
-// Grouped GEMV on the cluster kernel: rows beyond 8 become extra problems on
-// the same weight; problems sharing (bits, codebook) go out together, at most
-// kMaxBatch per launch, in the order given.
+// Row count from which an operand goes to the tensor-core GEMM instead of the
+// row-by-row GEMV kernels.  EXL3CU_GEMM_MIN_ROWS overrides it (0 disables the GEMM).
+size_t gemm_min_rows() {
+    static const size_t v = [] {
+        const char * env = std::getenv("EXL3CU_GEMM_MIN_ROWS");
+        if (env && env[0]) {
+            const long long r = std::atoll(env);
+            return r <= 0 ? size_t(SIZE_MAX) : size_t(r);
+        }
+        return size_t(9);
+    }();
+    return v;
+}
+
+// Tiled-activation scratch of the GEMM, one buffer per (device, stream) so
+// that operators on different streams never share it; work on one stream is
+// ordered, so consecutive calls reuse it.  It grows (synchronising that
+// stream) when a call needs more, which is refused while the stream is being
+// captured into a CUDA graph: run one call of the largest row count before
+// capturing.
+struct GemmScratch {
+    int device;
+    cudaStream_t stream;
+    void * ptr;
+    size_t bytes;
+};
+std::mutex g_gemm_scratch_mu;
+std::vector<GemmScratch> g_gemm_scratch;
+
+int gemm_scratch(int device, cudaStream_t st, size_t bytes, void ** out) {
+    std::lock_guard<std::mutex> lock(g_gemm_scratch_mu);
+    GemmScratch * s = nullptr;
+    for (auto & e : g_gemm_scratch)
+        if (e.device == device && e.stream == st) s = &e;
+    if (!s) {
+        g_gemm_scratch.push_back(GemmScratch{device, st, nullptr, 0});
+        s = &g_gemm_scratch.back();
+    }
+    if (s->bytes < bytes) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        CU_TRY(cudaStreamIsCapturing(st, &cs), "querying stream capture");
+        if (cs != cudaStreamCaptureStatusNone)
+            return fail(EXL3CU_NO_SUPPORT,
+                        "the GEMM scratch must grow to %zu bytes during stream capture: run one call with this many "
+                        "rows on the stream before capturing", bytes);
+        CU_TRY(cudaStreamSynchronize(st), "synchronising before the GEMM scratch grows");
+        cudaFree(s->ptr);
+        s->ptr = nullptr;
+        s->bytes = 0;
+        CU_TRY(cudaMalloc(&s->ptr, bytes), "allocating the GEMM scratch");
+        s->bytes = bytes;
+    }
+    *out = s->ptr;
+    return EXL3CU_OK;
+}
+
+// Rows per GEMM launch pair: bounds the scratch (2 KB per row per 1024 of k)
+// and keeps every index of the launch in 32 bits.
+constexpr size_t kGemmRowsPerLaunch = 2048;
+
+int run_gemm(const MmItem & it, cudaStream_t st) {
+    const exl3cu_weight * w = it.w;
+    DeviceGuard guard(w->device);
+    const size_t es = it.x_dtype == EXL3CU_F32 ? 4 : 2;
+    for (size_t r0 = 0; r0 < it.rows; r0 += kGemmRowsPerLaunch) {
+        const int rows = int(it.rows - r0 < kGemmRowsPerLaunch ? it.rows - r0 : kGemmRowsPerLaunch);
+        const GemmPlan p = plan_gemm(w->sms, w->k, w->nblocks, rows);
+        void * xt = nullptr;
+        int rc = gemm_scratch(w->device, st, p.xt_bytes, &xt);
+        if (rc) return rc;
+        cudaError_t e = launch_gemm_tc(p, w->lsc, w->su, w->sv, w->k, w->nblocks, w->bits, w->codebook, w->device,
+                                       static_cast<const char *>(it.x) + r0 * it.x_stride * es,
+                                       it.x_dtype == EXL3CU_F16, (long long)it.x_stride, rows, it.y + r0 * it.y_stride,
+                                       (long long)it.y_stride, static_cast<__half *>(xt), pdl_enabled(), st);
+        if (e != cudaSuccess) return cuda_fail(e, "launching the EXL3 tensor-core GEMM");
+    }
+    return EXL3CU_OK;
+}
+
+// Grouped GEMV on the cluster kernels: rows beyond a problem's share become
+// extra problems on the same weight; problems sharing (bits, codebook) go out
+// together, at most kMaxBatch per launch, in the order given.  Operands with
+// gemm_min_rows() rows or more run on the tensor-core GEMM instead, one
+// launch pair each.
 int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
+    std::vector<MmItem> gemv_items;
+    gemv_items.reserve(count);
+    for (size_t i = 0; i < count; ++i) {
+        if (items[i].rows >= gemm_min_rows()) {
+            int rc = run_gemm(items[i], st);
+            if (rc) return rc;
+        } else {
+            gemv_items.push_back(items[i]);
+        }
+    }
+    items = gemv_items.data();
+    count = gemv_items.size();
     struct Sub {
         const exl3cu_weight * w;
         const void * x;
@@ -502,7 +595,10 @@ int exl3cu_device_status(int device, unsigned * status, int clear) {
     DeviceGuard guard(device);
     if (!guard.ok) return fail(EXL3CU_INVALID_ARGUMENT, "cannot select device %d", device);
     CU_TRY(cudaDeviceSynchronize(), "synchronising before reading the device status");
-    CU_TRY(mul1_read_status(status, clear != 0), "reading the device status word");
+    unsigned gemv = 0, gemm = 0;
+    CU_TRY(mul1_read_status(&gemv, clear != 0), "reading the GEMV status word");
+    CU_TRY(gemm_read_status(&gemm, clear != 0), "reading the GEMM status word");
+    *status = gemv | gemm;
     return EXL3CU_OK;
 }
 

@@ -63,6 +63,24 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
                              cudaStream_t st);
 cudaError_t mul1_read_status(unsigned * out, bool clear);
 
+// tcgen05 GEMM for batches of rows (exl3cu_gemm_tc.cu).
+struct GemmPlan {
+    int T;          // token tiles of 128 per CTA (1..4)
+    int tgroups;    // groups of T token tiles
+    int tmem_cols;  // TMEM columns a CTA allocates (power of two >= T*128)
+    int splits;     // cluster size along K
+    int cps;        // chunks of 16 rows per cluster rank (multiple of 4)
+    size_t smem;    // dynamic shared memory per CTA
+    size_t xt_bytes;  // tiled activation scratch
+};
+
+GemmPlan plan_gemm(int sms, size_t k, size_t nblocks, int rows);
+cudaError_t launch_gemm_tc(const GemmPlan & p, const uint32_t * lsc, const __half * su, const __half * sv, size_t k,
+                           size_t nblocks, unsigned bits, unsigned cb, int device, const void * x, int x_f16,
+                           long long x_stride, int rows, float * y, long long y_stride, __half * xt, bool pdl,
+                           cudaStream_t st);
+cudaError_t gemm_read_status(unsigned * out, bool clear);
+
 struct GemvPlan {
     int cps;
     int splits;
