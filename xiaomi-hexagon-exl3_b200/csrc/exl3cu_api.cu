@@ -6,6 +6,7 @@
 #include "exl3cu.h"
 #include "exl3cu_internal.h"
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -243,18 +244,12 @@ bool pdl_enabled() {
 }
 
 // Row count from which an operand goes to the tensor-core GEMM instead of the
-// row-by-row GEMV kernels.  EXL3CU_GEMM_MIN_ROWS overrides it (0 disables the GEMM).
-size_t gemm_min_rows() {
-    static const size_t v = [] {
-        const char * env = std::getenv("EXL3CU_GEMM_MIN_ROWS");
-        if (env && env[0]) {
-            const long long r = std::atoll(env);
-            return r <= 0 ? size_t(SIZE_MAX) : size_t(r);
-        }
-        return size_t(9);
-    }();
-    return v;
-}
+// row-by-row GEMV kernels, and the plan overrides of exl3cu_gemm_config.
+std::atomic<size_t> g_gemm_min_rows{9};
+std::atomic<int> g_gemm_tiles{0};
+std::atomic<int> g_gemm_splits{0};
+
+size_t gemm_min_rows() { return g_gemm_min_rows.load(std::memory_order_relaxed); }
 
 // Tiled-activation scratch of the GEMM, one buffer per (device, stream) so
 // that operators on different streams never share it; work on one stream is
@@ -308,7 +303,8 @@ int run_gemm(const MmItem & it, cudaStream_t st) {
     const size_t es = it.x_dtype == EXL3CU_F32 ? 4 : 2;
     for (size_t r0 = 0; r0 < it.rows; r0 += kGemmRowsPerLaunch) {
         const int rows = int(it.rows - r0 < kGemmRowsPerLaunch ? it.rows - r0 : kGemmRowsPerLaunch);
-        const GemmPlan p = plan_gemm(w->sms, w->k, w->nblocks, rows);
+        const GemmPlan p = plan_gemm(w->sms, w->k, w->nblocks, rows, g_gemm_tiles.load(std::memory_order_relaxed),
+                                     g_gemm_splits.load(std::memory_order_relaxed));
         void * xt = nullptr;
         int rc = gemm_scratch(w->device, st, p.xt_bytes, &xt);
         if (rc) return rc;
@@ -589,6 +585,16 @@ int exl3cu_weight_decode_inner(const exl3cu_weight * w, uint16_t * d_out, void *
 }
 
 size_t exl3cu_mul_mat_workspace_bytes(const exl3cu_weight * w) { return w ? w->ws_bytes : 0; }
+
+int exl3cu_gemm_config(size_t min_rows, int tiles_per_cta, int splits) {
+    if (tiles_per_cta < 0 || tiles_per_cta > 4) return fail(EXL3CU_INVALID_ARGUMENT, "tiles_per_cta must be 0..4");
+    if (splits < 0 || splits > 16 || (splits & (splits - 1)))
+        return fail(EXL3CU_INVALID_ARGUMENT, "splits must be 0 or a power of two up to 16");
+    if (min_rows) g_gemm_min_rows.store(min_rows, std::memory_order_relaxed);
+    g_gemm_tiles.store(tiles_per_cta, std::memory_order_relaxed);
+    g_gemm_splits.store(splits, std::memory_order_relaxed);
+    return EXL3CU_OK;
+}
 
 int exl3cu_device_status(int device, unsigned * status, int clear) {
     if (!status) return fail(EXL3CU_INVALID_ARGUMENT, "status is NULL");

@@ -52,6 +52,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity) {
     return false;
 }
 
+// Same, but a thread whose phase is not complete sleeps (up to about a
+// microsecond per round, woken early when the phase completes) instead of
+// spinning, so that waiting warps leave their issue slots to the warps that
+// share the scheduler.  Bounded: false after kSleepWaitRounds rounds (about a
+// second).
+constexpr unsigned kSleepWaitRounds = 1u << 20;
+
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t * bar, uint32_t parity) {
+    const uint32_t addr = smem_addr(bar);
+    for (unsigned i = 0; i < kSleepWaitRounds; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(addr), "r"(parity), "r"(1000u)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
 // Bulk copy of `bytes` (multiple of 16; both addresses 16-byte aligned) into this
 // CTA's shared memory, completing transaction bytes on `bar`.  No multicast.
 __device__ __forceinline__ void bulk_g2s(void * dst_smem, const void * src_gmem, uint32_t bytes, uint64_t * bar) {

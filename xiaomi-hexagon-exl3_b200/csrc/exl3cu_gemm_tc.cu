@@ -40,14 +40,18 @@ namespace exl3cu {
 static __device__ unsigned g_gemm_status;
 
 constexpr int kDecodeWarps = 8;
-constexpr int kTThreads = 64 + 32 * kDecodeWarps;
-constexpr int kBStages = 8;         // decoded W tiles, 4 KB each (one 16-row chunk)
-constexpr int kXStages = 3;         // activation stages of 64 K (4 chunks)
-constexpr int kXTileBytes = 16384;  // 64 K x 128 tokens fp16: one token tile of a stage
+constexpr int kFirstDecodeWarp = 3;  // warps 0-2: weight copies + TMEM, MMA issue, activation copies
+constexpr int kTThreads = 32 * (kFirstDecodeWarp + kDecodeWarps);
+constexpr int kBGroups = 3;          // decoded W groups of 4 chunks (4 KB B tiles) in the ring
 constexpr int kBTileBytes = 4096;
-constexpr int kMaxTiles = 4;        // token tiles per CTA (T*128 TMEM columns <= 512)
-constexpr int kPartStride = 132;    // floats per row of the parked partial tile
-constexpr size_t kBarBytes = 256;
+constexpr int kBRingBytes = kBGroups * 4 * kBTileBytes;
+constexpr int kWRingBytes = 32768;   // trellis stages of 4 chunks in flight (>= 4 stages at 8 bits)
+constexpr int kMaxWStages = 16;
+constexpr int kMaxXStages = 3;       // activation stages of 64 K (4 chunks): 3 for T <= 2, else 2
+constexpr int kXTileBytes = 16384;   // 64 K x 128 tokens fp16: one token tile of a stage
+constexpr int kMaxTiles = 4;         // token tiles per CTA (T*128 TMEM columns <= 512)
+constexpr int kPartStride = 132;     // floats per row of the parked partial tile
+constexpr size_t kBarBytes = 512;
 // Shared memory is padded to at least this, so that one CTA fits an SM: two
 // CTAs could otherwise ask for more than the SM's 512 TMEM columns together,
 // and tcgen05.alloc would wait for columns that a cluster peer never frees.
@@ -69,6 +73,7 @@ struct GemmArgs {
     int cps;               // chunks per cluster rank, a multiple of 4
     int splits;
     int tmem_cols;
+    int xstages;           // activation stages in the ring (2 or 3)
 };
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -119,9 +124,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // Activation prologue: xh = H128(x * su) per (row, 128-group), rounded to fp16
 // (src/exl3-ggml.cpp:60-70 forms the same rotated row), written in the A
 // operand's tiled order: element (token, kk) of token tile `tile` at half
-//   ((tile * k/8 + kk/8) * 16 + (token%128)/8) * 64 + (token%8) * 8 + kk%8,
-// so a 64-K stage of one token tile is 16 contiguous KB.  Rows at or beyond M
-// are zero.  One warp per (row, group).
+//   tile*128*k + (kk/16)*2048 + ((token%128)/8)*128 + ((kk/8)%2)*64 + (token%8)*8 + kk%8,
+// i.e. per 16 columns of K a 4 KB block of 8x16-byte core matrices, row group
+// r and K half h at r*256 + h*128 bytes (the B tile's arrangement, which the
+// tensor cores read at full rate), so a group of 4 chunks of one token tile is
+// 16 contiguous KB.  Rows at or beyond M are zero.  One warp per (row, group).
 __global__ void k_tile_x(const void * __restrict__ x, int x_f16, long long x_stride, const __half * __restrict__ su,
                          int M, int k, int ntiles, __half * __restrict__ xt) {
     pdl_trigger();
@@ -153,7 +160,8 @@ __global__ void k_tile_x(const void * __restrict__ x, int x_f16, long long x_str
     }
     h128_warp4(v);
     const int tile = tok >> 7, tr = tok & 127;
-    const size_t off = ((size_t(tile) * (k / 8) + (kcol >> 3)) * 16 + (tr >> 3)) * 64 + (tr & 7) * 8 + (kcol & 7);
+    const size_t off = size_t(tile) * 128 * k + size_t(kcol >> 4) * 2048 + (tr >> 3) * 128 + ((kcol >> 3) & 1) * 64 +
+                       (tr & 7) * 8 + (kcol & 7);
     const __half2 o01 = __floats2half2_rn(v[0], v[1]);
     const __half2 o23 = __floats2half2_rn(v[2], v[3]);
     *reinterpret_cast<uint2 *>(xt + off) = make_uint2(half2_bits(o01), half2_bits(o23));
@@ -164,13 +172,16 @@ __global__ void k_tile_x(const void * __restrict__ x, int x_f16, long long x_str
 template <int BITS, unsigned CB>
 __global__ void __launch_bounds__(kTThreads, 1) k_gemm_tc(const GemmArgs a) {
     extern __shared__ __align__(1024) unsigned char smem[];
-    constexpr int SEGW = 2 * BITS;
-    constexpr int CHUNKW = 64 * BITS;
+    constexpr int SEGW = 2 * BITS;                   // words of one lane's segment of a chunk
+    constexpr int CHUNKB = 256 * BITS;               // bytes of one chunk
+    constexpr int WSTAGEB = 4 * CHUNKB;              // bytes of one weight stage (a group of 4 chunks)
+    constexpr int WST = kWRingBytes / WSTAGEB > kMaxWStages ? kMaxWStages : kWRingBytes / WSTAGEB;
     pdl_trigger();
 
     cg::cluster_group cluster = cg::this_cluster();
     const int S = a.splits;
     const int T = a.T;
+    const int XST = a.xstages;
     const int split = int(cluster.block_rank());
     const int unit = blockIdx.x / S;
     const int nb = unit / a.tgroups;
@@ -178,28 +189,35 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemm_tc(const GemmArgs a) {
     const int c0 = min(split * a.cps, a.nchunks);
     const int c1 = min(c0 + a.cps, a.nchunks);
     const int nch = c1 - c0;  // a multiple of 4: k and cps are
-    const int nxs = nch / 4;  // activation stages
+    const int ngr = nch / 4;  // groups of 4 chunks (64 rows of K): the unit of every ring
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int xstage_bytes = T * kXTileBytes;
 
-    unsigned char * bring = smem;                           // kBStages x 4 KB
-    unsigned char * xring = smem + kBStages * kBTileBytes;  // kXStages x T x 16 KB
-    uint64_t * bars = reinterpret_cast<uint64_t *>(xring + kXStages * xstage_bytes);
+    unsigned char * bring = smem;                 // kBGroups x 4 decoded B tiles of 4 KB
+    unsigned char * wring = bring + kBRingBytes;  // WST x 4 chunks of trellis
+    unsigned char * xring = wring + kWRingBytes;  // XST x T x 16 KB activations
+    uint64_t * bars = reinterpret_cast<uint64_t *>(xring + XST * xstage_bytes);
     uint64_t * fullB = bars;
-    uint64_t * emptyB = fullB + kBStages;
-    uint64_t * fullX = emptyB + kBStages;
-    uint64_t * emptyX = fullX + kXStages;
-    uint64_t * done = emptyX + kXStages;
+    uint64_t * emptyB = fullB + kBGroups;
+    uint64_t * fullW = emptyB + kBGroups;
+    uint64_t * emptyW = fullW + kMaxWStages;
+    uint64_t * fullX = emptyW + kMaxWStages;
+    uint64_t * emptyX = fullX + kMaxXStages;
+    uint64_t * done = emptyX + kMaxXStages;
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     float * part = reinterpret_cast<float *>(smem);  // epilogue reuse of the rings: [128][kPartStride]
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kBStages; ++i) {
-            mbar_init(&fullB[i], 1);
-            mbar_init(&emptyB[i], 1);
+        for (int i = 0; i < kBGroups; ++i) {
+            mbar_init(&fullB[i], 4);   // the four decode warps of the group's chunks
+            mbar_init(&emptyB[i], 1);  // the MMA commit
         }
-        for (int i = 0; i < kXStages; ++i) {
+        for (int i = 0; i < WST; ++i) {
+            mbar_init(&fullW[i], 1);
+            mbar_init(&emptyW[i], 4);
+        }
+        for (int i = 0; i < XST; ++i) {
             mbar_init(&fullX[i], 1);
             mbar_init(&emptyX[i], 1);
         }
@@ -217,66 +235,105 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemm_tc(const GemmArgs a) {
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ---- activation stages (written by the prologue kernel: wait for it first) ----
+        // ---- weight groups: static data, streamed from the first cycle (before the PDL wait) ----
         if (lane == 0) {
-            pdl_wait_primary();
-            const size_t tile_halves = size_t(a.nchunks) * 2 * 1024;  // one token tile, all of K
-            const __half * src = a.xt + size_t(tg) * T * tile_halves + size_t(c0) * 2 * 1024;
-            for (int st = 0; st < nxs; ++st) {
-                const int slot = st % kXStages;
-                if (st >= kXStages && !mbar_wait(&emptyX[slot], ((st / kXStages) - 1) & 1)) {
+            const unsigned char * src =
+                reinterpret_cast<const unsigned char *>(a.lsc) + (size_t(nb) * a.nchunks + c0) * CHUNKB;
+            for (int g = 0; g < ngr; ++g) {
+                const int slot = g % WST;
+                if (g >= WST && !mbar_wait_sleep(&emptyW[slot], ((g / WST) - 1) & 1)) {
                     atomicOr(&g_gemm_status, kStatusWaitTimeout);
                     break;
                 }
-                mbar_arrive_expect_tx(&fullX[slot], uint32_t(xstage_bytes));
-                for (int t = 0; t < T; ++t)
-                    bulk_g2s(xring + (slot * T + t) * kXTileBytes, src + size_t(t) * tile_halves + size_t(st) * 8 * 1024,
-                             kXTileBytes, &fullX[slot]);
+                mbar_arrive_expect_tx(&fullW[slot], uint32_t(WSTAGEB));
+                bulk_g2s(wring + slot * WSTAGEB, src + size_t(g) * WSTAGEB, uint32_t(WSTAGEB), &fullW[slot]);
             }
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ---- MMA issue: one thread ----
+        // ---- MMA issue: one thread, 4*T MMAs per group of 4 chunks ----
         if (lane == 0) {
-            for (int j = 0; j < nch; ++j) {
-                const int bs = j % kBStages, xs = (j >> 2) % kXStages;
-                if (!mbar_wait(&fullB[bs], (j / kBStages) & 1) ||
-                    ((j & 3) == 0 && !mbar_wait(&fullX[xs], ((j >> 2) / kXStages) & 1))) {
+            // start-address fields of the first B tile / activation tile; later tiles are constant offsets
+            const uint64_t bdesc0 = umma_desc(smem_addr(bring), 128, 256);
+            const uint64_t adesc0 = umma_desc(smem_addr(xring), 128, 256);
+            for (int g = 0; g < ngr; ++g) {
+                const int bs = g % kBGroups, xs = g % XST;
+                if (!mbar_wait_sleep(&fullB[bs], (g / kBGroups) & 1) || !mbar_wait_sleep(&fullX[xs], (g / XST) & 1)) {
                     atomicOr(&g_gemm_status, kStatusWaitTimeout);
                     break;
                 }
                 tc_fence_after();
-                const uint64_t bdesc = umma_desc(smem_addr(bring + bs * kBTileBytes), 128, 256);
-                for (int t = 0; t < T; ++t) {
-                    const uint64_t adesc =
-                        umma_desc(smem_addr(xring + (xs * T + t) * kXTileBytes + (j & 3) * 4096), 2048, 128);
-                    umma_f16(tmem + uint32_t(t * 128), adesc, bdesc, j > 0 ? 1u : 0u);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint64_t bdesc = bdesc0 + uint64_t(((bs * 4 + c) * kBTileBytes) >> 4);
+                    for (int t = 0; t < T; ++t) {
+                        const uint64_t adesc = adesc0 + uint64_t(((xs * T + t) * kXTileBytes + c * 4096) >> 4);
+                        umma_f16(tmem + uint32_t(t * 128), adesc, bdesc, (g | c) != 0 ? 1u : 0u);
+                    }
                 }
                 umma_commit(&emptyB[bs]);
-                if ((j & 3) == 3) umma_commit(&emptyX[xs]);
+                umma_commit(&emptyX[xs]);
             }
-            if (nch > 0)
+            if (ngr > 0)
                 umma_commit(done);  // arrives once every issued MMA has completed
             else
                 mbar_arrive(done);
         }
         __syncwarp();
+    } else if (warp == 2) {
+        // ---- activation groups (written by the prologue kernel: wait for it first) ----
+        if (lane == 0) {
+            pdl_wait_primary();
+            const size_t tile_halves = size_t(a.nchunks) * 2048;  // one token tile, all of K
+            const __half * src = a.xt + size_t(tg) * T * tile_halves + size_t(c0) * 2048;
+            for (int g = 0; g < ngr; ++g) {
+                const int slot = g % XST;
+                if (g >= XST && !mbar_wait_sleep(&emptyX[slot], ((g / XST) - 1) & 1)) {
+                    atomicOr(&g_gemm_status, kStatusWaitTimeout);
+                    break;
+                }
+                mbar_arrive_expect_tx(&fullX[slot], uint32_t(xstage_bytes));
+                for (int t = 0; t < T; ++t)
+                    bulk_g2s(xring + (slot * T + t) * kXTileBytes, src + size_t(t) * tile_halves + size_t(g) * 4 * 2048,
+                             kXTileBytes, &fullX[slot]);
+            }
+        }
+        __syncwarp();
     } else {
-        // ---- decode warps: the CTA's chunks, round robin ----
-        const int dw = warp - 2;
-        const uint32_t * wbase = a.lsc + (size_t(nb) * a.nchunks + c0) * CHUNKW + size_t(lane) * SEGW;
-        uint32_t w[SEGW];
-        if (dw < nch) load_segment<BITS>(wbase + size_t(dw) * CHUNKW, w);
+        // ---- decode warps: chunk j of the CTA's range goes to warp j % 8 ----
+        const int dw = warp - kFirstDecodeWarp;
         for (int j = dw; j < nch; j += kDecodeWarps) {
-            uint32_t frag[8][4];
-            decode_chunk<BITS, CB>(w, frag);
-            if (j + kDecodeWarps < nch) load_segment<BITS>(wbase + size_t(j + kDecodeWarps) * CHUNKW, w);
-            const int bs = j % kBStages;
-            if (j >= kBStages && !mbar_wait(&emptyB[bs], ((j / kBStages) - 1) & 1)) {
+            const int g = j >> 2, ws = g % WST;
+            if (!mbar_wait_sleep(&fullW[ws], (g / WST) & 1)) {
                 atomicOr(&g_gemm_status, kStatusWaitTimeout);
                 break;
             }
-            uint32_t * bt = reinterpret_cast<uint32_t *>(bring + bs * kBTileBytes);
+            uint32_t w[SEGW];
+            const uint32_t * seg = reinterpret_cast<const uint32_t *>(wring + ws * WSTAGEB + (j & 3) * CHUNKB) +
+                                   lane * SEGW;
+            if constexpr ((BITS & 1) == 0) {
+#pragma unroll
+                for (int i = 0; i < SEGW; i += 4) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(seg + i);
+                    w[i] = v.x; w[i + 1] = v.y; w[i + 2] = v.z; w[i + 3] = v.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < SEGW; i += 2) {
+                    const uint2 v = *reinterpret_cast<const uint2 *>(seg + i);
+                    w[i] = v.x; w[i + 1] = v.y;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&emptyW[ws]);
+            uint32_t frag[8][4];
+            decode_chunk<BITS, CB>(w, frag);
+            const int bs = g % kBGroups;
+            if (g >= kBGroups && !mbar_wait_sleep(&emptyB[bs], ((g / kBGroups) - 1) & 1)) {
+                atomicOr(&g_gemm_status, kStatusWaitTimeout);
+                break;
+            }
+            uint32_t * bt = reinterpret_cast<uint32_t *>(bring + (bs * 4 + (j & 3)) * kBTileBytes);
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 // core matrix (column group 2c or 2c+1, K half 0 or 1) at group*256 + half*128 bytes;
@@ -293,14 +350,16 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemm_tc(const GemmArgs a) {
     }
 
     // ---- epilogue: per token tile, park the partial, then reduce a row slice over the cluster ----
-    if (warp >= 2 && !mbar_wait(done, 0)) atomicOr(&g_gemm_status, kStatusWaitTimeout);
+    const bool epi = warp >= kFirstDecodeWarp;
+    if (epi && !mbar_wait_sleep(done, 0)) atomicOr(&g_gemm_status, kStatusWaitTimeout);
     tc_fence_after();
     __syncthreads();  // every MMA has completed: the rings are free for the partial tile
     const int rows_per_rank = 128 / S;
+    const int ew = warp - kFirstDecodeWarp;  // epilogue warp 0..7
     for (int t = 0; t < T; ++t) {
-        if (warp >= 2) {
-            const int q = warp & 3;         // TMEM lane quarter this warp may read
-            const int h = (warp - 2) >> 2;  // column half
+        if (epi) {
+            const int q = warp & 3;  // TMEM lane quarter this warp may read
+            const int h = ew >> 2;   // column half
             const int row = q * 32 + lane;
             float * dst = part + row * kPartStride + h * 64;
 #pragma unroll
@@ -318,10 +377,10 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemm_tc(const GemmArgs a) {
             }
         }
         cluster.sync();
-        if (warp >= 2) {
+        if (epi) {
             const uint2 sraw = *reinterpret_cast<const uint2 *>(a.sv + nb * 128 + lane * 4);
             const __half2 s01 = bits_half2(sraw.x), s23 = bits_half2(sraw.y);
-            for (int r = split * rows_per_rank + (warp - 2); r < (split + 1) * rows_per_rank; r += kDecodeWarps) {
+            for (int r = split * rows_per_rank + ew; r < (split + 1) * rows_per_rank; r += kDecodeWarps) {
                 float v[4] = {0.f, 0.f, 0.f, 0.f};
                 for (int s = 0; s < S; ++s) {
                     const float * rp = cluster.map_shared_rank(part, s) + r * kPartStride + lane * 4;
@@ -382,16 +441,21 @@ void * gemm_kernel_for(unsigned bits, unsigned cb) {
     }
 }
 
-constexpr size_t kGemmMaxSmem = size_t(kBStages) * kBTileBytes + size_t(kXStages) * kMaxTiles * kXTileBytes + kBarBytes;
-static_assert(kGemmMaxSmem <= 227 * 1024, "GEMM shared memory above the per-CTA limit");
-static_assert(size_t(128) * kPartStride * 4 <= size_t(kBStages) * kBTileBytes + size_t(kXStages) * kXTileBytes,
-              "the partial tile must fit in the rings of a one-tile CTA");
-static_assert(2 * kMinSmem > 228 * 1024, "the padding must keep a second CTA off the SM");
+int xstages_for(int T) { return T <= 2 ? 3 : 2; }
 
 size_t gemm_smem(int T) {
-    const size_t s = size_t(kBStages) * kBTileBytes + size_t(kXStages) * T * kXTileBytes + kBarBytes;
+    const size_t s = size_t(kBRingBytes) + kWRingBytes + size_t(xstages_for(T)) * T * kXTileBytes + kBarBytes;
     return s < kMinSmem ? kMinSmem : s;
 }
+
+constexpr size_t kGemmMaxSmem = size_t(kBRingBytes) + kWRingBytes + size_t(2) * kMaxTiles * kXTileBytes + kBarBytes;
+static_assert(kGemmMaxSmem <= 227 * 1024, "GEMM shared memory above the per-CTA limit");
+static_assert(size_t(kBRingBytes) + kWRingBytes + size_t(3) * 2 * kXTileBytes + kBarBytes <= kGemmMaxSmem,
+              "T = 2 with three activation stages must fit the same limit");
+static_assert(size_t(128) * kPartStride * 4 <= size_t(kBRingBytes) + kWRingBytes + 2 * kXTileBytes,
+              "the partial tile must fit in the rings of the smallest plan (T = 1, two activation stages)");
+static_assert(2 * kMinSmem > 228 * 1024, "the padding must keep a second CTA off the SM");
+static_assert((2 * kBGroups + 2 * kMaxWStages + 2 * kMaxXStages + 1) * 8 + 4 <= kBarBytes, "barrier area");
 
 bool gemm_prepare(int device, unsigned bits, unsigned cb) {
     static std::mutex mu;
@@ -409,10 +473,11 @@ bool gemm_prepare(int device, unsigned bits, unsigned cb) {
 
 }  // namespace
 
-GemmPlan plan_gemm(int sms, size_t k, size_t nblocks, int rows) {
+GemmPlan plan_gemm(int sms, size_t k, size_t nblocks, int rows, int tiles, int splits) {
     GemmPlan p{};
     const int ntiles = (rows + 127) / 128;
-    p.tgroups = (ntiles + kMaxTiles - 1) / kMaxTiles;
+    const int tmax = tiles > 0 ? (tiles < kMaxTiles ? tiles : kMaxTiles) : kMaxTiles;
+    p.tgroups = (ntiles + tmax - 1) / tmax;
     p.T = (ntiles + p.tgroups - 1) / p.tgroups;  // balanced: at most tgroups-1 padded tiles
     p.tmem_cols = p.T == 1 ? 128 : p.T == 2 ? 256 : 512;
     const int nchunks = int(k / 16);
@@ -420,6 +485,7 @@ GemmPlan plan_gemm(int sms, size_t k, size_t nblocks, int rows) {
     // K split over a cluster so that units x S fills the device once; at least 8 chunks per rank
     int S = 1;
     while (S < 8 && units * (S * 2) <= sms && nchunks / (S * 2) >= 8) S *= 2;
+    if (splits > 0) S = splits < 16 ? splits : 16;
     p.splits = S;
     const int cps = (nchunks + S - 1) / S;
     p.cps = (cps + 3) / 4 * 4;
@@ -465,6 +531,7 @@ cudaError_t launch_gemm_tc(const GemmPlan & p, const uint32_t * lsc, const __hal
     a.cps = p.cps;
     a.splits = p.splits;
     a.tmem_cols = p.tmem_cols;
+    a.xstages = xstages_for(p.T);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(nblocks * p.tgroups * p.splits), 1, 1);
     cfg.blockDim = dim3(kTThreads, 1, 1);

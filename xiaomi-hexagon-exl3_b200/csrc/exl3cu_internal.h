@@ -74,7 +74,8 @@ struct GemmPlan {
     size_t xt_bytes;  // tiled activation scratch
 };
 
-GemmPlan plan_gemm(int sms, size_t k, size_t nblocks, int rows);
+// tiles / splits > 0 replace the automatic choice of T / S.
+GemmPlan plan_gemm(int sms, size_t k, size_t nblocks, int rows, int tiles = 0, int splits = 0);
 cudaError_t launch_gemm_tc(const GemmPlan & p, const uint32_t * lsc, const __half * su, const __half * sv, size_t k,
                            size_t nblocks, unsigned bits, unsigned cb, int device, const void * x, int x_f16,
                            long long x_stride, int rows, float * y, long long y_stride, __half * xt, bool pdl,

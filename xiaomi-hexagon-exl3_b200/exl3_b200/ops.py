@@ -217,3 +217,19 @@ def reconstruct(packed, suh, svh, k: int, n: int, bits: int, codebook: int = CB_
 
 
 __all__ = ["Exl3Weight", "mul_mat_batch", "decode_codebook", "decode_inner", "hadamard128", "reconstruct", "_lib"]
+
+
+# -- plan and status ---------------------------------------------------------------------------
+
+def gemm_config(min_rows: int = 0, tiles_per_cta: int = 0, splits: int = 0) -> None:
+    """Process-wide overrides of the batched path (exl3cu_gemm_config): operands of at least
+    `min_rows` rows use the tensor-core GEMM; tiles_per_cta / splits replace its automatic plan
+    (0 = automatic; min_rows 0 = unchanged)."""
+    check(lib().exl3cu_gemm_config(int(min_rows), int(tiles_per_cta), int(splits)))
+
+
+def device_status(device: int = 0, clear: bool = True) -> int:
+    """Sticky kernel error bits of `device` (bit 0: a bounded wait ran out); synchronises it."""
+    st = ctypes.c_uint(0)
+    check(lib().exl3cu_device_status(int(device), ctypes.byref(st), int(bool(clear))))
+    return st.value
