@@ -118,13 +118,14 @@ int exl3cu_mul_mat_batch(size_t count, const exl3cu_weight * const * weights, co
                          const size_t * y_row_stride, void * stream);
 
 /* Plan overrides of the batched path, process-wide (for tuning).  Operands of
- * at least `min_rows` rows run on the tensor-core GEMM (tcgen05, accumulators
- * in TMEM; default 9), smaller ones on the decode GEMV.  `tiles_per_cta`
- * (1..4 token tiles of 128 that share each decoded weight tile) and `splits`
- * (1, 2, 4, 8 or 16 CTAs of a cluster along K) replace the automatic plan;
- * 0 leaves a value automatic, min_rows 0 leaves it unchanged.  No counterpart in
- * the reference (its DSP operator fixes its row chunking, src/exl3-htp.c:165-171). */
-int exl3cu_gemm_config(size_t min_rows, int tiles_per_cta, int splits);
+ * at least `min_rows` rows run on the tensor-core GEMM (tcgen05, decoded
+ * weights and accumulators in TMEM; default 9), smaller ones on the decode
+ * GEMV.  `tokens_per_cta` (a multiple of 32 up to 256: the MMA's N) and
+ * `splits` (1, 2, 4, 8 or 16 CTAs of a cluster along K) replace the automatic
+ * plan; 0 leaves a value automatic, min_rows 0 leaves it unchanged.  No
+ * counterpart in the reference (its DSP operator fixes its row chunking,
+ * src/exl3-htp.c:165-171). */
+int exl3cu_gemm_config(size_t min_rows, int tokens_per_cta, int splits);
 
 /* Sticky error bits the kernels of `device` raised since the last clear:
  * bit 0 = a bounded wait on an asynchronous copy ran out (the results of the

@@ -1,8 +1,9 @@
-"""GPU parity of the tensor-core GEMM path (operands of 9 rows or more) against the oracle.
+"""GPU parity of the tensor-core GEMM path (operands of 5 rows or more) against the oracle.
 
-Rows of a call go to the tcgen05 GEMM from 9 upwards: token tiles of 128 (up
-to four per CTA), K split over a cluster when the column blocks alone do not
-fill the device, ragged last tiles, launches of at most 2048 rows.  Same
+Rows of a call go to the tcgen05 GEMM from 5 upwards: decoded weights in TMEM
+as the A operand, up to 256 tokens per CTA as N, K split over a cluster when
+the column blocks alone do not fill the device, ragged last token groups,
+launches of at most 2048 rows.  Same
 tolerance as the GEMV path: max|y - y_ref| / max|y_ref| <= 2e-3 and NMSE < 1e-5
 (tests/test-exl3-graph.cpp:100); decoded weights are bit-exact, activations
 enter the tensor cores rotated and rounded to fp16, products accumulate in fp32.
@@ -57,7 +58,7 @@ SHAPES = [(2048, 256), (512, 128 * 80), (1024, 768)]
 
 
 @pytest.mark.parametrize("k,n", SHAPES)
-@pytest.mark.parametrize("rows", (9, 16, 100, 128, 129, 300, 512, 600))
+@pytest.mark.parametrize("rows", (5, 9, 16, 100, 128, 129, 300, 512, 600))
 def test_gemm_rows(ops, oracle, cuda_lib, k, n, rows):
     from exl3_b200 import synthetic
 
@@ -163,7 +164,7 @@ def test_gemm_rows_independent(ops):
 
 
 def test_gemm_batch_mixed_with_gemv(ops, oracle):
-    """A grouped call whose operands split between the GEMV (<= 8 rows) and the GEMM."""
+    """A grouped call whose operands split between the GEMV (<= 4 rows) and the GEMM."""
     from exl3_b200 import synthetic
 
     k, n, bits = 1024, 384, 4

@@ -245,8 +245,8 @@ bool pdl_enabled() {
 
 // Row count from which an operand goes to the tensor-core GEMM instead of the
 // row-by-row GEMV kernels, and the plan overrides of exl3cu_gemm_config.
-std::atomic<size_t> g_gemm_min_rows{9};
-std::atomic<int> g_gemm_tiles{0};
+std::atomic<size_t> g_gemm_min_rows{5};
+std::atomic<int> g_gemm_tokens{0};
 std::atomic<int> g_gemm_splits{0};
 
 size_t gemm_min_rows() { return g_gemm_min_rows.load(std::memory_order_relaxed); }
@@ -303,15 +303,17 @@ int run_gemm(const MmItem & it, cudaStream_t st) {
     const size_t es = it.x_dtype == EXL3CU_F32 ? 4 : 2;
     for (size_t r0 = 0; r0 < it.rows; r0 += kGemmRowsPerLaunch) {
         const int rows = int(it.rows - r0 < kGemmRowsPerLaunch ? it.rows - r0 : kGemmRowsPerLaunch);
-        const GemmPlan p = plan_gemm(w->sms, w->k, w->nblocks, rows, g_gemm_tiles.load(std::memory_order_relaxed),
+        const void * x = static_cast<const char *>(it.x) + r0 * it.x_stride * es;
+        float * y = it.y + r0 * it.y_stride;
+        const GemmPlan p = plan_gemm(w->device, w->sms, w->k, w->nblocks, w->bits, w->codebook, rows,
+                                     g_gemm_tokens.load(std::memory_order_relaxed),
                                      g_gemm_splits.load(std::memory_order_relaxed));
         void * xt = nullptr;
         int rc = gemm_scratch(w->device, st, p.xt_bytes, &xt);
         if (rc) return rc;
-        cudaError_t e = launch_gemm_tc(p, w->lsc, w->su, w->sv, w->k, w->nblocks, w->bits, w->codebook, w->device,
-                                       static_cast<const char *>(it.x) + r0 * it.x_stride * es,
-                                       it.x_dtype == EXL3CU_F16, (long long)it.x_stride, rows, it.y + r0 * it.y_stride,
-                                       (long long)it.y_stride, static_cast<__half *>(xt), pdl_enabled(), st);
+        const cudaError_t e = launch_gemm(p, w->lsc, w->su, w->sv, w->k, w->nblocks, w->bits, w->codebook, w->device,
+                                          x, it.x_dtype == EXL3CU_F16, (long long)it.x_stride, rows, y,
+                                          (long long)it.y_stride, static_cast<__half *>(xt), pdl_enabled(), st);
         if (e != cudaSuccess) return cuda_fail(e, "launching the EXL3 tensor-core GEMM");
     }
     return EXL3CU_OK;
@@ -586,12 +588,13 @@ int exl3cu_weight_decode_inner(const exl3cu_weight * w, uint16_t * d_out, void *
 
 size_t exl3cu_mul_mat_workspace_bytes(const exl3cu_weight * w) { return w ? w->ws_bytes : 0; }
 
-int exl3cu_gemm_config(size_t min_rows, int tiles_per_cta, int splits) {
-    if (tiles_per_cta < 0 || tiles_per_cta > 4) return fail(EXL3CU_INVALID_ARGUMENT, "tiles_per_cta must be 0..4");
+int exl3cu_gemm_config(size_t min_rows, int tokens_per_cta, int splits) {
+    if (tokens_per_cta < 0 || tokens_per_cta > 256 || tokens_per_cta % 32)
+        return fail(EXL3CU_INVALID_ARGUMENT, "tokens_per_cta must be 0 or a multiple of 32 up to 256");
     if (splits < 0 || splits > 16 || (splits & (splits - 1)))
         return fail(EXL3CU_INVALID_ARGUMENT, "splits must be 0 or a power of two up to 16");
     if (min_rows) g_gemm_min_rows.store(min_rows, std::memory_order_relaxed);
-    g_gemm_tiles.store(tiles_per_cta, std::memory_order_relaxed);
+    g_gemm_tokens.store(tokens_per_cta, std::memory_order_relaxed);
     g_gemm_splits.store(splits, std::memory_order_relaxed);
     return EXL3CU_OK;
 }

@@ -153,4 +153,58 @@ __device__ __forceinline__ void decode_chunk(const uint32_t (&w)[2 * BITS], uint
     }
 }
 
+// Tiles C0 and C0+1 of the chunk only (a quarter of decode_chunk's work):
+// out[i] = the mma A-fragment registers of tile C0+i.  All 32 lanes take part
+// (the window's prior bits come from the neighbouring lane).
+template <int BITS, unsigned CB, int C0, int NW>
+__device__ __forceinline__ void decode_tile_pair(const uint32_t (&w)[NW], uint32_t (&out)[2][4]) {
+    static_assert(C0 % 2 == 0 && C0 >= 0 && C0 < 8, "tile pair");
+    constexpr int SLICE = 8 * BITS;
+    constexpr int HEAD = SLICE < 16 ? SLICE : 16;
+    const int lane = threadIdx.x & 31;
+    const int src = (lane + 31) & 31;
+    uint32_t prior[2];
+    uint32_t head[2];
+    if constexpr (BITS >= 2) {
+        const uint32_t t0 = seg_field16(w, SLICE * (C0 + 1) - 16);
+        const uint32_t t1 = seg_field16(w, SLICE * (C0 + 2) - 16);
+        const uint32_t got = __shfl_sync(0xffffffffu, t0 | (t1 << 16), src);
+        prior[0] = got & 0xffffu;
+        prior[1] = got >> 16;
+        head[0] = seg_field16(w, SLICE * C0);
+        head[1] = seg_field16(w, SLICE * (C0 + 1));
+    } else {
+        // bits == 1: a lane owns 8 bits per tile; the window reaches two lanes back.
+        constexpr int WI = C0 < 4 ? 0 : 1;
+        constexpr int SH0 = 24 - 8 * (C0 & 3), SH1 = 24 - 8 * ((C0 + 1) & 3);
+        const uint32_t pw = __shfl_sync(0xffffffffu, w[WI], src);
+        head[0] = (w[WI] >> SH0) & 0xffu;
+        head[1] = (w[WI] >> SH1) & 0xffu;
+        const uint32_t l0 = (((pw >> SH0) & 0xffu) << 8) | head[0];
+        const uint32_t l1 = (((pw >> SH1) & 0xffu) << 8) | head[1];
+        const uint32_t got = __shfl_sync(0xffffffffu, l0 | (l1 << 16), src);
+        prior[0] = got & 0xffffu;
+        prior[1] = got >> 16;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int c = C0 + i;
+        const uint32_t z = (prior[i] << HEAD) | head[i];
+        uint32_t s[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int end = (e + 1) * BITS;
+            if (end <= HEAD) {
+                s[e] = (z >> (HEAD - end)) & 0xffffu;
+            } else {
+                s[e] = seg_field16(w, SLICE * c + end - 16);
+            }
+        }
+        out[i][0] = decode_pair<CB>(s[0], s[1]);
+        out[i][1] = decode_pair<CB>(s[4], s[5]);
+        out[i][2] = decode_pair<CB>(s[2], s[3]);
+        out[i][3] = decode_pair<CB>(s[6], s[7]);
+    }
+}
+
 }  // namespace exl3cu

@@ -2,30 +2,37 @@
 // TMEM) for batches of rows -- the ragged continuous-batching path.
 //
 // y = sv * H128( sum_kb H128(x * su)_kb . W_inner(kb) ) per 128-column block,
-// as ggml_exl3_mul_mat computes it (src/exl3-ggml.cpp:51-92).  Per MMA:
-//   A = rotated activations, M = 128 tokens x K = 16, fp16, K-major;
-//   B = W_inner^T, N = 128 output columns (one column block) x K = 16, fp16;
-//   D = fp32 in TMEM, 128 lanes (tokens) x 128 columns.
-// The decoded weights are the reference's fp16 values bit for bit (the same
-// decode_chunk the codec kernels use); the products accumulate in fp32.
+// as ggml_exl3_mul_mat computes it (src/exl3-ggml.cpp:51-92), with the
+// reference's decoded fp16 weights bit for bit and fp32 accumulation.
 //
-// Shared-memory operands use the canonical no-swizzle K-major layout: 8x16-byte
-// core matrices, LBO = stride between the two 8-element K halves, SBO = stride
-// between 8-row groups.  A decode lane's four mma-fragment registers of a
-// 16x16 tile fall on exactly four core matrices, one 32-bit store each, with
-// the 32 lanes of a warp covering a core matrix's 128 contiguous bytes.
+// Swap-AB form, per MMA (kind::f16, M = 128, N = NTOK tokens, K = 16):
+//   A = W_inner^T of one column block (128 output columns x 16 rows of K), in
+//       TENSOR MEMORY, written there by the decode warps with tcgen05.st;
+//   B = the rotated activations (NTOK tokens x 16), fp16, K-major in shared
+//       memory, bulk-copied from a buffer the prologue kernel writes;
+//   D = fp32 in TMEM: 128 lanes (output columns) x NTOK columns (tokens).
+// The decoded weights never touch shared memory, the MMA reads only the
+// activation tile, and its cost scales with the batch's tokens (32..256 per
+// CTA), not with a padded 128-token tile.
 //
-// A CTA owns one column block, T <= 4 token tiles of 128 and one K range: it
-// decodes each 16-row chunk of W once and issues T MMAs on it, one per token
-// tile, into T TMEM accumulators (T*128 columns).  Warp roles (320 threads):
-// warp 0 owns TMEM and issues the activation bulk copies; warp 1's elected
-// thread issues tcgen05.mma and the commits that recycle the rings; warps
-// 2-9 stream the CTA's trellis chunks from HBM and decode them into a ring of
-// B tiles, then run the epilogue.  The K split runs across a thread-block
-// cluster: every rank parks its fp32 partial tile in shared memory and rank r
-// reduces rows [r*128/S, (r+1)*128/S) over all ranks in rank order through
-// distributed shared memory, applies H128 and sv and stores y.  Every mbarrier
-// wait is bounded.
+// A in TMEM: lane m = output column, 32-bit column j = a pair of K values.  A
+// decode lane (g, t) holds, per 16x16 tile, K pairs {2t, 2t+1} and {2t+8, 2t+9}
+// of columns g and g+8 (the mma A-fragment layout of decode_tile_pair), and
+// tcgen05.st.16x256b puts thread (g, t)'s four registers at (lane g | g+8,
+// column 2t | 2t+1): column 2t holds K (2t, 2t+1), column 2t+1 holds K
+// (2t+8, 2t+9).  The activations are stored with the same permutation of K
+// inside every 16 (kperm16), so each dot product is an exact re-ordering of
+// the unpermuted one.  A warp may only address its own quarter of the TMEM
+// lanes, so a chunk's 8 tiles are decoded by a warpgroup: warp quarter q
+// decodes tiles 2q and 2q+1 (output columns 32q..32q+31).
+//
+// Warps (512 threads): 0-11 = three decode warpgroups (group g of 8 chunks
+// goes to warpgroup g % 3), later the epilogue; 12 = TMEM owner + trellis bulk
+// copies; 13 = MMA issue (one thread); 14 = activation bulk copies.  The K
+// split runs across a thread-block cluster: every rank parks its fp32 partial
+// [NTOK][128] in shared memory and rank r reduces tokens [r*NTOK/S,
+// (r+1)*NTOK/S) over all ranks in rank order through distributed shared
+// memory, applies H128 and sv and stores y.  Every mbarrier wait is bounded.
 #include "exl3cu_async.cuh"
 #include "exl3cu_internal.h"
 
@@ -39,42 +46,13 @@ namespace exl3cu {
 
 static __device__ unsigned g_gemm_status;
 
-constexpr int kDecodeWarps = 8;
-constexpr int kFirstDecodeWarp = 3;  // warps 0-2: weight copies + TMEM, MMA issue, activation copies
-constexpr int kTThreads = 32 * (kFirstDecodeWarp + kDecodeWarps);
-constexpr int kBGroups = 3;          // decoded W groups of 4 chunks (4 KB B tiles) in the ring
-constexpr int kBTileBytes = 4096;
-constexpr int kBRingBytes = kBGroups * 4 * kBTileBytes;
-constexpr int kWRingBytes = 32768;   // trellis stages of 4 chunks in flight (>= 4 stages at 8 bits)
 constexpr int kMaxWStages = 16;
-constexpr int kMaxXStages = 3;       // activation stages of 64 K (4 chunks): 3 for T <= 2, else 2
-constexpr int kXTileBytes = 16384;   // 64 K x 128 tokens fp16: one token tile of a stage
-constexpr int kMaxTiles = 4;         // token tiles per CTA (T*128 TMEM columns <= 512)
-constexpr int kPartStride = 132;     // floats per row of the parked partial tile
 constexpr size_t kBarBytes = 512;
 // Shared memory is padded to at least this, so that one CTA fits an SM: two
 // CTAs could otherwise ask for more than the SM's 512 TMEM columns together,
 // and tcgen05.alloc would wait for columns that a cluster peer never frees.
 constexpr size_t kMinSmem = 120 * 1024;
-// kind::f16: D fp32 (bit 4), A/B fp16, both K-major, N = 128 (>>3 at bit 17), M = 128 (>>4 at bit 24)
-constexpr uint32_t kIdescF16 = (1u << 4) | (16u << 17) | (8u << 24);
-
-struct GemmArgs {
-    const uint32_t * lsc;  // device-layout weights of the handle's column blocks
-    const __half * sv;     // [nblocks * 128]
-    const __half * xt;     // tiled rotated activations, see k_tile_x
-    float * y;             // [M][y_stride]
-    long long y_stride;
-    int M;                 // valid rows
-    int T;                 // token tiles per CTA
-    int tgroups;           // groups of T token tiles
-    int nchunks;           // k / 16
-    int nblocks;
-    int cps;               // chunks per cluster rank, a multiple of 4
-    int splits;
-    int tmem_cols;
-    int xstages;           // activation stages in the ring (2 or 3)
-};
+static_assert(2 * kMinSmem > 228 * 1024, "the padding must keep a second CTA off the SM");
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
     uint64_t d = 0;
@@ -85,15 +63,6 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
     return d;                // base offset 0, relative LBO, layout type 0 = no swizzle
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdescF16), "r"(accumulate)
-        : "memory");
-}
-
 // Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
 __device__ __forceinline__ void umma_commit(uint64_t * bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
@@ -102,7 +71,6 @@ __device__ __forceinline__ void umma_commit(uint64_t * bar) {
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // 32 consecutive fp32 TMEM columns of this thread's lane.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
@@ -120,23 +88,54 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// ---------------------------------------------------------------------------
-// Activation prologue: xh = H128(x * su) per (row, 128-group), rounded to fp16
-// (src/exl3-ggml.cpp:60-70 forms the same rotated row), written in the A
-// operand's tiled order: element (token, kk) of token tile `tile` at half
-//   tile*128*k + (kk/16)*2048 + ((token%128)/8)*128 + ((kk/8)%2)*64 + (token%8)*8 + kk%8,
-// i.e. per 16 columns of K a 4 KB block of 8x16-byte core matrices, row group
-// r and K half h at r*256 + h*128 bytes (the B tile's arrangement, which the
-// tensor cores read at full rate), so a group of 4 chunks of one token tile is
-// 16 contiguous KB.  Rows at or beyond M are zero.  One warp per (row, group).
-__global__ void k_tile_x(const void * __restrict__ x, int x_f16, long long x_stride, const __half * __restrict__ su,
-                         int M, int k, int ntiles, __half * __restrict__ xt) {
+constexpr int kDecodeGroups = 3;
+constexpr int kGemmThreads = 512;
+constexpr int kGroupChunks = 8;    // chunks (16 rows of K each) per pipeline group
+
+// Trellis ring of the swap-AB kernel: `wstages` groups, chosen per launch as
+// deep as shared memory allows next to the activation slots (up to ~96 KB, so
+// that an SM reading weights held by the other die still keeps enough bytes in
+// flight).  The depth is a multiple of the number of decode warpgroups, so that
+// each slot is only ever consumed by one warpgroup (group g goes to warpgroup
+// g % 3 and to slot g % wstages): a parity wait is only sound when the waiter
+// itself saw the barrier's previous phase complete, and bulk copies into
+// different slots may complete in any order.
+constexpr int kSlots = 3;          // groups in flight: TMEM A (64 columns each) + activations
+constexpr int kMaxTok = 256;       // tokens per CTA (the MMA's N)
+constexpr uint32_t kTmemCols = 512;
+constexpr int kACol0 = 256;        // first TMEM column of the A ring (D uses 0..NTOK-1)
+
+// Position inside a 16-block of K at which the A operand in TMEM holds k.
+__host__ __device__ constexpr int kperm16(int k) { return 4 * ((k & 7) >> 1) + 2 * (k >> 3) + (k & 1); }
+
+struct GemmArgs {
+    const uint32_t * lsc;
+    const __half * sv;
+    const __half * xt;  // [tgroups][k/16][NTOK/8][2][8][8] fp16, K permuted by kperm16
+    float * y;
+    long long y_stride;
+    int M;
+    int ntok;           // tokens per CTA, multiple of 32, <= 256
+    int tgroups;
+    int nchunks;
+    int cps;            // multiple of kGroupChunks
+    int splits;
+    int wstages;        // trellis ring depth in groups, a multiple of 3
+};
+
+// xh = H128(x * su) per (row, 128-group) in fp16, laid out as the B operand:
+// token group tg = token / ntok, tr = token % ntok, element k of chunk kc at half
+//   tg*ntok*k_total + kc*ntok*16 + (tr/8)*128 + (p/8)*64 + (tr%8)*8 + p%8,  p = kperm16(k % 16)
+// (8-token x 16-byte core matrices, 8-token groups 256 B apart, K halves 128 B apart).
+__global__ void k_tile_x(const void * __restrict__ x, int x_f16, long long x_stride,
+                            const __half * __restrict__ su, int M, int k, int ntok, int rows_pad,
+                            __half * __restrict__ xt) {
     pdl_trigger();
-    pdl_wait_primary();  // x comes from the previous kernel; xt may still be read by the previous GEMM
+    pdl_wait_primary();
     const int warp = int((blockIdx.x * size_t(blockDim.x) + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
     const int groups = k / 128;
-    if (warp >= ntiles * 128 * groups) return;  // whole warps only: the count is a multiple of 8
+    if (warp >= rows_pad * groups) return;  // whole warps: rows_pad is a multiple of 32
     const int tok = warp / groups, gi = warp % groups;
     const int kcol = gi * 128 + lane * 4;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -159,74 +158,113 @@ __global__ void k_tile_x(const void * __restrict__ x, int x_f16, long long x_str
         v[3] = __fmul_rn(v[3], __high2float(s23));
     }
     h128_warp4(v);
-    const int tile = tok >> 7, tr = tok & 127;
-    const size_t off = size_t(tile) * 128 * k + size_t(kcol >> 4) * 2048 + (tr >> 3) * 128 + ((kcol >> 3) & 1) * 64 +
-                       (tr & 7) * 8 + (kcol & 7);
-    const __half2 o01 = __floats2half2_rn(v[0], v[1]);
-    const __half2 o23 = __floats2half2_rn(v[2], v[3]);
-    *reinterpret_cast<uint2 *>(xt + off) = make_uint2(half2_bits(o01), half2_bits(o23));
+    const int tg = tok / ntok, tr = tok - tg * ntok;
+    const int kk = kcol & 15;  // 0, 4, 8 or 12: values go to p, p+1 and p+4, p+5
+    const int p = kperm16(kk);
+    const size_t base = size_t(tg) * ntok * k + size_t(kcol >> 4) * ntok * 16 + (tr >> 3) * 128 + (tr & 7) * 8;
+    __half * dst0 = xt + base + (p >> 3) * 64 + (p & 7);
+    __half * dst1 = xt + base + ((p + 4) >> 3) * 64 + ((p + 4) & 7);
+    *reinterpret_cast<uint32_t *>(dst0) = half2_bits(__floats2half2_rn(v[0], v[1]));
+    *reinterpret_cast<uint32_t *>(dst1) = half2_bits(__floats2half2_rn(v[2], v[3]));
 }
 
-// ---------------------------------------------------------------------------
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
 
+
+// This lane's part of tiles 2q and 2q+1 of one chunk (trellis at `chunk`):
+// bits [16*BITS*q, 16*BITS*(q+1)) of its 8*BITS-byte segment, realigned to
+// start at bit 0, so that one code path serves all four warp quarters (the
+// decode loop stays small enough for the instruction caches).  The loads may
+// run up to two words past the segment; they stay inside the CTA's shared
+// memory (the activation slots follow the trellis ring) and those bits are
+// never used.
 template <int BITS, unsigned CB>
-__global__ void __launch_bounds__(kTThreads, 1) k_gemm_tc(const GemmArgs a) {
+__device__ __forceinline__ void decode_pair_window(const unsigned char * chunk, int q, uint32_t (&f)[2][4]) {
+    constexpr int NW = BITS / 2 + 1;  // words holding 16*BITS bits at a 16-bit offset
+    const int lane = threadIdx.x & 31;
+    const int bq = BITS * q;           // first bit / 16
+    const uint32_t * seg = reinterpret_cast<const uint32_t *>(chunk) + lane * (2 * BITS) + (bq >> 1);
+    const uint32_t sh = uint32_t(bq & 1) * 16u;
+    uint32_t raw[NW + 1];
+#pragma unroll
+    for (int i = 0; i <= NW; ++i) raw[i] = seg[i];
+    uint32_t w[NW];
+#pragma unroll
+    for (int i = 0; i < NW; ++i) w[i] = __funnelshift_l(raw[i + 1], raw[i], sh);
+    decode_tile_pair<BITS, CB, 0>(w, f);
+}
+
+// 16 TMEM lanes x 8 columns (one chunk of one tile) from its four A-fragment
+// registers: (lane g, col 2t) = K 2t..2t+1 of column g, (g, 2t+1) = K 2t+8..2t+9,
+// and the same two for column g+8.
+__device__ __forceinline__ void tmem_st_tile(uint32_t taddr, const uint32_t (&f)[4]) {
+    asm volatile("tcgen05.st.sync.aligned.16x256b.x1.b32 [%0], {%1, %2, %3, %4};"
+                 ::"r"(taddr), "r"(f[0]), "r"(f[2]), "r"(f[1]), "r"(f[3]) : "memory");
+}
+
+// One CTA = one column block x NTOK tokens x one K range, in groups of 8 chunks
+// (128 rows of K).  A group occupies one of kSlots slots: 64 TMEM columns of
+// decoded weights plus NTOK x 128 fp16 activations in shared memory, guarded by
+// one full barrier (4 decode-warp arrivals + the activation copy's arrival and
+// bytes) and one empty barrier (the MMA commit, waited on by both producers).
+// The MMA thread's whole loop is: wait full, 8 MMAs, commit empty.
+template <int BITS, unsigned CB>
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const GemmArgs a) {
     extern __shared__ __align__(1024) unsigned char smem[];
-    constexpr int SEGW = 2 * BITS;                   // words of one lane's segment of a chunk
-    constexpr int CHUNKB = 256 * BITS;               // bytes of one chunk
-    constexpr int WSTAGEB = 4 * CHUNKB;              // bytes of one weight stage (a group of 4 chunks)
-    constexpr int WST = kWRingBytes / WSTAGEB > kMaxWStages ? kMaxWStages : kWRingBytes / WSTAGEB;
+    constexpr int CHUNKB = 256 * BITS;
+    constexpr int WSTAGEB = kGroupChunks * CHUNKB;  // one group of trellis
+    const int WST = a.wstages;
+    const int WRING = WST * WSTAGEB;
     pdl_trigger();
 
     cg::cluster_group cluster = cg::this_cluster();
     const int S = a.splits;
-    const int T = a.T;
-    const int XST = a.xstages;
+    const int NT = a.ntok;
     const int split = int(cluster.block_rank());
     const int unit = blockIdx.x / S;
     const int nb = unit / a.tgroups;
     const int tg = unit - nb * a.tgroups;
     const int c0 = min(split * a.cps, a.nchunks);
     const int c1 = min(c0 + a.cps, a.nchunks);
-    const int nch = c1 - c0;  // a multiple of 4: k and cps are
-    const int ngr = nch / 4;  // groups of 4 chunks (64 rows of K): the unit of every ring
+    const int ngr = (c1 - c0) / kGroupChunks;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int xstage_bytes = T * kXTileBytes;
+    const int xslot_bytes = NT * 16 * 2 * kGroupChunks;  // NT tokens x 128 K fp16
 
-    unsigned char * bring = smem;                 // kBGroups x 4 decoded B tiles of 4 KB
-    unsigned char * wring = bring + kBRingBytes;  // WST x 4 chunks of trellis
-    unsigned char * xring = wring + kWRingBytes;  // XST x T x 16 KB activations
-    uint64_t * bars = reinterpret_cast<uint64_t *>(xring + XST * xstage_bytes);
-    uint64_t * fullB = bars;
-    uint64_t * emptyB = fullB + kBGroups;
-    uint64_t * fullW = emptyB + kBGroups;
+    unsigned char * wring = smem;           // WST groups of trellis
+    unsigned char * xring = wring + WRING;  // kSlots groups of activations
+    uint64_t * bars = reinterpret_cast<uint64_t *>(xring + kSlots * xslot_bytes);
+    uint64_t * fullW = bars;
     uint64_t * emptyW = fullW + kMaxWStages;
-    uint64_t * fullX = emptyW + kMaxWStages;
-    uint64_t * emptyX = fullX + kMaxXStages;
-    uint64_t * done = emptyX + kMaxXStages;
+    uint64_t * full = emptyW + kMaxWStages;
+    uint64_t * empty = full + kSlots;
+    uint64_t * done = empty + kSlots;
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
-    float * part = reinterpret_cast<float *>(smem);  // epilogue reuse of the rings: [128][kPartStride]
+    float * part = reinterpret_cast<float *>(smem);  // epilogue reuse: [NT][128] fp32
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kBGroups; ++i) {
-            mbar_init(&fullB[i], 4);   // the four decode warps of the group's chunks
-            mbar_init(&emptyB[i], 1);  // the MMA commit
-        }
         for (int i = 0; i < WST; ++i) {
             mbar_init(&fullW[i], 1);
-            mbar_init(&emptyW[i], 4);
+            mbar_init(&emptyW[i], 4);  // the four warps of the decoding warpgroup
         }
-        for (int i = 0; i < XST; ++i) {
-            mbar_init(&fullX[i], 1);
-            mbar_init(&emptyX[i], 1);
+        for (int i = 0; i < kSlots; ++i) {
+            mbar_init(&full[i], 5);   // four decode warps + the activation copy
+            mbar_init(&empty[i], 1);  // the MMA commit
         }
         mbar_init(done, 1);
         mbar_init_fence();
     }
-    if (warp == 0) {
+    if (warp == 12) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     ::"r"(smem_addr(tmem_slot)), "r"(uint32_t(a.tmem_cols)) : "memory");
+                     ::"r"(smem_addr(tmem_slot)), "r"(kTmemCols) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
@@ -234,8 +272,8 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemm_tc(const GemmArgs a) {
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
-        // ---- weight groups: static data, streamed from the first cycle (before the PDL wait) ----
+    if (warp == 12) {
+        // ---- trellis groups: static data, streamed from the first cycle (before the PDL wait) ----
         if (lane == 0) {
             const unsigned char * src =
                 reinterpret_cast<const unsigned char *>(a.lsc) + (size_t(nb) * a.nchunks + c0) * CHUNKB;
@@ -250,166 +288,144 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemm_tc(const GemmArgs a) {
             }
         }
         __syncwarp();
-    } else if (warp == 1) {
-        // ---- MMA issue: one thread, 4*T MMAs per group of 4 chunks ----
+    } else if (warp == 13) {
+        // ---- MMA issue (one thread): ring position and phase carried incrementally ----
         if (lane == 0) {
-            // start-address fields of the first B tile / activation tile; later tiles are constant offsets
-            const uint64_t bdesc0 = umma_desc(smem_addr(bring), 128, 256);
-            const uint64_t adesc0 = umma_desc(smem_addr(xring), 128, 256);
+            const uint32_t idesc = (1u << 4) | (uint32_t(NT >> 3) << 17) | (8u << 24);
+            const uint64_t bdesc0 = umma_desc(smem_addr(xring), 128, 256);
+            const uint64_t bchunk = uint64_t((NT * 32) >> 4);
+            const uint64_t bslot = uint64_t(xslot_bytes >> 4);
+            uint32_t slot = 0, phase = 0, acc = 0;
+            uint64_t bd = bdesc0;
+            uint32_t acol = tmem + uint32_t(kACol0);
             for (int g = 0; g < ngr; ++g) {
-                const int bs = g % kBGroups, xs = g % XST;
-                if (!mbar_wait_sleep(&fullB[bs], (g / kBGroups) & 1) || !mbar_wait_sleep(&fullX[xs], (g / XST) & 1)) {
+                if (!mbar_wait(&full[slot], phase)) {
                     atomicOr(&g_gemm_status, kStatusWaitTimeout);
                     break;
                 }
-                tc_fence_after();
+                tc_fence_after();  // A was written to TMEM by other threads' tcgen05.st
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const uint64_t bdesc = bdesc0 + uint64_t(((bs * 4 + c) * kBTileBytes) >> 4);
-                    for (int t = 0; t < T; ++t) {
-                        const uint64_t adesc = adesc0 + uint64_t(((xs * T + t) * kXTileBytes + c * 4096) >> 4);
-                        umma_f16(tmem + uint32_t(t * 128), adesc, bdesc, (g | c) != 0 ? 1u : 0u);
-                    }
+                for (int c = 0; c < kGroupChunks; ++c) {
+                    umma_ts(tmem, acol + uint32_t(c * 8), bd + uint64_t(c) * bchunk, idesc, c == 0 ? acc : 1u);
                 }
-                umma_commit(&emptyB[bs]);
-                umma_commit(&emptyX[xs]);
+                acc = 1u;
+                umma_commit(&empty[slot]);
+                if (++slot == uint32_t(kSlots)) {
+                    slot = 0;
+                    phase ^= 1u;
+                    bd = bdesc0;
+                    acol = tmem + uint32_t(kACol0);
+                } else {
+                    bd += bslot;
+                    acol += uint32_t(kGroupChunks * 8);
+                }
             }
             if (ngr > 0)
-                umma_commit(done);  // arrives once every issued MMA has completed
+                umma_commit(done);
             else
                 mbar_arrive(done);
         }
         __syncwarp();
-    } else if (warp == 2) {
+    } else if (warp == 14) {
         // ---- activation groups (written by the prologue kernel: wait for it first) ----
         if (lane == 0) {
             pdl_wait_primary();
-            const size_t tile_halves = size_t(a.nchunks) * 2048;  // one token tile, all of K
-            const __half * src = a.xt + size_t(tg) * T * tile_halves + size_t(c0) * 2048;
+            const __half * src = a.xt + size_t(tg) * NT * (size_t(a.nchunks) * 16) + size_t(c0) * NT * 16;
             for (int g = 0; g < ngr; ++g) {
-                const int slot = g % XST;
-                if (g >= XST && !mbar_wait_sleep(&emptyX[slot], ((g / XST) - 1) & 1)) {
+                const int slot = g % kSlots;
+                if (g >= kSlots && !mbar_wait_sleep(&empty[slot], ((g / kSlots) - 1) & 1)) {
                     atomicOr(&g_gemm_status, kStatusWaitTimeout);
                     break;
                 }
-                mbar_arrive_expect_tx(&fullX[slot], uint32_t(xstage_bytes));
-                for (int t = 0; t < T; ++t)
-                    bulk_g2s(xring + (slot * T + t) * kXTileBytes, src + size_t(t) * tile_halves + size_t(g) * 4 * 2048,
-                             kXTileBytes, &fullX[slot]);
+                mbar_arrive_expect_tx(&full[slot], uint32_t(xslot_bytes));
+                bulk_g2s(xring + slot * xslot_bytes, src + size_t(g) * NT * 16 * kGroupChunks, uint32_t(xslot_bytes),
+                         &full[slot]);
             }
         }
         __syncwarp();
-    } else {
-        // ---- decode warps: chunk j of the CTA's range goes to warp j % 8 ----
-        const int dw = warp - kFirstDecodeWarp;
-        for (int j = dw; j < nch; j += kDecodeWarps) {
-            const int g = j >> 2, ws = g % WST;
-            if (!mbar_wait_sleep(&fullW[ws], (g / WST) & 1)) {
+    } else if (warp < 12) {
+        // ---- decode: warpgroup wg takes groups wg, wg+3, ...; warp quarter q its tiles 2q, 2q+1 ----
+        const int wg = warp >> 2, q = warp & 3;
+        const uint32_t lane0 = tmem + (uint32_t(q * 32) << 16);       // tile 2q:   lanes 32q..+15
+        const uint32_t lane1 = tmem + (uint32_t(q * 32 + 16) << 16);  // tile 2q+1: lanes 32q+16..+31
+        for (int g = wg; g < ngr; g += kDecodeGroups) {
+            const int ws = g % WST;
+            const int slot = g % kSlots;
+            if (!mbar_wait_sleep(&fullW[ws], (g / WST) & 1) ||
+                (g >= kSlots && !mbar_wait_sleep(&empty[slot], ((g / kSlots) - 1) & 1))) {
                 atomicOr(&g_gemm_status, kStatusWaitTimeout);
                 break;
             }
-            uint32_t w[SEGW];
-            const uint32_t * seg = reinterpret_cast<const uint32_t *>(wring + ws * WSTAGEB + (j & 3) * CHUNKB) +
-                                   lane * SEGW;
-            if constexpr ((BITS & 1) == 0) {
-#pragma unroll
-                for (int i = 0; i < SEGW; i += 4) {
-                    const uint4 v = *reinterpret_cast<const uint4 *>(seg + i);
-                    w[i] = v.x; w[i + 1] = v.y; w[i + 2] = v.z; w[i + 3] = v.w;
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < SEGW; i += 2) {
-                    const uint2 v = *reinterpret_cast<const uint2 *>(seg + i);
-                    w[i] = v.x; w[i + 1] = v.y;
-                }
+            tc_fence_after();  // the MMAs that read this slot have completed
+            const unsigned char * wst = wring + ws * WSTAGEB;
+            const uint32_t col = uint32_t(kACol0 + slot * kGroupChunks * 8);
+#pragma unroll 1
+            for (int c = 0; c < kGroupChunks; ++c) {
+                uint32_t f[2][4];
+                decode_pair_window<BITS, CB>(wst + c * CHUNKB, q, f);
+                tmem_st_tile(lane0 + col + uint32_t(c * 8), f[0]);
+                tmem_st_tile(lane1 + col + uint32_t(c * 8), f[1]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&emptyW[ws]);
-            uint32_t frag[8][4];
-            decode_chunk<BITS, CB>(w, frag);
-            const int bs = g % kBGroups;
-            if (g >= kBGroups && !mbar_wait_sleep(&emptyB[bs], ((g / kBGroups) - 1) & 1)) {
-                atomicOr(&g_gemm_status, kStatusWaitTimeout);
-                break;
-            }
-            uint32_t * bt = reinterpret_cast<uint32_t *>(bring + (bs * 4 + (j & 3)) * kBTileBytes);
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                // core matrix (column group 2c or 2c+1, K half 0 or 1) at group*256 + half*128 bytes;
-                // lane (g = lane/4, t = lane%4) holds columns 16c+g / 16c+8+g, K pairs 2t / 2t+8 of tile c
-                bt[(c * 512 + 0) / 4 + lane] = frag[c][0];    // column 16c+g,   K 2t..2t+1
-                bt[(c * 512 + 256) / 4 + lane] = frag[c][1];  // column 16c+8+g, K 2t..2t+1
-                bt[(c * 512 + 128) / 4 + lane] = frag[c][2];  // column 16c+g,   K 2t+8..2t+9
-                bt[(c * 512 + 384) / 4 + lane] = frag[c][3];  // column 16c+8+g, K 2t+8..2t+9
-            }
-            fence_proxy_async();  // the generic-proxy stores become visible to the tensor cores
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&fullB[bs]);
+            if (lane == 0) mbar_arrive(&full[slot]);
         }
     }
 
-    // ---- epilogue: per token tile, park the partial, then reduce a row slice over the cluster ----
-    const bool epi = warp >= kFirstDecodeWarp;
+    // ---- epilogue: D[col][token] -> part[token][col]; rank r reduces tokens [r*NT/S, (r+1)*NT/S) ----
+    const bool epi = warp < 12;
     if (epi && !mbar_wait_sleep(done, 0)) atomicOr(&g_gemm_status, kStatusWaitTimeout);
     tc_fence_after();
     __syncthreads();  // every MMA has completed: the rings are free for the partial tile
-    const int rows_per_rank = 128 / S;
-    const int ew = warp - kFirstDecodeWarp;  // epilogue warp 0..7
-    for (int t = 0; t < T; ++t) {
-        if (epi) {
-            const int q = warp & 3;  // TMEM lane quarter this warp may read
-            const int h = ew >> 2;   // column half
-            const int row = q * 32 + lane;
-            float * dst = part + row * kPartStride + h * 64;
+    if (epi) {
+        const int wg = warp >> 2, q = warp & 3;
+        for (int tc = wg; tc < NT / 32; tc += kDecodeGroups) {
+            float v[32];
+            if (ngr > 0) {
+                tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(tc * 32), v);
+            } else {
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float v[32];
-                if (nch > 0) {
-                    tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(t * 128 + h * 64 + c * 32), v);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = 0.f;
-                }
-#pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                    *reinterpret_cast<float4 *>(dst + c * 32 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                for (int i = 0; i < 32; ++i) v[i] = 0.f;
             }
+#pragma unroll
+            for (int r = 0; r < 32; ++r) part[(tc * 32 + r) * 128 + q * 32 + lane] = v[r];
         }
-        cluster.sync();
-        if (epi) {
-            const uint2 sraw = *reinterpret_cast<const uint2 *>(a.sv + nb * 128 + lane * 4);
-            const __half2 s01 = bits_half2(sraw.x), s23 = bits_half2(sraw.y);
-            for (int r = split * rows_per_rank + ew; r < (split + 1) * rows_per_rank; r += kDecodeWarps) {
-                float v[4] = {0.f, 0.f, 0.f, 0.f};
-                for (int s = 0; s < S; ++s) {
-                    const float * rp = cluster.map_shared_rank(part, s) + r * kPartStride + lane * 4;
-                    const float4 p = *reinterpret_cast<const float4 *>(rp);
-                    v[0] = __fadd_rn(v[0], p.x);
-                    v[1] = __fadd_rn(v[1], p.y);
-                    v[2] = __fadd_rn(v[2], p.z);
-                    v[3] = __fadd_rn(v[3], p.w);
-                }
-                h128_warp4(v);
-                const int token = (tg * T + t) * 128 + r;
-                if (token < a.M) {
-                    float4 o;
-                    o.x = __fmul_rn(v[0], __low2float(s01));
-                    o.y = __fmul_rn(v[1], __high2float(s01));
-                    o.z = __fmul_rn(v[2], __low2float(s23));
-                    o.w = __fmul_rn(v[3], __high2float(s23));
-                    *reinterpret_cast<float4 *>(a.y + size_t(token) * a.y_stride + nb * 128 + lane * 4) = o;
-                }
-            }
-        }
-        cluster.sync();  // the partials stay until every rank has read them
     }
+    cluster.sync();
+    if (epi) {
+        const int per = NT / S;
+        const uint2 sraw = *reinterpret_cast<const uint2 *>(a.sv + nb * 128 + lane * 4);
+        const __half2 s01 = bits_half2(sraw.x), s23 = bits_half2(sraw.y);
+        for (int t = split * per + warp; t < (split + 1) * per; t += 12) {
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int s = 0; s < S; ++s) {
+                const float4 p = *reinterpret_cast<const float4 *>(cluster.map_shared_rank(part, s) + t * 128 + lane * 4);
+                v[0] = __fadd_rn(v[0], p.x);
+                v[1] = __fadd_rn(v[1], p.y);
+                v[2] = __fadd_rn(v[2], p.z);
+                v[3] = __fadd_rn(v[3], p.w);
+            }
+            h128_warp4(v);
+            const int token = tg * NT + t;
+            if (token < a.M) {
+                float4 o;
+                o.x = __fmul_rn(v[0], __low2float(s01));
+                o.y = __fmul_rn(v[1], __high2float(s01));
+                o.z = __fmul_rn(v[2], __low2float(s23));
+                o.w = __fmul_rn(v[3], __high2float(s23));
+                *reinterpret_cast<float4 *>(a.y + size_t(token) * a.y_stride + nb * 128 + lane * 4) = o;
+            }
+        }
+    }
+    cluster.sync();  // the partials stay until every rank has read them
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 12) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(uint32_t(a.tmem_cols))
-                     : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
     }
 }
 
@@ -420,9 +436,9 @@ namespace {
 template <int BITS>
 void * gemm_kernel_cb(unsigned cb) {
     switch (cb) {
-        case CB_3INST: return reinterpret_cast<void *>(k_gemm_tc<BITS, CB_3INST>);
-        case CB_MCG: return reinterpret_cast<void *>(k_gemm_tc<BITS, CB_MCG>);
-        case CB_MUL1: return reinterpret_cast<void *>(k_gemm_tc<BITS, CB_MUL1>);
+        case CB_3INST: return reinterpret_cast<void *>(k_gemm<BITS, CB_3INST>);
+        case CB_MCG: return reinterpret_cast<void *>(k_gemm<BITS, CB_MCG>);
+        case CB_MUL1: return reinterpret_cast<void *>(k_gemm<BITS, CB_MUL1>);
         default: return nullptr;
     }
 }
@@ -441,21 +457,38 @@ void * gemm_kernel_for(unsigned bits, unsigned cb) {
     }
 }
 
-int xstages_for(int T) { return T <= 2 ? 3 : 2; }
+constexpr size_t kGemmMaxSmem = 227 * 1024;
 
-size_t gemm_smem(int T) {
-    const size_t s = size_t(kBRingBytes) + kWRingBytes + size_t(xstages_for(T)) * T * kXTileBytes + kBarBytes;
+size_t group_bytes(unsigned bits) { return size_t(kGroupChunks) * 256 * bits; }
+size_t xring_bytes(int ntok) { return size_t(kSlots) * ntok * 32 * kGroupChunks; }
+
+size_t gemm_smem(unsigned bits, int ntok, int wstages) {
+    const size_t s = size_t(wstages) * group_bytes(bits) + xring_bytes(ntok) + kBarBytes;
     return s < kMinSmem ? kMinSmem : s;
 }
 
-constexpr size_t kGemmMaxSmem = size_t(kBRingBytes) + kWRingBytes + size_t(2) * kMaxTiles * kXTileBytes + kBarBytes;
-static_assert(kGemmMaxSmem <= 227 * 1024, "GEMM shared memory above the per-CTA limit");
-static_assert(size_t(kBRingBytes) + kWRingBytes + size_t(3) * 2 * kXTileBytes + kBarBytes <= kGemmMaxSmem,
-              "T = 2 with three activation stages must fit the same limit");
-static_assert(size_t(128) * kPartStride * 4 <= size_t(kBRingBytes) + kWRingBytes + 2 * kXTileBytes,
-              "the partial tile must fit in the rings of the smallest plan (T = 1, two activation stages)");
-static_assert(2 * kMinSmem > 228 * 1024, "the padding must keep a second CTA off the SM");
-static_assert((2 * kBGroups + 2 * kMaxWStages + 2 * kMaxXStages + 1) * 8 + 4 <= kBarBytes, "barrier area");
+// Most tokens per CTA (a multiple of 32, <= 256) whose rings fit the shared
+// memory with the minimum trellis ring of three groups.
+int gemm_max_tokens(unsigned bits) {
+    const long long room = (long long)kGemmMaxSmem - kBarBytes - 3 * (long long)group_bytes(bits);
+    const int t = int(room / (kSlots * 32 * kGroupChunks)) / 32 * 32;
+    return t < kMaxTok ? t : kMaxTok;
+}
+
+// Deepest trellis ring (a multiple of 3 groups, <= 15 groups and ~96 KB) that fits next to the activation slots.
+int gemm_wstages(unsigned bits, int ntok) {
+    const long long room = (long long)kGemmMaxSmem - kBarBytes - (long long)xring_bytes(ntok);
+    long long by_room = room / (long long)group_bytes(bits);
+    long long by_bytes = (96 * 1024) / (long long)group_bytes(bits);
+    long long w = by_room < by_bytes ? by_room : by_bytes;
+    if (w > kMaxWStages - 1) w = kMaxWStages - 1;
+    w = w / 3 * 3;
+    return w < 3 ? 3 : int(w);
+}
+// the partial tile [NTOK][128] fp32 reuses the activation slots: 512 NTOK <= 768 NTOK
+static_assert(kSlots * 32 * kGroupChunks >= 128 * 4, "the partial tile must fit in the activation slots");
+static_assert((2 * kMaxWStages + 2 * kSlots + 1) * 8 + 4 <= kBarBytes, "barrier area");
+static_assert(kACol0 + kSlots * kGroupChunks * 8 <= int(kTmemCols) && kMaxTok <= kACol0, "TMEM columns");
 
 bool gemm_prepare(int device, unsigned bits, unsigned cb) {
     static std::mutex mu;
@@ -471,39 +504,79 @@ bool gemm_prepare(int device, unsigned bits, unsigned cb) {
     return true;
 }
 
+// Clusters of `splits` CTAs that can be resident at once (one CTA per SM; the
+// GPC layout caps the count below SMs / splits), cached per device.
+int max_active_clusters(int device, unsigned bits, unsigned cb, int splits) {
+    static std::mutex mu;
+    static int cache[64][5] = {};
+    int si = 0;
+    while ((1 << si) < splits && si < 4) ++si;
+    if (device < 0 || device >= 64) return 0;
+    std::lock_guard<std::mutex> g(mu);
+    if (cache[device][si]) return cache[device][si];
+    if (!gemm_prepare(device, bits, cb)) return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(splits) * 16, 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = kMinSmem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = unsigned(splits);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel_for(bits, cb), &cfg) != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    cache[device][si] = n;
+    return n;
+}
+
 }  // namespace
 
-GemmPlan plan_gemm(int sms, size_t k, size_t nblocks, int rows, int tiles, int splits) {
+// Tokens per CTA: as many as one CTA takes (<= 256, fewer at 6-8 bits where the
+// trellis ring is larger), split evenly over the token groups.  K split: the
+// largest S in 1, 2, 4, 8 whose clusters of all units are resident in one wave
+// and that leaves every rank at least 2 groups of 8 chunks; a second wave
+// costs more than the extra decode parallelism gains.
+GemmPlan plan_gemm(int device, int sms, size_t k, size_t nblocks, unsigned bits, unsigned cb, int rows, int tokens,
+                   int splits) {
     GemmPlan p{};
-    const int ntiles = (rows + 127) / 128;
-    const int tmax = tiles > 0 ? (tiles < kMaxTiles ? tiles : kMaxTiles) : kMaxTiles;
-    p.tgroups = (ntiles + tmax - 1) / tmax;
-    p.T = (ntiles + p.tgroups - 1) / p.tgroups;  // balanced: at most tgroups-1 padded tiles
-    p.tmem_cols = p.T == 1 ? 128 : p.T == 2 ? 256 : 512;
+    int tmax = gemm_max_tokens(bits);
+    if (tokens > 0 && tokens < tmax) tmax = tokens / 32 * 32 > 32 ? tokens / 32 * 32 : 32;
+    p.tgroups = (rows + tmax - 1) / tmax;
+    const int per = (rows + p.tgroups - 1) / p.tgroups;
+    p.ntok = (per + 31) / 32 * 32;
     const int nchunks = int(k / 16);
     const long long units = (long long)nblocks * p.tgroups;
-    // K split over a cluster so that units x S fills the device once; at least 8 chunks per rank
     int S = 1;
-    while (S < 8 && units * (S * 2) <= sms && nchunks / (S * 2) >= 8) S *= 2;
+    for (int c = 2; c <= 8; c *= 2) {
+        if (nchunks / c < 2 * kGroupChunks) break;
+        const int fit = max_active_clusters(device, bits, cb, c);
+        if (fit <= 0 || units > fit) break;
+        S = c;
+    }
+    if (units > sms) S = 1;
     if (splits > 0) S = splits < 16 ? splits : 16;
     p.splits = S;
     const int cps = (nchunks + S - 1) / S;
-    p.cps = (cps + 3) / 4 * 4;
-    p.smem = gemm_smem(p.T);
-    p.xt_bytes = size_t(p.tgroups) * p.T * 128 * k * sizeof(__half);
+    p.cps = (cps + kGroupChunks - 1) / kGroupChunks * kGroupChunks;
+    p.wstages = gemm_wstages(bits, p.ntok);
+    p.smem = gemm_smem(bits, p.ntok, p.wstages);
+    p.xt_bytes = size_t(p.tgroups) * p.ntok * k * sizeof(__half);
     return p;
 }
 
-// y[rows][n_local] for a handle's weights: tile the activations into `xt`
-// (GemmPlan::xt_bytes), then one cluster launch over (column block, token-tile
-// group) units x K splits.
-cudaError_t launch_gemm_tc(const GemmPlan & p, const uint32_t * lsc, const __half * su, const __half * sv, size_t k,
-                           size_t nblocks, unsigned bits, unsigned cb, int device, const void * x, int x_f16,
-                           long long x_stride, int rows, float * y, long long y_stride, __half * xt, bool pdl,
-                           cudaStream_t st) {
+cudaError_t launch_gemm(const GemmPlan & p, const uint32_t * lsc, const __half * su, const __half * sv, size_t k,
+                        size_t nblocks, unsigned bits, unsigned cb, int device, const void * x, int x_f16,
+                        long long x_stride, int rows, float * y, long long y_stride, __half * xt, bool pdl,
+                        cudaStream_t st) {
     if (!gemm_prepare(device, bits, cb)) return cudaErrorInvalidValue;
-    const int ntiles_pad = p.tgroups * p.T;
-    const long long warps = (long long)ntiles_pad * 128 * (long long)(k / 128);
+    const int rows_pad = p.tgroups * p.ntok;
+    const long long warps = (long long)rows_pad * (long long)(k / 128);
     {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(unsigned((warps * 32 + 255) / 256), 1, 1);
@@ -514,7 +587,7 @@ cudaError_t launch_gemm_tc(const GemmPlan & p, const uint32_t * lsc, const __hal
         attr.val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = &attr;
         cfg.numAttrs = pdl ? 1 : 0;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, k_tile_x, x, x_f16, x_stride, su, rows, int(k), ntiles_pad, xt);
+        cudaError_t e = cudaLaunchKernelEx(&cfg, k_tile_x, x, x_f16, x_stride, su, rows, int(k), p.ntok, rows_pad, xt);
         if (e != cudaSuccess) return e;
     }
     GemmArgs a;
@@ -524,17 +597,15 @@ cudaError_t launch_gemm_tc(const GemmPlan & p, const uint32_t * lsc, const __hal
     a.y = y;
     a.y_stride = y_stride;
     a.M = rows;
-    a.T = p.T;
+    a.ntok = p.ntok;
     a.tgroups = p.tgroups;
     a.nchunks = int(k / 16);
-    a.nblocks = int(nblocks);
     a.cps = p.cps;
     a.splits = p.splits;
-    a.tmem_cols = p.tmem_cols;
-    a.xstages = xstages_for(p.T);
+    a.wstages = p.wstages;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(nblocks * p.tgroups * p.splits), 1, 1);
-    cfg.blockDim = dim3(kTThreads, 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = st;
     cudaLaunchAttribute attrs[2];

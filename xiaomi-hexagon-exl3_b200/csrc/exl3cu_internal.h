@@ -63,23 +63,24 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
                              cudaStream_t st);
 cudaError_t mul1_read_status(unsigned * out, bool clear);
 
-// tcgen05 GEMM for batches of rows (exl3cu_gemm_tc.cu).
+// tcgen05 GEMM for batches of rows (exl3cu_gemm_tc.cu): decoded weights in TMEM
+// as the A operand, tokens as N (<= 256 per CTA).
 struct GemmPlan {
-    int T;          // token tiles of 128 per CTA (1..4)
-    int tgroups;    // groups of T token tiles
-    int tmem_cols;  // TMEM columns a CTA allocates (power of two >= T*128)
+    int ntok;       // tokens per CTA, multiple of 32
+    int tgroups;    // token groups
     int splits;     // cluster size along K
-    int cps;        // chunks of 16 rows per cluster rank (multiple of 4)
-    size_t smem;    // dynamic shared memory per CTA
+    int cps;        // chunks per cluster rank (multiple of 8)
+    int wstages;    // trellis ring depth in groups of 8 chunks (multiple of 3)
+    size_t smem;
     size_t xt_bytes;  // tiled activation scratch
 };
-
-// tiles / splits > 0 replace the automatic choice of T / S.
-GemmPlan plan_gemm(int sms, size_t k, size_t nblocks, int rows, int tiles = 0, int splits = 0);
-cudaError_t launch_gemm_tc(const GemmPlan & p, const uint32_t * lsc, const __half * su, const __half * sv, size_t k,
-                           size_t nblocks, unsigned bits, unsigned cb, int device, const void * x, int x_f16,
-                           long long x_stride, int rows, float * y, long long y_stride, __half * xt, bool pdl,
-                           cudaStream_t st);
+// tokens / splits > 0 override the automatic tokens per CTA / cluster size.
+GemmPlan plan_gemm(int device, int sms, size_t k, size_t nblocks, unsigned bits, unsigned cb, int rows, int tokens = 0,
+                   int splits = 0);
+cudaError_t launch_gemm(const GemmPlan & p, const uint32_t * lsc, const __half * su, const __half * sv, size_t k,
+                        size_t nblocks, unsigned bits, unsigned cb, int device, const void * x, int x_f16,
+                        long long x_stride, int rows, float * y, long long y_stride, __half * xt, bool pdl,
+                        cudaStream_t st);
 cudaError_t gemm_read_status(unsigned * out, bool clear);
 
 struct GemvPlan {

@@ -221,11 +221,11 @@ __all__ = ["Exl3Weight", "mul_mat_batch", "decode_codebook", "decode_inner", "ha
 
 # -- plan and status ---------------------------------------------------------------------------
 
-def gemm_config(min_rows: int = 0, tiles_per_cta: int = 0, splits: int = 0) -> None:
+def gemm_config(min_rows: int = 0, tokens_per_cta: int = 0, splits: int = 0) -> None:
     """Process-wide overrides of the batched path (exl3cu_gemm_config): operands of at least
-    `min_rows` rows use the tensor-core GEMM; tiles_per_cta / splits replace its automatic plan
-    (0 = automatic; min_rows 0 = unchanged)."""
-    check(lib().exl3cu_gemm_config(int(min_rows), int(tiles_per_cta), int(splits)))
+    `min_rows` rows use the tensor-core GEMM; tokens_per_cta (multiple of 32, <= 256) / splits
+    replace its automatic plan (0 = automatic; min_rows 0 = unchanged)."""
+    check(lib().exl3cu_gemm_config(int(min_rows), int(tokens_per_cta), int(splits)))
 
 
 def device_status(device: int = 0, clear: bool = True) -> int:
