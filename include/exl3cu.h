@@ -117,6 +117,30 @@ int exl3cu_mul_mat_batch(size_t count, const exl3cu_weight * const * weights, co
                          const int * x_dtype, const size_t * rows, const size_t * x_row_stride, float * const * d_y,
                          const size_t * y_row_stride, void * stream);
 
+/* ---- ragged continuous-admission batches ----------------------------------------- */
+
+/* GPU-side batch packer.  Sequence i asks for d_want[i] rows this step (1 for a
+ * decode token, a prefill chunk length otherwise) starting at position
+ * d_pos[i]; in the given order each is granted min(want, rows left of the
+ * max_rows budget), so the caller's order is its admission policy.  Writes
+ * d_row_offsets[n_seq + 1] (d_row_offsets[n_seq] = packed rows) and, for each of
+ * the max_rows rows, its sequence index and position in d_row_seq / d_row_pos
+ * (-1 past the packed rows).  Device int32 arrays of the current device.  No
+ * counterpart in the reference (the upstream llama-server slots do this on the
+ * host). */
+int exl3cu_pack_ragged(size_t n_seq, const int32_t * d_want, const int32_t * d_pos, int32_t max_rows,
+                       int32_t * d_row_offsets, int32_t * d_row_seq, int32_t * d_row_pos, void * stream);
+
+/* The operator over a packed ragged batch: y[r] = x[r] . W for the
+ * d_row_offsets[n_seq] rows that the packer (or the caller) wrote, a count read
+ * on the device, so one captured CUDA graph serves batches of any size up to
+ * max_rows; rows of y at or past the count are not written.  Runs on the
+ * tensor-core GEMM.  Rows are independent, so the result equals
+ * exl3cu_mul_mat over the same rows. */
+int exl3cu_mul_mat_ragged(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t x_row_stride,
+                          const int32_t * d_row_offsets, size_t n_seq, size_t max_rows, float * d_y,
+                          size_t y_row_stride, void * stream);
+
 /* Plan overrides of the batched path, process-wide (for tuning).  Operands of
  * at least `min_rows` rows run on the tensor-core GEMM (tcgen05, decoded
  * weights and accumulators in TMEM; default 9), smaller ones on the decode

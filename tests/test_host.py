@@ -59,6 +59,13 @@ def test_status_strings_and_validation_without_gpu():
     assert lib.exl3cu_decode_inner(None, 16, 16, 16, 16, 4, 2, None, None) == _lib.INVALID_ARGUMENT
     assert lib.exl3cu_decode_inner(None, 16, 16, 0, 16, 0, 2, None, None) == _lib.INVALID_ARGUMENT
     assert lib.exl3cu_mul_mat(None, None, 0, 1, 128, None, 128, None) == _lib.INVALID_ARGUMENT
+    # ragged entries: bounds are checked before any device call
+    assert lib.exl3cu_pack_ragged(0, None, None, 8, None, None, None, None) == _lib.INVALID_ARGUMENT
+    assert lib.exl3cu_pack_ragged(4, None, None, 0, None, None, None, None) == _lib.INVALID_ARGUMENT
+    assert lib.exl3cu_pack_ragged(70000, None, None, 8, None, None, None, None) == _lib.INVALID_ARGUMENT
+    assert lib.exl3cu_mul_mat_ragged(None, None, 1, 128, None, 1, 8, None, 128, None) == _lib.INVALID_ARGUMENT
+    assert lib.exl3cu_gemm_config(0, 48, 0) == _lib.INVALID_ARGUMENT  # tokens per CTA: multiples of 32
+    assert lib.exl3cu_gemm_config(0, 0, 3) == _lib.INVALID_ARGUMENT   # splits: powers of two
 
 
 @pytest.mark.parametrize("bits", range(1, 9))

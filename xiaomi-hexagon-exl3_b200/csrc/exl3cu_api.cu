@@ -293,11 +293,18 @@ int gemm_scratch(int device, cudaStream_t st, size_t bytes, void ** out) {
     return EXL3CU_OK;
 }
 
+// Limits of the ragged entries (sequences per batch, packed rows per batch).
+constexpr size_t kMaxRaggedSeqs = 65536;
+constexpr int32_t kMaxRaggedRows = 1 << 20;
+
 // Rows per GEMM launch pair: bounds the scratch (2 KB per row per 1024 of k)
 // and keeps every index of the launch in 32 bits.
 constexpr size_t kGemmRowsPerLaunch = 2048;
 
-int run_gemm(const MmItem & it, cudaStream_t st) {
+// The tensor-core GEMM over `it`'s rows in launch pairs of at most
+// kGemmRowsPerLaunch rows.  With m_dev set, it.rows is the capacity and the
+// live row count is read on the device (ragged batches).
+int run_gemm(const MmItem & it, cudaStream_t st, const int32_t * m_dev = nullptr) {
     const exl3cu_weight * w = it.w;
     DeviceGuard guard(w->device);
     const size_t es = it.x_dtype == EXL3CU_F32 ? 4 : 2;
@@ -312,8 +319,8 @@ int run_gemm(const MmItem & it, cudaStream_t st) {
         int rc = gemm_scratch(w->device, st, p.xt_bytes, &xt);
         if (rc) return rc;
         const cudaError_t e = launch_gemm(p, w->lsc, w->su, w->sv, w->k, w->nblocks, w->bits, w->codebook, w->device,
-                                          x, it.x_dtype == EXL3CU_F16, (long long)it.x_stride, rows, y,
-                                          (long long)it.y_stride, static_cast<__half *>(xt), pdl_enabled(), st);
+                                          x, it.x_dtype == EXL3CU_F16, (long long)it.x_stride, rows, m_dev, int(r0),
+                                          y, (long long)it.y_stride, static_cast<__half *>(xt), pdl_enabled(), st);
         if (e != cudaSuccess) return cuda_fail(e, "launching the EXL3 tensor-core GEMM");
     }
     return EXL3CU_OK;
@@ -639,6 +646,40 @@ int exl3cu_mul_mat_batch(size_t count, const exl3cu_weight * const * weights, co
         items[i] = MmItem{weights[i], d_x[i], x_dtype[i], rows[i], x_row_stride[i], d_y[i], y_row_stride[i]};
     }
     return run_cluster(items.data(), count, static_cast<cudaStream_t>(stream));
+}
+
+int exl3cu_pack_ragged(size_t n_seq, const int32_t * d_want, const int32_t * d_pos, int32_t max_rows,
+                       int32_t * d_row_offsets, int32_t * d_row_seq, int32_t * d_row_pos, void * stream) {
+    if (n_seq == 0 || n_seq > kMaxRaggedSeqs)
+        return fail(EXL3CU_INVALID_ARGUMENT, "n_seq must be 1..%zu", kMaxRaggedSeqs);
+    if (max_rows < 1 || max_rows > kMaxRaggedRows)
+        return fail(EXL3CU_INVALID_ARGUMENT, "max_rows must be 1..%d", kMaxRaggedRows);
+    int dev = 0, rc;
+    if ((rc = current_device(&dev))) return rc;
+    if ((rc = check_device_ptr(d_want, dev, "want"))) return rc;
+    if ((rc = check_device_ptr(d_pos, dev, "pos"))) return rc;
+    if ((rc = check_device_ptr(d_row_offsets, dev, "row_offsets"))) return rc;
+    if ((rc = check_device_ptr(d_row_seq, dev, "row_seq"))) return rc;
+    if ((rc = check_device_ptr(d_row_pos, dev, "row_pos"))) return rc;
+    CU_TRY(launch_pack_ragged(int(n_seq), d_want, d_pos, max_rows, d_row_offsets, d_row_seq, d_row_pos,
+                              static_cast<cudaStream_t>(stream)),
+           "launching the ragged batch packer");
+    return EXL3CU_OK;
+}
+
+int exl3cu_mul_mat_ragged(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t x_row_stride,
+                          const int32_t * d_row_offsets, size_t n_seq, size_t max_rows, float * d_y,
+                          size_t y_row_stride, void * stream) {
+    int rc = validate_mm(w, d_x, x_dtype, max_rows, x_row_stride, d_y, y_row_stride);
+    if (rc) return rc;
+    if (n_seq == 0 || n_seq > kMaxRaggedSeqs)
+        return fail(EXL3CU_INVALID_ARGUMENT, "n_seq must be 1..%zu", kMaxRaggedSeqs);
+    if (max_rows > size_t(kMaxRaggedRows)) return fail(EXL3CU_INVALID_ARGUMENT, "max_rows above %d", kMaxRaggedRows);
+    if ((rc = check_device_ptr(d_x, w->device, "x"))) return rc;
+    if ((rc = check_device_ptr(d_y, w->device, "y"))) return rc;
+    if ((rc = check_device_ptr(d_row_offsets, w->device, "row_offsets"))) return rc;
+    const MmItem item{w, d_x, x_dtype, max_rows, x_row_stride, d_y, y_row_stride};
+    return run_gemm(item, static_cast<cudaStream_t>(stream), d_row_offsets + n_seq);
 }
 
 int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,

@@ -114,7 +114,9 @@ struct GemmArgs {
     const __half * xt;  // [tgroups][k/16][NTOK/8][2][8][8] fp16, K permuted by kperm16
     float * y;
     long long y_stride;
-    int M;
+    int M;                 // rows (capacity when m_dev is set)
+    const int32_t * m_dev;  // optional: the live row count, min'd with M (ragged batches)
+    int m_base;             // rows of the batch before this launch's first row (m_dev counts from 0)
     int ntok;           // tokens per CTA, multiple of 32, <= 256
     int tgroups;
     int nchunks;
@@ -128,10 +130,11 @@ struct GemmArgs {
 //   tg*ntok*k_total + kc*ntok*16 + (tr/8)*128 + (p/8)*64 + (tr%8)*8 + p%8,  p = kperm16(k % 16)
 // (8-token x 16-byte core matrices, 8-token groups 256 B apart, K halves 128 B apart).
 __global__ void k_tile_x(const void * __restrict__ x, int x_f16, long long x_stride,
-                            const __half * __restrict__ su, int M, int k, int ntok, int rows_pad,
-                            __half * __restrict__ xt) {
+                         const __half * __restrict__ su, int M, const int32_t * __restrict__ m_dev, int m_base, int k,
+                         int ntok, int rows_pad, __half * __restrict__ xt) {
     pdl_trigger();
     pdl_wait_primary();
+    if (m_dev) M = min(M, max(0, *m_dev - m_base));  // written by an earlier kernel: read after the wait
     const int warp = int((blockIdx.x * size_t(blockDim.x) + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
     const int groups = k / 128;
@@ -232,6 +235,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const GemmArgs a) {
     const int unit = blockIdx.x / S;
     const int nb = unit / a.tgroups;
     const int tg = unit - nb * a.tgroups;
+    int M = a.M;
+    if (a.m_dev) {
+        // Ragged batch: the live row count comes from an earlier kernel, so every
+        // thread waits for the preceding grids before reading it; token groups
+        // wholly past it exit at once (all ranks of a cluster share the group).
+        pdl_wait_primary();
+        M = min(M, max(0, *a.m_dev - a.m_base));
+        if (tg * NT >= M) return;
+    }
     const int c0 = min(split * a.cps, a.nchunks);
     const int c1 = min(c0 + a.cps, a.nchunks);
     const int ngr = (c1 - c0) / kGroupChunks;
@@ -410,7 +422,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const GemmArgs a) {
             }
             h128_warp4(v);
             const int token = tg * NT + t;
-            if (token < a.M) {
+            if (token < M) {
                 float4 o;
                 o.x = __fmul_rn(v[0], __low2float(s01));
                 o.y = __fmul_rn(v[1], __high2float(s01));
@@ -572,8 +584,8 @@ GemmPlan plan_gemm(int device, int sms, size_t k, size_t nblocks, unsigned bits,
 
 cudaError_t launch_gemm(const GemmPlan & p, const uint32_t * lsc, const __half * su, const __half * sv, size_t k,
                         size_t nblocks, unsigned bits, unsigned cb, int device, const void * x, int x_f16,
-                        long long x_stride, int rows, float * y, long long y_stride, __half * xt, bool pdl,
-                        cudaStream_t st) {
+                        long long x_stride, int rows, const int32_t * m_dev, int m_base, float * y, long long y_stride,
+                        __half * xt, bool pdl, cudaStream_t st) {
     if (!gemm_prepare(device, bits, cb)) return cudaErrorInvalidValue;
     const int rows_pad = p.tgroups * p.ntok;
     const long long warps = (long long)rows_pad * (long long)(k / 128);
@@ -587,7 +599,8 @@ cudaError_t launch_gemm(const GemmPlan & p, const uint32_t * lsc, const __half *
         attr.val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = &attr;
         cfg.numAttrs = pdl ? 1 : 0;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, k_tile_x, x, x_f16, x_stride, su, rows, int(k), p.ntok, rows_pad, xt);
+        cudaError_t e = cudaLaunchKernelEx(&cfg, k_tile_x, x, x_f16, x_stride, su, rows, m_dev, m_base, int(k), p.ntok,
+                                           rows_pad, xt);
         if (e != cudaSuccess) return e;
     }
     GemmArgs a;
@@ -597,6 +610,8 @@ cudaError_t launch_gemm(const GemmPlan & p, const uint32_t * lsc, const __half *
     a.y = y;
     a.y_stride = y_stride;
     a.M = rows;
+    a.m_dev = m_dev;
+    a.m_base = m_base;
     a.ntok = p.ntok;
     a.tgroups = p.tgroups;
     a.nchunks = int(k / 16);

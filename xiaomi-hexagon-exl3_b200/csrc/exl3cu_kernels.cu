@@ -301,4 +301,64 @@ cudaError_t launch_reconstruct_blocks(uint16_t * io, size_t k, size_t column_cou
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Ragged continuous-admission batch packer.  Sequence i asks for want[i] rows
+// this step (1 for a decode token, a chunk length for prefill) starting at
+// position pos[i]; in the given order each is granted min(want, rows left of
+// the max_rows budget), so the caller's order is its admission policy (e.g.
+// decode tokens first).  Outputs row_offsets[n_seq + 1] (row_offsets[n_seq] =
+// the packed row count) and, per packed row r < max_rows, its sequence and
+// position (-1 past the packed rows).  One CTA: a capped exclusive scan in
+// 64-bit arithmetic, then a binary search over the offsets per row.
+constexpr int kPackThreads = 1024;
+
+__global__ void __launch_bounds__(kPackThreads) k_pack_ragged(int n_seq, const int32_t * __restrict__ want,
+                                                              const int32_t * __restrict__ pos, int32_t max_rows,
+                                                              int32_t * __restrict__ row_offsets,
+                                                              int32_t * __restrict__ row_seq,
+                                                              int32_t * __restrict__ row_pos) {
+    __shared__ long long part[kPackThreads];
+    const int t = threadIdx.x;
+    const int per = (n_seq + kPackThreads - 1) / kPackThreads;
+    const int i0 = min(t * per, n_seq), i1 = min(i0 + per, n_seq);
+    long long sum = 0;
+    for (int i = i0; i < i1; ++i) sum += max(want[i], 0);
+    part[t] = sum;
+    __syncthreads();
+    for (int off = 1; off < kPackThreads; off <<= 1) {  // inclusive Hillis-Steele scan
+        const long long v = t >= off ? part[t - off] : 0;
+        __syncthreads();
+        part[t] += v;
+        __syncthreads();
+    }
+    long long run = t > 0 ? part[t - 1] : 0;
+    for (int i = i0; i < i1; ++i) {
+        row_offsets[i] = int32_t(run < max_rows ? run : max_rows);
+        run += max(want[i], 0);
+    }
+    if (t == kPackThreads - 1) row_offsets[n_seq] = int32_t(part[t] < max_rows ? part[t] : max_rows);
+    __syncthreads();  // the offsets are visible to the whole block
+    const int rows = row_offsets[n_seq];
+    for (int r = t; r < max_rows; r += kPackThreads) {
+        if (r >= rows) {
+            row_seq[r] = -1;
+            row_pos[r] = -1;
+            continue;
+        }
+        int lo = 0, hi = n_seq - 1;  // last i with row_offsets[i] <= r
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (row_offsets[mid] <= r) lo = mid; else hi = mid - 1;
+        }
+        row_seq[r] = lo;
+        row_pos[r] = pos[lo] + (r - row_offsets[lo]);
+    }
+}
+
+cudaError_t launch_pack_ragged(int n_seq, const int32_t * want, const int32_t * pos, int32_t max_rows,
+                               int32_t * row_offsets, int32_t * row_seq, int32_t * row_pos, cudaStream_t st) {
+    k_pack_ragged<<<1, kPackThreads, 0, st>>>(n_seq, want, pos, max_rows, row_offsets, row_seq, row_pos);
+    return cudaGetLastError();
+}
+
 }  // namespace exl3cu

@@ -132,6 +132,24 @@ class Exl3Weight:
                                           _ptr(workspace), workspace.numel() * workspace.element_size(), st))
         return out
 
+    def mul_mat_ragged(self, x: torch.Tensor, row_offsets: torch.Tensor, out: torch.Tensor | None = None,
+                       stream=None) -> torch.Tensor:
+        """y = x . W over the row_offsets[-1] packed rows of x [max_rows, k] (a count read on the
+        device; exl3cu_mul_mat_ragged).  Rows of `out` at or past the count are not written."""
+        if x.dtype not in (torch.float32, torch.float16):
+            raise TypeError("x must be float32 or float16")
+        if row_offsets.dtype != torch.int32 or row_offsets.dim() != 1 or row_offsets.numel() < 2:
+            raise ValueError("row_offsets must be a 1-D int32 device tensor of n_seq + 1 entries")
+        x2 = x if x.stride(-1) == 1 else x.contiguous()
+        max_rows = x2.shape[0]
+        if out is None:
+            out = torch.empty((max_rows, self.n), dtype=torch.float32, device=x.device)
+        dt = F32 if x.dtype == torch.float32 else F16
+        check(lib().exl3cu_mul_mat_ragged(self._h, _ptr(x2), dt, x2.stride(0), _ptr(row_offsets),
+                                          row_offsets.numel() - 1, max_rows, _ptr(out), out.stride(0),
+                                          _stream_handle(stream)))
+        return out
+
     def mul_mat_host(self, x: np.ndarray, out: np.ndarray | None = None, synchronize: bool = True,
                      stream=None) -> np.ndarray:
         """Host-buffer form (copies inside the call), the ggml CPU-backend contract."""
@@ -217,6 +235,29 @@ def reconstruct(packed, suh, svh, k: int, n: int, bits: int, codebook: int = CB_
 
 
 __all__ = ["Exl3Weight", "mul_mat_batch", "decode_codebook", "decode_inner", "hadamard128", "reconstruct", "_lib"]
+
+
+# -- ragged batches -----------------------------------------------------------------------------
+
+def pack_ragged(want: torch.Tensor, pos: torch.Tensor, max_rows: int, stream=None,
+                out: tuple | None = None):
+    """GPU-side packer (exl3cu_pack_ragged): sequence i is granted min(want[i], rows left of
+    max_rows) rows in order.  Returns (row_offsets [n_seq+1], row_seq [max_rows], row_pos [max_rows]),
+    device int32; row_offsets[-1] is the packed row count, -1 marks rows past it."""
+    if want.dtype != torch.int32 or pos.dtype != torch.int32 or want.shape != pos.shape or want.dim() != 1:
+        raise ValueError("want and pos must be 1-D int32 device tensors of one length")
+    n_seq = want.numel()
+    if out is None:
+        dev = want.device
+        out = (torch.empty(n_seq + 1, dtype=torch.int32, device=dev),
+               torch.empty(max_rows, dtype=torch.int32, device=dev),
+               torch.empty(max_rows, dtype=torch.int32, device=dev))
+    offs, rseq, rpos = out
+    if not (want.is_contiguous() and pos.is_contiguous()):
+        raise ValueError("want and pos must be contiguous")
+    check(lib().exl3cu_pack_ragged(n_seq, _ptr(want), _ptr(pos), int(max_rows),
+                                   _ptr(offs), _ptr(rseq), _ptr(rpos), _stream_handle(stream)))
+    return offs, rseq, rpos
 
 
 # -- plan and status ---------------------------------------------------------------------------
