@@ -64,8 +64,10 @@ def parse_args(argv=None):
     ap.add_argument("--no-sweep", action="store_true", help="skip the 2/3/5/6-bit side measurements")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--e2e-steps", type=int, default=30)
-    ap.add_argument("--config", choices=("sweep", "large"), default="sweep",
-                    help="sweep: configs[1] decode GEMV sweep (default); large: configs[4] column-split matrix")
+    ap.add_argument("--config", choices=("sweep", "large", "ragged"), default="sweep",
+                    help="sweep: configs[1] decode GEMV sweep (default); large: configs[4] column-split matrix; "
+                         "ragged: configs[2] packed continuous-admission batches on the tensor-core GEMM")
+    ap.add_argument("--no-ragged", action="store_true", help="skip the configs[2] summary in the default run")
     return ap.parse_args(argv)
 
 
@@ -429,6 +431,173 @@ def run_large(args, torch, dist, ops, rank, world, local):
     return 0
 
 
+# ---------------------------------------------------------------------------------------------
+# ragged continuous-admission batches through the mixed-bit layer stack
+
+RAGGED_BUCKETS = (32, 64, 128, 256, 512)
+RAGGED_MAX_ROWS = 512
+
+
+def ragged_batches(count, seed=2024):
+    """Seeded step compositions: 8..64 sequences, each a decode token, plus 0..3 prefill chunks of
+    16..512 rows; decode tokens are admitted first, the packed batch is capped at 512 rows."""
+    import numpy as np
+
+    rng = np.random.Generator(np.random.PCG64(seed))
+    out = []
+    for _ in range(count):
+        n_seq = int(rng.integers(8, 65))
+        n_pre = int(rng.integers(0, 4))
+        n_dec = max(n_seq - n_pre, 1)
+        want = [1] * n_dec + [int(v) for v in rng.integers(16, 513, n_pre)]
+        pos = [int(v) for v in rng.integers(32, 1025, len(want))]
+        rows = min(sum(want), RAGGED_MAX_ROWS)
+        out.append({"want": want, "pos": pos, "rows": rows,
+                    "bucket": next(b for b in RAGGED_BUCKETS if b >= rows)})
+    return out
+
+
+def build_mixed_stack(torch, ops, layers, device, seed, frac6=0.25):
+    """The 2B decoder's 196 matrices with a seeded 25% of them at 6 bpw, the rest at 4 bpw."""
+    import numpy as np
+
+    dev = f"cuda:{device}"
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    names = [name for name, _ in shapes()]
+    total = layers * len(names)
+    rng = np.random.Generator(np.random.PCG64(seed))
+    six = set(int(i) for i in rng.choice(total, size=int(round(frac6 * total)), replace=False))
+    stack, bits_bytes, weights = [], 0, 0
+    for layer in range(layers):
+        mats = {}
+        for j, (name, (k, n)) in enumerate(shapes()):
+            bits = 6 if layer * len(names) + j in six else 4
+            trellis = torch.randint(0, 65536, (k // 16, n // 16, 16 * bits), generator=g, device=dev,
+                                    dtype=torch.int32).to(torch.int16)
+            suh = (torch.randint(0, 2, (k,), generator=g, device=dev) * 2 - 1).to(torch.float16)
+            svh = ((torch.randint(0, 2, (n,), generator=g, device=dev) * 2 - 1).float() *
+                   (0.01 + 0.02 * torch.rand(n, generator=g, device=dev))).to(torch.float16)
+            w = ops.Exl3Weight.from_trellis(trellis, suh.view(torch.int16), svh.view(torch.int16), device=device)
+            mats[name] = {"k": k, "n": n, "bits": bits, "w": w}
+            bits_bytes += k * n * bits
+            weights += k * n
+            del trellis
+        stack.append(mats)
+    torch.cuda.synchronize(device)
+    return stack, bits_bytes / weights
+
+
+def run_ragged_measure(torch, ops, device, layers, reps, seed):
+    """Per-bucket CUDA graphs of one step (GPU packer + 196 exl3cu_mul_mat_ragged calls, row count read
+    on the device), replayed over seeded batch compositions; returns the summary dict."""
+    dev = f"cuda:{device}"
+    stack, avg_bpw = build_mixed_stack(torch, ops, layers, device, seed)
+    gx = torch.Generator(device=dev)
+    gx.manual_seed(seed + 1)
+    xs = {k: torch.randn((RAGGED_MAX_ROWS, k), generator=gx, device=dev).to(torch.float16)
+          for k in sorted({k for _, (k, _) in shapes()})}
+    ys = {name: torch.empty((RAGGED_MAX_ROWS, n), dtype=torch.float32, device=dev) for name, (_, n) in shapes()}
+    n_seq_max = 64
+    want = torch.zeros(n_seq_max, dtype=torch.int32, device=dev)
+    pos = torch.zeros(n_seq_max, dtype=torch.int32, device=dev)
+    packed = (torch.empty(n_seq_max + 1, dtype=torch.int32, device=dev),
+              torch.empty(RAGGED_MAX_ROWS, dtype=torch.int32, device=dev),
+              torch.empty(RAGGED_MAX_ROWS, dtype=torch.int32, device=dev))
+    stream = torch.cuda.Stream()
+
+    def step(cap):
+        ops.pack_ragged(want, pos, cap, stream=stream, out=packed)
+        for mats in stack:
+            for name, m in mats.items():
+                m["w"].mul_mat_ragged(xs[m["k"]][:cap], packed[0], out=ys[name][:cap], stream=stream)
+
+    graphs = {}
+    for cap in RAGGED_BUCKETS:
+        want.fill_(cap // n_seq_max + 1)
+        with torch.cuda.stream(stream):
+            step(cap)  # grows the scratch outside capture
+        stream.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream, capture_error_mode="relaxed"):
+            step(cap)
+        graphs[cap] = gr
+    batches = ragged_batches(16, seed=seed + 2)
+    flop_per_row = 2 * layers * sum(k * n for _, (k, n) in shapes())
+    total_ms, total_rows, per_bucket = 0.0, 0, {}
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for b in batches:
+        w = torch.zeros(n_seq_max, dtype=torch.int32)
+        p = torch.zeros(n_seq_max, dtype=torch.int32)
+        w[:len(b["want"])] = torch.tensor(b["want"][:n_seq_max], dtype=torch.int32)
+        p[:len(b["pos"])] = torch.tensor(b["pos"][:n_seq_max], dtype=torch.int32)
+        want.copy_(w)
+        pos.copy_(p)
+        gr = graphs[b["bucket"]]
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                gr.replay()
+            ev[0].record(stream)
+            for _ in range(reps):
+                gr.replay()
+            ev[1].record(stream)
+        ev[1].synchronize()
+        ms = ev[0].elapsed_time(ev[1]) / reps
+        total_ms += ms
+        total_rows += b["rows"]
+        e = per_bucket.setdefault(b["bucket"], {"steps": 0, "rows": 0, "ms": 0.0})
+        e["steps"] += 1
+        e["rows"] += b["rows"]
+        e["ms"] += ms
+    for e in per_bucket.values():
+        e["tflops"] = round(flop_per_row * e["rows"] / (e["ms"] * 1e-3) / 1e12, 1)
+        e["ms_per_step"] = round(e["ms"] / e["steps"], 3)
+        del e["ms"]
+    for gr in graphs.values():
+        del gr
+    graphs.clear()
+    for mats in stack:
+        for m in mats.values():
+            m["w"].free()
+    torch.cuda.synchronize(device)
+    tflops = flop_per_row * total_rows / (total_ms * 1e-3) / 1e12
+    return {"tokens_per_s": round(total_rows / (total_ms * 1e-3), 1), "tflops": round(tflops, 1),
+            "ms_per_step": round(total_ms / len(batches), 3), "avg_rows": round(total_rows / len(batches), 1),
+            "steps": len(batches), "avg_bpw": round(avg_bpw, 3), "by_bucket": per_bucket,
+            "launches_per_step": 1 + 2 * layers * len(shapes())}
+
+
+def run_ragged(args, torch, dist, ops, rank, world, local):
+    """configs[2] as its own bench line (replicas on N GPUs: every rank runs its own batches)."""
+    pk, pk_kind = peaks()
+    peak = float(pk.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        r = run_ragged_measure(torch, ops, local, args.layers, max(3, args.steps // 100), seed=77 + rank)
+    tps = r["tokens_per_s"]
+    if world > 1:
+        t = torch.tensor([r["ms_per_step"]], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        tps = r["avg_rows"] / (float(t.item()) * 1e-3)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "EXL3 ragged continuous-admission batch, tokens/s through the 196-matrix stack (configs[2])",
+            "value": round(tps * world, 1), "unit": "tokens/s", "n_gpus": world, "steps": r["steps"],
+            "warmup": 2, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "configs[2]: 8-64 sequences per step (decode tokens + 0-3 prefill chunks of "
+                                   "16-512 rows), packed on the GPU to <= 512 rows; 28 layers x 7 shapes, 25% of the "
+                                   "matrices at 6 bpw, 75% at 4 bpw", "avg_bpw": r["avg_bpw"],
+                       "parallelism": f"dp{world} replicas", "bucket_graphs": list(RAGGED_BUCKETS)},
+            "roofline": {"bound": "tensor", "achieved": r["tflops"], "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(r["tflops"] / peak, 4), "peak_source": f"{pk_kind} bf16_tflops",
+                         "kernel": "exl3cu::k_gemm"},
+            "gpu_launches": r["launches_per_step"] * r["steps"],
+            "clocks": clk.summary(), "ragged": r}), flush=True)
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -446,8 +615,9 @@ def main(argv=None):
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device(f"cuda:{local}"))
-    if args.config == "large":
-        rc = run_large(args, torch, dist, ops, rank, world, local)
+    if args.config in ("large", "ragged"):
+        run = run_large if args.config == "large" else run_ragged
+        rc = run(args, torch, dist, ops, rank, world, local)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
@@ -502,6 +672,9 @@ def main(argv=None):
         sweep[str(args.bits)] = round(value / world, 1)
 
     cpu = cpu_baseline(stack, args.bits) if want_cpu else None
+    ragged = None
+    if not args.no_ragged:
+        ragged = run_ragged_measure(torch, ops, local, args.layers, 3, seed=77 + rank)
 
     traffic = None
     tf = ROOT / "profiles" / "gemv_traffic.json"
@@ -551,6 +724,7 @@ def main(argv=None):
             "patterns": patterns,
             "per_shape_kernel_us": shape_us,
             "sweep_gbs_by_bits": sweep,
+            "ragged_configs2": ragged,
         }
         print(json.dumps(line), flush=True)
     for layer in stack:

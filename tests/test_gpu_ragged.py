@@ -142,3 +142,34 @@ def test_ragged_beyond_one_launch(ops, oracle):
         assert_close(yn[:rows], oracle.mul_mat(rec, bits, k, n, x[:rows], nth=16), f"rows={rows}")
         assert np.all(np.isnan(yn[rows:]))
     w.free()
+
+
+def test_graphs_survive_scratch_growth(ops, oracle):
+    """Graphs captured at a small capacity stay valid after a larger call grows the stream's
+    GEMM scratch (the outgrown buffer is retired, not freed)."""
+    from exl3_b200 import synthetic
+
+    k, n, bits = 1024, 384, 4
+    w, rec = _weight(ops, k, n, bits, 21)
+    x_np = synthetic.activations(512, k, seed=22)
+    x = torch.from_numpy(x_np).cuda()
+    st = torch.cuda.Stream()
+    graphs, outs = [], []
+    for cap in (32, 128, 512):  # each warm-up grows the scratch past the previous graph's
+        offs = torch.tensor([0, cap], dtype=torch.int32, device="cuda")
+        y = torch.empty((cap, n), dtype=torch.float32, device="cuda")
+        with torch.cuda.stream(st):
+            w.mul_mat_ragged(x[:cap], offs, out=y, stream=st)
+        st.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            w.mul_mat_ragged(x[:cap], offs, out=y, stream=st)
+        graphs.append(g)
+        outs.append((cap, y, offs))
+    for g, (cap, y, _) in zip(graphs, outs):
+        y.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        assert_close(y.cpu().numpy(), oracle.mul_mat(rec, bits, k, n, x_np[:cap], nth=16), f"cap={cap}")
+    del graphs
+    w.free()

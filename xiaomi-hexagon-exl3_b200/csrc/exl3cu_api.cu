@@ -37,6 +37,7 @@ struct exl3cu_weight {
     size_t stage_x_bytes;
     float * stage_y;
     size_t stage_y_bytes;
+    std::vector<void *> retired;  // outgrown staging, kept until the handle is freed (graphs may hold it)
 };
 
 namespace {
@@ -131,6 +132,7 @@ void release(exl3cu_weight * w) {
     cudaFree(w->ws);
     cudaFree(w->stage_x);
     cudaFree(w->stage_y);
+    for (void * p : w->retired) cudaFree(p);
     delete w;
 }
 
@@ -253,15 +255,18 @@ size_t gemm_min_rows() { return g_gemm_min_rows.load(std::memory_order_relaxed);
 
 // Tiled-activation scratch of the GEMM, one buffer per (device, stream) so
 // that operators on different streams never share it; work on one stream is
-// ordered, so consecutive calls reuse it.  It grows (synchronising that
-// stream) when a call needs more, which is refused while the stream is being
-// captured into a CUDA graph: run one call of the largest row count before
-// capturing.
+// ordered, so consecutive calls reuse it.  When a call needs more it gets a
+// larger buffer and the old one is retired, not freed: a CUDA graph captured
+// earlier on the stream keeps its pointer, and every such pointer stays valid
+// for the life of the process (growth is geometric, so retired buffers add at
+// most the size of the live one).  Growth allocates, which is refused while the
+// stream is being captured: run one call of the largest row count first.
 struct GemmScratch {
     int device;
     cudaStream_t stream;
     void * ptr;
     size_t bytes;
+    std::vector<void *> retired;
 };
 std::mutex g_gemm_scratch_mu;
 std::vector<GemmScratch> g_gemm_scratch;
@@ -272,7 +277,7 @@ int gemm_scratch(int device, cudaStream_t st, size_t bytes, void ** out) {
     for (auto & e : g_gemm_scratch)
         if (e.device == device && e.stream == st) s = &e;
     if (!s) {
-        g_gemm_scratch.push_back(GemmScratch{device, st, nullptr, 0});
+        g_gemm_scratch.push_back(GemmScratch{device, st, nullptr, 0, {}});
         s = &g_gemm_scratch.back();
     }
     if (s->bytes < bytes) {
@@ -282,12 +287,12 @@ int gemm_scratch(int device, cudaStream_t st, size_t bytes, void ** out) {
             return fail(EXL3CU_NO_SUPPORT,
                         "the GEMM scratch must grow to %zu bytes during stream capture: run one call with this many "
                         "rows on the stream before capturing", bytes);
-        CU_TRY(cudaStreamSynchronize(st), "synchronising before the GEMM scratch grows");
-        cudaFree(s->ptr);
-        s->ptr = nullptr;
-        s->bytes = 0;
-        CU_TRY(cudaMalloc(&s->ptr, bytes), "allocating the GEMM scratch");
-        s->bytes = bytes;
+        const size_t want = bytes > 2 * s->bytes ? bytes : 2 * s->bytes;
+        void * p = nullptr;
+        CU_TRY(cudaMalloc(&p, want), "allocating the GEMM scratch");
+        if (s->ptr) s->retired.push_back(s->ptr);
+        s->ptr = p;
+        s->bytes = want;
     }
     *out = s->ptr;
     return EXL3CU_OK;
@@ -714,20 +719,20 @@ int exl3cu_mul_mat_host(exl3cu_weight * w, const void * h_x, int x_dtype, size_t
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const size_t es = x_dtype == EXL3CU_F32 ? 4 : 2;
     const size_t xb = rows * w->k * es, yb = rows * n_local * sizeof(float);
+    // Staging grows by retiring the old buffers, not freeing them: work still in
+    // flight, or a captured graph, may reference them until the handle is freed.
     if (w->stage_x_bytes < xb) {
-        CU_TRY(cudaStreamSynchronize(st), "synchronising before staging growth");
-        cudaFree(w->stage_x);
-        w->stage_x = nullptr;
-        w->stage_x_bytes = 0;
-        CU_TRY(cudaMalloc(&w->stage_x, xb), "allocating x staging");
+        void * p = nullptr;
+        CU_TRY(cudaMalloc(&p, xb), "allocating x staging");
+        if (w->stage_x) w->retired.push_back(w->stage_x);
+        w->stage_x = p;
         w->stage_x_bytes = xb;
     }
     if (w->stage_y_bytes < yb) {
-        CU_TRY(cudaStreamSynchronize(st), "synchronising before staging growth");
-        cudaFree(w->stage_y);
-        w->stage_y = nullptr;
-        w->stage_y_bytes = 0;
-        CU_TRY(cudaMalloc(&w->stage_y, yb), "allocating y staging");
+        void * p = nullptr;
+        CU_TRY(cudaMalloc(&p, yb), "allocating y staging");
+        if (w->stage_y) w->retired.push_back(w->stage_y);
+        w->stage_y = static_cast<float *>(p);
         w->stage_y_bytes = yb;
     }
     CU_TRY(cudaMemcpy2DAsync(w->stage_x, w->k * es, h_x, x_row_stride * es, w->k * es, rows, cudaMemcpyHostToDevice, st),
