@@ -117,6 +117,20 @@ int exl3cu_mul_mat_batch(size_t count, const exl3cu_weight * const * weights, co
                          const int * x_dtype, const size_t * rows, const size_t * x_row_stride, float * const * d_y,
                          const size_t * y_row_stride, void * stream);
 
+/* A sequence of up to 256 problems in one persistent launch: y_i = x_i . W_i
+ * with 1..4 rows each, for mul1 weights of one bit width (2..8) on one device.
+ * group[i] (non-decreasing) orders the work: with depend != 0 a problem of a
+ * group reads its x only after every problem of the previous group has
+ * stored its y, so a later group may consume an earlier group's output (a
+ * decode step: q,k,v | o | gate,up | down of each layer, the attention and
+ * activation between them done elsewhere).  Weights of later problems stream
+ * while earlier groups compute.  Same numerics as exl3cu_mul_mat.  No
+ * counterpart in the reference (its graph runs one operator call per matmul). */
+int exl3cu_mul_mat_sequence(size_t count, const exl3cu_weight * const * weights, const void * const * d_x,
+                            const int * x_dtype, const size_t * rows, const size_t * x_row_stride,
+                            float * const * d_y, const size_t * y_row_stride, const int * group, int depend,
+                            void * stream);
+
 /* ---- ragged continuous-admission batches ----------------------------------------- */
 
 /* GPU-side batch packer.  Sequence i asks for d_want[i] rows this step (1 for a

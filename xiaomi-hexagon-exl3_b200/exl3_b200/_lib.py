@@ -24,6 +24,7 @@ EXPORTS = (
     "exl3cu_weight_decode_inner", "exl3cu_mul_mat", "exl3cu_mul_mat_workspace_bytes", "exl3cu_mul_mat_ws",
     "exl3cu_mul_mat_host", "exl3cu_mul_mat_noalloc", "exl3cu_mul_mat_batch",
     "exl3cu_device_status", "exl3cu_gemm_config", "exl3cu_pack_ragged", "exl3cu_mul_mat_ragged",
+    "exl3cu_mul_mat_sequence",
 )
 
 
@@ -71,6 +72,9 @@ def _declare(L):
     L.exl3cu_gemm_config.argtypes = [_sz, _c.c_int, _c.c_int]
     L.exl3cu_pack_ragged.argtypes = [_sz, _vp, _vp, _c.c_int32, _vp, _vp, _vp, _vp]
     L.exl3cu_mul_mat_ragged.argtypes = [_vp, _vp, _c.c_int, _sz, _vp, _sz, _sz, _vp, _sz, _vp]
+    L.exl3cu_mul_mat_sequence.argtypes = [_sz, _c.POINTER(_vp), _c.POINTER(_vp), _c.POINTER(_c.c_int),
+                                          _c.POINTER(_sz), _c.POINTER(_sz), _c.POINTER(_vp), _c.POINTER(_sz),
+                                          _c.POINTER(_c.c_int), _c.c_int, _vp]
     L.exl3cu_mul_mat_batch.argtypes = [_sz, _c.POINTER(_vp), _c.POINTER(_vp), _c.POINTER(_c.c_int),
                                        _c.POINTER(_sz), _c.POINTER(_sz), _c.POINTER(_vp), _c.POINTER(_sz), _vp]
     non_status = ("exl3cu_status_string", "exl3cu_last_error", "exl3cu_mul_mat_workspace_bytes")
