@@ -167,7 +167,8 @@ int exl3cu_gemm_config(size_t min_rows, int tokens_per_cta, int splits);
 
 /* Sticky error bits the kernels of `device` raised since the last clear:
  * bit 0 = a bounded wait on an asynchronous copy ran out (the results of the
- * calls since are unreliable).  Synchronises the device.  No counterpart in
+ * calls since are unreliable); bit 1 = exl3cu_get_rows read an id outside the
+ * handle's columns (that row was filled with NaN).  Synchronises the device.  No counterpart in
  * the reference (its DSP operator returns statuses synchronously). */
 int exl3cu_device_status(int device, unsigned * status, int clear);
 
@@ -188,6 +189,24 @@ int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, si
  * pinned.  Staging buffers are owned by the handle. */
 int exl3cu_mul_mat_host(exl3cu_weight * w, const void * h_x, int x_dtype, size_t rows, size_t x_row_stride,
                         float * h_y, size_t y_row_stride, int synchronize, void * stream);
+
+/* EXL3 get_rows (replaces ggml_exl3_get_rows, src/exl3-ggml.cpp:19-49; the
+ * reference patch dispatches GET_ROWS on an EXL3 src0 to it,
+ * patches/llama-exl3.patch:114-121): for each of `count` column ids (local to
+ * the handle's column range), writes the original-basis column W[:, id] -- k
+ * values, each the fp16 the reference's exl3::reconstruct produces, widened to
+ * f32 -- to d_out + i * out_row_stride.  This is the tied-embedding lookup:
+ * token id -> hidden vector.  One CTA per (id, 128-row group).  count <= 65535.
+ * Stream-ordered; ids are read on the device, and an id out of range yields a
+ * NaN row and sets bit 1 of exl3cu_device_status. */
+int exl3cu_get_rows(const exl3cu_weight * w, const int32_t * d_ids, size_t count, float * d_out,
+                    size_t out_row_stride, void * stream);
+
+/* Host-buffer form of exl3cu_get_rows (the ggml CPU-backend contract): checks
+ * every id on the host first (EXL3CU_INVALID_ARGUMENT naming the first bad one,
+ * where the reference asserts), stages ids and rows in the handle's buffers. */
+int exl3cu_get_rows_host(exl3cu_weight * w, const int32_t * h_ids, size_t count, float * h_out,
+                         size_t out_row_stride, int synchronize, void * stream);
 
 /* No counterpart in the reference.  exl3cu_mul_mat for callers that may not
  * allocate device memory: the split-K scratch is a fixed 4 MiB array inside the

@@ -35,9 +35,9 @@ def test_ggml_adapter_exports():
 
     _lib.lib()
     g = ctypes.CDLL(str(_lib.GGML_LIB_PATH))
-    for name in _declared("exl3-block.h", "ggml_exl3_"):
-        if name == "ggml_exl3_get_rows":
-            continue  # declared for the interface; its GPU implementation is listed in DESIGN.md as pending
+    names = _declared("exl3-block.h", "ggml_exl3_")
+    assert {"ggml_exl3_mul_mat", "ggml_exl3_get_rows"} <= set(names)
+    for name in names:
         assert hasattr(g, name), name
 
 

@@ -1,8 +1,13 @@
-// ggml_exl3_mul_mat for ggml's CPU backend, executed on a B200 through the
-// exl3cu C ABI.  Drop-in for the reference's src/exl3-ggml.cpp:51-92: same
-// symbol, same tensor contract (src0 EXL3_4/6/8 [k, n] runtime records, src1
-// F32/F16 [k, r1, r2, r3] with byte strides nb[], dst F32 [n, r1, r2, r3]),
-// same GGML_ASSERT checks.
+// ggml_exl3_mul_mat and ggml_exl3_get_rows for ggml's CPU backend, executed
+// on a B200 through the exl3cu C ABI.  Drop-in for the reference's
+// src/exl3-ggml.cpp: same symbols, same tensor contracts, same GGML_ASSERT
+// checks.
+//  * mul_mat (src/exl3-ggml.cpp:51-92): src0 EXL3_4/6/8 [k, n] runtime
+//    records, src1 F32/F16 [k, r1, r2, r3] with byte strides nb[], dst F32
+//    [n, r1, r2, r3].
+//  * get_rows (src/exl3-ggml.cpp:19-49): src0 as above, src1 I32 ids of any
+//    shape (element r = row r / ne[0], column r % ne[0]), dst F32 with one
+//    k-wide row per id (rows addressed through ne[1], ne[2] and nb[1..3]).
 //
 // ggml calls an op from nth threads with ith = 0..nth-1 and joins them on a
 // barrier before the next op.  Thread 0 alone drives the GPU -- it uploads the
@@ -22,9 +27,11 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <vector>
 
 namespace {
 
@@ -54,7 +61,62 @@ exl3cu_weight * weight_for(const ggml_tensor * w, unsigned bits, size_t k, size_
     return h;
 }
 
+// Byte offset of row `row` of t, rows counted across ne[1], ne[2], ne[3].
+size_t row_offset(const ggml_tensor * t, size_t row) {
+    const size_t i1 = row % size_t(t->ne[1]);
+    row /= size_t(t->ne[1]);
+    const size_t i2 = row % size_t(t->ne[2]);
+    const size_t i3 = row / size_t(t->ne[2]);
+    return i1 * t->nb[1] + i2 * t->nb[2] + i3 * t->nb[3];
+}
+
 }  // namespace
+
+extern "C" void ggml_exl3_get_rows(const ggml_compute_params * params, ggml_tensor * dst) {
+    const ggml_tensor * weight = dst->src[0];
+    const ggml_tensor * ids = dst->src[1];
+    const size_t k = size_t(weight->ne[0]), n = size_t(weight->ne[1]);
+    const unsigned bits = exl3_type_bits(weight->type);
+    GGML_ASSERT(bits && k && n && k % 128 == 0 && n % 128 == 0 && weight->ne[2] == 1 && weight->ne[3] == 1);
+    GGML_ASSERT(ids->type == GGML_TYPE_I32 && dst->type == GGML_TYPE_F32);
+    if (params->ith != 0) return;
+    const size_t count = size_t(ggml_nelements(ids));
+    if (!count) return;
+    GGML_ASSERT(dst->nb[0] == 4 && size_t(dst->ne[0]) >= k);
+    std::vector<int32_t> id(count);
+    for (size_t r = 0; r < count; ++r) {
+        const size_t row = r / size_t(ids->ne[0]), col = r % size_t(ids->ne[0]);
+        std::memcpy(&id[r], static_cast<const char *>(ids->data) + row_offset(ids, row) + col * ids->nb[0], 4);
+        GGML_ASSERT(id[r] >= 0 && size_t(id[r]) < n);
+    }
+    exl3cu_weight * h = weight_for(weight, bits, k, n);
+    // Rows of dst that are evenly spaced (the usual contiguous [k, count]
+    // result) are written in place; otherwise through a contiguous buffer.
+    bool even = true;
+    const size_t stride = count > 1 ? row_offset(dst, 1) : k * 4;
+    for (size_t r = 0; r < count && even; ++r) even = row_offset(dst, r) == r * stride;
+    even = even && stride % 4 == 0 && stride >= k * 4;
+    // one call per kMaxIds ids (the library's per-call limit)
+    constexpr size_t kMaxIds = 65535;
+    if (even) {
+        for (size_t r0 = 0; r0 < count; r0 += kMaxIds) {
+            const size_t c = count - r0 < kMaxIds ? count - r0 : kMaxIds;
+            const int rc = exl3cu_get_rows_host(h, id.data() + r0, c,
+                                                reinterpret_cast<float *>(static_cast<char *>(dst->data) + r0 * stride),
+                                                stride / 4, 1, nullptr);
+            if (rc) die("ggml_exl3_get_rows", rc);
+        }
+        return;
+    }
+    std::vector<float> tmp(count * k);
+    for (size_t r0 = 0; r0 < count; r0 += kMaxIds) {
+        const size_t c = count - r0 < kMaxIds ? count - r0 : kMaxIds;
+        const int rc = exl3cu_get_rows_host(h, id.data() + r0, c, tmp.data() + r0 * k, k, 1, nullptr);
+        if (rc) die("ggml_exl3_get_rows", rc);
+    }
+    for (size_t r = 0; r < count; ++r)
+        std::memcpy(static_cast<char *>(dst->data) + row_offset(dst, r), tmp.data() + r * k, k * 4);
+}
 
 extern "C" void ggml_exl3_mul_mat(const ggml_compute_params * params, ggml_tensor * dst) {
     const ggml_tensor * weight = dst->src[0];

@@ -305,6 +305,23 @@ int gemm_scratch(int device, cudaStream_t st, size_t bytes, void ** out) {
 constexpr size_t kMaxRaggedSeqs = 65536;
 constexpr int32_t kMaxRaggedRows = 1 << 20;
 
+// Ids per get_rows call (the launch grid's y extent is 65535).
+constexpr size_t kMaxGetRows = 65535;
+
+// Grow one of a handle's host-form staging buffers to at least `want` bytes.
+// The outgrown buffer is retired, not freed: work still in flight, or a
+// captured graph, may reference it until the handle is freed.
+int grow_stage(exl3cu_weight * w, void ** buf, size_t * bytes, size_t want) {
+    if (*bytes >= want) return EXL3CU_OK;
+    void * p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, want);
+    if (e != cudaSuccess) return cuda_fail(e, "allocating host-form staging");
+    if (*buf) w->retired.push_back(*buf);
+    *buf = p;
+    *bytes = want;
+    return EXL3CU_OK;
+}
+
 // Rows per GEMM launch pair: bounds the scratch (2 KB per row per 1024 of k)
 // and keeps every index of the launch in 32 bits.
 constexpr size_t kGemmRowsPerLaunch = 2048;
@@ -619,11 +636,12 @@ int exl3cu_device_status(int device, unsigned * status, int clear) {
     DeviceGuard guard(device);
     if (!guard.ok) return fail(EXL3CU_INVALID_ARGUMENT, "cannot select device %d", device);
     CU_TRY(cudaDeviceSynchronize(), "synchronising before reading the device status");
-    unsigned gemv = 0, gemm = 0, seq = 0;
+    unsigned gemv = 0, gemm = 0, seq = 0, rows = 0;
     CU_TRY(mul1_read_status(&gemv, clear != 0), "reading the GEMV status word");
     CU_TRY(gemm_read_status(&gemm, clear != 0), "reading the GEMM status word");
     CU_TRY(seq_read_status(&seq, clear != 0), "reading the sequence status word");
-    *status = gemv | gemm | seq;
+    CU_TRY(rows_read_status(&rows, clear != 0), "reading the get_rows status word");
+    *status = gemv | gemm | seq | rows;
     return EXL3CU_OK;
 }
 
@@ -841,6 +859,54 @@ int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, si
                   static_cast<cudaStream_t>(stream));
 }
 
+int exl3cu_get_rows(const exl3cu_weight * w, const int32_t * d_ids, size_t count, float * d_out,
+                    size_t out_row_stride, void * stream) {
+    if (!w) return fail(EXL3CU_INVALID_ARGUMENT, "weight handle is NULL");
+    if (!count) return EXL3CU_OK;
+    if (count > kMaxGetRows) return fail(EXL3CU_INVALID_ARGUMENT, "count above %zu", kMaxGetRows);
+    if (!d_ids || !d_out) return fail(EXL3CU_INVALID_ARGUMENT, "ids and out are required");
+    if (out_row_stride < w->k) return fail(EXL3CU_INVALID_ARGUMENT, "out row stride shorter than k");
+    int rc;
+    if ((rc = check_device_ptr(d_ids, w->device, "ids"))) return rc;
+    if ((rc = check_device_ptr(d_out, w->device, "out"))) return rc;
+    DeviceGuard guard(w->device);
+    CU_TRY(launch_get_rows(w->lsc, reinterpret_cast<const uint16_t *>(w->su), reinterpret_cast<const uint16_t *>(w->sv),
+                           w->k, w->nblocks * 128, w->bits, w->codebook, d_ids, count, d_out, out_row_stride,
+                           static_cast<cudaStream_t>(stream)),
+           "launching get_rows");
+    return EXL3CU_OK;
+}
+
+int exl3cu_get_rows_host(exl3cu_weight * w, const int32_t * h_ids, size_t count, float * h_out,
+                         size_t out_row_stride, int synchronize, void * stream) {
+    if (!w) return fail(EXL3CU_INVALID_ARGUMENT, "weight handle is NULL");
+    if (!count) return EXL3CU_OK;
+    if (count > kMaxGetRows) return fail(EXL3CU_INVALID_ARGUMENT, "count above %zu", kMaxGetRows);
+    if (!h_ids || !h_out) return fail(EXL3CU_INVALID_ARGUMENT, "ids and out are required");
+    if (out_row_stride < w->k) return fail(EXL3CU_INVALID_ARGUMENT, "out row stride shorter than k");
+    const size_t ncols = w->nblocks * 128;
+    for (size_t i = 0; i < count; ++i)
+        if (h_ids[i] < 0 || size_t(h_ids[i]) >= ncols)
+            return fail(EXL3CU_INVALID_ARGUMENT, "id %d at %zu outside 0..%zu", int(h_ids[i]), i, ncols - 1);
+    DeviceGuard guard(w->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t ib = (count * sizeof(int32_t) + 255) & ~size_t(255), ob = count * w->k * sizeof(float);
+    int rc;
+    if ((rc = grow_stage(w, &w->stage_x, &w->stage_x_bytes, ib))) return rc;
+    if ((rc = grow_stage(w, reinterpret_cast<void **>(&w->stage_y), &w->stage_y_bytes, ob))) return rc;
+    CU_TRY(cudaMemcpyAsync(w->stage_x, h_ids, count * sizeof(int32_t), cudaMemcpyHostToDevice, st),
+           "copying ids to the device");
+    CU_TRY(launch_get_rows(w->lsc, reinterpret_cast<const uint16_t *>(w->su), reinterpret_cast<const uint16_t *>(w->sv),
+                           w->k, ncols, w->bits, w->codebook, static_cast<const int32_t *>(w->stage_x), count,
+                           w->stage_y, w->k, st),
+           "launching get_rows");
+    CU_TRY(cudaMemcpy2DAsync(h_out, out_row_stride * sizeof(float), w->stage_y, w->k * sizeof(float),
+                             w->k * sizeof(float), count, cudaMemcpyDeviceToHost, st),
+           "copying rows to the host");
+    if (synchronize) CU_TRY(cudaStreamSynchronize(st), "synchronising the stream");
+    return EXL3CU_OK;
+}
+
 int exl3cu_mul_mat_host(exl3cu_weight * w, const void * h_x, int x_dtype, size_t rows, size_t x_row_stride,
                         float * h_y, size_t y_row_stride, int synchronize, void * stream) {
     if (!h_x || !h_y) return fail(EXL3CU_INVALID_ARGUMENT, "x and y are required");
@@ -855,26 +921,13 @@ int exl3cu_mul_mat_host(exl3cu_weight * w, const void * h_x, int x_dtype, size_t
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const size_t es = x_dtype == EXL3CU_F32 ? 4 : 2;
     const size_t xb = rows * w->k * es, yb = rows * n_local * sizeof(float);
-    // Staging grows by retiring the old buffers, not freeing them: work still in
-    // flight, or a captured graph, may reference them until the handle is freed.
-    if (w->stage_x_bytes < xb) {
-        void * p = nullptr;
-        CU_TRY(cudaMalloc(&p, xb), "allocating x staging");
-        if (w->stage_x) w->retired.push_back(w->stage_x);
-        w->stage_x = p;
-        w->stage_x_bytes = xb;
-    }
-    if (w->stage_y_bytes < yb) {
-        void * p = nullptr;
-        CU_TRY(cudaMalloc(&p, yb), "allocating y staging");
-        if (w->stage_y) w->retired.push_back(w->stage_y);
-        w->stage_y = static_cast<float *>(p);
-        w->stage_y_bytes = yb;
-    }
+    int rc;
+    if ((rc = grow_stage(w, &w->stage_x, &w->stage_x_bytes, xb))) return rc;
+    if ((rc = grow_stage(w, reinterpret_cast<void **>(&w->stage_y), &w->stage_y_bytes, yb))) return rc;
     CU_TRY(cudaMemcpy2DAsync(w->stage_x, w->k * es, h_x, x_row_stride * es, w->k * es, rows, cudaMemcpyHostToDevice, st),
            "copying x to the device");
     const MmItem item{w, w->stage_x, x_dtype, rows, w->k, w->stage_y, n_local};
-    int rc = run_cluster(&item, 1, st);
+    rc = run_cluster(&item, 1, st);
     if (rc) return rc;
     CU_TRY(cudaMemcpy2DAsync(h_y, y_row_stride * sizeof(float), w->stage_y, n_local * sizeof(float),
                              n_local * sizeof(float), rows, cudaMemcpyDeviceToHost, st),

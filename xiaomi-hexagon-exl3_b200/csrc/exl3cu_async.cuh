@@ -13,6 +13,7 @@
 namespace exl3cu {
 
 constexpr unsigned kStatusWaitTimeout = 1u;
+constexpr unsigned kStatusBadIndex = 2u;   // an index argument read on the device was out of range
 constexpr unsigned kWaitSpins = 1u << 22;  // try_wait rounds before giving up (each may suspend briefly)
 
 __device__ __forceinline__ uint32_t smem_addr(const void * p) {

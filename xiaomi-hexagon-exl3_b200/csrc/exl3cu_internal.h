@@ -155,6 +155,10 @@ cudaError_t launch_trellis_to_lsc(const uint16_t * trellis, size_t k, size_t n, 
 cudaError_t launch_lsc_decode(const uint32_t * lsc, size_t k, size_t nbc, unsigned bits, unsigned cb, uint16_t * out,
                               cudaStream_t st);
 cudaError_t launch_hadamard128(float * v, size_t count, cudaStream_t st);
+cudaError_t launch_get_rows(const uint32_t * lsc, const uint16_t * suh, const uint16_t * svh, size_t k, size_t ncols,
+                            unsigned bits, unsigned cb, const int32_t * ids, size_t count, float * out,
+                            size_t out_stride, cudaStream_t st);
+cudaError_t rows_read_status(unsigned * out, bool clear);
 cudaError_t launch_reconstruct_blocks(uint16_t * io, size_t k, size_t column_count, size_t first_column,
                                       const uint16_t * suh, const uint16_t * svh, cudaStream_t st);
 

@@ -4,6 +4,7 @@
 //
 // These back the exl3_codec.h host API (reference include/exl3_codec.h:10-29)
 // and the weight upload path; the GEMV hot loop lives in exl3cu_gemv.cu.
+#include "exl3cu_async.cuh"
 #include "exl3cu_internal.h"
 
 namespace exl3cu {
@@ -221,6 +222,121 @@ __global__ void k_reconstruct_blocks(uint16_t * __restrict__ io, size_t ld, size
             io[(rk + r) * ld + cn + c] = __half_as_ushort(__float2half_rn(val));
         }
     }
+}
+
+// ---------------------------------------------------------------------------
+// get_rows (src/exl3-ggml.cpp:19-49): for token id, the original-basis column
+// W[:, id] over all k rows as f32.  One CTA per (id, 128-row group kb), as the
+// reference reconstructs one 128x128 group per (id, kb): the group is decoded
+// into shared memory (fp16 -> fp32 exact), every row is rotated (H128 along
+// the row, the reference's butterfly), the id's column is kept, rotated along
+// the k direction, scaled by suh[row] then svh[id] and rounded to fp16 -- the
+// operations of exl3::reconstruct (src/exl3_codec.cpp:169-204) in its order.
+// ids are local to the handle's column range; an id outside it yields a row
+// of NaN and raises kStatusBadIndex.
+static __device__ unsigned g_rows_status;
+
+template <int BITS, unsigned CB>
+__global__ void __launch_bounds__(256) k_get_rows(const uint32_t * __restrict__ lsc, const uint16_t * __restrict__ suh,
+                                                  const uint16_t * __restrict__ svh, size_t k, size_t ncols,
+                                                  const int32_t * __restrict__ ids, float * __restrict__ out,
+                                                  size_t out_stride) {
+    __shared__ uint16_t blk[128 * 130];  // decoded fp16 bits (exact), row pitch 65 words
+    __shared__ float col[128];
+    const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const size_t kb = blockIdx.x, r_out = blockIdx.y;
+    const int32_t id = ids[r_out];
+    float * dst = out + r_out * out_stride + kb * 128;
+    if (id < 0 || size_t(id) >= ncols) {
+        if (threadIdx.x < 128) dst[threadIdx.x] = __int_as_float(0x7fc00000);
+        if (threadIdx.x == 0) atomicOr(&g_rows_status, kStatusBadIndex);
+        return;
+    }
+    const size_t nb = size_t(id) / 128, c_in = size_t(id) % 128, nchunks = k / 16;
+    {
+        // warp w decodes chunk (nb, 8*kb + w): rows 16w..16w+15 of the group, all 128 columns
+        const size_t chunk = nb * nchunks + kb * 8 + warp;
+        uint32_t w[2 * BITS];
+        load_segment<BITS>(lsc + chunk * 64u * BITS + lane * 2u * BITS, w);
+        uint32_t frag[8][4];
+        decode_chunk<BITS, CB>(w, frag);
+        const unsigned g = lane >> 2, t = lane & 3u;
+        const unsigned r0 = warp * 16 + 2 * t;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            // A-fragment of W^T: reg0 = rows 2t, 2t+1 of column g; reg1 column g+8; reg2/3 rows +8
+            const unsigned cg0 = c * 16 + g, cg8 = cg0 + 8;
+            const uint32_t f0 = frag[c][0], f1 = frag[c][1], f2 = frag[c][2], f3 = frag[c][3];
+            blk[(r0) * 130 + cg0] = uint16_t(f0 & 0xffffu);
+            blk[(r0 + 1) * 130 + cg0] = uint16_t(f0 >> 16);
+            blk[(r0) * 130 + cg8] = uint16_t(f1 & 0xffffu);
+            blk[(r0 + 1) * 130 + cg8] = uint16_t(f1 >> 16);
+            blk[(r0 + 8) * 130 + cg0] = uint16_t(f2 & 0xffffu);
+            blk[(r0 + 9) * 130 + cg0] = uint16_t(f2 >> 16);
+            blk[(r0 + 8) * 130 + cg8] = uint16_t(f3 & 0xffffu);
+            blk[(r0 + 9) * 130 + cg8] = uint16_t(f3 >> 16);
+        }
+    }
+    __syncthreads();
+    for (int r = warp; r < 128; r += 8) {
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] = __half2float(__ushort_as_half(blk[r * 130 + lane * 4 + q]));
+        h128_warp4(v);
+        if (lane == c_in / 4) col[r] = v[c_in % 4];
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] = col[lane * 4 + q];
+        h128_warp4(v);
+        const float sv = __half2float(__ushort_as_half(svh[id]));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const size_t row = kb * 128 + lane * 4 + q;
+            const float su = __half2float(__ushort_as_half(suh[row]));
+            const float val = __fmul_rn(__fmul_rn(v[q], su), sv);
+            dst[lane * 4 + q] = __half2float(__float2half_rn(val));
+        }
+    }
+}
+
+template <int BITS>
+static cudaError_t get_rows_bits(const uint32_t * lsc, const uint16_t * suh, const uint16_t * svh, size_t k,
+                                 size_t ncols, unsigned cb, const int32_t * ids, size_t count, float * out,
+                                 size_t out_stride, cudaStream_t st) {
+    const dim3 grid(unsigned(k / 128), unsigned(count));
+    if (cb == CB_MUL1) k_get_rows<BITS, CB_MUL1><<<grid, 256, 0, st>>>(lsc, suh, svh, k, ncols, ids, out, out_stride);
+    else if (cb == CB_MCG) k_get_rows<BITS, CB_MCG><<<grid, 256, 0, st>>>(lsc, suh, svh, k, ncols, ids, out, out_stride);
+    else k_get_rows<BITS, CB_3INST><<<grid, 256, 0, st>>>(lsc, suh, svh, k, ncols, ids, out, out_stride);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_get_rows(const uint32_t * lsc, const uint16_t * suh, const uint16_t * svh, size_t k, size_t ncols,
+                            unsigned bits, unsigned cb, const int32_t * ids, size_t count, float * out,
+                            size_t out_stride, cudaStream_t st) {
+    if (!count) return cudaSuccess;
+    switch (bits) {
+        case 1: return get_rows_bits<1>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
+        case 2: return get_rows_bits<2>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
+        case 3: return get_rows_bits<3>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
+        case 4: return get_rows_bits<4>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
+        case 5: return get_rows_bits<5>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
+        case 6: return get_rows_bits<6>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
+        case 7: return get_rows_bits<7>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
+        case 8: return get_rows_bits<8>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t rows_read_status(unsigned * out, bool clear) {
+    cudaError_t e = cudaMemcpyFromSymbol(out, g_rows_status, sizeof(unsigned));
+    if (e == cudaSuccess && clear && *out) {
+        const unsigned zero = 0;
+        e = cudaMemcpyToSymbol(g_rows_status, &zero, sizeof(unsigned));
+    }
+    return e;
 }
 
 // ---------------------------------------------------------------------------

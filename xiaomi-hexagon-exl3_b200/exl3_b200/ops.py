@@ -165,6 +165,30 @@ class Exl3Weight:
                                         int(synchronize), _stream_handle(stream)))
         return out
 
+    def get_rows(self, ids: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """Original-basis columns W[:, id] for each id as float32 rows [count, k]
+        (exl3cu_get_rows; the reference's ggml_exl3_get_rows).  ids: int32 device tensor,
+        local to this handle's columns; an id out of range gives a NaN row and sets bit 1
+        of device_status()."""
+        if ids.dtype != torch.int32:
+            raise TypeError("ids must be int32")
+        ids2 = ids.reshape(-1).contiguous()
+        if out is None:
+            out = torch.empty((ids2.numel(), self.k), dtype=torch.float32, device=ids.device)
+        if out.dim() != 2 or out.stride(1) != 1 or out.shape[0] < ids2.numel() or out.shape[1] < self.k:
+            raise ValueError("out must be a row-major float32 [count, >=k] tensor")
+        check(lib().exl3cu_get_rows(self._h, _ptr(ids2), ids2.numel(), _ptr(out), out.stride(0),
+                                    _stream_handle(stream)))
+        return out
+
+    def get_rows_host(self, ids: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        """Host-buffer form of get_rows (ids checked on the host; synchronous)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32).reshape(-1)
+        if out is None:
+            out = np.empty((ids.size, self.k), np.float32)
+        check(lib().exl3cu_get_rows_host(self._h, _ptr(ids), ids.size, _ptr(out), out.shape[1], 1, None))
+        return out
+
     def decode_inner(self, stream=None) -> np.ndarray:
         """The handle's device-layout weights decoded back to row-major inner fp16 bits [k, n]."""
         out = torch.empty((self.k, self.n), dtype=torch.int16, device=f"cuda:{self.device}")
