@@ -49,6 +49,14 @@ enum exl3cu_dtype { EXL3CU_F32 = 0, EXL3CU_F16 = 1 };
 enum exl3cu_codebook { EXL3CU_CB_3INST = 0, EXL3CU_CB_MCG = 1, EXL3CU_CB_MUL1 = 2 };
 
 typedef struct exl3cu_weight exl3cu_weight;
+typedef struct exl3cu_model exl3cu_model;
+
+/* Storage dtypes of model tensors (the safetensors dtypes exl3::Model accepts,
+ * src/exl3_model.cpp:87). */
+enum exl3cu_storage_dtype { EXL3CU_ST_F16 = 0, EXL3CU_ST_BF16 = 1, EXL3CU_ST_I16 = 2, EXL3CU_ST_F32 = 3, EXL3CU_ST_I32 = 4 };
+
+/* exl3cu_model_open flags. */
+#define EXL3CU_MODEL_VALIDATE_ONLY 1u
 
 int exl3cu_abi_version(void);
 const char * exl3cu_status_string(int status);
@@ -218,6 +226,51 @@ int exl3cu_get_rows_host(exl3cu_weight * w, const int32_t * h_ids, size_t count,
  * array holds. */
 int exl3cu_mul_mat_noalloc(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
                            float * d_y, size_t y_row_stride, void * stream);
+
+/* ------------------------------------------------------------------------
+ * Model loader (replaces exl3::Model's constructor, src/exl3_model.cpp:79-157,
+ * and extends it from the tied head to every EXL3 matrix).
+ *
+ * exl3cu_model_open reads <directory>/model.safetensors and
+ * <directory>/hexagon-exl3.json and applies exl3::Model's checks in its order
+ * and with its messages (spans, dtypes, manifest, <= 5.0 bits-per-weight
+ * budget, head geometry, codebook markers); any failure returns
+ * EXL3CU_INVALID_ARGUMENT with that message.  Then, on `device`:
+ *   - every X.trellis (3-D I16, 16*bits last dimension) with F16 X.suh/X.svh
+ *     becomes a persistent weight handle at its own bit width (mixed-bit
+ *     models), codebook from its X.mul1 / X.mcg marker;
+ *   - every other tensor is copied into one device arena.
+ * With flags = EXL3CU_MODEL_VALIDATE_ONLY nothing touches a GPU and weight and
+ * tensor pointers read back as NULL.  The weight handles belong to the model:
+ * exl3cu_weight_free refuses them; exl3cu_model_free releases everything.
+ * Matrices and tensors are indexed in name order. */
+int exl3cu_model_open(const char * directory, int device, unsigned flags, exl3cu_model ** out);
+int exl3cu_model_free(exl3cu_model * m);
+/* tensor_count / payload_bytes / hidden_size / vocab_size / bits_per_weight are
+ * exl3::Model's accessors (src/exl3_model.cpp:162-166); any pointer may be NULL. */
+int exl3cu_model_info(const exl3cu_model * m, size_t * tensor_count, size_t * payload_bytes, size_t * hidden_size,
+                      size_t * vocab_size, size_t * parameter_count, double * bits_per_weight);
+size_t exl3cu_model_matrix_count(const exl3cu_model * m);
+/* Matrix `index`: its name (the X of X.trellis; valid while m lives), shape,
+ * bit width, codebook and weight handle. */
+int exl3cu_model_matrix(const exl3cu_model * m, size_t index, const char ** name, size_t * k, size_t * n,
+                        unsigned * bits, unsigned * codebook, exl3cu_weight ** weight);
+int exl3cu_model_find_matrix(const exl3cu_model * m, const char * name, size_t * index);
+/* Matrix index of the tied head (input_embedding.source). */
+int exl3cu_model_head(const exl3cu_model * m, size_t * index);
+/* Tensor `index` (0 .. tensor_count-1): name, storage dtype, shape, bytes, and
+ * its device copy (NULL for the parts of an EXL3 matrix, which live in the
+ * weight handle, and for validate-only models). */
+int exl3cu_model_tensor(const exl3cu_model * m, size_t index, const char ** name, int * dtype, size_t * ndim,
+                        const size_t ** shape, size_t * bytes, void ** d_data);
+int exl3cu_model_find_tensor(const exl3cu_model * m, const char * name, size_t * index);
+/* exl3::Model::embedding (src/exl3_model.cpp:168-187): the hidden_size fp16
+ * values of token's original-basis column of the tied head, into host memory.
+ * Synchronous.  token >= vocab_size -> EXL3CU_INVALID_ARGUMENT. */
+int exl3cu_model_embedding(exl3cu_model * m, uint32_t token, uint16_t * h_out);
+/* Batched, stream-ordered form on the device: exl3cu_get_rows on the head. */
+int exl3cu_model_embed(const exl3cu_model * m, const int32_t * d_ids, size_t count, float * d_out,
+                       size_t out_row_stride, void * stream);
 
 #ifdef __cplusplus
 }

@@ -23,6 +23,7 @@ using namespace exl3cu;
 
 struct exl3cu_weight {
     int device;
+    bool model_owned;    // freed with its model handle, not by exl3cu_weight_free
     size_t k;
     size_t n_total;
     size_t first_block;
@@ -591,6 +592,7 @@ int exl3cu_weight_from_trellis(const uint16_t * trellis, const uint16_t * suh, c
 }
 
 int exl3cu_weight_free(exl3cu_weight * w) {
+    if (w && w->model_owned) return fail(EXL3CU_INVALID_ARGUMENT, "this weight belongs to a model handle; free the model");
     release(w);
     return EXL3CU_OK;
 }
@@ -871,7 +873,7 @@ int exl3cu_get_rows(const exl3cu_weight * w, const int32_t * d_ids, size_t count
     if ((rc = check_device_ptr(d_out, w->device, "out"))) return rc;
     DeviceGuard guard(w->device);
     CU_TRY(launch_get_rows(w->lsc, reinterpret_cast<const uint16_t *>(w->su), reinterpret_cast<const uint16_t *>(w->sv),
-                           w->k, w->nblocks * 128, w->bits, w->codebook, d_ids, count, d_out, out_row_stride,
+                           w->k, w->nblocks * 128, w->bits, w->codebook, d_ids, count, d_out, out_row_stride, false,
                            static_cast<cudaStream_t>(stream)),
            "launching get_rows");
     return EXL3CU_OK;
@@ -898,7 +900,7 @@ int exl3cu_get_rows_host(exl3cu_weight * w, const int32_t * h_ids, size_t count,
            "copying ids to the device");
     CU_TRY(launch_get_rows(w->lsc, reinterpret_cast<const uint16_t *>(w->su), reinterpret_cast<const uint16_t *>(w->sv),
                            w->k, ncols, w->bits, w->codebook, static_cast<const int32_t *>(w->stage_x), count,
-                           w->stage_y, w->k, st),
+                           w->stage_y, w->k, false, st),
            "launching get_rows");
     CU_TRY(cudaMemcpy2DAsync(h_out, out_row_stride * sizeof(float), w->stage_y, w->k * sizeof(float),
                              w->k * sizeof(float), count, cudaMemcpyDeviceToHost, st),
@@ -1013,3 +1015,22 @@ extern "C" int exl3cu_mul_mat_noalloc(const exl3cu_weight * w, const void * d_x,
     }
     return run_mm(w, d_x, x_dtype, rows, x_row_stride, d_y, y_row_stride, scratch, st);
 }
+
+// ---------------------------------------------------------------------------
+// Internal hooks for the other C-ABI translation units (the model loader).
+namespace exl3cu {
+
+int api_fail(int status, const char * message) { return fail(status, "%s", message); }
+
+int api_cuda_fail(cudaError_t e, const char * what) { return cuda_fail(e, what); }
+
+void weight_set_model_owned(::exl3cu_weight * w) { w->model_owned = true; }
+
+void weight_free_owned(::exl3cu_weight * w) { release(w); }
+
+WeightGeometry weight_geometry(const ::exl3cu_weight * w) {
+    return WeightGeometry{w->k,      w->nblocks * 128, w->bits, w->codebook, w->device, w->lsc,
+                          reinterpret_cast<const uint16_t *>(w->su), reinterpret_cast<const uint16_t *>(w->sv)};
+}
+
+}  // namespace exl3cu

@@ -8,6 +8,8 @@
 #include "exl3cu_common.cuh"
 #include "exl3cu_decode.cuh"
 
+struct exl3cu_weight;
+
 namespace exl3cu {
 
 struct GemvArgs {
@@ -155,11 +157,31 @@ cudaError_t launch_trellis_to_lsc(const uint16_t * trellis, size_t k, size_t n, 
 cudaError_t launch_lsc_decode(const uint32_t * lsc, size_t k, size_t nbc, unsigned bits, unsigned cb, uint16_t * out,
                               cudaStream_t st);
 cudaError_t launch_hadamard128(float * v, size_t count, cudaStream_t st);
+// out: f32 rows, or fp16 rows (the bits exl3::reconstruct produces) with out_f16.
 cudaError_t launch_get_rows(const uint32_t * lsc, const uint16_t * suh, const uint16_t * svh, size_t k, size_t ncols,
-                            unsigned bits, unsigned cb, const int32_t * ids, size_t count, float * out,
-                            size_t out_stride, cudaStream_t st);
+                            unsigned bits, unsigned cb, const int32_t * ids, size_t count, void * out,
+                            size_t out_stride, bool out_f16, cudaStream_t st);
 cudaError_t rows_read_status(unsigned * out, bool clear);
 cudaError_t launch_reconstruct_blocks(uint16_t * io, size_t k, size_t column_count, size_t first_column,
                                       const uint16_t * suh, const uint16_t * svh, cudaStream_t st);
+
+// Shared by the C-ABI translation units (defined in exl3cu_api.cu): record
+// the calling thread's last error and return `status`; the CUDA form also
+// clears a non-sticky CUDA error.
+int api_fail(int status, const char * message);
+int api_cuda_fail(cudaError_t e, const char * what);
+// Weights owned by a model handle: exl3cu_weight_free refuses them and the
+// model frees them with weight_free_owned.
+void weight_set_model_owned(struct ::exl3cu_weight * w);
+void weight_free_owned(struct ::exl3cu_weight * w);
+struct WeightGeometry {
+    size_t k, n_local;
+    unsigned bits, codebook;
+    int device;
+    const uint32_t * lsc;
+    const uint16_t * su;
+    const uint16_t * sv;
+};
+WeightGeometry weight_geometry(const struct ::exl3cu_weight * w);
 
 }  // namespace exl3cu

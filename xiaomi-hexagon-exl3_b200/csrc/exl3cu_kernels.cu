@@ -239,16 +239,21 @@ static __device__ unsigned g_rows_status;
 template <int BITS, unsigned CB>
 __global__ void __launch_bounds__(256) k_get_rows(const uint32_t * __restrict__ lsc, const uint16_t * __restrict__ suh,
                                                   const uint16_t * __restrict__ svh, size_t k, size_t ncols,
-                                                  const int32_t * __restrict__ ids, float * __restrict__ out,
-                                                  size_t out_stride) {
+                                                  const int32_t * __restrict__ ids, void * __restrict__ out,
+                                                  size_t out_stride, bool out_f16) {
     __shared__ uint16_t blk[128 * 130];  // decoded fp16 bits (exact), row pitch 65 words
     __shared__ float col[128];
     const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const size_t kb = blockIdx.x, r_out = blockIdx.y;
     const int32_t id = ids[r_out];
-    float * dst = out + r_out * out_stride + kb * 128;
+    const size_t dst_off = r_out * out_stride + kb * 128;
+    float * dst = static_cast<float *>(out) + dst_off;
+    uint16_t * dst16 = static_cast<uint16_t *>(out) + dst_off;
     if (id < 0 || size_t(id) >= ncols) {
-        if (threadIdx.x < 128) dst[threadIdx.x] = __int_as_float(0x7fc00000);
+        if (threadIdx.x < 128) {
+            if (out_f16) dst16[threadIdx.x] = 0x7e00u;
+            else dst[threadIdx.x] = __int_as_float(0x7fc00000);
+        }
         if (threadIdx.x == 0) atomicOr(&g_rows_status, kStatusBadIndex);
         return;
     }
@@ -296,36 +301,37 @@ __global__ void __launch_bounds__(256) k_get_rows(const uint32_t * __restrict__ 
         for (int q = 0; q < 4; ++q) {
             const size_t row = kb * 128 + lane * 4 + q;
             const float su = __half2float(__ushort_as_half(suh[row]));
-            const float val = __fmul_rn(__fmul_rn(v[q], su), sv);
-            dst[lane * 4 + q] = __half2float(__float2half_rn(val));
+            const __half h = __float2half_rn(__fmul_rn(__fmul_rn(v[q], su), sv));
+            if (out_f16) dst16[lane * 4 + q] = __half_as_ushort(h);
+            else dst[lane * 4 + q] = __half2float(h);
         }
     }
 }
 
 template <int BITS>
 static cudaError_t get_rows_bits(const uint32_t * lsc, const uint16_t * suh, const uint16_t * svh, size_t k,
-                                 size_t ncols, unsigned cb, const int32_t * ids, size_t count, float * out,
-                                 size_t out_stride, cudaStream_t st) {
+                                 size_t ncols, unsigned cb, const int32_t * ids, size_t count, void * out,
+                                 size_t out_stride, bool f16, cudaStream_t st) {
     const dim3 grid(unsigned(k / 128), unsigned(count));
-    if (cb == CB_MUL1) k_get_rows<BITS, CB_MUL1><<<grid, 256, 0, st>>>(lsc, suh, svh, k, ncols, ids, out, out_stride);
-    else if (cb == CB_MCG) k_get_rows<BITS, CB_MCG><<<grid, 256, 0, st>>>(lsc, suh, svh, k, ncols, ids, out, out_stride);
-    else k_get_rows<BITS, CB_3INST><<<grid, 256, 0, st>>>(lsc, suh, svh, k, ncols, ids, out, out_stride);
+    if (cb == CB_MUL1) k_get_rows<BITS, CB_MUL1><<<grid, 256, 0, st>>>(lsc, suh, svh, k, ncols, ids, out, out_stride, f16);
+    else if (cb == CB_MCG) k_get_rows<BITS, CB_MCG><<<grid, 256, 0, st>>>(lsc, suh, svh, k, ncols, ids, out, out_stride, f16);
+    else k_get_rows<BITS, CB_3INST><<<grid, 256, 0, st>>>(lsc, suh, svh, k, ncols, ids, out, out_stride, f16);
     return cudaGetLastError();
 }
 
 cudaError_t launch_get_rows(const uint32_t * lsc, const uint16_t * suh, const uint16_t * svh, size_t k, size_t ncols,
-                            unsigned bits, unsigned cb, const int32_t * ids, size_t count, float * out,
-                            size_t out_stride, cudaStream_t st) {
+                            unsigned bits, unsigned cb, const int32_t * ids, size_t count, void * out,
+                            size_t out_stride, bool out_f16, cudaStream_t st) {
     if (!count) return cudaSuccess;
     switch (bits) {
-        case 1: return get_rows_bits<1>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
-        case 2: return get_rows_bits<2>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
-        case 3: return get_rows_bits<3>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
-        case 4: return get_rows_bits<4>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
-        case 5: return get_rows_bits<5>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
-        case 6: return get_rows_bits<6>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
-        case 7: return get_rows_bits<7>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
-        case 8: return get_rows_bits<8>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, st);
+        case 1: return get_rows_bits<1>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, out_f16, st);
+        case 2: return get_rows_bits<2>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, out_f16, st);
+        case 3: return get_rows_bits<3>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, out_f16, st);
+        case 4: return get_rows_bits<4>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, out_f16, st);
+        case 5: return get_rows_bits<5>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, out_f16, st);
+        case 6: return get_rows_bits<6>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, out_f16, st);
+        case 7: return get_rows_bits<7>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, out_f16, st);
+        case 8: return get_rows_bits<8>(lsc, suh, svh, k, ncols, cb, ids, count, out, out_stride, out_f16, st);
         default: return cudaErrorInvalidValue;
     }
 }

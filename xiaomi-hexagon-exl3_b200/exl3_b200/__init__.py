@@ -20,4 +20,9 @@ def __getattr__(name):
 
         mod = importlib.import_module(".ops", __name__)
         return mod if name == "ops" else mod.Exl3Weight
+    if name in ("model", "Exl3Model"):
+        import importlib
+
+        mod = importlib.import_module(".model", __name__)
+        return mod if name == "model" else mod.Exl3Model
     raise AttributeError(name)

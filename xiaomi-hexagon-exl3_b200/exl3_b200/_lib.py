@@ -15,6 +15,8 @@ GGML_LIB_PATH = PKG_DIR / "libexl3cu_ggml.so"
 OK, INVALID_ARGUMENT, NO_SUPPORT, OUT_OF_MEMORY, CUDA_ERROR = range(5)
 F32, F16 = 0, 1
 CB_3INST, CB_MCG, CB_MUL1 = 0, 1, 2
+ST_F16, ST_BF16, ST_I16, ST_F32, ST_I32 = range(5)
+MODEL_VALIDATE_ONLY = 1
 
 # every symbol include/exl3cu.h declares
 EXPORTS = (
@@ -25,6 +27,9 @@ EXPORTS = (
     "exl3cu_mul_mat_host", "exl3cu_mul_mat_noalloc", "exl3cu_mul_mat_batch",
     "exl3cu_device_status", "exl3cu_gemm_config", "exl3cu_pack_ragged", "exl3cu_mul_mat_ragged",
     "exl3cu_mul_mat_sequence", "exl3cu_get_rows", "exl3cu_get_rows_host",
+    "exl3cu_model_open", "exl3cu_model_free", "exl3cu_model_info", "exl3cu_model_matrix_count",
+    "exl3cu_model_matrix", "exl3cu_model_find_matrix", "exl3cu_model_head", "exl3cu_model_tensor",
+    "exl3cu_model_find_tensor", "exl3cu_model_embedding", "exl3cu_model_embed",
 )
 
 
@@ -32,6 +37,7 @@ class Exl3Error(RuntimeError):
     def __init__(self, status: int, message: str):
         super().__init__(f"exl3cu status {status}: {message}")
         self.status = status
+        self.message = message
 
 
 class Exl3InvalidArgument(Exl3Error, ValueError):
@@ -79,7 +85,23 @@ def _declare(L):
                                           _c.POINTER(_c.c_int), _c.c_int, _vp]
     L.exl3cu_mul_mat_batch.argtypes = [_sz, _c.POINTER(_vp), _c.POINTER(_vp), _c.POINTER(_c.c_int),
                                        _c.POINTER(_sz), _c.POINTER(_sz), _c.POINTER(_vp), _c.POINTER(_sz), _vp]
-    non_status = ("exl3cu_status_string", "exl3cu_last_error", "exl3cu_mul_mat_workspace_bytes")
+    _P = _c.POINTER
+    L.exl3cu_model_open.argtypes = [_c.c_char_p, _c.c_int, _c.c_uint, _P(_vp)]
+    L.exl3cu_model_free.argtypes = [_vp]
+    L.exl3cu_model_info.argtypes = [_vp, _P(_sz), _P(_sz), _P(_sz), _P(_sz), _P(_sz), _P(_c.c_double)]
+    L.exl3cu_model_matrix_count.restype = _sz
+    L.exl3cu_model_matrix_count.argtypes = [_vp]
+    L.exl3cu_model_matrix.argtypes = [_vp, _sz, _P(_c.c_char_p), _P(_sz), _P(_sz), _P(_c.c_uint), _P(_c.c_uint),
+                                      _P(_vp)]
+    L.exl3cu_model_find_matrix.argtypes = [_vp, _c.c_char_p, _P(_sz)]
+    L.exl3cu_model_head.argtypes = [_vp, _P(_sz)]
+    L.exl3cu_model_tensor.argtypes = [_vp, _sz, _P(_c.c_char_p), _P(_c.c_int), _P(_sz), _P(_P(_sz)), _P(_sz),
+                                      _P(_vp)]
+    L.exl3cu_model_find_tensor.argtypes = [_vp, _c.c_char_p, _P(_sz)]
+    L.exl3cu_model_embedding.argtypes = [_vp, _c.c_uint32, _vp]
+    L.exl3cu_model_embed.argtypes = [_vp, _vp, _sz, _vp, _sz, _vp]
+    non_status = ("exl3cu_status_string", "exl3cu_last_error", "exl3cu_mul_mat_workspace_bytes",
+                  "exl3cu_model_matrix_count")
     for name in EXPORTS:
         if name not in non_status:
             getattr(L, name).restype = _c.c_int

@@ -48,9 +48,10 @@ def _as_u16_tensor(a, device) -> torch.Tensor:
 class Exl3Weight:
     """An EXL3 matrix resident in device memory (column blocks [first_block, +block_count))."""
 
-    def __init__(self, handle: _vp, device: int):
+    def __init__(self, handle: _vp, device: int, owner=None):
         self._h = handle
         self.device = device
+        self._owner = owner  # an Exl3Model that owns the handle (kept alive by this reference)
         k, n_local, dev_bytes = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
         bits, cb = ctypes.c_uint(), ctypes.c_uint()
         check(lib().exl3cu_weight_info(self._h, ctypes.byref(k), ctypes.byref(n_local), ctypes.byref(bits),
@@ -94,7 +95,8 @@ class Exl3Weight:
 
     def free(self) -> None:
         if getattr(self, "_h", None):
-            lib().exl3cu_weight_free(self._h)
+            if getattr(self, "_owner", None) is None:
+                lib().exl3cu_weight_free(self._h)
             self._h = None
 
     def __del__(self):  # pragma: no cover - interpreter shutdown order
