@@ -64,10 +64,11 @@ def parse_args(argv=None):
     ap.add_argument("--no-sweep", action="store_true", help="skip the 2/3/5/6-bit side measurements")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--e2e-steps", type=int, default=30)
-    ap.add_argument("--config", choices=("sweep", "large", "ragged"), default="sweep",
+    ap.add_argument("--config", choices=("sweep", "large", "ragged", "model"), default="sweep",
                     help="sweep: configs[1] decode GEMV sweep (default); large: configs[4] column-split matrix; "
                          "ragged: configs[2] packed continuous-admission batches on the tensor-core GEMM")
     ap.add_argument("--no-ragged", action="store_true", help="skip the configs[2] summary in the default run")
+    ap.add_argument("--no-model", action="store_true", help="skip the configs[3] hybrid decoder summary")
     return ap.parse_args(argv)
 
 
@@ -314,6 +315,152 @@ def per_shape_us(torch, stack, reps=4):
         t.synchronize()
         out[name] = round(s.elapsed_time(t) * 1e3 / (reps * len(ms)), 2)
     return out
+
+
+# ---------------------------------------------------------------------------------------------
+# the synthetic 2B hybrid decoder (exl3_b200.hybrid)
+
+def run_model_measure(torch, dist, local, rank, world, new_tokens=256, single_prompt=512, seed=2024):
+    import numpy as np
+
+    """Decode tokens/s of the 28-layer hybrid decoder on this GPU (DP replica per rank).
+
+    single: one request, 512-token prompt prefilled, then `new_tokens` greedy steps replayed from one
+            captured step with device-side token feedback (CUDA events around the replays);
+    single_e2e: the same request served step by step through the engine API: pinned H2D of the step
+            metadata, the captured step, D2H of the next token, host loop (events around the loop);
+    ragged8: 8 requests, prompts U[32,1024] seeded, `new_tokens` greedy tokens each, continuous
+            admission (decode rows of running requests + 512-row prefill chunks of the next one per
+            step), host scheduler in the loop; tokens/s = generated tokens / elapsed."""
+    from exl3_b200.hybrid import DecodeGraph, HybridConfig, HybridEngine, Request, run_requests, _StepGraph
+
+    dev = f"cuda:{local}"
+    cfg = HybridConfig()
+    w = synthetic_weights_cached(cfg, seed + rank)
+    eng = HybridEngine(w, device=local, slots=8, max_len=1536, max_rows=512)
+    del w
+    rng = np.random.Generator(np.random.PCG64(seed + 17 * rank))
+    stream = torch.cuda.Stream(device=dev)
+    # -- single request ---------------------------------------------------------------------------
+    prompt = rng.integers(0, cfg.vocab, single_prompt).astype(np.int32)
+    eng.reset_slot(0)
+    n = len(prompt)
+    eng.meta.fill(prompt, np.zeros(n), np.arange(n), [0, n], [0], [n - 1])
+    with torch.cuda.stream(stream):
+        eng.meta.upload(stream)
+        eng.forward(n, 1, 1, stream)
+    stream.synchronize()
+    tok = int(eng.out_tokens[0].item())
+    eng.meta.fill([tok], [0], [n], [0, 1], [0], [0])
+    with torch.cuda.stream(stream):
+        eng.meta.upload(stream)
+    stream.synchronize()
+    dg = DecodeGraph(eng, 1, new_tokens + 8, stream)  # its eager warm-up and capture advance nothing
+    for _ in range(3):
+        dg.replay()
+    stream.synchronize()
+    dg.reset()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(new_tokens):
+            dg.replay()
+    e_ev.record(stream)
+    e_ev.synchronize()
+    single_ms = s_ev.elapsed_time(e_ev)
+    # -- single request, host in the loop ---------------------------------------------------------
+    eng.reset_slot(1)
+    eng.meta.fill(prompt, np.zeros(n), np.arange(n), [0, n], [1], [n - 1])
+    with torch.cuda.stream(stream):
+        eng.meta.upload(stream)
+        eng.forward(n, 1, 1, stream)
+    stream.synchronize()
+    tok = int(eng.out_tokens[0].item())
+    eng.meta.fill([tok], [0], [n], [0, 1], [1], [0])
+    with torch.cuda.stream(stream):
+        eng.meta.upload(stream)
+        eng.forward(1, 1, 1, stream)  # eager step at this shape before capture
+    stream.synchronize()
+    sg = _StepGraph(eng, 1, stream)
+    pos = n + 1
+    tok = int(eng.out_tokens[0].item())
+    e2e_steps = min(new_tokens, 128)
+    out_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    s_ev.record(stream)
+    for _ in range(e2e_steps):
+        eng.meta.fill([tok], [0], [pos], [0, 1], [1], [0])
+        with torch.cuda.stream(stream):
+            eng.meta.upload(stream)
+            sg.replay()
+            out_host.copy_(eng.out_tokens[:1], non_blocking=True)
+        stream.synchronize()
+        tok = int(out_host[0])
+        pos += 1
+    e_ev.record(stream)
+    e_ev.synchronize()
+    e2e_ms = s_ev.elapsed_time(e_ev)
+    del dg, sg
+    # -- 8 ragged requests ------------------------------------------------------------------------
+    lens = rng.integers(32, 1025, 8)
+    reqs = [Request(rng.integers(0, cfg.vocab, int(L)).astype(np.int32), max_new=new_tokens) for L in lens]
+    graphs = {}
+    warm = [Request(rng.integers(0, cfg.vocab, 40).astype(np.int32), max_new=3) for _ in range(8)]
+    run_requests(eng, warm, chunk=512, stream=stream, graphs=graphs)  # first-time shapes and captures
+    torch.cuda.synchronize(dev)
+    s_ev.record(stream)
+    steps, rows = run_requests(eng, reqs, chunk=512, stream=stream, graphs=graphs)
+    e_ev.record(stream)
+    e_ev.synchronize()
+    ragged_ms = s_ev.elapsed_time(e_ev)
+    generated = sum(len(r.generated) for r in reqs)
+
+    def over_ranks(v, op):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    single_ms = over_ranks(single_ms, dist.ReduceOp.MAX) if world > 1 else single_ms
+    e2e_ms = over_ranks(e2e_ms, dist.ReduceOp.MAX) if world > 1 else e2e_ms
+    ragged_ms_max = over_ranks(ragged_ms, dist.ReduceOp.MAX) if world > 1 else ragged_ms
+    gen_total = over_ranks(float(generated), dist.ReduceOp.SUM) if world > 1 else float(generated)
+    from exl3_b200 import ops
+
+    status = ops.device_status(local)
+    eng.free()
+    del eng
+    torch.cuda.empty_cache()
+    if status:
+        raise RuntimeError(f"device status {status:#x} after the hybrid decoder run")
+    return {
+        "model": "synthetic 2B hybrid: 28 layers (21 gated delta rule + 7 GQA 16q/4kv), hidden 2048, FFN 6144, "
+                 "vocab 151936 fp16 tied embed/head, EXL3 4 bpw linear layers (random trellis)",
+        "single_tok_s": round(world * new_tokens / (single_ms * 1e-3), 1),
+        "single_ms_per_token": round(single_ms / new_tokens, 4),
+        "single_timing": "one captured decode step replayed with device-side token feedback; CUDA events",
+        "single_e2e_tok_s": round(world * e2e_steps / (e2e_ms * 1e-3), 1),
+        "single_e2e_api": "per token: pinned H2D of the step metadata (92 B), captured step, D2H of the token",
+        "ragged8_tok_s": round(gen_total / (ragged_ms_max * 1e-3), 1),
+        "ragged8": {"requests_per_gpu": 8, "prompt_tokens": [int(x) for x in lens], "new_tokens": new_tokens,
+                    "steps": steps, "rows": rows, "ms": round(ragged_ms_max, 1),
+                    "timing": "host scheduler loop with H2D metadata / D2H tokens per step; CUDA events"},
+        "parallelism": f"dp{world} replicas (weights replicated, requests per GPU)",
+        "prompt_tokens_single": single_prompt,
+    }
+
+
+_WEIGHTS_CACHE = {}
+
+
+def synthetic_weights_cached(cfg, seed):
+    from exl3_b200.hybrid import synthetic_weights
+
+    key = (seed, cfg.layers, cfg.vocab)
+    if key not in _WEIGHTS_CACHE:
+        _WEIGHTS_CACHE.clear()
+        _WEIGHTS_CACHE[key] = synthetic_weights(cfg, seed)
+    return _WEIGHTS_CACHE[key]
 
 
 # ---------------------------------------------------------------------------------------------
@@ -654,6 +801,20 @@ def main(argv=None):
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device(f"cuda:{local}"))
+    if args.config == "model":
+        with ClockSampler(local) as clk:
+            m = run_model_measure(torch, dist, local, rank, world)
+        if rank == 0:
+            print(json.dumps({
+                "metric": "2B hybrid decode tok/s (configs[3])", "value": m["ragged8_tok_s"], "unit": "tok/s",
+                "n_gpus": world, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+                "data": "synthetic", "config": {"workload": "configs[3]: 8 ragged requests per GPU, 256 greedy steps",
+                                                "parallelism": f"dp{world}"},
+                "clocks": clk.summary(), "detail": m}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
     if args.config in ("large", "ragged"):
         run = run_large if args.config == "large" else run_ragged
         rc = run(args, torch, dist, ops, rank, world, local)
@@ -714,6 +875,9 @@ def main(argv=None):
     ragged = None
     if not args.no_ragged:
         ragged = run_ragged_measure(torch, ops, local, args.layers, 3, seed=77 + rank)
+    model = None
+    if not args.no_model:
+        model = run_model_measure(torch, dist, local, rank, world)
 
     traffic = None
     tf = ROOT / "profiles" / "gemv_traffic.json"
@@ -766,6 +930,7 @@ def main(argv=None):
             "per_shape_kernel_us": shape_us,
             "sweep_gbs_by_bits": sweep,
             "ragged_configs2": ragged,
+            "decode_configs3": model,
         }
         print(json.dumps(line), flush=True)
     for layer in stack:

@@ -25,7 +25,8 @@ GGML_LIB = PKG / "libexl3cu_ggml.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_SOURCES = ["exl3cu_api.cu", "exl3cu_kernels.cu", "exl3cu_gemv.cu", "exl3cu_gemv_cluster.cu", "exl3cu_gemv_mul1.cu",
-                "exl3cu_gemm_tc.cu", "exl3cu_gemv_persist.cu", "exl3cu_model.cu"]
+                "exl3cu_gemm_tc.cu", "exl3cu_gemv_persist.cu", "exl3cu_model.cu",
+                "exl3cu_hybrid.cu"]
 CXX_SOURCES = ["exl3_codec_host.cpp"]
 HEADERS = ["exl3cu_internal.h", "exl3cu_decode.cuh", "exl3cu_common.cuh", "exl3cu_async.cuh", "exl3cu_mul1.cuh",
            "exl3cu_json.h"]
@@ -56,7 +57,8 @@ def build(verbose_ptxas: bool = False, force: bool = False, quiet: bool = True) 
     BUILD.mkdir(exist_ok=True)
     cc = nvcc()
     common = ["-std=c++17", "-O3", "-Xcompiler", "-fPIC,-O3", f"-I{INCLUDE}", f"-I{CSRC}"]
-    hdrs = [CSRC / h for h in HEADERS] + [INCLUDE / "exl3cu.h", INCLUDE / "exl3_codec.h", INCLUDE / "exl3_model.h"]
+    hdrs = [CSRC / h for h in HEADERS] + [INCLUDE / "exl3cu.h", INCLUDE / "exl3_codec.h", INCLUDE / "exl3_model.h",
+                                                 INCLUDE / "exl3cu_hybrid.h"]
     jobs = []
     for src in CUDA_SOURCES:
         obj = BUILD / (src + ".o")

@@ -58,10 +58,10 @@ struct Mul1Layout {
 // partial; slot: the other cluster ranks' partials (written remotely, read by
 // rank 0); gmax: max |xh| per (row, own group); then the mbarriers and per-row
 // scale / digit sum.
-__host__ __device__ inline Mul1Layout mul1_layout(int bits, int cps, int rows, int splits) {
+__host__ __device__ inline Mul1Layout mul1_layout(int bits, int cps, int rows, int splits, int stages) {
     Mul1Layout L;
     const int ng = (cps + 7) / 8 + 1;
-    const size_t ring = size_t(kMStages) * kMW * 256 * bits;
+    const size_t ring = size_t(stages) * kMW * 256 * bits;
     const size_t xq = size_t(cps) * 128 * rows;
     const size_t acc = size_t(rows) * 128 * 2 * 4;
     const size_t part = size_t(rows) * 128 * 4;
@@ -74,7 +74,7 @@ __host__ __device__ inline Mul1Layout mul1_layout(int bits, int cps, int rows, i
     L.slot_off = int(L.part_off + part);
     L.gmax_off = int(L.slot_off + slot);
     L.bar_off = int((L.gmax_off + gmax + 15) & ~size_t(15));
-    L.bytes = L.bar_off + 2 * kMStages * 8 + 2 * 4 * kMRows;
+    L.bytes = L.bar_off + 2 * stages * 8 + 2 * 4 * kMRows;
     return L;
 }
 
@@ -102,7 +102,8 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    const Mul1Layout L = mul1_layout(BITS, P.cps, rows, S);
+    const int NS = b.stages;
+    const Mul1Layout L = mul1_layout(BITS, P.cps, rows, S, NS);
     unsigned char * ring = smem + L.ring_off;
     unsigned char * xq = smem + L.xq_off;
     int * acc = reinterpret_cast<int *>(smem + L.acc_off);          // [rows][128][2]
@@ -110,13 +111,13 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
     float * slots = reinterpret_cast<float *>(smem + L.slot_off);   // [S-1][rows][128]
     float * gmax = reinterpret_cast<float *>(smem + L.gmax_off);    // [rows][ng]
     uint64_t * full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
-    uint64_t * empty = full + kMStages;
-    float * scale_s = reinterpret_cast<float *>(empty + kMStages);
+    uint64_t * empty = full + NS;
+    float * scale_s = reinterpret_cast<float *>(empty + NS);
     int * xsum_s = reinterpret_cast<int *>(scale_s + kMRows);
     const int nacc = rows * 256;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kMStages; ++s) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kMW);
         }
@@ -134,9 +135,8 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
         if (lane == 0 && nch > 0) {
             const unsigned char * src = reinterpret_cast<const unsigned char *>(P.lsc) +
                                         (size_t(nb) * P.nchunks + c0) * CHUNKB;
-            for (int j = 0; j < nstage; ++j) {
-                const int s = j % kMStages;
-                if (j >= kMStages && !mbar_wait(&empty[s], ((j / kMStages) - 1) & 1)) {
+            for (int j = 0, s = 0, round = 0; j < nstage; ++j) {
+                if (j >= NS && !mbar_wait(&empty[s], (round - 1) & 1)) {
                     atomicOr(&g_mul1_status, kStatusWaitTimeout);
                     break;
                 }
@@ -144,6 +144,10 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
                 mbar_arrive_expect_tx(&full[s], uint32_t(nc * CHUNKB));
                 bulk_g2s(ring + size_t(s) * kMW * CHUNKB, src + size_t(j) * kMW * CHUNKB, uint32_t(nc * CHUNKB),
                          &full[s]);
+                if (++s == NS) {
+                    s = 0;
+                    ++round;
+                }
             }
         }
         __syncwarp();
@@ -248,13 +252,12 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
         int D[8][4];
 #pragma unroll
         for (int c = 0; c < 8; ++c) D[c][0] = D[c][1] = D[c][2] = D[c][3] = 0;
-        for (int j = 0; j < nstage; ++j) {
+        for (int j = 0, s = 0, round = 0; j < nstage; ++j) {
             const int cl = warp + j * kMW;
             if (cl >= nch) break;
-            const int s = j % kMStages;
             uint4 bq = make_uint4(0, 0, 0, 0);
             if (b_live) bq = *reinterpret_cast<const uint4 *>(xq + size_t(cl) * 128 * rows + lane * 16);
-            if (!mbar_wait(&full[s], (j / kMStages) & 1)) {
+            if (!mbar_wait(&full[s], round & 1)) {
                 atomicOr(&g_mul1_status, kStatusWaitTimeout);
                 break;
             }
@@ -289,6 +292,10 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             for (int c = 0; c < 8; ++c) imma_u8s8(D[c], pr[c][0], pr[c][4], pr[c][1], pr[c][5], bq.x, bq.y);
 #pragma unroll
             for (int c = 0; c < 8; ++c) imma_u8s8(D[c], pr[c][2], pr[c][6], pr[c][3], pr[c][7], bq.z, bq.w);
+            if (++s == NS) {
+                s = 0;
+                ++round;
+            }
         }
         // (4) the warps' integer sums meet in shared memory (exact, any order) ...
         const int g = lane >> 2, t = lane & 3;
@@ -413,6 +420,16 @@ int mul1_active_clusters(int device, unsigned bits, int cs, size_t smem) {
 
 }  // namespace
 
+// Weight ring depth in stages of kMW chunks: EXL3CU_MUL1_STAGES (tuning
+// experiments), else kMStages.
+int mul1_stages(unsigned bits) {
+    const char * env = std::getenv("EXL3CU_MUL1_STAGES");
+    int ns = env ? std::atoi(env) : 0;
+    if (ns <= 0) ns = kMStages;
+    (void)bits;
+    return std::min(ns, kMStagesMax);
+}
+
 bool mul1_supported(unsigned bits, int rows) { return bits >= 2 && bits <= 8 && rows >= 1 && rows <= kMRows; }
 
 // Picks the cluster size (K split) so the grid fills the device in one wave:
@@ -428,6 +445,7 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
         max_rows = std::max(max_rows, b.prob[i].rows);
     }
     const char * env = std::getenv("EXL3CU_CLUSTER_SPLITS");  // tuning experiments only
+    const int NS = mul1_stages(bits);
     int S = 0;
     if (env && std::atoi(env) > 0) {
         S = std::min(16, std::atoi(env));
@@ -437,7 +455,7 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
         for (int cand = 16; cand >= 1; --cand) {
             if (cand > 1 && min_nchunks / cand < kMW) continue;
             const int cps = (max_nchunks + cand - 1) / cand;
-            const Mul1Layout L = mul1_layout(int(bits), cps, max_rows, cand);
+            const Mul1Layout L = mul1_layout(int(bits), cps, max_rows, cand, NS);
             if (L.bytes > kMul1MaxSmem) break;  // fewer splits only grow the per-CTA range
             const int fit = mul1_active_clusters(device, bits, cand, L.bytes);
             if (fit <= 0) continue;
@@ -457,8 +475,9 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
         b.prob[i].cps = (b.prob[i].nchunks + S - 1) / S;
         max_cps = std::max(max_cps, b.prob[i].cps);
     }
-    const Mul1Layout L = mul1_layout(int(bits), max_cps, max_rows, S);
+    const Mul1Layout L = mul1_layout(int(bits), max_cps, max_rows, S, NS);
     if (L.bytes > kMul1MaxSmem) return cudaErrorInvalidConfiguration;
+    b.stages = NS;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(nunits * S), 1, 1);
     cfg.blockDim = dim3(kMThreads, 1, 1);

@@ -53,6 +53,7 @@ struct GemvBatch {
     GemvProblem prob[kMaxBatch];
     int count;
     int splits;     // cluster size: CTAs per unit along K
+    int stages;     // mul1 kernel: weight ring depth (stages of kMW chunks)
 };
 
 int choose_cluster_splits(int sms, int nunits, int min_nchunks);

@@ -9,6 +9,7 @@ namespace exl3cu {
 constexpr int kMW = 8;                      // consumer warps
 constexpr int kMThreads = (kMW + 1) * 32;   // + one producer warp
 constexpr int kMStages = 4;
+constexpr int kMStagesMax = 16;
 constexpr int kMRows = 4;                   // rows per launch: 2 digits each fill N = 8
 constexpr float kCodeA = 1774.0f / 262144.0f;
 constexpr float kCodeC = -3.453125f;

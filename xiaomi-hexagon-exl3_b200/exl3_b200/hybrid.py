@@ -1,0 +1,493 @@
+"""Hybrid decoder on the EXL3 operator: a Qwen3.5-style 3:1 gated-delta-rule /
+full-attention stack whose linear layers are packed EXL3 weights.
+
+What runs on the GPU, per scheduler step of R packed rows (ragged: decode
+tokens and prefill chunks of several sequences together):
+
+    h = embed(tokens)                                     exl3cu_hyb_embed
+    per layer:
+        xn = rmsnorm(h += previous delta)                 exl3cu_hyb_rmsnorm
+        full attention:  [q|k|v] = xn . W_{q,k,v}         exl3cu_mul_mat_batch (EXL3)
+                         q/k norm, RoPE, KV append        exl3cu_hyb_attn_prep
+                         a = attn(q, K, V)                exl3cu_hyb_attn
+        delta rule:      [q|k|v|z] = xn . W_{q,k,v,z}     exl3cu_mul_mat_batch (EXL3)
+                         a = gdn(...)                     exl3cu_hyb_gdn (conv, gates, state update, gated norm)
+        o = a . W_o                                       exl3cu_mul_mat (EXL3)
+        xn = rmsnorm(h += o)
+        [g|u] = xn . W_{gate,up}; d = swiglu . W_down     exl3cu_mul_mat_batch, exl3cu_hyb_swiglu, exl3cu_mul_mat
+    xn = rmsnorm(h += d); token = argmax(xn . E^T)        exl3cu_hyb_head (tied fp16 embedding)
+
+The model is synthetic (no checkpoints offline): random-init parameters with
+the stated shapes; each linear layer is an EXL3 matrix with a seeded random
+trellis bitstream, +-1 input signs and U(0.01, 0.03) output scales (the same
+recipe as the operator benchmarks), i.e. random weights in EXL3 form.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from ._lib import check, lib
+
+
+@dataclass
+class HybridConfig:
+    layers: int = 28
+    hidden: int = 2048
+    ffn: int = 6144
+    vocab: int = 151936
+    heads: int = 16          # q heads and delta-rule heads, dim 128
+    kv_heads: int = 4
+    head_dim: int = 128
+    full_every: int = 4      # layer i is full attention when i % full_every == full_every - 1 (3:1)
+    rope_theta: float = 10_000_000.0
+    eps: float = 1e-6
+    bits: int = 4
+
+    def is_full(self, i: int) -> bool:
+        return i % self.full_every == self.full_every - 1
+
+    @property
+    def inv_freq(self) -> np.ndarray:
+        i = np.arange(self.head_dim // 2, dtype=np.float64)
+        return (1.0 / self.rope_theta ** (2.0 * i / self.head_dim)).astype(np.float32)
+
+    def matrix_shapes(self, i: int) -> dict:
+        H, F, D = self.hidden, self.ffn, self.heads * self.head_dim
+        KV = self.kv_heads * self.head_dim
+        if self.is_full(i):
+            mats = {"q": (H, D), "k": (H, KV), "v": (H, KV), "o": (D, H)}
+        else:
+            mats = {"q": (H, D), "k": (H, D), "v": (H, D), "z": (H, D), "o": (D, H)}
+        mats.update({"gate": (H, F), "up": (H, F), "down": (F, H)})
+        return mats
+
+
+@dataclass
+class EXL3Matrix:
+    k: int
+    n: int
+    bits: int
+    trellis: np.ndarray  # uint16 [k/16, n/16, 16*bits]
+    suh: np.ndarray      # fp16 bits [k]
+    svh: np.ndarray      # fp16 bits [n]
+
+
+@dataclass
+class LayerWeights:
+    kind: str                      # "full" or "gdn"
+    mats: dict
+    in_norm: np.ndarray            # f32 [H]
+    post_norm: np.ndarray          # f32 [H]
+    extra: dict = field(default_factory=dict)
+
+
+@dataclass
+class HybridWeights:
+    cfg: HybridConfig
+    embed: np.ndarray              # fp16 [V, H] (tied head)
+    final_norm: np.ndarray         # f32 [H]
+    layers: list
+
+
+def _exl3(rng, k, n, bits) -> EXL3Matrix:
+    trellis = rng.integers(0, 65536, size=(k // 16, n // 16, 16 * bits), dtype=np.uint16)
+    suh = rng.choice(np.array([-1.0, 1.0], np.float32), size=k).astype(np.float16).view(np.uint16)
+    sign = rng.choice(np.array([-1.0, 1.0], np.float32), size=n)
+    svh = (sign * rng.uniform(0.01, 0.03, size=n)).astype(np.float16).view(np.uint16)
+    return EXL3Matrix(k, n, bits, trellis, suh, svh)
+
+
+def synthetic_weights(cfg: HybridConfig, seed: int = 1234) -> HybridWeights:
+    """Seeded random-init parameters (numpy PCG64), EXL3 matrices as random trellis streams."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    H = cfg.hidden
+    emb = np.empty((cfg.vocab, H), np.float16)
+    for r0 in range(0, cfg.vocab, 8192):  # bounded temporaries
+        r1 = min(cfg.vocab, r0 + 8192)
+        emb[r0:r1] = (rng.standard_normal((r1 - r0, H), dtype=np.float32) * 0.05).astype(np.float16)
+    layers = []
+    for i in range(cfg.layers):
+        mats = {name: _exl3(rng, k, n, cfg.bits) for name, (k, n) in cfg.matrix_shapes(i).items()}
+        in_norm = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        post_norm = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        if cfg.is_full(i):
+            extra = {"q_norm": (1.0 + 0.1 * rng.standard_normal(cfg.head_dim)).astype(np.float32),
+                     "k_norm": (1.0 + 0.1 * rng.standard_normal(cfg.head_dim)).astype(np.float32)}
+            layers.append(LayerWeights("full", mats, in_norm, post_norm, extra))
+        else:
+            nh, D = cfg.heads, cfg.heads * cfg.head_dim
+            extra = {"wab": (rng.standard_normal((2 * nh, H), dtype=np.float32) * 0.02).astype(np.float16),
+                     "conv_w": (rng.standard_normal((3 * D, 4), dtype=np.float32) * 0.5).astype(np.float32),
+                     "A_log": rng.uniform(-1.0, 1.0, nh).astype(np.float32),
+                     "dt_bias": (0.5 * rng.standard_normal(nh)).astype(np.float32),
+                     "gnorm": (1.0 + 0.1 * rng.standard_normal(cfg.head_dim)).astype(np.float32)}
+            layers.append(LayerWeights("gdn", mats, in_norm, post_norm, extra))
+    final_norm = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    return HybridWeights(cfg, emb, final_norm, layers)
+
+
+# ---------------------------------------------------------------------------------------------
+
+def _vp(t) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _declare(L):
+    if getattr(L, "_hyb_declared", False):
+        return
+    I, F, S, P = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
+    L.exl3cu_hyb_embed.argtypes = [P, I, P, I, I, P, P]
+    L.exl3cu_hyb_rmsnorm.argtypes = [P, P, I, P, F, I, I, P, P]
+    L.exl3cu_hyb_swiglu.argtypes = [P, I, I, P, P]
+    L.exl3cu_hyb_attn_prep.argtypes = [P, I, P, P, P, P, P, P, F, P, P, I, I, P, P]
+    L.exl3cu_hyb_attn.argtypes = [P, I, P, P, P, P, P, I, I, F, P, P]
+    L.exl3cu_hyb_gdn_smem_bytes.restype = S
+    L.exl3cu_hyb_gdn.argtypes = [P, P, P, I, P, P, P, P, P, F, P, P, P, I, I, P, P]
+    L.exl3cu_hyb_head.argtypes = [P, P, I, I, P, I, P, P, P, P]
+    for n in ("exl3cu_hyb_embed", "exl3cu_hyb_rmsnorm", "exl3cu_hyb_swiglu", "exl3cu_hyb_attn_prep",
+              "exl3cu_hyb_attn", "exl3cu_hyb_gdn", "exl3cu_hyb_head"):
+        getattr(L, n).restype = ctypes.c_int
+    L._hyb_declared = True
+
+
+class StepMeta:
+    """Device int32 row metadata of one step, filled from one pinned host buffer by one copy:
+    [tokens R | row_seq R | row_pos R | row_offsets n_seq+1 | seq_slot n_seq | logit_rows nout]."""
+
+    def __init__(self, torch, device, max_rows: int, max_seq: int, max_out: int):
+        self.cap = (max_rows, max_seq, max_out)
+        n = 3 * max_rows + 2 * max_seq + 1 + max_out
+        self.host = torch.zeros(n, dtype=torch.int32, pin_memory=True)
+        self.dev = torch.zeros(n, dtype=torch.int32, device=device)
+        R, Q, O = max_rows, max_seq, max_out
+        self.off = {"tokens": 0, "row_seq": R, "row_pos": 2 * R, "row_offsets": 3 * R, "seq_slot": 3 * R + Q + 1,
+                    "logit_rows": 3 * R + 2 * Q + 1}
+        self.len = {"tokens": R, "row_seq": R, "row_pos": R, "row_offsets": Q + 1, "seq_slot": Q, "logit_rows": O}
+
+    def view(self, name):
+        o = self.off[name]
+        return self.dev[o:o + self.len[name]]
+
+    def fill(self, tokens, row_seq, row_pos, row_offsets, seq_slot, logit_rows):
+        h = self.host.numpy()
+        for name, arr in (("tokens", tokens), ("row_seq", row_seq), ("row_pos", row_pos),
+                          ("row_offsets", row_offsets), ("seq_slot", seq_slot), ("logit_rows", logit_rows)):
+            a = np.asarray(arr, np.int32)
+            if a.size > self.len[name]:
+                raise ValueError(f"{name}: {a.size} entries, capacity {self.len[name]}")
+            h[self.off[name]:self.off[name] + a.size] = a
+
+    def upload(self, stream):
+        self.dev.copy_(self.host, non_blocking=True)
+
+
+class HybridEngine:
+    """The hybrid decoder resident on one GPU: EXL3 weights, fp16 embedding/head, fp16 KV caches and
+    fp32 delta-rule states for `slots` concurrent sequences of up to `max_len` positions."""
+
+    def __init__(self, weights: HybridWeights, device: int = 0, slots: int = 8, max_len: int = 1536,
+                 max_rows: int = 512):
+        import torch
+
+        from .ops import Exl3Weight
+
+        self.torch = torch
+        self.cfg = cfg = weights.cfg
+        self.device = device
+        dev = f"cuda:{device}"
+        self.dev = dev
+        self.slots, self.max_len, self.max_rows = slots, max_len, max_rows
+        L = lib()
+        _declare(L)
+        self.L = L
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+        self.embed = t(weights.embed)
+        self.final_norm = t(weights.final_norm)
+        self.inv_freq = t(cfg.inv_freq)
+        self.layers = []
+        for lw in weights.layers:
+            mats = {name: Exl3Weight.from_trellis(m.trellis, m.suh, m.svh, device=device)
+                    for name, m in lw.mats.items()}
+            d = {"kind": lw.kind, "mats": mats, "in_norm": t(lw.in_norm), "post_norm": t(lw.post_norm)}
+            d.update({k: t(v) for k, v in lw.extra.items()})
+            self.layers.append(d)
+        H, F, D = cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim
+        KV = cfg.kv_heads * cfg.head_dim
+        R = max_rows
+        f32, f16 = torch.float32, torch.float16
+        self.h = torch.zeros((R, H), dtype=f32, device=dev)
+        self.xn = torch.zeros((R, H), dtype=f16, device=dev)
+        self.proj = torch.zeros((R, 4 * D), dtype=f32, device=dev)      # [q|k|v|z] or [q|k|v]
+        self.q = torch.zeros((R, D), dtype=f32, device=dev)
+        self.mix = torch.zeros((R, D), dtype=f16, device=dev)           # attention / delta-rule output
+        self.o = torch.zeros((R, H), dtype=f32, device=dev)
+        self.gu = torch.zeros((R, 2 * F), dtype=f32, device=dev)
+        self.act = torch.zeros((R, F), dtype=f16, device=dev)
+        self.down = torch.zeros((R, H), dtype=f32, device=dev)
+        n_full = sum(1 for d in self.layers if d["kind"] == "full")
+        n_gdn = len(self.layers) - n_full
+        self.kc = torch.zeros((max(n_full, 1), slots, cfg.kv_heads, max_len, cfg.head_dim), dtype=f16, device=dev)
+        self.vc = torch.zeros_like(self.kc)
+        self.state = torch.zeros((max(n_gdn, 1), slots, cfg.heads, cfg.head_dim, cfg.head_dim), dtype=f32,
+                                 device=dev)
+        self.conv = torch.zeros((max(n_gdn, 1), slots, 3 * D, 3), dtype=f32, device=dev)
+        fi = gi = 0
+        for d in self.layers:
+            if d["kind"] == "full":
+                d["cache"] = fi
+                fi += 1
+            else:
+                d["cache"] = gi
+                gi += 1
+        self.meta = StepMeta(torch, dev, R, slots, 8)
+        self.best = torch.zeros(8, dtype=torch.int64, device=dev)
+        self.out_tokens = torch.zeros(8, dtype=torch.int32, device=dev)
+        self.KV = KV
+        self._batch_args = {}
+
+    # -- slot management --------------------------------------------------------------------------
+    def reset_slot(self, slot: int):
+        self.state[:, slot].zero_()
+        self.conv[:, slot].zero_()
+
+    # -- one step ---------------------------------------------------------------------------------
+    def _mm_batch(self, names, mats, x, out_cols, rows, st):
+        """Projections sharing input x into column ranges of self.proj / self.gu."""
+        key = (tuple(names), id(mats), out_cols[0].data_ptr(), rows)
+        args = self._batch_args.get(key)
+        if args is None:
+            n = len(names)
+            VP, SZ, IN = ctypes.c_void_p * n, ctypes.c_size_t * n, ctypes.c_int * n
+            args = (n, VP(*[mats[nm].handle.value for nm in names]), VP(*[x.data_ptr()] * n), IN(*[1] * n),
+                    SZ(*[rows] * n), SZ(*[x.stride(0)] * n), VP(*[o.data_ptr() for o in out_cols]),
+                    SZ(*[o.stride(0) for o in out_cols]))
+            self._batch_args[key] = args
+        check(self.L.exl3cu_mul_mat_batch(*args, st))
+
+    def _mm(self, w, x, out, rows, st):
+        check(self.L.exl3cu_mul_mat(w.handle, _vp(x), 1, rows, x.stride(0), _vp(out), out.stride(0), st))
+
+    def forward(self, rows: int, n_seq: int, nout: int, stream=None):
+        """Run the step whose metadata is in self.meta.dev; next tokens land in self.out_tokens[:nout]."""
+        torch, cfg, L = self.torch, self.cfg, self.L
+        st = ctypes.c_void_p((stream or torch.cuda.current_stream()).cuda_stream)
+        H, F, D, KV = cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim, self.KV
+        m = self.meta
+        tokens, row_seq, row_pos = m.view("tokens"), m.view("row_seq"), m.view("row_pos")
+        row_offsets, seq_slot, logit_rows = m.view("row_offsets"), m.view("seq_slot"), m.view("logit_rows")
+        check(L.exl3cu_hyb_embed(_vp(self.embed), cfg.vocab, _vp(tokens), rows, H, _vp(self.h), st))
+        delta = None
+        scale = 1.0 / float(np.sqrt(cfg.head_dim))
+        for d in self.layers:
+            mats = d["mats"]
+            check(L.exl3cu_hyb_rmsnorm(_vp(self.h), _vp(delta) if delta is not None else None, H, _vp(d["in_norm"]),
+                                       cfg.eps, rows, H, _vp(self.xn), st))
+            if d["kind"] == "full":
+                p = self.proj
+                # the prep kernel reads [q|k|v] rows packed (D + 2 KV wide): a packed view of self.proj
+                qkv = p.view(-1)[: self.max_rows * (D + 2 * KV)].view(self.max_rows, D + 2 * KV)
+                outs = [qkv[:, 0:D], qkv[:, D:D + KV], qkv[:, D + KV:D + 2 * KV]]
+                self._mm_batch(("q", "k", "v"), mats, self.xn, outs, rows, st)
+                c = d["cache"]
+                kc, vc = self.kc[c], self.vc[c]
+                check(L.exl3cu_hyb_attn_prep(_vp(qkv), rows, _vp(row_seq), _vp(row_pos), _vp(seq_slot),
+                                             _vp(d["q_norm"]), _vp(d["k_norm"]), _vp(self.inv_freq), cfg.eps,
+                                             _vp(kc), _vp(vc), self.max_len, self.slots, _vp(self.q), st))
+                check(L.exl3cu_hyb_attn(_vp(self.q), rows, _vp(row_seq), _vp(row_pos), _vp(seq_slot), _vp(kc),
+                                        _vp(vc), self.max_len, self.slots, scale, _vp(self.mix), st))
+            else:
+                p = self.proj
+                outs = [p[:, 0:D], p[:, D:2 * D], p[:, 2 * D:3 * D], p[:, 3 * D:4 * D]]
+                self._mm_batch(("q", "k", "v", "z"), mats, self.xn, outs, rows, st)
+                c = d["cache"]
+                check(L.exl3cu_hyb_gdn(_vp(p), _vp(self.xn), _vp(d["wab"]), H, _vp(d["conv_w"]), _vp(self.conv[c]),
+                                       _vp(d["A_log"]), _vp(d["dt_bias"]), _vp(d["gnorm"]), cfg.eps,
+                                       _vp(self.state[c]), _vp(row_offsets), _vp(seq_slot), n_seq, self.slots,
+                                       _vp(self.mix), st))
+            self._mm(mats["o"], self.mix, self.o, rows, st)
+            check(L.exl3cu_hyb_rmsnorm(_vp(self.h), _vp(self.o), H, _vp(d["post_norm"]), cfg.eps, rows, H,
+                                       _vp(self.xn), st))
+            self._mm_batch(("gate", "up"), mats, self.xn, [self.gu[:, 0:F], self.gu[:, F:2 * F]], rows, st)
+            check(L.exl3cu_hyb_swiglu(_vp(self.gu), rows, F, _vp(self.act), st))
+            self._mm(mats["down"], self.act, self.down, rows, st)
+            delta = self.down
+        check(L.exl3cu_hyb_rmsnorm(_vp(self.h), _vp(delta), H, _vp(self.final_norm), cfg.eps, rows, H, _vp(self.xn),
+                                   st))
+        check(L.exl3cu_hyb_head(_vp(self.xn), _vp(logit_rows), nout, H, _vp(self.embed), cfg.vocab, None,
+                                _vp(self.best), _vp(self.out_tokens), st))
+
+    def head_logits(self, nout: int, stream=None):
+        """Logits of the last step's logit rows (f32 [nout, vocab]); recomputes the head only."""
+        torch, cfg = self.torch, self.cfg
+        st = ctypes.c_void_p((stream or torch.cuda.current_stream()).cuda_stream)
+        out = torch.empty((nout, cfg.vocab), dtype=torch.float32, device=self.dev)
+        check(self.L.exl3cu_hyb_head(_vp(self.xn), _vp(self.meta.view("logit_rows")), nout, cfg.hidden,
+                                     _vp(self.embed), cfg.vocab, _vp(out), _vp(self.best), _vp(self.out_tokens), st))
+        return out
+
+    def free(self):
+        for d in self.layers:
+            for w in d["mats"].values():
+                w.free()
+        self.layers = []
+
+
+# ---------------------------------------------------------------------------------------------
+# Continuous-admission scheduler
+
+@dataclass
+class Request:
+    prompt: np.ndarray        # int32 token ids
+    max_new: int
+    slot: int = -1
+    pos: int = 0              # tokens already in the caches
+    generated: list = field(default_factory=list)
+
+    @property
+    def done(self) -> bool:
+        return len(self.generated) >= self.max_new
+
+
+def plan_step(active, waiting, slots_free, max_rows: int, chunk: int):
+    """Rows of one step: every decoding request contributes its last token; the oldest prefilling
+    request (admitted into a free slot when needed) contributes a chunk of its prompt.
+    Returns (seqs, tokens, row_seq, row_pos, row_offsets, seq_slot, logit_rows, logit_seq)."""
+    seqs, tokens, row_seq, row_pos, offsets, slots_, logit_rows, logit_seq = [], [], [], [], [0], [], [], []
+    budget = max_rows
+    for rq in active:
+        if rq.pos >= len(rq.prompt) and not rq.done and budget > 0 and len(logit_rows) < 8:
+            s = len(seqs)
+            seqs.append(rq)
+            tokens.append(rq.generated[-1])
+            row_seq.append(s)
+            row_pos.append(rq.pos)
+            offsets.append(offsets[-1] + 1)
+            slots_.append(rq.slot)
+            logit_rows.append(len(tokens) - 1)
+            logit_seq.append(rq)
+            budget -= 1
+    prefilling = [rq for rq in active if rq.pos < len(rq.prompt)]
+    if not prefilling and waiting and slots_free:
+        rq = waiting.pop(0)
+        rq.slot = slots_free.pop(0)
+        active.append(rq)
+        prefilling = [rq]
+    if prefilling and budget > 0 and len(logit_rows) < 8:
+        rq = prefilling[0]
+        n = min(chunk, budget, len(rq.prompt) - rq.pos)
+        s = len(seqs)
+        seqs.append(rq)
+        for j in range(n):
+            tokens.append(int(rq.prompt[rq.pos + j]))
+            row_seq.append(s)
+            row_pos.append(rq.pos + j)
+        offsets.append(offsets[-1] + n)
+        slots_.append(rq.slot)
+        if rq.pos + n == len(rq.prompt):
+            logit_rows.append(len(tokens) - 1)
+            logit_seq.append(rq)
+    return seqs, tokens, row_seq, row_pos, offsets, slots_, logit_rows, logit_seq
+
+
+def run_requests(engine: HybridEngine, requests, chunk: int = 512, stream=None, graphs: dict | None = None):
+    """Serve `requests` to completion with continuous admission; returns (steps, rows_total).
+
+    Pure decode steps of n sequences replay a captured step (one per n, kept in `graphs` when given,
+    captured after the first eager step of that shape); steps with prefill rows run eagerly.  Every
+    step copies its metadata in and its next tokens out (the host schedules the next step)."""
+    torch = engine.torch
+    stream = stream or torch.cuda.Stream(device=engine.dev)
+    graphs = {} if graphs is None else graphs
+    seen = set()
+    waiting = list(requests)
+    active = []
+    free = list(range(engine.slots))
+    steps = rows_total = 0
+    while waiting or active:
+        seqs, tokens, row_seq, row_pos, offsets, slots_, logit_rows, logit_seq = plan_step(
+            active, waiting, free, engine.max_rows, chunk)
+        for s, rq in enumerate(seqs):
+            if rq.pos == 0:
+                engine.reset_slot(rq.slot)
+        engine.meta.fill(tokens, row_seq, row_pos, offsets, slots_, logit_rows)
+        n = len(tokens)
+        pure_decode = n == len(seqs) == len(logit_rows)
+        with torch.cuda.stream(stream):
+            engine.meta.upload(stream)
+            g = graphs.get(n) if pure_decode else None
+            if g is not None:
+                g.replay()
+            else:
+                engine.forward(n, len(seqs), len(logit_rows), stream)
+            out = engine.out_tokens[:len(logit_rows)].to("cpu", non_blocking=False)
+        if pure_decode and n not in graphs:
+            if n in seen:
+                graphs[n] = _StepGraph(engine, n, stream)
+            seen.add(n)
+        # advance positions
+        for s, rq in enumerate(seqs):
+            rq.pos += offsets[s + 1] - offsets[s]
+        for o, rq in enumerate(logit_seq):
+            rq.generated.append(int(out[o]))
+        for rq in list(active):
+            if rq.done:
+                active.remove(rq)
+                free.append(rq.slot)
+        steps += 1
+        rows_total += len(tokens)
+    return steps, rows_total
+
+
+class _StepGraph:
+    """A captured pure decode step of n sequences (metadata read from the device buffer as it is)."""
+
+    def __init__(self, engine, n, stream):
+        torch = engine.torch
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            engine.forward(n, n, n, stream)
+
+    def replay(self):
+        self.graph.replay()
+
+
+class DecodeGraph:
+    """One captured decode step for `n` sequences (one row each, rows 0..n-1 in the step metadata):
+    the step, then on the device: tokens[:n] <- next tokens, row_pos[:n] += 1, and the tokens appended
+    to a log.  Replaying it runs greedy decoding with no host round trip; the metadata must hold a
+    pure decode step for n sequences before the first replay."""
+
+    def __init__(self, engine: HybridEngine, n: int, max_steps: int, stream=None):
+        torch = engine.torch
+        self.engine, self.n = engine, n
+        self.stream = stream or torch.cuda.Stream(device=engine.dev)
+        self.log = torch.zeros(max_steps * n, dtype=torch.int32, device=engine.dev)
+        self.counter = torch.zeros(1, dtype=torch.int64, device=engine.dev)
+        self.ar = torch.arange(n, dtype=torch.int64, device=engine.dev)
+        self.max_steps = max_steps
+        m = engine.meta
+        self._tok, self._pos = m.view("tokens")[:n], m.view("row_pos")[:n]
+        with torch.cuda.stream(self.stream):
+            self._body()  # eager warm-up at this shape (GEMM scratch, kernel attributes)
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self._body()
+
+    def _body(self):
+        e, n = self.engine, self.n
+        e.forward(n, n, n, self.stream)
+        self._tok.copy_(e.out_tokens[:n])
+        self._pos.add_(1)
+        idx = (self.counter * n + self.ar).clamp_(max=self.log.numel() - 1)
+        self.log.scatter_(0, idx, e.out_tokens[:n])
+        self.counter.add_(1)
+
+    def reset(self):
+        self.counter.zero_()
+
+    def replay(self):
+        self.graph.replay()
