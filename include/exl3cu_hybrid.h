@@ -47,10 +47,16 @@ int exl3cu_hyb_attn_prep(const float * d_qkv, int rows, const int32_t * d_row_se
                          int n_slots, float * d_q, void * stream);
 
 /* GQA attention of each row's 16 q heads over positions 0..row_pos of its
- * sequence (4 q heads per kv head), softmax(q.k * scale); out fp16 [rows][16*128]. */
+ * sequence (4 q heads per kv head), softmax(q.k * scale); out fp16 [rows][16*128].
+ * splits > 1 divides each row's positions over that many CTAs (flash-decoding);
+ * it needs d_part of exl3cu_hyb_attn_scratch_bytes(rows, splits) bytes and
+ * d_tickets of rows*16 unsigned, zero before the first call (the kernel leaves
+ * them zero). */
+size_t exl3cu_hyb_attn_scratch_bytes(int rows, int splits);
 int exl3cu_hyb_attn(const float * d_q, int rows, const int32_t * d_row_seq, const int32_t * d_row_pos,
                     const int32_t * d_seq_slot, const uint16_t * d_kcache, const uint16_t * d_vcache, int max_len,
-                    int n_slots, float scale, uint16_t * d_out, void * stream);
+                    int n_slots, float scale, int splits, float * d_part, size_t part_bytes, unsigned * d_tickets,
+                    uint16_t * d_out, void * stream);
 
 /* Dynamic shared memory one exl3cu_hyb_gdn CTA uses (the 128x128 state and scratch). */
 size_t exl3cu_hyb_gdn_smem_bytes(void);
@@ -70,9 +76,13 @@ int exl3cu_hyb_gdn(const float * d_qkvz, const uint16_t * d_xn, const uint16_t *
 /* Tied fp16 head with greedy choice: for o < nout (<= 8), logits[o][v] =
  * sum_i xn[rows[o]][i] * embed[v][i] (fp32 sums; written when d_logits is not
  * NULL), tokens[o] = argmax_v (lowest index on ties).  d_best: nout 64-bit
- * scratch words.  hidden must be a multiple of 256. */
+ * scratch words.  hidden is 1024, 2048, 4096 or 8192. */
 int exl3cu_hyb_head(const uint16_t * d_xn, const int32_t * d_rows, int nout, int hidden, const uint16_t * d_embed,
                     int vocab, float * d_logits, unsigned long long * d_best, int32_t * d_tokens, void * stream);
+
+/* Sticky error bits of these kernels on the current device (bit 0: the
+ * delta-rule state copy never arrived).  Synchronises the device. */
+int exl3cu_hyb_status(int clear, unsigned * status);
 
 #ifdef __cplusplus
 }

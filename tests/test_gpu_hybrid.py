@@ -110,3 +110,51 @@ def test_head_argmax_and_embedding(model):
     ref = x.astype(np.float64) @ E.T.astype(np.float64)
     assert np.max(np.abs(lg - ref)) / np.max(np.abs(ref)) < 1e-5
     assert list(eng.out_tokens[:3].cpu().numpy()) == list(np.argmax(lg, axis=1))
+
+
+def test_attention_splits_agree(model):
+    """The split (flash-decoding) attention against the single-CTA form on the same cache, rows at
+    several positions; then the split scratch's tickets are back at zero."""
+    import ctypes
+
+    from exl3_b200.hybrid import _vp
+
+    eng, _ = model
+    L = eng.L
+    c = 0
+    g = torch.Generator(device="cuda").manual_seed(11)
+    eng.kc[c].copy_(torch.randn(eng.kc[c].shape, generator=g, device="cuda").half())
+    eng.vc[c].copy_(torch.randn(eng.vc[c].shape, generator=g, device="cuda").half())
+    rows = 5
+    q = torch.randn((rows, 16 * 128), generator=g, device="cuda")
+    pos = [0, 3, 31, 100, 159]
+    eng.meta.fill([0] * rows, [0, 1, 2, 0, 1], pos, [0, 1, 2, 3], [0, 1, 2], [0])
+    eng.meta.upload(None)
+    m = eng.meta
+    outs = []
+    for sp in (1, 2, 8):
+        o = torch.zeros((rows, 16 * 128), dtype=torch.float16, device="cuda")
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        rc = L.exl3cu_hyb_attn(_vp(q), rows, _vp(m.view("row_seq")), _vp(m.view("row_pos")), _vp(m.view("seq_slot")),
+                               _vp(eng.kc[c]), _vp(eng.vc[c]), eng.max_len, eng.slots, 0.088388, sp,
+                               _vp(eng.attn_part), eng.attn_part.numel() * 4, _vp(eng.attn_tickets), _vp(o), st)
+        assert rc == 0
+        outs.append(o.float().cpu().numpy())
+    # fp32 reference on the host
+    K = eng.kc[c].float().cpu().numpy()
+    V = eng.vc[c].float().cpu().numpy()
+    qq = q.cpu().numpy().reshape(rows, 16, 128)
+    slots = [0, 1, 2, 0, 1]
+    ref = np.zeros((rows, 16, 128))
+    for r in range(rows):
+        for h in range(16):
+            k = K[slots[r], h // 4, :pos[r] + 1]
+            s = k @ qq[r, h] * 0.088388
+            p = np.exp(s - s.max())
+            ref[r, h] = (p / p.sum()) @ V[slots[r], h // 4, :pos[r] + 1]
+    ref = ref.reshape(rows, -1)
+    for o in outs:
+        assert np.max(np.abs(o - ref)) < 2e-3
+    assert int(eng.attn_tickets.abs().sum()) == 0
+    st = ctypes.c_uint(0)
+    assert L.exl3cu_hyb_status(1, ctypes.byref(st)) == 0 and st.value == 0

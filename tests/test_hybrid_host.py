@@ -41,3 +41,23 @@ def test_plan_step_respects_row_budget():
         active.append(r)
     seqs, tok, rs, rp, off, sl, lr, ls = plan_step(active, [], [], max_rows=2, chunk=4)
     assert len(tok) == 2 and lr == [0, 1]
+
+
+def test_hybrid_c_abi_exports_every_declared_symbol():
+    import re
+    from pathlib import Path
+
+    from exl3_b200 import _lib
+
+    lib = _lib.lib()
+    text = (Path(__file__).resolve().parents[1] / "include" / "exl3cu_hybrid.h").read_text()
+    names = sorted(set(re.findall(r"\b(exl3cu_hyb_\w+)\s*\(", text)))
+    assert len(names) >= 10
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_attention_split_policy():
+    from exl3_b200.hybrid import attn_splits
+
+    assert attn_splits(1) == 8 and attn_splits(8) == 8 and attn_splits(9) == 2 and attn_splits(512) == 1

@@ -22,11 +22,21 @@
 // per-head RMSNorm of q and k, rotary embedding on the two halves of each
 // head, softmax(q k^T / sqrt(128)) v over positions 0..pos, 4 q heads per kv
 // head.
+//
+// Every kernel is launched with programmatic dependent launch: it lets the
+// next kernel be scheduled at once (griddepcontrol.launch_dependents) and
+// reads or writes nothing before its own griddepcontrol.wait, which returns
+// when the preceding grid has completed and flushed -- so a chain of these
+// kernels and the EXL3 operator keeps stream order while each launch's
+// latency overlaps the tail of the one before.
 #include "exl3cu.h"
+#include "exl3cu_async.cuh"
 #include "exl3cu_hybrid.h"
 #include "exl3cu_internal.h"
 
 #include <cuda_fp16.h>
+
+#include <atomic>
 
 namespace exl3cu {
 
@@ -62,6 +72,8 @@ __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1p
 
 __global__ void k_embed(const __half * __restrict__ table, const int32_t * __restrict__ ids, int vocab, int H,
                         float * __restrict__ h) {
+    pdl_trigger();
+    pdl_wait_primary();
     const int r = blockIdx.x;
     const int32_t id = ids[r];
     const bool ok = id >= 0 && id < vocab;  // an id outside the table gives a zero row
@@ -69,29 +81,59 @@ __global__ void k_embed(const __half * __restrict__ table, const int32_t * __res
         h[size_t(r) * H + i] = ok ? __half2float(table[size_t(id) * H + i]) : 0.f;
 }
 
-// h += delta (when given), then out = fp16(h / sqrt(mean(h^2) + eps) * w).  One CTA per row.
-__global__ void k_rmsnorm(float * __restrict__ h, const float * __restrict__ delta, int delta_stride,
-                          const float * __restrict__ w, float eps, int H, __half * __restrict__ out) {
-    __shared__ float red[32];
+// h += delta (when given), then out = fp16(h / sqrt(mean(h^2) + eps) * w).
+// One CTA of 256 threads per row; the row (H <= 8192, H % 4 == 0) stays in
+// registers between the sum and the scaling.
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxVec = 8;  // float4 per thread: H <= 8192
+
+__global__ void __launch_bounds__(kNormThreads)
+k_rmsnorm(float * __restrict__ h, const float * __restrict__ delta, int delta_stride, const float * __restrict__ w,
+          float eps, int H, __half * __restrict__ out) {
+    __shared__ float red[kNormThreads / 32];
+    pdl_trigger();
+    pdl_wait_primary();
     const int r = blockIdx.x;
-    float * hr = h + size_t(r) * H;
+    float4 * hr = reinterpret_cast<float4 *>(h + size_t(r) * H);
+    const float4 * dr = delta ? reinterpret_cast<const float4 *>(delta + size_t(r) * delta_stride) : nullptr;
+    const int nv = H / 4;
+    float4 v[kNormMaxVec];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) {
-        float v = hr[i];
-        if (delta) {
-            v += delta[size_t(r) * delta_stride + i];
-            hr[i] = v;
+#pragma unroll
+    for (int q = 0; q < kNormMaxVec; ++q) {
+        const int e = threadIdx.x + q * kNormThreads;
+        if (e < nv) {
+            float4 x = hr[e];
+            if (dr) {
+                const float4 d = dr[e];
+                x.x += d.x; x.y += d.y; x.z += d.z; x.w += d.w;
+                hr[e] = x;
+            }
+            v[q] = x;
+            ss = fmaf(x.x, x.x, ss);
+            ss = fmaf(x.y, x.y, ss);
+            ss = fmaf(x.z, x.z, ss);
+            ss = fmaf(x.w, x.w, ss);
         }
-        ss = fmaf(v, v, ss);
     }
-    const float tot = block_sum(ss, red, blockDim.x >> 5);
-    const float inv = rsqrtf(tot / float(H) + eps);
-    for (int i = threadIdx.x; i < H; i += blockDim.x)
-        out[size_t(r) * H + i] = __float2half_rn(hr[i] * inv * w[i]);
+    const float inv = rsqrtf(block_sum(ss, red, kNormThreads / 32) / float(H) + eps);
+    const float4 * wr = reinterpret_cast<const float4 *>(w);
+    __half2 * o2 = reinterpret_cast<__half2 *>(out + size_t(r) * H);
+#pragma unroll
+    for (int q = 0; q < kNormMaxVec; ++q) {
+        const int e = threadIdx.x + q * kNormThreads;
+        if (e < nv) {
+            const float4 wv = wr[e];
+            o2[2 * e] = __floats2half2_rn(v[q].x * inv * wv.x, v[q].y * inv * wv.y);
+            o2[2 * e + 1] = __floats2half2_rn(v[q].z * inv * wv.z, v[q].w * inv * wv.w);
+        }
+    }
 }
 
 // out = fp16(silu(gate) * up); gu row = [gate (F) | up (F)].
 __global__ void k_swiglu(const float * __restrict__ gu, int F, __half * __restrict__ out) {
+    pdl_trigger();
+    pdl_wait_primary();
     const int r = blockIdx.y;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= F) return;
@@ -108,6 +150,8 @@ __global__ void k_attn_prep(const float * __restrict__ qkv, const int32_t * __re
                             const float * __restrict__ qn_w, const float * __restrict__ kn_w,
                             const float * __restrict__ inv_freq, float eps, __half * __restrict__ kc,
                             __half * __restrict__ vc, int max_len, int n_slots, float * __restrict__ q_out) {
+    pdl_trigger();
+    pdl_wait_primary();
     const int r = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = row_pos[r];
@@ -151,26 +195,39 @@ __global__ void k_attn_prep(const float * __restrict__ qkv, const int32_t * __re
     }
 }
 
-// softmax(q K^T * scale) V over positions 0..pos of the row's sequence, one
-// CTA (4 warps) per (q head, row); warp w takes positions w, w+4, ...; lane
-// holds 4 consecutive dims.  Online softmax per warp, merged in fixed order.
-__global__ void k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq,
-                       const int32_t * __restrict__ row_pos, const int32_t * __restrict__ seq_slot,
-                       const __half * __restrict__ kc, const __half * __restrict__ vc, int max_len, int n_slots,
-                       float scale, __half * __restrict__ out) {
+// softmax(q K^T * scale) V over positions 0..pos of the row's sequence.
+// Grid (q head, row, split): the CTA (4 warps) covers split `z` of the
+// positions; warp w takes positions w, w+4, ... of that range, lane holds 4
+// consecutive dims; online softmax per warp, merged in warp order.  With
+// more than one split each CTA stores (max, sum, acc[128]) to `part`, and the
+// last CTA of the (row, head) to arrive (ticket) merges the splits in split
+// order and resets the ticket.
+constexpr int kAttnPart = kHD + 2;
+
+__global__ void __launch_bounds__(128)
+k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const int32_t * __restrict__ row_pos,
+       const int32_t * __restrict__ seq_slot, const __half * __restrict__ kc, const __half * __restrict__ vc,
+       int max_len, int n_slots, float scale, float * __restrict__ part, unsigned * __restrict__ tickets,
+       __half * __restrict__ out) {
     __shared__ float sm_m[4], sm_l[4], sm_acc[4][kHD];
-    const int head = blockIdx.x, r = blockIdx.y;
+    __shared__ unsigned sm_last;
+    pdl_trigger();
+    pdl_wait_primary();
+    const int head = blockIdx.x, r = blockIdx.y, z = blockIdx.z, S = gridDim.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int slot = seq_slot[row_seq[r]];
     if (slot < 0 || slot >= n_slots) return;
-    const int pos = min(row_pos[r], max_len - 1);
+    const int npos = min(row_pos[r], max_len - 1) + 1;
+    const int chunk = (npos + S - 1) / S;
+    const int p0 = z * chunk, p1 = min(npos, p0 + chunk);
     const int kvh = head / (kNH / kNKV);
     const float4 qv = *reinterpret_cast<const float4 *>(q + size_t(r) * kNH * kHD + head * kHD + lane * 4);
     const __half * kb = kc + (size_t(slot) * kNKV + kvh) * max_len * kHD;
     const __half * vb = vc + (size_t(slot) * kNKV + kvh) * max_len * kHD;
     float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int p = warp; p <= pos; p += 4) {
+    for (int p = p0 + warp; p < p1; p += 4) {
         const uint2 kr = *reinterpret_cast<const uint2 *>(kb + size_t(p) * kHD + lane * 4);
+        const uint2 vr = *reinterpret_cast<const uint2 *>(vb + size_t(p) * kHD + lane * 4);
         const float2 k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.x));
         const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.y));
         float s = qv.x * k01.x;
@@ -180,7 +237,6 @@ __global__ void k_attn(const float * __restrict__ q, const int32_t * __restrict_
         s = warp_sum(s) * scale;
         const float mn = fmaxf(m, s);
         const float corr = expf(m - mn), e = expf(s - mn);
-        const uint2 vr = *reinterpret_cast<const uint2 *>(vb + size_t(p) * kHD + lane * 4);
         const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.x));
         const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
         l = l * corr + e;
@@ -197,29 +253,82 @@ __global__ void k_attn(const float * __restrict__ q, const int32_t * __restrict_
 #pragma unroll
     for (int q2 = 0; q2 < 4; ++q2) sm_acc[warp][lane * 4 + q2] = acc[q2];
     __syncthreads();
+    // merge the warps (warp 0): M, L, A over this CTA's range
+    float M = -INFINITY, L = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
     if (warp == 0) {
-        float M = -INFINITY;
         for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_m[w]);
-        float L = 0.f, a[4] = {0.f, 0.f, 0.f, 0.f};
         for (int w = 0; w < 4; ++w) {
             if (sm_m[w] == -INFINITY) continue;  // a warp that saw no position
             const float c = expf(sm_m[w] - M);
             L = fmaf(sm_l[w], c, L);
 #pragma unroll
-            for (int q2 = 0; q2 < 4; ++q2) a[q2] = fmaf(sm_acc[w][lane * 4 + q2], c, a[q2]);
+            for (int q2 = 0; q2 < 4; ++q2) A[q2] = fmaf(sm_acc[w][lane * 4 + q2], c, A[q2]);
         }
-        const float invL = 1.0f / L;
-#pragma unroll
-        for (int q2 = 0; q2 < 4; ++q2)
-            out[size_t(r) * kNH * kHD + head * kHD + lane * 4 + q2] = __float2half_rn(a[q2] * invL);
     }
+    __half * dst = out + size_t(r) * kNH * kHD + head * kHD + lane * 4;
+    if (S == 1) {
+        if (warp == 0) {
+            const float invL = 1.0f / L;
+#pragma unroll
+            for (int q2 = 0; q2 < 4; ++q2) dst[q2] = __float2half_rn(A[q2] * invL);
+        }
+        return;
+    }
+    float * mine = part + ((size_t(r) * kNH + head) * S + z) * kAttnPart;
+    if (warp == 0) {
+        if (lane == 0) {
+            mine[0] = M;
+            mine[1] = L;
+        }
+#pragma unroll
+        for (int q2 = 0; q2 < 4; ++q2) mine[2 + lane * 4 + q2] = A[q2];
+        __threadfence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) sm_last = atomicAdd(tickets + size_t(r) * kNH + head, 1u) == unsigned(S - 1);
+    __syncthreads();
+    if (!sm_last || warp != 0) return;
+    __threadfence();
+    const float * all = part + (size_t(r) * kNH + head) * S * kAttnPart;
+    float GM = -INFINITY;
+    for (int zz = 0; zz < S; ++zz) GM = fmaxf(GM, __ldcg(all + zz * kAttnPart));
+    float GL = 0.f, G[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int zz = 0; zz < S; ++zz) {
+        const float mz = __ldcg(all + zz * kAttnPart);
+        if (mz == -INFINITY) continue;
+        const float c = expf(mz - GM);
+        GL = fmaf(__ldcg(all + zz * kAttnPart + 1), c, GL);
+#pragma unroll
+        for (int q2 = 0; q2 < 4; ++q2) G[q2] = fmaf(__ldcg(all + zz * kAttnPart + 2 + lane * 4 + q2), c, G[q2]);
+    }
+    const float invL = 1.0f / GL;
+#pragma unroll
+    for (int q2 = 0; q2 < 4; ++q2) dst[q2] = __float2half_rn(G[q2] * invL);
+    if (lane == 0) tickets[size_t(r) * kNH + head] = 0u;  // ready for the next launch
 }
 
 // Gated delta rule for one (head, step sequence): the sequence's rows in
 // order.  256 threads; the head's 128 x 128 fp32 state lives in shared memory
-// for the CTA's lifetime (loaded from and stored back to S).  Thread t: v
-// column j = t & 127, k half = t >> 7.
+// for the CTA's lifetime: one bulk copy brings it in while the first row's
+// convolution and gate projections run, one bulk copy stores it back.
+// Thread t: v column j = t & 127, k half = t >> 7.
 constexpr int kGdnThreads = 256;
+constexpr uint32_t kStateBytes = kHD * kHD * sizeof(float);
+
+static __device__ unsigned g_hyb_status;  // kStatusWaitTimeout when the state copy never arrived
+
+__device__ __forceinline__ void bulk_s2g(void * dst_gmem, const void * src_smem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_gmem),
+                 "r"(smem_addr(src_smem)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 __global__ void __launch_bounds__(kGdnThreads)
 k_gdn(const float * __restrict__ qkvz, const __half * __restrict__ xn, const __half * __restrict__ wab, int H,
@@ -227,27 +336,35 @@ k_gdn(const float * __restrict__ qkvz, const __half * __restrict__ xn, const __h
       const float * __restrict__ dt_bias, const float * __restrict__ norm_w, float eps, float * __restrict__ S,
       const int32_t * __restrict__ row_offsets, const int32_t * __restrict__ seq_slot, int n_slots,
       __half * __restrict__ out) {
-    extern __shared__ __align__(16) float sm[];
+    extern __shared__ __align__(128) float sm[];
     float * St = sm;                          // [128 k][128 v]
     float * cq = St + kHD * kHD;              // conv outputs q, k, v of the current row
     float * ck = cq + kHD;
     float * cv = ck + kHD;
     float * red = cv + kHD;                   // [4][128]: k-half sums of S^T k and S^T q; then o
-    float * scal = red + 4 * kHD;             // [32]: per-warp gate sums, alpha, beta
+    float * scal = red + 4 * kHD;             // [32]: per-warp gate sums, alpha, beta, k.q
+    uint64_t * bar = reinterpret_cast<uint64_t *>(scal + 32);
+    pdl_trigger();
+    pdl_wait_primary();
     const int h = blockIdx.x, s = blockIdx.y;
     const int slot = seq_slot[s];
     if (slot < 0 || slot >= n_slots) return;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int j = t & (kHD - 1), half = t >> 7;
     float * Sg = S + (size_t(slot) * kNH + h) * kHD * kHD;
-    for (int e = t; e < kHD * kHD / 4; e += kGdnThreads)
-        reinterpret_cast<float4 *>(St)[e] = reinterpret_cast<const float4 *>(Sg)[e];
     const int r0 = row_offsets[s], r1 = row_offsets[s + 1];
+    if (r1 <= r0) return;
+    if (t == 0) {
+        mbar_init(bar, 1);
+        mbar_init_fence();
+        mbar_arrive_expect_tx(bar, kStateBytes);
+        bulk_g2s(St, Sg, kStateBytes, bar);
+    }
+    bool state_ready = false, ok = true;
     constexpr int QKVZ = 4 * kNH * kHD;
     constexpr int CH = 3 * kNH * kHD;  // convolved channels (q, k, v)
     const float A = -expf(A_log[h]);
     const float qscale = rsqrtf(float(kHD));
-    __syncthreads();
     for (int r = r0; r < r1; ++r) {
         // (1) causal conv + SiLU on this head's 384 channels; the conv state keeps the last 3 inputs
         for (int c = t; c < 3 * kHD; c += kGdnThreads) {
@@ -274,13 +391,12 @@ k_gdn(const float * __restrict__ qkvz, const __half * __restrict__ xn, const __h
         }
         pa = warp_sum(pa);
         pb = warp_sum(pb);
-        __syncthreads();  // conv outputs complete; scal free
         if (lane == 0) {
             scal[warp] = pa;
             scal[8 + warp] = pb;
         }
-        __syncthreads();
-        // (3) L2 norms of q and k (warp 0: q, warp 1: k), gates (thread 64)
+        __syncthreads();  // conv outputs and gate sums complete
+        // (3) L2 norms of q and k (warps 0, 1), gates (warp 2, lane 0)
         if (warp < 2) {
             float * vec = warp == 0 ? cq : ck;
             float ss = 0.f;
@@ -296,12 +412,23 @@ k_gdn(const float * __restrict__ qkvz, const __half * __restrict__ xn, const __h
             scal[16] = expf(A * softplus(a + dt_bias[h]));  // alpha
             scal[17] = 1.0f / (1.0f + expf(-b));              // beta
         }
+        if (!state_ready) {
+            ok = mbar_wait(bar, 0);
+            if (!ok && t == 0) atomicOr(&g_hyb_status, kStatusWaitTimeout);
+            state_ready = true;
+        }
         __syncthreads();
+        if (warp == 0) {  // k . q after normalisation (every thread reads it below)
+            float kq = 0.f;
+            for (int d = lane; d < kHD; d += 32) kq = fmaf(ck[d], cq[d], kq);
+            kq = warp_sum(kq);
+            if (lane == 0) scal[18] = kq;
+        }
         const float alpha = scal[16], beta = scal[17];
         // (4) a_j = sum_i S[i][j] k[i], c_j = sum_i S[i][j] q[i] over this thread's k half
         float ak = 0.f, cqs = 0.f;
         const int i0 = half * (kHD / 2);
-#pragma unroll 8
+#pragma unroll 16
         for (int i = i0; i < i0 + kHD / 2; ++i) {
             const float sv = St[i * kHD + j];
             ak = fmaf(sv, ck[i], ak);
@@ -310,19 +437,18 @@ k_gdn(const float * __restrict__ qkvz, const __half * __restrict__ xn, const __h
         red[half * kHD + j] = ak;
         red[2 * kHD + half * kHD + j] = cqs;
         __syncthreads();
-        float kq = 0.f;
-        for (int i = 0; i < kHD; ++i) kq = fmaf(ck[i], cq[i], kq);  // every thread, same order
+        const float kq = scal[18];
         const float a_j = red[j] + red[kHD + j];
         const float c_j = red[2 * kHD + j] + red[3 * kHD + j];
         const float u_j = beta * (cv[j] - alpha * a_j);
         const float o_j = fmaf(kq, u_j, alpha * c_j);
         // (5) S = alpha S + k u^T on this thread's half
-#pragma unroll 8
+#pragma unroll 16
         for (int i = i0; i < i0 + kHD / 2; ++i) St[i * kHD + j] = fmaf(ck[i], u_j, alpha * St[i * kHD + j]);
-        // (6) RMSNorm of o over the head, times norm_w, gated by SiLU(z)
-        __syncthreads();  // red reused
+        __syncthreads();  // everyone has read red
         if (half == 0) red[j] = o_j;
         __syncthreads();
+        // (6) RMSNorm of o over the head, times norm_w, gated by SiLU(z)
         if (warp == 0) {
             float ss = 0.f;
             for (int d = lane; d < kHD; d += 32) ss = fmaf(red[d], red[d], ss);
@@ -332,10 +458,15 @@ k_gdn(const float * __restrict__ qkvz, const __half * __restrict__ xn, const __h
                 out[size_t(r) * kNH * kHD + h * kHD + d] = __float2half_rn(red[d] * inv * norm_w[d] * silu(z));
             }
         }
-        __syncthreads();
+        __syncthreads();  // next row overwrites cq, ck, cv, red, scal
     }
-    for (int e = t; e < kHD * kHD / 4; e += kGdnThreads)
-        reinterpret_cast<float4 *>(Sg)[e] = reinterpret_cast<const float4 *>(St)[e];
+    if (!ok) return;  // the state never arrived: leave the stored state untouched
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (t == 0) {
+        bulk_s2g(Sg, St, kStateBytes);
+        bulk_wait_all();
+    }
 }
 
 // Order-preserving key of a float (larger float, larger key).
@@ -346,14 +477,18 @@ __device__ __forceinline__ uint32_t float_key(float f) {
 
 // logits[o][v] = sum_i xn[rows[o]][i] * E[v][i] (fp16 inputs, fp32 sums) for
 // nout <= 8 rows; best[o] = max over v of (key(logit) << 32 | ~v) (the first
-// index wins ties).  Warp per vocab row, activations staged in shared memory.
+// index wins ties).  Warp per vocab row, activations staged in shared memory;
+// ITER = H / 256 16-byte loads per lane per vocab row, issued together.
 constexpr int kHeadMaxRows = 8;
 constexpr int kHeadThreads = 256;
 
+template <int ITER>
 __global__ void __launch_bounds__(kHeadThreads)
 k_head(const __half * __restrict__ xn, const int32_t * __restrict__ rows, int nout, int H,
        const __half * __restrict__ E, int V, float * __restrict__ logits, unsigned long long * __restrict__ best) {
     extern __shared__ __align__(16) __half xs[];  // [nout][H]
+    pdl_trigger();
+    pdl_wait_primary();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int e = threadIdx.x; e < nout * H / 8; e += kHeadThreads) {
         const int o = (e * 8) / H, i = (e * 8) % H;
@@ -365,20 +500,23 @@ k_head(const __half * __restrict__ xn, const int32_t * __restrict__ rows, int no
     for (int o = 0; o < kHeadMaxRows; ++o) mine[o] = 0ull;
     const int nwarps = gridDim.x * (kHeadThreads / 32);
     for (int v = blockIdx.x * (kHeadThreads / 32) + warp; v < V; v += nwarps) {
+        const __half * er = E + size_t(v) * H + lane * 8;
+        uint4 raw[ITER];
+#pragma unroll
+        for (int it = 0; it < ITER; ++it) raw[it] = __ldcs(reinterpret_cast<const uint4 *>(er + it * 256));
         float acc[kHeadMaxRows];
 #pragma unroll
         for (int o = 0; o < kHeadMaxRows; ++o) acc[o] = 0.f;
-        const __half * er = E + size_t(v) * H;
-        for (int i = lane * 8; i < H; i += 256) {
-            const uint4 raw = *reinterpret_cast<const uint4 *>(er + i);
-            const __half2 * e2 = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+        for (int it = 0; it < ITER; ++it) {
+            const __half2 * e2 = reinterpret_cast<const __half2 *>(&raw[it]);
             float2 ef[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) ef[q] = __half22float2(e2[q]);
 #pragma unroll
             for (int o = 0; o < kHeadMaxRows; ++o) {
                 if (o >= nout) break;
-                const uint4 xr = *reinterpret_cast<const uint4 *>(xs + o * H + i);
+                const uint4 xr = *reinterpret_cast<const uint4 *>(xs + o * H + it * 256 + lane * 8);
                 const __half2 * x2 = reinterpret_cast<const __half2 *>(&xr);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -406,7 +544,16 @@ k_head(const __half * __restrict__ xn, const int32_t * __restrict__ rows, int no
     }
 }
 
+// The head's memset of best[] folded in: one launch before the head clears it.
+__global__ void k_head_clear(unsigned long long * __restrict__ best, int nout) {
+    pdl_trigger();
+    pdl_wait_primary();
+    if (threadIdx.x < nout) best[threadIdx.x] = 0ull;
+}
+
 __global__ void k_head_tokens(const unsigned long long * __restrict__ best, int nout, int32_t * __restrict__ tokens) {
+    pdl_trigger();
+    pdl_wait_primary();
     const int o = threadIdx.x;
     if (o < nout) tokens[o] = int32_t(~uint32_t(best[o] & 0xffffffffull));
 }
@@ -427,6 +574,38 @@ int status_of(cudaError_t e) {
 
 int bad(const char * what) { return api_fail(EXL3CU_INVALID_ARGUMENT, what); }
 
+// Launch with programmatic stream serialization (the kernels wait for their
+// predecessor with griddepcontrol.wait before touching memory).
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void * stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return status_of(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
+// Per-device one-time kernel attributes.
+bool set_smem_attr_once(const void * fn, int bytes, std::atomic<unsigned long long> & done_mask) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    const unsigned long long bit = 1ull << dev;
+    if (done_mask.load() & bit) return true;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+    done_mask.fetch_or(bit);
+    return true;
+}
+
+std::atomic<unsigned long long> g_gdn_attr{0}, g_head_attr_4{0}, g_head_attr_8{0}, g_head_attr_16{0},
+    g_head_attr_32{0};
+constexpr int kHeadSmemMax = 200 * 1024;
+
 }  // namespace
 
 extern "C" {
@@ -435,27 +614,25 @@ int exl3cu_hyb_embed(const uint16_t * d_table, int vocab, const int32_t * d_ids,
                      void * stream) {
     if (!d_table || !d_ids || !d_h || rows < 0 || hidden <= 0 || vocab <= 0) return bad("embed: bad arguments");
     if (!rows) return EXL3CU_OK;
-    k_embed<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(reinterpret_cast<const __half *>(d_table), d_ids,
-                                                                  vocab, hidden, d_h);
-    return status_of(cudaGetLastError());
+    return launch_pdl(k_embed, dim3(unsigned(rows)), dim3(256), 0, stream,
+                      reinterpret_cast<const __half *>(d_table), d_ids, vocab, hidden, d_h);
 }
 
 int exl3cu_hyb_rmsnorm(float * d_h, const float * d_delta, int delta_stride, const float * d_w, float eps, int rows,
                        int hidden, uint16_t * d_out, void * stream) {
-    if (!d_h || !d_w || !d_out || rows < 0 || hidden <= 0 || (d_delta && delta_stride < hidden))
-        return bad("rmsnorm: bad arguments");
+    if (!d_h || !d_w || !d_out || rows < 0 || hidden <= 0 || hidden % 4 || hidden > 4 * kNormThreads * kNormMaxVec ||
+        (d_delta && (delta_stride < hidden || delta_stride % 4)))
+        return bad("rmsnorm: bad arguments (hidden a multiple of 4 up to 8192)");
     if (!rows) return EXL3CU_OK;
-    k_rmsnorm<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_h, d_delta, delta_stride, d_w, eps, hidden,
-                                                                    reinterpret_cast<__half *>(d_out));
-    return status_of(cudaGetLastError());
+    return launch_pdl(k_rmsnorm, dim3(unsigned(rows)), dim3(kNormThreads), 0, stream, d_h, d_delta, delta_stride, d_w,
+                      eps, hidden, reinterpret_cast<__half *>(d_out));
 }
 
 int exl3cu_hyb_swiglu(const float * d_gu, int rows, int ffn, uint16_t * d_out, void * stream) {
     if (!d_gu || !d_out || rows < 0 || ffn <= 0) return bad("swiglu: bad arguments");
     if (!rows) return EXL3CU_OK;
-    const dim3 grid(unsigned((ffn + 255) / 256), unsigned(rows));
-    k_swiglu<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_gu, ffn, reinterpret_cast<__half *>(d_out));
-    return status_of(cudaGetLastError());
+    return launch_pdl(k_swiglu, dim3(unsigned((ffn + 255) / 256), unsigned(rows)), dim3(256), 0, stream, d_gu, ffn,
+                      reinterpret_cast<__half *>(d_out));
 }
 
 int exl3cu_hyb_attn_prep(const float * d_qkv, int rows, const int32_t * d_row_seq, const int32_t * d_row_pos,
@@ -466,29 +643,35 @@ int exl3cu_hyb_attn_prep(const float * d_qkv, int rows, const int32_t * d_row_se
         !d_vcache || !d_q || rows < 0 || max_len <= 0 || n_slots <= 0)
         return bad("attn_prep: bad arguments");
     if (!rows) return EXL3CU_OK;
-    k_attn_prep<<<rows, (kNH + kNKV) * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-        d_qkv, d_row_seq, d_row_pos, d_seq_slot, d_qn_w, d_kn_w, d_inv_freq, eps, reinterpret_cast<__half *>(d_kcache),
-        reinterpret_cast<__half *>(d_vcache), max_len, n_slots, d_q);
-    return status_of(cudaGetLastError());
+    return launch_pdl(k_attn_prep, dim3(unsigned(rows)), dim3((kNH + kNKV) * 32), 0, stream, d_qkv, d_row_seq,
+                      d_row_pos, d_seq_slot, d_qn_w, d_kn_w, d_inv_freq, eps, reinterpret_cast<__half *>(d_kcache),
+                      reinterpret_cast<__half *>(d_vcache), max_len, n_slots, d_q);
+}
+
+size_t exl3cu_hyb_attn_scratch_bytes(int rows, int splits) {
+    return rows <= 0 || splits <= 1 ? 0 : size_t(rows) * kNH * splits * kAttnPart * sizeof(float);
 }
 
 int exl3cu_hyb_attn(const float * d_q, int rows, const int32_t * d_row_seq, const int32_t * d_row_pos,
                     const int32_t * d_seq_slot, const uint16_t * d_kcache, const uint16_t * d_vcache, int max_len,
-                    int n_slots, float scale, uint16_t * d_out, void * stream) {
+                    int n_slots, float scale, int splits, float * d_part, size_t part_bytes, unsigned * d_tickets,
+                    uint16_t * d_out, void * stream) {
     if (!d_q || !d_row_seq || !d_row_pos || !d_seq_slot || !d_kcache || !d_vcache || !d_out || rows < 0 ||
-        max_len <= 0 || n_slots <= 0)
+        max_len <= 0 || n_slots <= 0 || splits < 1 || splits > 64)
         return bad("attn: bad arguments");
     if (!rows) return EXL3CU_OK;
     if (rows > 65535) return bad("attn: at most 65535 rows");
-    const dim3 grid(kNH, unsigned(rows));
-    k_attn<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(d_q, d_row_seq, d_row_pos, d_seq_slot,
-                                                                 reinterpret_cast<const __half *>(d_kcache),
-                                                                 reinterpret_cast<const __half *>(d_vcache), max_len,
-                                                                 n_slots, scale, reinterpret_cast<__half *>(d_out));
-    return status_of(cudaGetLastError());
+    if (splits > 1 && (!d_part || !d_tickets || part_bytes < exl3cu_hyb_attn_scratch_bytes(rows, splits)))
+        return bad("attn: split scratch missing or too small (exl3cu_hyb_attn_scratch_bytes; tickets rows*16, zeroed)");
+    return launch_pdl(k_attn, dim3(kNH, unsigned(rows), unsigned(splits)), dim3(128), 0, stream, d_q, d_row_seq,
+                      d_row_pos, d_seq_slot, reinterpret_cast<const __half *>(d_kcache),
+                      reinterpret_cast<const __half *>(d_vcache), max_len, n_slots, scale, d_part, d_tickets,
+                      reinterpret_cast<__half *>(d_out));
 }
 
-size_t exl3cu_hyb_gdn_smem_bytes(void) { return size_t(kHD * kHD + 3 * kHD + 4 * kHD + 32) * sizeof(float); }
+size_t exl3cu_hyb_gdn_smem_bytes(void) {
+    return size_t(kHD * kHD + 3 * kHD + 4 * kHD + 32) * sizeof(float) + 16;  // + the state copy's mbarrier
+}
 
 int exl3cu_hyb_gdn(const float * d_qkvz, const uint16_t * d_xn, const uint16_t * d_wab, int hidden,
                    const float * d_conv_w, float * d_conv_state, const float * d_A_log, const float * d_dt_bias,
@@ -498,48 +681,62 @@ int exl3cu_hyb_gdn(const float * d_qkvz, const uint16_t * d_xn, const uint16_t *
         !d_state || !d_row_offsets || !d_seq_slot || !d_out || hidden <= 0 || n_seq < 0 || n_seq > 65535 ||
         n_slots <= 0)
         return bad("gdn: bad arguments");
+    if (reinterpret_cast<uintptr_t>(d_state) % 16) return bad("gdn: state must be 16-byte aligned");
     if (!n_seq) return EXL3CU_OK;
-    static bool attr_set = false;
     const size_t smem = exl3cu_hyb_gdn_smem_bytes();
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(k_gdn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return status_of(e);
-        attr_set = true;
-    }
-    const dim3 grid(kNH, unsigned(n_seq));
-    k_gdn<<<grid, kGdnThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-        d_qkvz, reinterpret_cast<const __half *>(d_xn), reinterpret_cast<const __half *>(d_wab), hidden, d_conv_w,
-        d_conv_state, d_A_log, d_dt_bias, d_norm_w, eps, d_state, d_row_offsets, d_seq_slot, n_slots,
-        reinterpret_cast<__half *>(d_out));
-    return status_of(cudaGetLastError());
+    if (!set_smem_attr_once(reinterpret_cast<const void *>(k_gdn), int(smem), g_gdn_attr))
+        return status_of(cudaGetLastError());
+    return launch_pdl(k_gdn, dim3(kNH, unsigned(n_seq)), dim3(kGdnThreads), smem, stream, d_qkvz,
+                      reinterpret_cast<const __half *>(d_xn), reinterpret_cast<const __half *>(d_wab), hidden,
+                      d_conv_w, d_conv_state, d_A_log, d_dt_bias, d_norm_w, eps, d_state, d_row_offsets, d_seq_slot,
+                      n_slots, reinterpret_cast<__half *>(d_out));
 }
 
 int exl3cu_hyb_head(const uint16_t * d_xn, const int32_t * d_rows, int nout, int hidden, const uint16_t * d_embed,
                     int vocab, float * d_logits, unsigned long long * d_best, int32_t * d_tokens, void * stream) {
     if (!d_xn || !d_rows || !d_embed || !d_best || !d_tokens || nout < 0 || nout > kHeadMaxRows || hidden <= 0 ||
-        hidden % 256 || vocab <= 0)
-        return bad("head: bad arguments (nout <= 8, hidden a multiple of 256)");
+        hidden % 256 || hidden > 8192 || vocab <= 0)
+        return bad("head: bad arguments (nout <= 8, hidden a multiple of 256 up to 8192)");
     if (!nout) return EXL3CU_OK;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemsetAsync(d_best, 0, sizeof(unsigned long long) * size_t(nout), st);
-    if (e != cudaSuccess) return status_of(e);
     const size_t smem = size_t(nout) * hidden * sizeof(__half);
-    static bool attr_set = false;
-    if (!attr_set) {
-        e = cudaFuncSetAttribute(k_head, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e != cudaSuccess) return status_of(e);
-        attr_set = true;
-    }
-    if (smem > 200 * 1024) return bad("head: activations exceed shared memory");
+    if (smem > size_t(kHeadSmemMax)) return bad("head: activations exceed shared memory");
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    k_head<<<sms * 4, kHeadThreads, smem, st>>>(reinterpret_cast<const __half *>(d_xn), d_rows, nout, hidden,
-                                                reinterpret_cast<const __half *>(d_embed), vocab, d_logits, d_best);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return status_of(e);
-    k_head_tokens<<<1, 32, 0, st>>>(d_best, nout, d_tokens);
-    return status_of(cudaGetLastError());
+    int rc = launch_pdl(k_head_clear, dim3(1), dim3(32), 0, stream, d_best, nout);
+    if (rc) return rc;
+    const dim3 grid(unsigned(sms * 4)), block(kHeadThreads);
+    const auto * xn = reinterpret_cast<const __half *>(d_xn);
+    const auto * E = reinterpret_cast<const __half *>(d_embed);
+    switch (hidden / 256) {
+#define EXL3CU_HEAD_CASE(N)                                                                                        \
+    case N:                                                                                                        \
+        if (!set_smem_attr_once(reinterpret_cast<const void *>(k_head<N>), kHeadSmemMax, g_head_attr_##N))        \
+            return status_of(cudaGetLastError());                                                                  \
+        rc = launch_pdl(k_head<N>, grid, block, smem, stream, xn, d_rows, nout, hidden, E, vocab, d_logits, d_best); \
+        break;
+        EXL3CU_HEAD_CASE(4)
+        EXL3CU_HEAD_CASE(8)
+        EXL3CU_HEAD_CASE(16)
+        EXL3CU_HEAD_CASE(32)
+#undef EXL3CU_HEAD_CASE
+        default:
+            return bad("head: hidden must be 1024, 2048, 4096 or 8192");
+    }
+    if (rc) return rc;
+    return launch_pdl(k_head_tokens, dim3(1), dim3(32), 0, stream, static_cast<const unsigned long long *>(d_best),
+                      nout, d_tokens);
+}
+
+int exl3cu_hyb_status(int clear, unsigned * status) {
+    if (!status) return bad("status is NULL");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(status, g_hyb_status, sizeof(unsigned));
+    if (e == cudaSuccess && clear && *status) {
+        const unsigned zero = 0;
+        e = cudaMemcpyToSymbol(g_hyb_status, &zero, sizeof(unsigned));
+    }
+    return status_of(e);
 }
 
 }  // extern "C"

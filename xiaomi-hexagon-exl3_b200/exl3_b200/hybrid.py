@@ -143,14 +143,23 @@ def _declare(L):
     L.exl3cu_hyb_rmsnorm.argtypes = [P, P, I, P, F, I, I, P, P]
     L.exl3cu_hyb_swiglu.argtypes = [P, I, I, P, P]
     L.exl3cu_hyb_attn_prep.argtypes = [P, I, P, P, P, P, P, P, F, P, P, I, I, P, P]
-    L.exl3cu_hyb_attn.argtypes = [P, I, P, P, P, P, P, I, I, F, P, P]
+    L.exl3cu_hyb_attn.argtypes = [P, I, P, P, P, P, P, I, I, F, I, P, S, P, P, P]
+    L.exl3cu_hyb_attn_scratch_bytes.restype = S
+    L.exl3cu_hyb_attn_scratch_bytes.argtypes = [I, I]
+    L.exl3cu_hyb_status.argtypes = [I, ctypes.POINTER(ctypes.c_uint)]
     L.exl3cu_hyb_gdn_smem_bytes.restype = S
     L.exl3cu_hyb_gdn.argtypes = [P, P, P, I, P, P, P, P, P, F, P, P, P, I, I, P, P]
     L.exl3cu_hyb_head.argtypes = [P, P, I, I, P, I, P, P, P, P]
     for n in ("exl3cu_hyb_embed", "exl3cu_hyb_rmsnorm", "exl3cu_hyb_swiglu", "exl3cu_hyb_attn_prep",
-              "exl3cu_hyb_attn", "exl3cu_hyb_gdn", "exl3cu_hyb_head"):
+              "exl3cu_hyb_attn", "exl3cu_hyb_gdn", "exl3cu_hyb_head", "exl3cu_hyb_status"):
         getattr(L, n).restype = ctypes.c_int
     L._hyb_declared = True
+
+
+def attn_splits(rows: int) -> int:
+    """Position splits per (row, head) of the attention kernel: many for decode steps (few rows, long
+    contexts), one when the rows alone fill the GPU."""
+    return 8 if rows <= 8 else (2 if rows <= 64 else 1)
 
 
 class StepMeta:
@@ -243,6 +252,9 @@ class HybridEngine:
                 d["cache"] = gi
                 gi += 1
         self.meta = StepMeta(torch, dev, R, slots, 8)
+        cap = max(r * attn_splits(r) for r in range(1, R + 1))
+        self.attn_part = torch.zeros(cap * cfg.heads * (cfg.head_dim + 2), dtype=f32, device=dev)
+        self.attn_tickets = torch.zeros(R * cfg.heads, dtype=torch.int32, device=dev)
         self.best = torch.zeros(8, dtype=torch.int64, device=dev)
         self.out_tokens = torch.zeros(8, dtype=torch.int32, device=dev)
         self.KV = KV
@@ -296,8 +308,10 @@ class HybridEngine:
                 check(L.exl3cu_hyb_attn_prep(_vp(qkv), rows, _vp(row_seq), _vp(row_pos), _vp(seq_slot),
                                              _vp(d["q_norm"]), _vp(d["k_norm"]), _vp(self.inv_freq), cfg.eps,
                                              _vp(kc), _vp(vc), self.max_len, self.slots, _vp(self.q), st))
+                sp = attn_splits(rows)
                 check(L.exl3cu_hyb_attn(_vp(self.q), rows, _vp(row_seq), _vp(row_pos), _vp(seq_slot), _vp(kc),
-                                        _vp(vc), self.max_len, self.slots, scale, _vp(self.mix), st))
+                                        _vp(vc), self.max_len, self.slots, scale, sp, _vp(self.attn_part),
+                                        self.attn_part.numel() * 4, _vp(self.attn_tickets), _vp(self.mix), st))
             else:
                 p = self.proj
                 outs = [p[:, 0:D], p[:, D:2 * D], p[:, 2 * D:3 * D], p[:, 3 * D:4 * D]]
