@@ -450,14 +450,18 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
     if (env && std::atoi(env) > 0) {
         S = std::min(16, std::atoi(env));
     } else {
-        // largest cluster size whose grid is one wave; else the largest that can run at all
+        // largest cluster size whose grid is one wave; else the largest that can run at all.
+        // EXL3CU_MUL1_CTAS_PER_SM (tuning experiments) caps the grid at that many CTAs per SM, leaving
+        // room for the next launch's CTAs to start under programmatic dependent launch.
+        const char * cap_env = std::getenv("EXL3CU_MUL1_CTAS_PER_SM");
+        const int cap = cap_env && std::atoi(cap_env) > 0 ? std::atoi(cap_env) * sms : 1 << 30;
         int feasible = 0;
         for (int cand = 16; cand >= 1; --cand) {
             if (cand > 1 && min_nchunks / cand < kMW) continue;
             const int cps = (max_nchunks + cand - 1) / cand;
             const Mul1Layout L = mul1_layout(int(bits), cps, max_rows, cand, NS);
             if (L.bytes > kMul1MaxSmem) break;  // fewer splits only grow the per-CTA range
-            const int fit = mul1_active_clusters(device, bits, cand, L.bytes);
+            const int fit = std::min(mul1_active_clusters(device, bits, cand, L.bytes), cap / cand);
             if (fit <= 0) continue;
             if (!feasible) feasible = cand;
             if (nunits <= fit) {
@@ -466,7 +470,6 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
             }
         }
         if (!S) S = feasible;
-        (void)sms;
     }
     if (S <= 0) return cudaErrorInvalidConfiguration;
     b.splits = S;
