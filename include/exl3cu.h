@@ -198,6 +198,15 @@ int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, si
 int exl3cu_mul_mat_host(exl3cu_weight * w, const void * h_x, int x_dtype, size_t rows, size_t x_row_stride,
                         float * h_y, size_t y_row_stride, int synchronize, void * stream);
 
+/* No counterpart in the reference.  Hint the GPU to bring the packed weights
+ * (and scales) of `count` handles (at most 21, one device) into L2, on
+ * `stream`: a one-warp kernel issuing bulk L2 prefetches, which waits for
+ * nothing and changes no data.  A decoder issues it on a side stream for the
+ * next layer's matrices while the current layer runs, so that the next
+ * launches read their weights from L2 (126 MB) and the HBM stream overlaps the
+ * dependency chain. */
+int exl3cu_prefetch_l2(size_t count, const exl3cu_weight * const * weights, void * stream);
+
 /* EXL3 get_rows (replaces ggml_exl3_get_rows, src/exl3-ggml.cpp:19-49; the
  * reference patch dispatches GET_ROWS on an EXL3 src0 to it,
  * patches/llama-exl3.patch:114-121): for each of `count` column ids (local to

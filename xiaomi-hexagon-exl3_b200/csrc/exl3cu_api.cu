@@ -861,6 +861,30 @@ int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, si
                   static_cast<cudaStream_t>(stream));
 }
 
+int exl3cu_prefetch_l2(size_t count, const exl3cu_weight * const * weights, void * stream) {
+    if (!count) return EXL3CU_OK;
+    if (!weights) return fail(EXL3CU_INVALID_ARGUMENT, "weights is NULL");
+    if (count * 3 > size_t(kPrefetchMax))
+        return fail(EXL3CU_INVALID_ARGUMENT, "at most %d weights per prefetch", kPrefetchMax / 3);
+    PrefetchList list{};
+    int dev = -1;
+    for (size_t i = 0; i < count; ++i) {
+        const exl3cu_weight * w = weights[i];
+        if (!w) return fail(EXL3CU_INVALID_ARGUMENT, "weight %zu is NULL", i);
+        if (dev >= 0 && w->device != dev) return fail(EXL3CU_INVALID_ARGUMENT, "weights on different devices");
+        dev = w->device;
+        list.ptr[list.count] = w->lsc;
+        list.bytes[list.count++] = w->nblocks * (w->k / 16) * 256u * w->bits;
+        list.ptr[list.count] = w->su;
+        list.bytes[list.count++] = (w->k * 2) & ~size_t(15);
+        list.ptr[list.count] = w->sv;
+        list.bytes[list.count++] = (w->nblocks * 256) & ~size_t(15);
+    }
+    DeviceGuard guard(dev);
+    CU_TRY(launch_prefetch_l2(list, static_cast<cudaStream_t>(stream)), "launching the L2 prefetch");
+    return EXL3CU_OK;
+}
+
 int exl3cu_get_rows(const exl3cu_weight * w, const int32_t * d_ids, size_t count, float * d_out,
                     size_t out_row_stride, void * stream) {
     if (!w) return fail(EXL3CU_INVALID_ARGUMENT, "weight handle is NULL");

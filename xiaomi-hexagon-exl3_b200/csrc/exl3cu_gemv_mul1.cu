@@ -153,10 +153,39 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
         __syncwarp();
     } else {
         // ---- consumers ----
-        pdl_wait_primary();  // activations may be written by the previous kernel
         const int g0 = c0 >> 3;
         const int ng = nch > 0 ? ((c1 - 1) >> 3) - g0 + 1 : 0;
         const int kbeg = c0 * 16, kend = c1 * 16;
+        constexpr int kItems = 4;
+        const int nitems = ng * rows;
+        // the input signs are constants: fetch the register-cached items' su before the wait
+        uint2 su_pre[kItems];
+#pragma unroll
+        for (int ii = 0; ii < kItems; ++ii) {
+            const int item = warp + ii * kMW;
+            su_pre[ii] = make_uint2(0, 0);
+            if (item < nitems) su_pre[ii] = *reinterpret_cast<const uint2 *>(P.su + (g0 + item / rows) * 128 + lane * 4);
+        }
+        pdl_wait_primary();  // activations may be written by the previous kernel
+        auto load_x = [&](int r, int kcol, float (&o)[4]) {
+            if (P.x_f16) {
+                const uint2 raw = *reinterpret_cast<const uint2 *>(static_cast<const __half *>(P.x) +
+                                                                   size_t(r) * P.x_stride + kcol);
+                const __half2 lo = bits_half2(raw.x), hi = bits_half2(raw.y);
+                o[0] = __low2float(lo); o[1] = __high2float(lo); o[2] = __low2float(hi); o[3] = __high2float(hi);
+            } else {
+                const float4 f = *reinterpret_cast<const float4 *>(static_cast<const float *>(P.x) +
+                                                                   size_t(r) * P.x_stride + kcol);
+                o[0] = f.x; o[1] = f.y; o[2] = f.z; o[3] = f.w;
+            }
+        };
+        auto apply_su = [&](uint2 sraw, float (&o)[4]) {
+            const __half2 s01 = bits_half2(sraw.x), s23 = bits_half2(sraw.y);
+            o[0] = __fmul_rn(o[0], __low2float(s01));
+            o[1] = __fmul_rn(o[1], __high2float(s01));
+            o[2] = __fmul_rn(o[2], __low2float(s23));
+            o[3] = __fmul_rn(o[3], __high2float(s23));
+        };
         auto load_xsu = [&](int r, int kcol, float (&o)[4]) {
             if (P.x_f16) {
                 const uint2 raw = *reinterpret_cast<const uint2 *>(static_cast<const __half *>(P.x) +
@@ -177,23 +206,37 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
         };
         // (1) the CTA's (group, row) items round robin over warps: xh = H128(x * su), the
         //     first kItems kept in registers, each group's max |xh| published
-        constexpr int kItems = 4;
         float v[kItems][4];
-        const int nitems = ng * rows;
-        auto rotate = [&](int item, float (&o)[4]) {
+        auto rotate_from = [&](int item, float (&o)[4]) {  // o already holds x * su
             const int gi = item / rows;
             const int r = item - gi * rows;
-            load_xsu(r, (g0 + gi) * 128 + lane * 4, o);
             h128_warp4(o);
             float m = fmaxf(fmaxf(fabsf(o[0]), fabsf(o[1])), fmaxf(fabsf(o[2]), fabsf(o[3])));
 #pragma unroll
             for (int sh = 16; sh; sh >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, sh));
             if (lane == 0) gmax[r * ng + gi] = m;
         };
+        auto rotate = [&](int item, float (&o)[4]) {
+            const int gi = item / rows;
+            const int r = item - gi * rows;
+            load_xsu(r, (g0 + gi) * 128 + lane * 4, o);
+            rotate_from(item, o);
+        };
 #pragma unroll
         for (int ii = 0; ii < kItems; ++ii) {
             const int item = warp + ii * kMW;
-            if (item < nitems) rotate(item, v[ii]);
+            if (item < nitems) {
+                const int gi = item / rows;
+                load_x(item - gi * rows, (g0 + gi) * 128 + lane * 4, v[ii]);
+            }
+        }
+#pragma unroll
+        for (int ii = 0; ii < kItems; ++ii) {
+            const int item = warp + ii * kMW;
+            if (item < nitems) {
+                apply_su(su_pre[ii], v[ii]);
+                rotate_from(item, v[ii]);
+            }
         }
         for (int item = warp + kItems * kMW; item < nitems; item += kMW) {
             float o[4];

@@ -158,6 +158,15 @@ cudaError_t launch_trellis_to_lsc(const uint16_t * trellis, size_t k, size_t n, 
 cudaError_t launch_lsc_decode(const uint32_t * lsc, size_t k, size_t nbc, unsigned bits, unsigned cb, uint16_t * out,
                               cudaStream_t st);
 cudaError_t launch_hadamard128(float * v, size_t count, cudaStream_t st);
+// Ranges (16-byte aligned start) to prefetch into L2.
+constexpr int kPrefetchMax = 64;
+struct PrefetchList {
+    const void * ptr[kPrefetchMax];
+    size_t bytes[kPrefetchMax];
+    int count;
+};
+cudaError_t launch_prefetch_l2(const PrefetchList & list, cudaStream_t st);
+
 // out: f32 rows, or fp16 rows (the bits exl3::reconstruct produces) with out_f16.
 cudaError_t launch_get_rows(const uint32_t * lsc, const uint16_t * suh, const uint16_t * svh, size_t k, size_t ncols,
                             unsigned bits, unsigned cb, const int32_t * ids, size_t count, void * out,

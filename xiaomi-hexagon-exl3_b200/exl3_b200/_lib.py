@@ -26,7 +26,7 @@ EXPORTS = (
     "exl3cu_weight_decode_inner", "exl3cu_mul_mat", "exl3cu_mul_mat_workspace_bytes", "exl3cu_mul_mat_ws",
     "exl3cu_mul_mat_host", "exl3cu_mul_mat_noalloc", "exl3cu_mul_mat_batch",
     "exl3cu_device_status", "exl3cu_gemm_config", "exl3cu_pack_ragged", "exl3cu_mul_mat_ragged",
-    "exl3cu_mul_mat_sequence", "exl3cu_get_rows", "exl3cu_get_rows_host",
+    "exl3cu_mul_mat_sequence", "exl3cu_get_rows", "exl3cu_get_rows_host", "exl3cu_prefetch_l2",
     "exl3cu_model_open", "exl3cu_model_free", "exl3cu_model_info", "exl3cu_model_matrix_count",
     "exl3cu_model_matrix", "exl3cu_model_find_matrix", "exl3cu_model_head", "exl3cu_model_tensor",
     "exl3cu_model_find_tensor", "exl3cu_model_embedding", "exl3cu_model_embed",
@@ -74,6 +74,7 @@ def _declare(L):
     L.exl3cu_mul_mat_ws.argtypes = [_vp, _vp, _c.c_int, _sz, _sz, _vp, _sz, _vp, _sz, _vp]
     L.exl3cu_mul_mat_host.argtypes = [_vp, _vp, _c.c_int, _sz, _sz, _vp, _sz, _c.c_int, _vp]
     L.exl3cu_get_rows.argtypes = [_vp, _vp, _sz, _vp, _sz, _vp]
+    L.exl3cu_prefetch_l2.argtypes = [_sz, _c.POINTER(_vp), _vp]
     L.exl3cu_get_rows_host.argtypes = [_vp, _vp, _sz, _vp, _sz, _c.c_int, _vp]
     L.exl3cu_mul_mat_noalloc.argtypes = [_vp, _vp, _c.c_int, _sz, _sz, _vp, _sz, _vp]
     L.exl3cu_device_status.argtypes = [_c.c_int, _c.POINTER(_c.c_uint), _c.c_int]

@@ -25,6 +25,7 @@ recipe as the operator benchmarks), i.e. random weights in EXL3 form.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -259,6 +260,14 @@ class HybridEngine:
         self.out_tokens = torch.zeros(8, dtype=torch.int32, device=dev)
         self.KV = KV
         self._batch_args = {}
+        # L2 prefetch of layer i+1's weights while layer i runs (side stream, joined per step)
+        self.prefetch = os.environ.get("EXL3_HYB_PREFETCH", "0") != "0"  # measured: no gain (see DESIGN)
+        self._pf_args = []
+        for d in self.layers:
+            ws = list(d["mats"].values())
+            self._pf_args.append((len(ws), (ctypes.c_void_p * len(ws))(*[w.handle.value for w in ws])))
+        self._pf_stream = torch.cuda.Stream(device=dev)
+        self._pf_events = [torch.cuda.Event() for _ in range(len(self.layers) + 1)]
 
     # -- slot management --------------------------------------------------------------------------
     def reset_slot(self, slot: int):
@@ -290,11 +299,23 @@ class HybridEngine:
         m = self.meta
         tokens, row_seq, row_pos = m.view("tokens"), m.view("row_seq"), m.view("row_pos")
         row_offsets, seq_slot, logit_rows = m.view("row_offsets"), m.view("seq_slot"), m.view("logit_rows")
+        main = stream or torch.cuda.current_stream()
+        pf = self.prefetch and rows <= 4  # weight-streaming steps only; larger steps are compute-bound
+        if pf:
+            n0, a0 = self._pf_args[0]
+            self._pf_events[0].record(main)
+            self._pf_stream.wait_event(self._pf_events[0])
+            check(L.exl3cu_prefetch_l2(n0, a0, ctypes.c_void_p(self._pf_stream.cuda_stream)))
         check(L.exl3cu_hyb_embed(_vp(self.embed), cfg.vocab, _vp(tokens), rows, H, _vp(self.h), st))
         delta = None
         scale = 1.0 / float(np.sqrt(cfg.head_dim))
-        for d in self.layers:
+        for li, d in enumerate(self.layers):
             mats = d["mats"]
+            if pf and li + 1 < len(self.layers):
+                n1, a1 = self._pf_args[li + 1]
+                self._pf_events[li + 1].record(main)
+                self._pf_stream.wait_event(self._pf_events[li + 1])
+                check(L.exl3cu_prefetch_l2(n1, a1, ctypes.c_void_p(self._pf_stream.cuda_stream)))
             check(L.exl3cu_hyb_rmsnorm(_vp(self.h), _vp(delta) if delta is not None else None, H, _vp(d["in_norm"]),
                                        cfg.eps, rows, H, _vp(self.xn), st))
             if d["kind"] == "full":
@@ -332,6 +353,10 @@ class HybridEngine:
                                    st))
         check(L.exl3cu_hyb_head(_vp(self.xn), _vp(logit_rows), nout, H, _vp(self.embed), cfg.vocab, None,
                                 _vp(self.best), _vp(self.out_tokens), st))
+        if pf:  # join the prefetch stream (required inside a capture; cheap otherwise)
+            ev = self._pf_events[-1]
+            ev.record(self._pf_stream)
+            main.wait_event(ev)
 
     def head_logits(self, nout: int, stream=None):
         """Logits of the last step's logit rows (f32 [nout, vocab]); recomputes the head only."""
