@@ -408,7 +408,8 @@ def run_model_measure(torch, dist, local, rank, world, new_tokens=256, single_pr
     run_requests(eng, warm, chunk=512, stream=stream, graphs=graphs)  # first-time shapes and captures
     torch.cuda.synchronize(dev)
     s_ev.record(stream)
-    steps, rows = run_requests(eng, reqs, chunk=512, stream=stream, graphs=graphs)
+    rstats = {}
+    steps, rows = run_requests(eng, reqs, chunk=512, stream=stream, graphs=graphs, stats=rstats)
     e_ev.record(stream)
     e_ev.synchronize()
     ragged_ms = s_ev.elapsed_time(e_ev)
@@ -444,6 +445,7 @@ def run_model_measure(torch, dist, local, rank, world, new_tokens=256, single_pr
         "ragged8_tok_s": round(gen_total / (ragged_ms_max * 1e-3), 1),
         "ragged8": {"requests_per_gpu": 8, "prompt_tokens": [int(x) for x in lens], "new_tokens": new_tokens,
                     "steps": steps, "rows": rows, "ms": round(ragged_ms_max, 1),
+                    "by_step_kind_host_ms": {k: (round(v, 1) if isinstance(v, float) else v) for k, v in rstats.items()},
                     "timing": "host scheduler loop with H2D metadata / D2H tokens per step; CUDA events"},
         "parallelism": f"dp{world} replicas (weights replicated, requests per GPU)",
         "prompt_tokens_single": single_prompt,

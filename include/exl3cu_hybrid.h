@@ -80,8 +80,8 @@ int exl3cu_hyb_gdn(const float * d_qkvz, const uint16_t * d_xn, const uint16_t *
 int exl3cu_hyb_head(const uint16_t * d_xn, const int32_t * d_rows, int nout, int hidden, const uint16_t * d_embed,
                     int vocab, float * d_logits, unsigned long long * d_best, int32_t * d_tokens, void * stream);
 
-/* Sticky error bits of these kernels on the current device (bit 0: the
- * delta-rule state copy never arrived).  Synchronises the device. */
+/* Sticky error bits of these kernels on the current device (reserved: the
+ * current kernels wait on nothing and raise none).  Synchronises the device. */
 int exl3cu_hyb_status(int clear, unsigned * status);
 
 #ifdef __cplusplus

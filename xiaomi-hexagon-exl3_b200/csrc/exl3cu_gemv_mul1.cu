@@ -367,18 +367,22 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
     cluster.sync();
     if (split == 0 && warp < kMW) {
         const int elems = rows * 128;
+        if (S > 1) {
+            // every consumer thread sums a few elements over the ranks (in rank order), in place
+            for (int e = threadIdx.x; e < elems; e += kMW * 32) {
+                float a = part[e];
+                for (int rk = 1; rk < S; ++rk) a = __fadd_rn(a, slots[size_t(rk - 1) * elems + e]);
+                part[e] = a;
+            }
+            consumer_sync();
+        }
+        const uint2 sraw = *reinterpret_cast<const uint2 *>(P.sv + nb * 128 + lane * 4);
+        const __half2 s01 = bits_half2(sraw.x), s23 = bits_half2(sraw.y);
         for (int r = warp; r < rows; r += kMW) {
             float v[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int e = r * 128 + lane * 4 + q;
-                float a = part[e];
-                for (int rk = 1; rk < S; ++rk) a = __fadd_rn(a, slots[size_t(rk - 1) * elems + e]);
-                v[q] = a;
-            }
+            for (int q = 0; q < 4; ++q) v[q] = part[r * 128 + lane * 4 + q];
             h128_warp4(v);
-            const uint2 sraw = *reinterpret_cast<const uint2 *>(P.sv + nb * 128 + lane * 4);
-            const __half2 s01 = bits_half2(sraw.x), s23 = bits_half2(sraw.y);
             float4 o;
             o.x = __fmul_rn(v[0], __low2float(s01));
             o.y = __fmul_rn(v[1], __high2float(s01));

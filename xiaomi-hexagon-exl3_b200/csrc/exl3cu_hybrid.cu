@@ -308,27 +308,39 @@ k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const
 }
 
 // Gated delta rule for one (head, step sequence): the sequence's rows in
-// order.  256 threads; the head's 128 x 128 fp32 state lives in shared memory
-// for the CTA's lifetime: one bulk copy brings it in while the first row's
-// convolution and gate projections run, one bulk copy stores it back.
-// Thread t: v column j = t & 127, k half = t >> 7.
+// order, in tiles of kGdnTile rows.  256 threads; thread t owns column
+// j = t & 127 of the head's 128 x 128 fp32 state for k rows [64 (t >> 7),
+// +64): 64 registers, loaded from and stored to HBM coalesced (for each k
+// row the CTA touches 128 consecutive floats).  Per tile:
+//   A (rows in parallel): the tile's conv inputs staged in shared memory,
+//     causal conv + SiLU of the head's q, k, v channels, L2 norms (q also x
+//     1/sqrt(128)), k.q, the gates a = x.W_a, b = x.W_b -> alpha =
+//     exp(-exp(A_log) softplus(a + dt_bias)), beta = sigmoid(b);
+//   B (rows in order, the only sequential part, one barrier per row): S^T k
+//     and S^T q, u = beta (v - alpha S^T k), o = alpha S^T q + (k.q) u,
+//     S = alpha S + k u^T;
+//   C (rows in parallel): RMSNorm(o) * norm_w * SiLU(z) -> fp16 out.
+// The conv state (last three inputs per channel) is read as it was before the
+// step and rewritten at the end.
 constexpr int kGdnThreads = 256;
-constexpr uint32_t kStateBytes = kHD * kHD * sizeof(float);
+constexpr int kGdnTile = 16;
+constexpr int kGdnKHalf = kHD / 2;
 
-static __device__ unsigned g_hyb_status;  // kStatusWaitTimeout when the state copy never arrived
+static __device__ unsigned g_hyb_status;  // reserved: sticky error bits of these kernels (none raised today)
 
-__device__ __forceinline__ void bulk_s2g(void * dst_gmem, const void * src_smem, uint32_t bytes) {
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_gmem),
-                 "r"(smem_addr(src_smem)), "r"(bytes)
-                 : "memory");
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
+// Shared-memory layout of k_gdn (floats unless noted).
+struct GdnSmem {
+    static constexpr int Q = 0;                               // [T][128] conv+norm q
+    static constexpr int K = Q + kGdnTile * kHD;              // [T][128] k
+    static constexpr int V = K + kGdnTile * kHD;              // [T][128] v
+    static constexpr int O = V + kGdnTile * kHD;              // [T][128] o
+    static constexpr int RED = O + kGdnTile * kHD;            // [2 buffers][4][128]
+    static constexpr int CW = RED + 2 * 4 * kHD;              // [384][4] conv weights of the head
+    static constexpr int GATE = CW + 3 * kHD * kConvW;        // [T][4]: alpha, beta, k.q
+    static constexpr int CX = GATE + kGdnTile * 4;            // [T+3][384] conv inputs of the tile
+    static constexpr int WAB = CX + (kGdnTile + kConvW - 1) * 3 * kHD;  // fp16 [2][H] gate rows (H <= 8192)
+    static constexpr int floats_without_wab = WAB;
+};
 
 __global__ void __launch_bounds__(kGdnThreads)
 k_gdn(const float * __restrict__ qkvz, const __half * __restrict__ xn, const __half * __restrict__ wab, int H,
@@ -337,13 +349,15 @@ k_gdn(const float * __restrict__ qkvz, const __half * __restrict__ xn, const __h
       const int32_t * __restrict__ row_offsets, const int32_t * __restrict__ seq_slot, int n_slots,
       __half * __restrict__ out) {
     extern __shared__ __align__(128) float sm[];
-    float * St = sm;                          // [128 k][128 v]
-    float * cq = St + kHD * kHD;              // conv outputs q, k, v of the current row
-    float * ck = cq + kHD;
-    float * cv = ck + kHD;
-    float * red = cv + kHD;                   // [4][128]: k-half sums of S^T k and S^T q; then o
-    float * scal = red + 4 * kHD;             // [32]: per-warp gate sums, alpha, beta, k.q
-    uint64_t * bar = reinterpret_cast<uint64_t *>(scal + 32);
+    float * tq = sm + GdnSmem::Q;
+    float * tk = sm + GdnSmem::K;
+    float * tv = sm + GdnSmem::V;
+    float * to = sm + GdnSmem::O;
+    float * red = sm + GdnSmem::RED;
+    float * cw = sm + GdnSmem::CW;
+    float * gate = sm + GdnSmem::GATE;
+    float * cx = sm + GdnSmem::CX;
+    __half * wab_s = reinterpret_cast<__half *>(sm + GdnSmem::WAB);
     pdl_trigger();
     pdl_wait_primary();
     const int h = blockIdx.x, s = blockIdx.y;
@@ -351,122 +365,178 @@ k_gdn(const float * __restrict__ qkvz, const __half * __restrict__ xn, const __h
     if (slot < 0 || slot >= n_slots) return;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int j = t & (kHD - 1), half = t >> 7;
+    const int i0 = half * kGdnKHalf;
     float * Sg = S + (size_t(slot) * kNH + h) * kHD * kHD;
     const int r0 = row_offsets[s], r1 = row_offsets[s + 1];
     if (r1 <= r0) return;
-    if (t == 0) {
-        mbar_init(bar, 1);
-        mbar_init_fence();
-        mbar_arrive_expect_tx(bar, kStateBytes);
-        bulk_g2s(St, Sg, kStateBytes, bar);
-    }
-    bool state_ready = false, ok = true;
+    float Sr[kGdnKHalf];  // S[i0 + i][j]
+#pragma unroll
+    for (int i = 0; i < kGdnKHalf; ++i) Sr[i] = Sg[(i0 + i) * kHD + j];
     constexpr int QKVZ = 4 * kNH * kHD;
     constexpr int CH = 3 * kNH * kHD;  // convolved channels (q, k, v)
+    constexpr int C3 = 3 * kHD;
+    // the head's conv weights and gate rows, once
+    for (int c = t; c < C3; c += kGdnThreads) {
+        const int ch = (c / kHD) * kNH * kHD + h * kHD + c % kHD;
+#pragma unroll
+        for (int w = 0; w < kConvW; ++w) cw[c * kConvW + w] = conv_w[size_t(ch) * kConvW + w];
+    }
+    for (int i = t; i < H; i += kGdnThreads) {
+        wab_s[i] = wab[size_t(h) * H + i];
+        wab_s[H + i] = wab[size_t(kNH + h) * H + i];
+    }
     const float A = -expf(A_log[h]);
+    const float dtb = dt_bias[h];
     const float qscale = rsqrtf(float(kHD));
-    for (int r = r0; r < r1; ++r) {
-        // (1) causal conv + SiLU on this head's 384 channels; the conv state keeps the last 3 inputs
-        for (int c = t; c < 3 * kHD; c += kGdnThreads) {
-            const int part = c / kHD, d = c % kHD;                // 0 q, 1 k, 2 v
-            const int ch = part * kNH * kHD + h * kHD + d;        // channel in [0, CH)
-            const float x = qkvz[size_t(r) * QKVZ + ch];
-            float * st = conv_state + (size_t(slot) * CH + ch) * (kConvW - 1);
-            const float * wc = conv_w + size_t(ch) * kConvW;
-            float acc = st[0] * wc[0];
-            acc = fmaf(st[1], wc[1], acc);
-            acc = fmaf(st[2], wc[2], acc);
-            acc = fmaf(x, wc[3], acc);
-            st[0] = st[1];
-            st[1] = st[2];
-            st[2] = x;
-            (part == 0 ? cq : part == 1 ? ck : cv)[d] = silu(acc);
-        }
-        // (2) the gates' projections a = x . W_a[h], b = x . W_b[h] (fp16 x and weights, fp32 sums)
-        float pa = 0.f, pb = 0.f;
-        for (int i = t; i < H; i += kGdnThreads) {
-            const float x = __half2float(xn[size_t(r) * H + i]);
-            pa = fmaf(x, __half2float(wab[size_t(h) * H + i]), pa);
-            pb = fmaf(x, __half2float(wab[size_t(kNH + h) * H + i]), pb);
-        }
-        pa = warp_sum(pa);
-        pb = warp_sum(pb);
-        if (lane == 0) {
-            scal[warp] = pa;
-            scal[8 + warp] = pb;
-        }
-        __syncthreads();  // conv outputs and gate sums complete
-        // (3) L2 norms of q and k (warps 0, 1), gates (warp 2, lane 0)
-        if (warp < 2) {
-            float * vec = warp == 0 ? cq : ck;
-            float ss = 0.f;
-            for (int d = lane; d < kHD; d += 32) ss = fmaf(vec[d], vec[d], ss);
-            const float inv = rsqrtf(warp_sum(ss) + 1e-6f) * (warp == 0 ? qscale : 1.0f);
-            for (int d = lane; d < kHD; d += 32) vec[d] *= inv;
-        } else if (t == 64) {
-            float a = 0.f, b = 0.f;
-            for (int w = 0; w < 8; ++w) {
-                a += scal[w];
-                b += scal[8 + w];
-            }
-            scal[16] = expf(A * softplus(a + dt_bias[h]));  // alpha
-            scal[17] = 1.0f / (1.0f + expf(-b));              // beta
-        }
-        if (!state_ready) {
-            ok = mbar_wait(bar, 0);
-            if (!ok && t == 0) atomicOr(&g_hyb_status, kStatusWaitTimeout);
-            state_ready = true;
-        }
-        __syncthreads();
-        if (warp == 0) {  // k . q after normalisation (every thread reads it below)
-            float kq = 0.f;
-            for (int d = lane; d < kHD; d += 32) kq = fmaf(ck[d], cq[d], kq);
-            kq = warp_sum(kq);
-            if (lane == 0) scal[18] = kq;
-        }
-        const float alpha = scal[16], beta = scal[17];
-        // (4) a_j = sum_i S[i][j] k[i], c_j = sum_i S[i][j] q[i] over this thread's k half
-        float ak = 0.f, cqs = 0.f;
-        const int i0 = half * (kHD / 2);
-#pragma unroll 16
-        for (int i = i0; i < i0 + kHD / 2; ++i) {
-            const float sv = St[i * kHD + j];
-            ak = fmaf(sv, ck[i], ak);
-            cqs = fmaf(sv, cq[i], cqs);
-        }
-        red[half * kHD + j] = ak;
-        red[2 * kHD + half * kHD + j] = cqs;
-        __syncthreads();
-        const float kq = scal[18];
-        const float a_j = red[j] + red[kHD + j];
-        const float c_j = red[2 * kHD + j] + red[3 * kHD + j];
-        const float u_j = beta * (cv[j] - alpha * a_j);
-        const float o_j = fmaf(kq, u_j, alpha * c_j);
-        // (5) S = alpha S + k u^T on this thread's half
-#pragma unroll 16
-        for (int i = i0; i < i0 + kHD / 2; ++i) St[i * kHD + j] = fmaf(ck[i], u_j, alpha * St[i * kHD + j]);
-        __syncthreads();  // everyone has read red
-        if (half == 0) red[j] = o_j;
-        __syncthreads();
-        // (6) RMSNorm of o over the head, times norm_w, gated by SiLU(z)
-        if (warp == 0) {
-            float ss = 0.f;
-            for (int d = lane; d < kHD; d += 32) ss = fmaf(red[d], red[d], ss);
-            const float inv = rsqrtf(warp_sum(ss) / float(kHD) + eps);
-            for (int d = lane; d < kHD; d += 32) {
-                const float z = qkvz[size_t(r) * QKVZ + 3 * kNH * kHD + h * kHD + d];
-                out[size_t(r) * kNH * kHD + h * kHD + d] = __float2half_rn(red[d] * inv * norm_w[d] * silu(z));
-            }
-        }
-        __syncthreads();  // next row overwrites cq, ck, cv, red, scal
-    }
-    if (!ok) return;  // the state never arrived: leave the stored state untouched
-    fence_proxy_async_smem();
+    int rb = 0;  // reduction buffer of the current row
     __syncthreads();
-    if (t == 0) {
-        bulk_s2g(Sg, St, kStateBytes);
-        bulk_wait_all();
+    for (int tr0 = r0; tr0 < r1; tr0 += kGdnTile) {
+        const int nt = min(kGdnTile, r1 - tr0);
+        // ---- A: stage the conv inputs x[tr0-3 .. tr0+nt-1] of the head's 384 channels ----
+        // (rows before the sequence's first come from the conv state)
+        for (int e = t; e < (nt + kConvW - 1) * (C3 / 4); e += kGdnThreads) {
+            const int rr = e / (C3 / 4), c4 = (e % (C3 / 4)) * 4;  // row tr0 - 3 + rr, channels c4..c4+3
+            const int ri = tr0 - (kConvW - 1) + rr;
+            const int part = c4 / kHD, d = c4 % kHD;
+            const int ch = part * kNH * kHD + h * kHD + d;
+            float4 x;
+            if (ri >= r0) {
+                x = *reinterpret_cast<const float4 *>(qkvz + size_t(ri) * QKVZ + ch);
+            } else {
+                const float * st = conv_state + (size_t(slot) * CH + ch) * (kConvW - 1) + (ri - r0 + kConvW - 1);
+                x = make_float4(st[0], st[kConvW - 1], st[2 * (kConvW - 1)], st[3 * (kConvW - 1)]);
+            }
+            *reinterpret_cast<float4 *>(cx + rr * C3 + c4) = x;
+        }
+        __syncthreads();
+        // conv + SiLU for every (row, channel) of the tile, from shared memory
+        for (int e = t; e < nt * C3; e += kGdnThreads) {
+            const int rr = e / C3, c = e % C3;
+            float acc = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConvW; ++w) acc = fmaf(cx[(rr + w) * C3 + c], cw[c * kConvW + w], acc);
+            const int part = c / kHD, d = c % kHD;
+            (part == 0 ? tq : part == 1 ? tk : tv)[rr * kHD + d] = silu(acc);
+        }
+        // gate projections: warp per row, 16-byte loads of the row in flight together
+        for (int rr = warp; rr < nt; rr += kGdnThreads / 32) {
+            const __half * xr = xn + size_t(tr0 + rr) * H;
+            float pa = 0.f, pb = 0.f;
+            for (int ib0 = lane * 8; ib0 < H; ib0 += 32 * 8 * 4) {
+                uint4 raw[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    raw[u] = ib0 + u * 256 < H ? *reinterpret_cast<const uint4 *>(xr + ib0 + u * 256)
+                                               : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int ib = ib0 + u * 256;
+                    if (ib >= H) break;
+                    const __half * xh = reinterpret_cast<const __half *>(&raw[u]);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const float x = __half2float(xh[q]);
+                        pa = fmaf(x, __half2float(wab_s[ib + q]), pa);
+                        pb = fmaf(x, __half2float(wab_s[H + ib + q]), pb);
+                    }
+                }
+            }
+            pa = warp_sum(pa);
+            pb = warp_sum(pb);
+            if (lane == 0) {
+                gate[rr * 4 + 0] = expf(A * softplus(pa + dtb));  // alpha
+                gate[rr * 4 + 1] = 1.0f / (1.0f + expf(-pb));     // beta
+            }
+        }
+        __syncthreads();
+        // L2 norms and k.q: warp per row
+        for (int rr = warp; rr < nt; rr += kGdnThreads / 32) {
+            float * qv = tq + rr * kHD;
+            float * kv = tk + rr * kHD;
+            float sq = 0.f, sk = 0.f;
+            for (int d = lane; d < kHD; d += 32) {
+                sq = fmaf(qv[d], qv[d], sq);
+                sk = fmaf(kv[d], kv[d], sk);
+            }
+            const float iq = rsqrtf(warp_sum(sq) + 1e-6f) * qscale;
+            const float ik = rsqrtf(warp_sum(sk) + 1e-6f);
+            float kq = 0.f;
+            for (int d = lane; d < kHD; d += 32) {
+                qv[d] *= iq;
+                kv[d] *= ik;
+                kq = fmaf(kv[d], qv[d], kq);
+            }
+            kq = warp_sum(kq);
+            if (lane == 0) gate[rr * 4 + 2] = kq;
+        }
+        __syncthreads();
+        // ---- B: the recurrence, row by row (state in registers) ----
+        for (int rr = 0; rr < nt; ++rr) {
+            const float4 * kv4 = reinterpret_cast<const float4 *>(tk + rr * kHD + i0);
+            const float4 * qv4 = reinterpret_cast<const float4 *>(tq + rr * kHD + i0);
+            float ak = 0.f, cqs = 0.f;
+#pragma unroll
+            for (int i = 0; i < kGdnKHalf / 4; ++i) {
+                const float4 kk = kv4[i], qq = qv4[i];
+                ak = fmaf(Sr[4 * i], kk.x, ak);
+                ak = fmaf(Sr[4 * i + 1], kk.y, ak);
+                ak = fmaf(Sr[4 * i + 2], kk.z, ak);
+                ak = fmaf(Sr[4 * i + 3], kk.w, ak);
+                cqs = fmaf(Sr[4 * i], qq.x, cqs);
+                cqs = fmaf(Sr[4 * i + 1], qq.y, cqs);
+                cqs = fmaf(Sr[4 * i + 2], qq.z, cqs);
+                cqs = fmaf(Sr[4 * i + 3], qq.w, cqs);
+            }
+            float * rd = red + rb * 4 * kHD;
+            rd[half * kHD + j] = ak;
+            rd[2 * kHD + half * kHD + j] = cqs;
+            __syncthreads();
+            const float alpha = gate[rr * 4 + 0], beta = gate[rr * 4 + 1], kq = gate[rr * 4 + 2];
+            const float a_j = rd[j] + rd[kHD + j];
+            const float c_j = rd[2 * kHD + j] + rd[3 * kHD + j];
+            const float u_j = beta * (tv[rr * kHD + j] - alpha * a_j);
+            if (half == 0) to[rr * kHD + j] = fmaf(kq, u_j, alpha * c_j);
+#pragma unroll
+            for (int i = 0; i < kGdnKHalf / 4; ++i) {
+                const float4 kk = kv4[i];
+                Sr[4 * i] = fmaf(kk.x, u_j, alpha * Sr[4 * i]);
+                Sr[4 * i + 1] = fmaf(kk.y, u_j, alpha * Sr[4 * i + 1]);
+                Sr[4 * i + 2] = fmaf(kk.z, u_j, alpha * Sr[4 * i + 2]);
+                Sr[4 * i + 3] = fmaf(kk.w, u_j, alpha * Sr[4 * i + 3]);
+            }
+            rb ^= 1;  // the next row writes the other buffer: no second barrier needed
+        }
+        __syncthreads();  // every row's o is in `to`
+        // ---- C: gated RMSNorm of o, warp per row ----
+        for (int rr = warp; rr < nt; rr += kGdnThreads / 32) {
+            const float * ov = to + rr * kHD;
+            float ss = 0.f;
+            for (int d = lane; d < kHD; d += 32) ss = fmaf(ov[d], ov[d], ss);
+            const float inv = rsqrtf(warp_sum(ss) / float(kHD) + eps);
+            const size_t r = size_t(tr0 + rr);
+            for (int d = lane; d < kHD; d += 32) {
+                const float z = qkvz[r * QKVZ + 3 * kNH * kHD + h * kHD + d];
+                out[r * kNH * kHD + h * kHD + d] = __float2half_rn(ov[d] * inv * norm_w[d] * silu(z));
+            }
+        }
+        __syncthreads();  // the next tile overwrites tq, tk, tv, to, gate, cx
     }
+    // the conv state: the last three inputs of the sequence so far
+    const int n = r1 - r0;
+    for (int c = t; c < C3; c += kGdnThreads) {
+        const int ch = (c / kHD) * kNH * kHD + h * kHD + c % kHD;
+        float * st = conv_state + (size_t(slot) * CH + ch) * (kConvW - 1);
+        float nv[kConvW - 1];
+#pragma unroll
+        for (int w = 0; w < kConvW - 1; ++w) {
+            const int ri = r1 - (kConvW - 1) + w;  // input index for new slot w
+            nv[w] = ri >= r0 ? qkvz[size_t(ri) * QKVZ + ch] : st[w + n];
+        }
+#pragma unroll
+        for (int w = 0; w < kConvW - 1; ++w) st[w] = nv[w];
+    }
+#pragma unroll
+    for (int i = 0; i < kGdnKHalf; ++i) Sg[(i0 + i) * kHD + j] = Sr[i];
 }
 
 // Order-preserving key of a float (larger float, larger key).
@@ -669,9 +739,12 @@ int exl3cu_hyb_attn(const float * d_q, int rows, const int32_t * d_row_seq, cons
                       reinterpret_cast<__half *>(d_out));
 }
 
-size_t exl3cu_hyb_gdn_smem_bytes(void) {
-    return size_t(kHD * kHD + 3 * kHD + 4 * kHD + 32) * sizeof(float) + 16;  // + the state copy's mbarrier
+size_t exl3cu_hyb_gdn_smem_bytes_for(int hidden) {
+    // fixed part and the fp16 gate rows (2 x hidden)
+    return size_t(GdnSmem::floats_without_wab) * sizeof(float) + size_t(2 * hidden) * 2;
 }
+
+size_t exl3cu_hyb_gdn_smem_bytes(void) { return exl3cu_hyb_gdn_smem_bytes_for(8192); }
 
 int exl3cu_hyb_gdn(const float * d_qkvz, const uint16_t * d_xn, const uint16_t * d_wab, int hidden,
                    const float * d_conv_w, float * d_conv_state, const float * d_A_log, const float * d_dt_bias,
@@ -682,9 +755,10 @@ int exl3cu_hyb_gdn(const float * d_qkvz, const uint16_t * d_xn, const uint16_t *
         n_slots <= 0)
         return bad("gdn: bad arguments");
     if (reinterpret_cast<uintptr_t>(d_state) % 16) return bad("gdn: state must be 16-byte aligned");
+    if (hidden > 8192 || hidden % 8) return bad("gdn: hidden must be a multiple of 8 up to 8192");
     if (!n_seq) return EXL3CU_OK;
-    const size_t smem = exl3cu_hyb_gdn_smem_bytes();
-    if (!set_smem_attr_once(reinterpret_cast<const void *>(k_gdn), int(smem), g_gdn_attr))
+    const size_t smem = exl3cu_hyb_gdn_smem_bytes_for(hidden);
+    if (!set_smem_attr_once(reinterpret_cast<const void *>(k_gdn), int(exl3cu_hyb_gdn_smem_bytes()), g_gdn_attr))
         return status_of(cudaGetLastError());
     return launch_pdl(k_gdn, dim3(kNH, unsigned(n_seq)), dim3(kGdnThreads), smem, stream, d_qkvz,
                       reinterpret_cast<const __half *>(d_xn), reinterpret_cast<const __half *>(d_wab), hidden,

@@ -431,7 +431,8 @@ def plan_step(active, waiting, slots_free, max_rows: int, chunk: int):
     return seqs, tokens, row_seq, row_pos, offsets, slots_, logit_rows, logit_seq
 
 
-def run_requests(engine: HybridEngine, requests, chunk: int = 512, stream=None, graphs: dict | None = None):
+def run_requests(engine: HybridEngine, requests, chunk: int = 512, stream=None, graphs: dict | None = None,
+                 stats: dict | None = None):
     """Serve `requests` to completion with continuous admission; returns (steps, rows_total).
 
     Pure decode steps of n sequences replay a captured step (one per n, kept in `graphs` when given,
@@ -445,7 +446,10 @@ def run_requests(engine: HybridEngine, requests, chunk: int = 512, stream=None, 
     active = []
     free = list(range(engine.slots))
     steps = rows_total = 0
+    import time
+
     while waiting or active:
+        t0 = time.perf_counter()
         seqs, tokens, row_seq, row_pos, offsets, slots_, logit_rows, logit_seq = plan_step(
             active, waiting, free, engine.max_rows, chunk)
         for s, rq in enumerate(seqs):
@@ -477,6 +481,11 @@ def run_requests(engine: HybridEngine, requests, chunk: int = 512, stream=None, 
                 free.append(rq.slot)
         steps += 1
         rows_total += len(tokens)
+        if stats is not None:
+            kind = "decode" if pure_decode else "prefill"
+            stats[kind + "_steps"] = stats.get(kind + "_steps", 0) + 1
+            stats[kind + "_rows"] = stats.get(kind + "_rows", 0) + n
+            stats[kind + "_ms"] = stats.get(kind + "_ms", 0.0) + 1e3 * (time.perf_counter() - t0)
     return steps, rows_total
 
 
