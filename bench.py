@@ -331,7 +331,8 @@ def run_model_measure(torch, dist, local, rank, world, new_tokens=256, single_pr
             metadata, the captured step, D2H of the next token, host loop (events around the loop);
     ragged8: 8 requests, prompts U[32,1024] seeded, `new_tokens` greedy tokens each, continuous
             admission (decode rows of running requests + 512-row prefill chunks of the next one per
-            step), host scheduler in the loop; tokens/s = generated tokens / elapsed."""
+            step), host scheduler in the loop; runs of pure decode steps with nothing to admit go
+            to the device as multi-step blocks; tokens/s = generated tokens / elapsed."""
     from exl3_b200.hybrid import DecodeGraph, HybridConfig, HybridEngine, Request, run_requests, _StepGraph
 
     dev = f"cuda:{local}"
@@ -404,8 +405,10 @@ def run_model_measure(torch, dist, local, rank, world, new_tokens=256, single_pr
     lens = rng.integers(32, 1025, 8)
     reqs = [Request(rng.integers(0, cfg.vocab, int(L)).astype(np.int32), max_new=new_tokens) for L in lens]
     graphs = {}
-    warm = [Request(rng.integers(0, cfg.vocab, 40).astype(np.int32), max_new=3) for _ in range(8)]
-    run_requests(eng, warm, chunk=512, stream=stream, graphs=graphs)  # first-time shapes and captures
+    # warm-up: first-time shapes and captures (eager steps, per-size step graphs, the 8-row multi-step
+    # decode block), as a server does at start-up
+    warm = [Request(rng.integers(0, cfg.vocab, 40).astype(np.int32), max_new=6) for _ in range(8)]
+    run_requests(eng, warm, chunk=512, stream=stream, graphs=graphs)
     torch.cuda.synchronize(dev)
     s_ev.record(stream)
     rstats = {}

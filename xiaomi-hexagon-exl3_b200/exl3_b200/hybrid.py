@@ -432,24 +432,69 @@ def plan_step(active, waiting, slots_free, max_rows: int, chunk: int):
 
 
 def run_requests(engine: HybridEngine, requests, chunk: int = 512, stream=None, graphs: dict | None = None,
-                 stats: dict | None = None):
+                 stats: dict | None = None, multi_step: bool = True):
     """Serve `requests` to completion with continuous admission; returns (steps, rows_total).
 
     Pure decode steps of n sequences replay a captured step (one per n, kept in `graphs` when given,
     captured after the first eager step of that shape); steps with prefill rows run eagerly.  Every
-    step copies its metadata in and its next tokens out (the host schedules the next step)."""
+    step copies its metadata in and its next tokens out (the host schedules the next step), except
+    with multi_step, where runs of pure decode steps with no admission possible go to the device
+    as one block (see below) and come back as one copy of their tokens."""
     torch = engine.torch
     stream = stream or torch.cuda.Stream(device=engine.dev)
     graphs = {} if graphs is None else graphs
-    seen = set()
     waiting = list(requests)
     active = []
     free = list(range(engine.slots))
     steps = rows_total = 0
     import time
 
+    seen = graphs.setdefault("seen", set())
     while waiting or active:
         t0 = time.perf_counter()
+        # Multi-step decoding: when every running request is decoding and nothing can be admitted,
+        # replay a captured step with device-side token feedback K times (K = the fewest tokens a
+        # running request still needs) and read the K x n tokens back in one copy.
+        # With requests waiting, K is the fewest tokens a running request still needs (its slot frees
+        # at the block's end); with none waiting, the block runs to the longest one, the finished
+        # requests' extra rows computed and discarded, so the batch keeps its shape and graph.
+        n_act = len(active)
+        if (multi_step and active and not (waiting and free) and n_act <= 8 and n_act in seen
+                and all(rq.pos >= len(rq.prompt) and not rq.done for rq in active)):
+            rem = [rq.max_new - len(rq.generated) for rq in active]
+            K = min(rem) if waiting else max(rem)
+            K = min(K, 256, engine.max_len - 1 - max(rq.pos for rq in active))
+            if K >= 2:
+                engine.meta.fill([rq.generated[-1] for rq in active], list(range(n_act)),
+                                 [rq.pos for rq in active], list(range(n_act + 1)), [rq.slot for rq in active],
+                                 list(range(n_act)))
+                with torch.cuda.stream(stream):
+                    engine.meta.upload(stream)
+                dg = graphs.get(("decode", n_act))
+                if dg is None:
+                    stream.synchronize()
+                    dg = graphs[("decode", n_act)] = DecodeGraph(engine, n_act, 256, stream, warm=False)
+                with torch.cuda.stream(stream):
+                    dg.reset()
+                    for _ in range(K):
+                        dg.replay()
+                    log = dg.log[:K * n_act].to("cpu", non_blocking=False).numpy().reshape(K, n_act)
+                for i, rq in enumerate(active):
+                    need = rq.max_new - len(rq.generated)
+                    rq.generated.extend(int(x) for x in log[:min(K, need), i])
+                    rq.pos += K
+                for rq in list(active):
+                    if rq.done:
+                        active.remove(rq)
+                        free.append(rq.slot)
+                steps += K
+                rows_total += K * n_act
+                if stats is not None:
+                    stats["multistep_blocks"] = stats.get("multistep_blocks", 0) + 1
+                    stats["decode_steps"] = stats.get("decode_steps", 0) + K
+                    stats["decode_rows"] = stats.get("decode_rows", 0) + K * n_act
+                    stats["decode_ms"] = stats.get("decode_ms", 0.0) + 1e3 * (time.perf_counter() - t0)
+                continue
         seqs, tokens, row_seq, row_pos, offsets, slots_, logit_rows, logit_seq = plan_step(
             active, waiting, free, engine.max_rows, chunk)
         for s, rq in enumerate(seqs):
@@ -508,7 +553,9 @@ class DecodeGraph:
     to a log.  Replaying it runs greedy decoding with no host round trip; the metadata must hold a
     pure decode step for n sequences before the first replay."""
 
-    def __init__(self, engine: HybridEngine, n: int, max_steps: int, stream=None):
+    def __init__(self, engine: HybridEngine, n: int, max_steps: int, stream=None, warm: bool = True):
+        """warm=True runs the step once eagerly before capturing (one real decode step, logged first);
+        warm=False requires an earlier eager step of n rows on this engine (buffers, kernel attributes)."""
         torch = engine.torch
         self.engine, self.n = engine, n
         self.stream = stream or torch.cuda.Stream(device=engine.dev)
@@ -518,8 +565,9 @@ class DecodeGraph:
         self.max_steps = max_steps
         m = engine.meta
         self._tok, self._pos = m.view("tokens")[:n], m.view("row_pos")[:n]
-        with torch.cuda.stream(self.stream):
-            self._body()  # eager warm-up at this shape (GEMM scratch, kernel attributes)
+        if warm:
+            with torch.cuda.stream(self.stream):
+                self._body()
         self.stream.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=self.stream):
