@@ -7,7 +7,8 @@
  * Qwen3.5-style 3:1 gated-delta-rule / full-attention decoder with 16 heads of
  * 128 (4 kv heads), driven by a host scheduler that packs ragged steps with
  * exl3cu_pack_ragged.  All pointers are device pointers on the current device;
- * calls are stream-ordered; fp16 buffers are passed as uint16_t.
+ * calls are stream-ordered; fp16 buffers (KV cache, embedding, gate rows) are
+ * passed as uint16_t; activations are f32.
  *
  * Row conventions: row r of a step belongs to step sequence row_seq[r] at
  * position row_pos[r]; step sequence s uses cache slot seq_slot[s] (0 ..
@@ -28,12 +29,12 @@ int exl3cu_hyb_embed(const uint16_t * d_table, int vocab, const int32_t * d_ids,
                      void * stream);
 
 /* h += delta (when d_delta is not NULL, row stride delta_stride), then
- * out = fp16(h * rsqrt(mean(h^2) + eps) * w), per row of `hidden` values. */
+ * out = h * rsqrt(mean(h^2) + eps) * w, per row of `hidden` values (f32). */
 int exl3cu_hyb_rmsnorm(float * d_h, const float * d_delta, int delta_stride, const float * d_w, float eps, int rows,
-                       int hidden, uint16_t * d_out, void * stream);
+                       int hidden, float * d_out, void * stream);
 
-/* out = fp16(silu(gate) * up) with gu rows [gate (ffn) | up (ffn)]. */
-int exl3cu_hyb_swiglu(const float * d_gu, int rows, int ffn, uint16_t * d_out, void * stream);
+/* out = silu(gate) * up with gu rows [gate (ffn) | up (ffn)] (f32). */
+int exl3cu_hyb_swiglu(const float * d_gu, int rows, int ffn, float * d_out, void * stream);
 
 /* Full-attention prologue: qkv rows [q 16x128 | k 4x128 | v 4x128] (f32);
  * per-head RMSNorm of q and k (weights qn_w / kn_w [128], eps), rotary
@@ -47,7 +48,7 @@ int exl3cu_hyb_attn_prep(const float * d_qkv, int rows, const int32_t * d_row_se
                          int n_slots, float * d_q, void * stream);
 
 /* GQA attention of each row's 16 q heads over positions 0..row_pos of its
- * sequence (4 q heads per kv head), softmax(q.k * scale); out fp16 [rows][16*128].
+ * sequence (4 q heads per kv head), softmax(q.k * scale); out f32 [rows][16*128].
  * splits > 1 divides each row's positions over that many CTAs (flash-decoding);
  * it needs d_part of exl3cu_hyb_attn_scratch_bytes(rows, splits) bytes and
  * d_tickets of rows*16 unsigned, zero before the first call (the kernel leaves
@@ -56,28 +57,28 @@ size_t exl3cu_hyb_attn_scratch_bytes(int rows, int splits);
 int exl3cu_hyb_attn(const float * d_q, int rows, const int32_t * d_row_seq, const int32_t * d_row_pos,
                     const int32_t * d_seq_slot, const uint16_t * d_kcache, const uint16_t * d_vcache, int max_len,
                     int n_slots, float scale, int splits, float * d_part, size_t part_bytes, unsigned * d_tickets,
-                    uint16_t * d_out, void * stream);
+                    float * d_out, void * stream);
 
 /* Dynamic shared memory one exl3cu_hyb_gdn CTA uses (the 128x128 state and scratch). */
 size_t exl3cu_hyb_gdn_smem_bytes(void);
 
 /* Gated delta rule over each step sequence's rows in order, per head:
  *   qkvz rows [q | k | v | z] (4 x 16 x 128, f32, the projections' outputs);
- *   xn: the layer's normed fp16 input rows (for the gate projections);
+ *   xn: the layer's normed input rows, f32 (for the gate projections);
  *   wab: fp16 [32][hidden], rows 0..15 W_a, 16..31 W_b;
  *   conv_w f32 [3*2048][4], conv_state f32 [n_slots][3*2048][3] (last three inputs);
  *   A_log, dt_bias f32 [16]; norm_w f32 [128]; state f32 [n_slots][16][128 (k)][128 (v)].
- * Writes fp16 [rows][16*128] = RMSNorm(o_head) * norm_w * silu(z_head). */
-int exl3cu_hyb_gdn(const float * d_qkvz, const uint16_t * d_xn, const uint16_t * d_wab, int hidden,
+ * Writes f32 [rows][16*128] = RMSNorm(o_head) * norm_w * silu(z_head). */
+int exl3cu_hyb_gdn(const float * d_qkvz, const float * d_xn, const uint16_t * d_wab, int hidden,
                    const float * d_conv_w, float * d_conv_state, const float * d_A_log, const float * d_dt_bias,
                    const float * d_norm_w, float eps, float * d_state, const int32_t * d_row_offsets,
-                   const int32_t * d_seq_slot, int n_seq, int n_slots, uint16_t * d_out, void * stream);
+                   const int32_t * d_seq_slot, int n_seq, int n_slots, float * d_out, void * stream);
 
 /* Tied fp16 head with greedy choice: for o < nout (<= 8), logits[o][v] =
- * sum_i xn[rows[o]][i] * embed[v][i] (fp32 sums; written when d_logits is not
+ * sum_i xn[rows[o]][i] * embed[v][i] (f32 xn, fp32 sums; written when d_logits is not
  * NULL), tokens[o] = argmax_v (lowest index on ties).  d_best: nout 64-bit
  * scratch words.  hidden is 1024, 2048, 4096 or 8192. */
-int exl3cu_hyb_head(const uint16_t * d_xn, const int32_t * d_rows, int nout, int hidden, const uint16_t * d_embed,
+int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hidden, const uint16_t * d_embed,
                     int vocab, float * d_logits, unsigned long long * d_best, int32_t * d_tokens, void * stream);
 
 /* Sticky error bits of these kernels on the current device (reserved: the

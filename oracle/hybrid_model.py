@@ -22,8 +22,8 @@ EXL3 weights enter as the dense fp16 matrices the reference codec
 reconstructs (oracle C library, bit-exact to exl3::reconstruct), so the only
 model-level differences from the GPU are the packed operator's own rounding
 (activations quantised inside the GEMV / fp16 in the GEMM, fp32 sums) and
-summation order.  Rounding points mirror the engine: inputs of every packed
-matmul are fp16, the KV cache is fp16, everything else float32/float64.
+summation order.  Rounding points mirror the engine: the KV cache is fp16,
+everything else float32/float64 (activations enter the packed matmuls as f32).
 Parity of this model with the reference's own graph is unpinned: that graph
 is not in the reference tree.
 """
@@ -76,8 +76,8 @@ class OracleHybrid:
                            "conv": np.zeros((3 * D, 3), np.float64)})
         return st
 
-    def _mm(self, x16, W):
-        return (x16.astype(np.float64) @ W).astype(np.float32)
+    def _mm(self, x, W):
+        return (np.asarray(x, np.float64) @ W).astype(np.float32)
 
     def step(self, seq, token: int, pos: int):
         """Feed one token at position pos; returns the f32 logits of the next token."""
@@ -90,7 +90,7 @@ class OracleHybrid:
             W = self.dense[li]
             if delta is not None:
                 h = (h + delta).astype(np.float32)
-            xn = _rms(h, lw.in_norm, cfg.eps).astype(np.float16)
+            xn = _rms(h, lw.in_norm, cfg.eps).astype(np.float32)
             if lw.kind == "full":
                 q = self._mm(xn, W["q"]).reshape(cfg.heads, HD)
                 k = self._mm(xn, W["k"]).reshape(cfg.kv_heads, HD)
@@ -116,7 +116,7 @@ class OracleHybrid:
                     s = K[:, hq // g, :] @ q[hq].astype(np.float64) / np.sqrt(HD)
                     p = np.exp(s - s.max())
                     out[hq] = (p / p.sum()) @ V[:, hq // g, :]
-                mix = out.reshape(D).astype(np.float16)
+                mix = out.reshape(D).astype(np.float32)
             else:
                 ex = lw.extra
                 proj = self._mm(xn, W["qkvz"])
@@ -146,13 +146,13 @@ class OracleHybrid:
                     S[hh] = alpha * Sh + np.outer(kh[hh], u)
                     on = o / np.sqrt(np.mean(o * o) + cfg.eps)
                     out[hh] = on * ex["gnorm"] * _silu(z[hh])
-                mix = out.reshape(D).astype(np.float16)
+                mix = out.reshape(D).astype(np.float32)
             o = self._mm(mix, W["o"])
             h = (h + o).astype(np.float32)
-            xn = _rms(h, lw.post_norm, cfg.eps).astype(np.float16)
+            xn = _rms(h, lw.post_norm, cfg.eps).astype(np.float32)
             gu = self._mm(xn, W["gu"]).astype(np.float64)
-            act = (_silu(gu[:cfg.ffn]) * gu[cfg.ffn:]).astype(np.float16)
+            act = (_silu(gu[:cfg.ffn]) * gu[cfg.ffn:]).astype(np.float32)
             delta = self._mm(act, W["down"])
         h = (h + delta).astype(np.float32)
-        xn = _rms(h, self.w.final_norm, cfg.eps).astype(np.float16)
+        xn = _rms(h, self.w.final_norm, cfg.eps).astype(np.float32)
         return (self.E @ xn.astype(np.float64)).astype(np.float32)

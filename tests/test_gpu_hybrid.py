@@ -102,7 +102,7 @@ def test_head_argmax_and_embedding(model):
     """The fused head: argmax over fp32 logits of the tied fp16 embedding, lowest index on ties."""
     eng, _ = model
     E = eng.embed.float().cpu().numpy()
-    x = (np.random.default_rng(5).standard_normal((3, eng.cfg.hidden)) * 0.5).astype(np.float16)
+    x = (np.random.default_rng(5).standard_normal((3, eng.cfg.hidden)) * 0.5).astype(np.float32)
     eng.xn[:3].copy_(torch.from_numpy(x).cuda())
     eng.meta.fill([0], [0], [0], [0, 1], [0], [0, 1, 2])
     eng.meta.upload(None)
@@ -133,13 +133,13 @@ def test_attention_splits_agree(model):
     m = eng.meta
     outs = []
     for sp in (1, 2, 8):
-        o = torch.zeros((rows, 16 * 128), dtype=torch.float16, device="cuda")
+        o = torch.zeros((rows, 16 * 128), dtype=torch.float32, device="cuda")
         st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         rc = L.exl3cu_hyb_attn(_vp(q), rows, _vp(m.view("row_seq")), _vp(m.view("row_pos")), _vp(m.view("seq_slot")),
                                _vp(eng.kc[c]), _vp(eng.vc[c]), eng.max_len, eng.slots, 0.088388, sp,
                                _vp(eng.attn_part), eng.attn_part.numel() * 4, _vp(eng.attn_tickets), _vp(o), st)
         assert rc == 0
-        outs.append(o.float().cpu().numpy())
+        outs.append(o.cpu().numpy())
     # fp32 reference on the host
     K = eng.kc[c].float().cpu().numpy()
     V = eng.vc[c].float().cpu().numpy()
@@ -154,7 +154,7 @@ def test_attention_splits_agree(model):
             ref[r, h] = (p / p.sum()) @ V[slots[r], h // 4, :pos[r] + 1]
     ref = ref.reshape(rows, -1)
     for o in outs:
-        assert np.max(np.abs(o - ref)) < 2e-3
+        assert np.max(np.abs(o - ref)) < 1e-4
     assert int(eng.attn_tickets.abs().sum()) == 0
     st = ctypes.c_uint(0)
     assert L.exl3cu_hyb_status(1, ctypes.byref(st)) == 0 and st.value == 0

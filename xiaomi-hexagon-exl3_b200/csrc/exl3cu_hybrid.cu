@@ -7,9 +7,9 @@
 // Rows are the packed tokens of one scheduler step (exl3cu_pack_ragged's
 // output): row r belongs to step sequence row_seq[r] at position row_pos[r];
 // step sequence s owns cache slot seq_slot[s] and the rows
-// [row_offsets[s], row_offsets[s+1]).  All arithmetic is fp32; activations
-// that feed a packed matmul are rounded to fp16 (the operator's input type),
-// the KV cache is fp16, the residual stream and recurrent state are fp32.
+// [row_offsets[s], row_offsets[s+1]).  All arithmetic and every activation is
+// fp32 (the packed operator takes f32 inputs and quantises them itself, more
+// finely than fp16 would); the KV cache and the embedding/head are fp16.
 //
 // The math is the published one (the reference's own graph code is upstream
 // llama.cpp and not part of its tree): gated delta rule (Yang et al., "Gated
@@ -81,7 +81,7 @@ __global__ void k_embed(const __half * __restrict__ table, const int32_t * __res
         h[size_t(r) * H + i] = ok ? __half2float(table[size_t(id) * H + i]) : 0.f;
 }
 
-// h += delta (when given), then out = fp16(h / sqrt(mean(h^2) + eps) * w).
+// h += delta (when given), then out = h / sqrt(mean(h^2) + eps) * w.
 // One CTA of 256 threads per row; the row (H <= 8192, H % 4 == 0) stays in
 // registers between the sum and the scaling.
 constexpr int kNormThreads = 256;
@@ -89,7 +89,7 @@ constexpr int kNormMaxVec = 8;  // float4 per thread: H <= 8192
 
 __global__ void __launch_bounds__(kNormThreads)
 k_rmsnorm(float * __restrict__ h, const float * __restrict__ delta, int delta_stride, const float * __restrict__ w,
-          float eps, int H, __half * __restrict__ out) {
+          float eps, int H, float * __restrict__ out) {
     __shared__ float red[kNormThreads / 32];
     pdl_trigger();
     pdl_wait_primary();
@@ -118,27 +118,26 @@ k_rmsnorm(float * __restrict__ h, const float * __restrict__ delta, int delta_st
     }
     const float inv = rsqrtf(block_sum(ss, red, kNormThreads / 32) / float(H) + eps);
     const float4 * wr = reinterpret_cast<const float4 *>(w);
-    __half2 * o2 = reinterpret_cast<__half2 *>(out + size_t(r) * H);
+    float4 * o4 = reinterpret_cast<float4 *>(out + size_t(r) * H);
 #pragma unroll
     for (int q = 0; q < kNormMaxVec; ++q) {
         const int e = threadIdx.x + q * kNormThreads;
         if (e < nv) {
             const float4 wv = wr[e];
-            o2[2 * e] = __floats2half2_rn(v[q].x * inv * wv.x, v[q].y * inv * wv.y);
-            o2[2 * e + 1] = __floats2half2_rn(v[q].z * inv * wv.z, v[q].w * inv * wv.w);
+            o4[e] = make_float4(v[q].x * inv * wv.x, v[q].y * inv * wv.y, v[q].z * inv * wv.z, v[q].w * inv * wv.w);
         }
     }
 }
 
-// out = fp16(silu(gate) * up); gu row = [gate (F) | up (F)].
-__global__ void k_swiglu(const float * __restrict__ gu, int F, __half * __restrict__ out) {
+// out = silu(gate) * up; gu row = [gate (F) | up (F)].
+__global__ void k_swiglu(const float * __restrict__ gu, int F, float * __restrict__ out) {
     pdl_trigger();
     pdl_wait_primary();
     const int r = blockIdx.y;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= F) return;
     const float g = gu[size_t(r) * 2 * F + i], u = gu[size_t(r) * 2 * F + F + i];
-    out[size_t(r) * F + i] = __float2half_rn(silu(g) * u);
+    out[size_t(r) * F + i] = silu(g) * u;
 }
 
 // Per row: RMSNorm of each q and k head (weights qn_w / kn_w), rotary
@@ -208,7 +207,7 @@ __global__ void __launch_bounds__(128)
 k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const int32_t * __restrict__ row_pos,
        const int32_t * __restrict__ seq_slot, const __half * __restrict__ kc, const __half * __restrict__ vc,
        int max_len, int n_slots, float scale, float * __restrict__ part, unsigned * __restrict__ tickets,
-       __half * __restrict__ out) {
+       float * __restrict__ out) {
     __shared__ float sm_m[4], sm_l[4], sm_acc[4][kHD];
     __shared__ unsigned sm_last;
     pdl_trigger();
@@ -265,12 +264,12 @@ k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const
             for (int q2 = 0; q2 < 4; ++q2) A[q2] = fmaf(sm_acc[w][lane * 4 + q2], c, A[q2]);
         }
     }
-    __half * dst = out + size_t(r) * kNH * kHD + head * kHD + lane * 4;
+    float * dst = out + size_t(r) * kNH * kHD + head * kHD + lane * 4;
     if (S == 1) {
         if (warp == 0) {
             const float invL = 1.0f / L;
 #pragma unroll
-            for (int q2 = 0; q2 < 4; ++q2) dst[q2] = __float2half_rn(A[q2] * invL);
+            for (int q2 = 0; q2 < 4; ++q2) dst[q2] = A[q2] * invL;
         }
         return;
     }
@@ -303,7 +302,7 @@ k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const
     }
     const float invL = 1.0f / GL;
 #pragma unroll
-    for (int q2 = 0; q2 < 4; ++q2) dst[q2] = __float2half_rn(G[q2] * invL);
+    for (int q2 = 0; q2 < 4; ++q2) dst[q2] = G[q2] * invL;
     if (lane == 0) tickets[size_t(r) * kNH + head] = 0u;  // ready for the next launch
 }
 
@@ -319,7 +318,7 @@ k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const
 //   B (rows in order, the only sequential part, one barrier per row): S^T k
 //     and S^T q, u = beta (v - alpha S^T k), o = alpha S^T q + (k.q) u,
 //     S = alpha S + k u^T;
-//   C (rows in parallel): RMSNorm(o) * norm_w * SiLU(z) -> fp16 out.
+//   C (rows in parallel): RMSNorm(o) * norm_w * SiLU(z) -> out (f32).
 // The conv state (last three inputs per channel) is read as it was before the
 // step and rewritten at the end.
 constexpr int kGdnThreads = 256;
@@ -343,11 +342,11 @@ struct GdnSmem {
 };
 
 __global__ void __launch_bounds__(kGdnThreads)
-k_gdn(const float * __restrict__ qkvz, const __half * __restrict__ xn, const __half * __restrict__ wab, int H,
+k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const __half * __restrict__ wab, int H,
       const float * __restrict__ conv_w, float * __restrict__ conv_state, const float * __restrict__ A_log,
       const float * __restrict__ dt_bias, const float * __restrict__ norm_w, float eps, float * __restrict__ S,
       const int32_t * __restrict__ row_offsets, const int32_t * __restrict__ seq_slot, int n_slots,
-      __half * __restrict__ out) {
+      float * __restrict__ out) {
     extern __shared__ __align__(128) float sm[];
     float * tq = sm + GdnSmem::Q;
     float * tk = sm + GdnSmem::K;
@@ -420,24 +419,23 @@ k_gdn(const float * __restrict__ qkvz, const __half * __restrict__ xn, const __h
         }
         // gate projections: warp per row, 16-byte loads of the row in flight together
         for (int rr = warp; rr < nt; rr += kGdnThreads / 32) {
-            const __half * xr = xn + size_t(tr0 + rr) * H;
+            const float * xr = xn + size_t(tr0 + rr) * H;
             float pa = 0.f, pb = 0.f;
-            for (int ib0 = lane * 8; ib0 < H; ib0 += 32 * 8 * 4) {
-                uint4 raw[4];
+            for (int ib0 = lane * 4; ib0 < H; ib0 += 32 * 4 * 4) {
+                float4 raw[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
-                    raw[u] = ib0 + u * 256 < H ? *reinterpret_cast<const uint4 *>(xr + ib0 + u * 256)
-                                               : make_uint4(0, 0, 0, 0);
+                    raw[u] = ib0 + u * 128 < H ? *reinterpret_cast<const float4 *>(xr + ib0 + u * 128)
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    const int ib = ib0 + u * 256;
+                    const int ib = ib0 + u * 128;
                     if (ib >= H) break;
-                    const __half * xh = reinterpret_cast<const __half *>(&raw[u]);
+                    const float xv[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const float x = __half2float(xh[q]);
-                        pa = fmaf(x, __half2float(wab_s[ib + q]), pa);
-                        pb = fmaf(x, __half2float(wab_s[H + ib + q]), pb);
+                    for (int q = 0; q < 4; ++q) {
+                        pa = fmaf(xv[q], __half2float(wab_s[ib + q]), pa);
+                        pb = fmaf(xv[q], __half2float(wab_s[H + ib + q]), pb);
                     }
                 }
             }
@@ -516,7 +514,7 @@ k_gdn(const float * __restrict__ qkvz, const __half * __restrict__ xn, const __h
             const size_t r = size_t(tr0 + rr);
             for (int d = lane; d < kHD; d += 32) {
                 const float z = qkvz[r * QKVZ + 3 * kNH * kHD + h * kHD + d];
-                out[r * kNH * kHD + h * kHD + d] = __float2half_rn(ov[d] * inv * norm_w[d] * silu(z));
+                out[r * kNH * kHD + h * kHD + d] = ov[d] * inv * norm_w[d] * silu(z);
             }
         }
         __syncthreads();  // the next tile overwrites tq, tk, tv, to, gate, cx
@@ -545,7 +543,7 @@ __device__ __forceinline__ uint32_t float_key(float f) {
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-// logits[o][v] = sum_i xn[rows[o]][i] * E[v][i] (fp16 inputs, fp32 sums) for
+// logits[o][v] = sum_i xn[rows[o]][i] * E[v][i] (f32 x, fp16 E, fp32 sums) for
 // nout <= 8 rows; best[o] = max over v of (key(logit) << 32 | ~v) (the first
 // index wins ties).  Warp per vocab row, activations staged in shared memory;
 // ITER = H / 256 16-byte loads per lane per vocab row, issued together.
@@ -554,15 +552,15 @@ constexpr int kHeadThreads = 256;
 
 template <int ITER>
 __global__ void __launch_bounds__(kHeadThreads)
-k_head(const __half * __restrict__ xn, const int32_t * __restrict__ rows, int nout, int H,
+k_head(const float * __restrict__ xn, const int32_t * __restrict__ rows, int nout, int H,
        const __half * __restrict__ E, int V, float * __restrict__ logits, unsigned long long * __restrict__ best) {
-    extern __shared__ __align__(16) __half xs[];  // [nout][H]
+    extern __shared__ __align__(16) float xs[];  // [nout][H]
     pdl_trigger();
     pdl_wait_primary();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int e = threadIdx.x; e < nout * H / 8; e += kHeadThreads) {
-        const int o = (e * 8) / H, i = (e * 8) % H;
-        reinterpret_cast<uint4 *>(xs)[e] = *reinterpret_cast<const uint4 *>(xn + size_t(rows[o]) * H + i);
+    for (int e = threadIdx.x; e < nout * H / 4; e += kHeadThreads) {
+        const int o = (e * 4) / H, i = (e * 4) % H;
+        reinterpret_cast<float4 *>(xs)[e] = *reinterpret_cast<const float4 *>(xn + size_t(rows[o]) * H + i);
     }
     __syncthreads();
     unsigned long long mine[kHeadMaxRows];
@@ -586,14 +584,16 @@ k_head(const __half * __restrict__ xn, const int32_t * __restrict__ rows, int no
 #pragma unroll
             for (int o = 0; o < kHeadMaxRows; ++o) {
                 if (o >= nout) break;
-                const uint4 xr = *reinterpret_cast<const uint4 *>(xs + o * H + it * 256 + lane * 8);
-                const __half2 * x2 = reinterpret_cast<const __half2 *>(&xr);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float2 xf = __half22float2(x2[q]);
-                    acc[o] = fmaf(xf.x, ef[q].x, acc[o]);
-                    acc[o] = fmaf(xf.y, ef[q].y, acc[o]);
-                }
+                const float4 * xr = reinterpret_cast<const float4 *>(xs + o * H + it * 256 + lane * 8);
+                const float4 x0 = xr[0], x1 = xr[1];
+                acc[o] = fmaf(x0.x, ef[0].x, acc[o]);
+                acc[o] = fmaf(x0.y, ef[0].y, acc[o]);
+                acc[o] = fmaf(x0.z, ef[1].x, acc[o]);
+                acc[o] = fmaf(x0.w, ef[1].y, acc[o]);
+                acc[o] = fmaf(x1.x, ef[2].x, acc[o]);
+                acc[o] = fmaf(x1.y, ef[2].y, acc[o]);
+                acc[o] = fmaf(x1.z, ef[3].x, acc[o]);
+                acc[o] = fmaf(x1.w, ef[3].y, acc[o]);
             }
         }
 #pragma unroll
@@ -689,20 +689,20 @@ int exl3cu_hyb_embed(const uint16_t * d_table, int vocab, const int32_t * d_ids,
 }
 
 int exl3cu_hyb_rmsnorm(float * d_h, const float * d_delta, int delta_stride, const float * d_w, float eps, int rows,
-                       int hidden, uint16_t * d_out, void * stream) {
+                       int hidden, float * d_out, void * stream) {
     if (!d_h || !d_w || !d_out || rows < 0 || hidden <= 0 || hidden % 4 || hidden > 4 * kNormThreads * kNormMaxVec ||
         (d_delta && (delta_stride < hidden || delta_stride % 4)))
         return bad("rmsnorm: bad arguments (hidden a multiple of 4 up to 8192)");
     if (!rows) return EXL3CU_OK;
     return launch_pdl(k_rmsnorm, dim3(unsigned(rows)), dim3(kNormThreads), 0, stream, d_h, d_delta, delta_stride, d_w,
-                      eps, hidden, reinterpret_cast<__half *>(d_out));
+                      eps, hidden, d_out);
 }
 
-int exl3cu_hyb_swiglu(const float * d_gu, int rows, int ffn, uint16_t * d_out, void * stream) {
+int exl3cu_hyb_swiglu(const float * d_gu, int rows, int ffn, float * d_out, void * stream) {
     if (!d_gu || !d_out || rows < 0 || ffn <= 0) return bad("swiglu: bad arguments");
     if (!rows) return EXL3CU_OK;
     return launch_pdl(k_swiglu, dim3(unsigned((ffn + 255) / 256), unsigned(rows)), dim3(256), 0, stream, d_gu, ffn,
-                      reinterpret_cast<__half *>(d_out));
+                      d_out);
 }
 
 int exl3cu_hyb_attn_prep(const float * d_qkv, int rows, const int32_t * d_row_seq, const int32_t * d_row_pos,
@@ -725,7 +725,7 @@ size_t exl3cu_hyb_attn_scratch_bytes(int rows, int splits) {
 int exl3cu_hyb_attn(const float * d_q, int rows, const int32_t * d_row_seq, const int32_t * d_row_pos,
                     const int32_t * d_seq_slot, const uint16_t * d_kcache, const uint16_t * d_vcache, int max_len,
                     int n_slots, float scale, int splits, float * d_part, size_t part_bytes, unsigned * d_tickets,
-                    uint16_t * d_out, void * stream) {
+                    float * d_out, void * stream) {
     if (!d_q || !d_row_seq || !d_row_pos || !d_seq_slot || !d_kcache || !d_vcache || !d_out || rows < 0 ||
         max_len <= 0 || n_slots <= 0 || splits < 1 || splits > 64)
         return bad("attn: bad arguments");
@@ -735,8 +735,7 @@ int exl3cu_hyb_attn(const float * d_q, int rows, const int32_t * d_row_seq, cons
         return bad("attn: split scratch missing or too small (exl3cu_hyb_attn_scratch_bytes; tickets rows*16, zeroed)");
     return launch_pdl(k_attn, dim3(kNH, unsigned(rows), unsigned(splits)), dim3(128), 0, stream, d_q, d_row_seq,
                       d_row_pos, d_seq_slot, reinterpret_cast<const __half *>(d_kcache),
-                      reinterpret_cast<const __half *>(d_vcache), max_len, n_slots, scale, d_part, d_tickets,
-                      reinterpret_cast<__half *>(d_out));
+                      reinterpret_cast<const __half *>(d_vcache), max_len, n_slots, scale, d_part, d_tickets, d_out);
 }
 
 size_t exl3cu_hyb_gdn_smem_bytes_for(int hidden) {
@@ -746,10 +745,10 @@ size_t exl3cu_hyb_gdn_smem_bytes_for(int hidden) {
 
 size_t exl3cu_hyb_gdn_smem_bytes(void) { return exl3cu_hyb_gdn_smem_bytes_for(8192); }
 
-int exl3cu_hyb_gdn(const float * d_qkvz, const uint16_t * d_xn, const uint16_t * d_wab, int hidden,
+int exl3cu_hyb_gdn(const float * d_qkvz, const float * d_xn, const uint16_t * d_wab, int hidden,
                    const float * d_conv_w, float * d_conv_state, const float * d_A_log, const float * d_dt_bias,
                    const float * d_norm_w, float eps, float * d_state, const int32_t * d_row_offsets,
-                   const int32_t * d_seq_slot, int n_seq, int n_slots, uint16_t * d_out, void * stream) {
+                   const int32_t * d_seq_slot, int n_seq, int n_slots, float * d_out, void * stream) {
     if (!d_qkvz || !d_xn || !d_wab || !d_conv_w || !d_conv_state || !d_A_log || !d_dt_bias || !d_norm_w ||
         !d_state || !d_row_offsets || !d_seq_slot || !d_out || hidden <= 0 || n_seq < 0 || n_seq > 65535 ||
         n_slots <= 0)
@@ -760,19 +759,19 @@ int exl3cu_hyb_gdn(const float * d_qkvz, const uint16_t * d_xn, const uint16_t *
     const size_t smem = exl3cu_hyb_gdn_smem_bytes_for(hidden);
     if (!set_smem_attr_once(reinterpret_cast<const void *>(k_gdn), int(exl3cu_hyb_gdn_smem_bytes()), g_gdn_attr))
         return status_of(cudaGetLastError());
-    return launch_pdl(k_gdn, dim3(kNH, unsigned(n_seq)), dim3(kGdnThreads), smem, stream, d_qkvz,
-                      reinterpret_cast<const __half *>(d_xn), reinterpret_cast<const __half *>(d_wab), hidden,
+    return launch_pdl(k_gdn, dim3(kNH, unsigned(n_seq)), dim3(kGdnThreads), smem, stream, d_qkvz, d_xn,
+                      reinterpret_cast<const __half *>(d_wab), hidden,
                       d_conv_w, d_conv_state, d_A_log, d_dt_bias, d_norm_w, eps, d_state, d_row_offsets, d_seq_slot,
-                      n_slots, reinterpret_cast<__half *>(d_out));
+                      n_slots, d_out);
 }
 
-int exl3cu_hyb_head(const uint16_t * d_xn, const int32_t * d_rows, int nout, int hidden, const uint16_t * d_embed,
+int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hidden, const uint16_t * d_embed,
                     int vocab, float * d_logits, unsigned long long * d_best, int32_t * d_tokens, void * stream) {
     if (!d_xn || !d_rows || !d_embed || !d_best || !d_tokens || nout < 0 || nout > kHeadMaxRows || hidden <= 0 ||
         hidden % 256 || hidden > 8192 || vocab <= 0)
         return bad("head: bad arguments (nout <= 8, hidden a multiple of 256 up to 8192)");
     if (!nout) return EXL3CU_OK;
-    const size_t smem = size_t(nout) * hidden * sizeof(__half);
+    const size_t smem = size_t(nout) * hidden * sizeof(float);
     if (smem > size_t(kHeadSmemMax)) return bad("head: activations exceed shared memory");
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -780,7 +779,7 @@ int exl3cu_hyb_head(const uint16_t * d_xn, const int32_t * d_rows, int nout, int
     int rc = launch_pdl(k_head_clear, dim3(1), dim3(32), 0, stream, d_best, nout);
     if (rc) return rc;
     const dim3 grid(unsigned(sms * 4)), block(kHeadThreads);
-    const auto * xn = reinterpret_cast<const __half *>(d_xn);
+    const float * xn = d_xn;
     const auto * E = reinterpret_cast<const __half *>(d_embed);
     switch (hidden / 256) {
 #define EXL3CU_HEAD_CASE(N)                                                                                        \

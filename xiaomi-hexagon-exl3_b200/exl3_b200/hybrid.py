@@ -229,13 +229,13 @@ class HybridEngine:
         R = max_rows
         f32, f16 = torch.float32, torch.float16
         self.h = torch.zeros((R, H), dtype=f32, device=dev)
-        self.xn = torch.zeros((R, H), dtype=f16, device=dev)
+        self.xn = torch.zeros((R, H), dtype=f32, device=dev)
         self.proj = torch.zeros((R, 4 * D), dtype=f32, device=dev)      # [q|k|v|z] or [q|k|v]
         self.q = torch.zeros((R, D), dtype=f32, device=dev)
-        self.mix = torch.zeros((R, D), dtype=f16, device=dev)           # attention / delta-rule output
+        self.mix = torch.zeros((R, D), dtype=f32, device=dev)           # attention / delta-rule output
         self.o = torch.zeros((R, H), dtype=f32, device=dev)
         self.gu = torch.zeros((R, 2 * F), dtype=f32, device=dev)
-        self.act = torch.zeros((R, F), dtype=f16, device=dev)
+        self.act = torch.zeros((R, F), dtype=f32, device=dev)
         self.down = torch.zeros((R, H), dtype=f32, device=dev)
         n_full = sum(1 for d in self.layers if d["kind"] == "full")
         n_gdn = len(self.layers) - n_full
@@ -282,14 +282,14 @@ class HybridEngine:
         if args is None:
             n = len(names)
             VP, SZ, IN = ctypes.c_void_p * n, ctypes.c_size_t * n, ctypes.c_int * n
-            args = (n, VP(*[mats[nm].handle.value for nm in names]), VP(*[x.data_ptr()] * n), IN(*[1] * n),
+            args = (n, VP(*[mats[nm].handle.value for nm in names]), VP(*[x.data_ptr()] * n), IN(*[0] * n),
                     SZ(*[rows] * n), SZ(*[x.stride(0)] * n), VP(*[o.data_ptr() for o in out_cols]),
                     SZ(*[o.stride(0) for o in out_cols]))
             self._batch_args[key] = args
         check(self.L.exl3cu_mul_mat_batch(*args, st))
 
     def _mm(self, w, x, out, rows, st):
-        check(self.L.exl3cu_mul_mat(w.handle, _vp(x), 1, rows, x.stride(0), _vp(out), out.stride(0), st))
+        check(self.L.exl3cu_mul_mat(w.handle, _vp(x), 0, rows, x.stride(0), _vp(out), out.stride(0), st))
 
     def forward(self, rows: int, n_seq: int, nout: int, stream=None):
         """Run the step whose metadata is in self.meta.dev; next tokens land in self.out_tokens[:nout]."""
