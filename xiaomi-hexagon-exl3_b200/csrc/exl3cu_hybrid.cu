@@ -34,9 +34,12 @@
 #include "exl3cu_hybrid.h"
 #include "exl3cu_internal.h"
 
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 #include <atomic>
+
+namespace cg = cooperative_groups;
 
 namespace exl3cu {
 
@@ -307,23 +310,30 @@ k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const
 }
 
 // Gated delta rule for one (head, step sequence): the sequence's rows in
-// order, in tiles of kGdnTile rows.  256 threads; thread t owns column
-// j = t & 127 of the head's 128 x 128 fp32 state for k rows [64 (t >> 7),
-// +64): 64 registers, loaded from and stored to HBM coalesced (for each k
-// row the CTA touches 128 consecutive floats).  Per tile:
-//   A (rows in parallel): the tile's conv inputs staged in shared memory,
-//     causal conv + SiLU of the head's q, k, v channels, L2 norms (q also x
-//     1/sqrt(128)), k.q, the gates a = x.W_a, b = x.W_b -> alpha =
+// order, in tiles of kGdnTile rows.  A cluster of kGdnSplit CTAs serves one
+// head; CTA rank q owns v columns [32 q, 32 q + 32) of the head's 128 x 128
+// fp32 state.  Thread t owns column 32 q + (t & 31) for k rows
+// [16 (t >> 5), +16): 16 registers, loaded from and stored to HBM coalesced.
+// The recurrence of a column needs only that column, so the ranks run it
+// independently.  Per tile:
+//   A (rows in parallel, every rank): the tile's conv inputs staged in shared
+//     memory, causal conv + SiLU of the head's q, k, v channels, L2 norms (q
+//     also x 1/sqrt(128)), k.q, the gates a = x.W_a, b = x.W_b -> alpha =
 //     exp(-exp(A_log) softplus(a + dt_bias)), beta = sigmoid(b);
 //   B (rows in order, the only sequential part, one barrier per row): S^T k
-//     and S^T q, u = beta (v - alpha S^T k), o = alpha S^T q + (k.q) u,
-//     S = alpha S + k u^T;
-//   C (rows in parallel): RMSNorm(o) * norm_w * SiLU(z) -> out (f32).
+//     and S^T q over the eight k slices, u = beta (v - alpha S^T k),
+//     o = alpha S^T q + (k.q) u, S = alpha S + k u^T;
+//   C (rows in parallel): each rank's share of sum(o^2) per row goes to its
+//     peers through distributed shared memory (one cluster barrier per tile,
+//     double-buffered), then RMSNorm(o) * norm_w * SiLU(z) -> out (f32).
 // The conv state (last three inputs per channel) is read as it was before the
-// step and rewritten at the end.
+// step and rewritten at the end by rank 0.
 constexpr int kGdnThreads = 256;
 constexpr int kGdnTile = 16;
-constexpr int kGdnKHalf = kHD / 2;
+constexpr int kGdnSplit = 4;                  // CTAs (v-column slices) per head
+constexpr int kGdnCols = kHD / kGdnSplit;     // 32 columns per CTA
+constexpr int kGdnKParts = kGdnThreads / kGdnCols;  // 8 k slices
+constexpr int kGdnKRows = kHD / kGdnKParts;   // 16 k rows per thread
 
 static __device__ unsigned g_hyb_status;  // reserved: sticky error bits of these kernels (none raised today)
 
@@ -332,16 +342,17 @@ struct GdnSmem {
     static constexpr int Q = 0;                               // [T][128] conv+norm q
     static constexpr int K = Q + kGdnTile * kHD;              // [T][128] k
     static constexpr int V = K + kGdnTile * kHD;              // [T][128] v
-    static constexpr int O = V + kGdnTile * kHD;              // [T][128] o
-    static constexpr int RED = O + kGdnTile * kHD;            // [2 buffers][4][128]
-    static constexpr int CW = RED + 2 * 4 * kHD;              // [384][4] conv weights of the head
+    static constexpr int O = V + kGdnTile * kHD;              // [T][32] o of this rank's columns
+    static constexpr int RED = O + kGdnTile * kGdnCols;       // [2 buffers][2][8][32]
+    static constexpr int PSUM = RED + 2 * 2 * kGdnKParts * kGdnCols;  // [2 tiles][T] sum(o^2) of this rank
+    static constexpr int CW = PSUM + 2 * kGdnTile;            // [384][4] conv weights of the head
     static constexpr int GATE = CW + 3 * kHD * kConvW;        // [T][4]: alpha, beta, k.q
     static constexpr int CX = GATE + kGdnTile * 4;            // [T+3][384] conv inputs of the tile
     static constexpr int WAB = CX + (kGdnTile + kConvW - 1) * 3 * kHD;  // fp16 [2][H] gate rows (H <= 8192)
     static constexpr int floats_without_wab = WAB;
 };
 
-__global__ void __launch_bounds__(kGdnThreads)
+__global__ void __launch_bounds__(kGdnThreads, 1)
 k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const __half * __restrict__ wab, int H,
       const float * __restrict__ conv_w, float * __restrict__ conv_state, const float * __restrict__ A_log,
       const float * __restrict__ dt_bias, const float * __restrict__ norm_w, float eps, float * __restrict__ S,
@@ -353,24 +364,28 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const __ha
     float * tv = sm + GdnSmem::V;
     float * to = sm + GdnSmem::O;
     float * red = sm + GdnSmem::RED;
+    float * psum = sm + GdnSmem::PSUM;
     float * cw = sm + GdnSmem::CW;
     float * gate = sm + GdnSmem::GATE;
     float * cx = sm + GdnSmem::CX;
     __half * wab_s = reinterpret_cast<__half *>(sm + GdnSmem::WAB);
+    cg::cluster_group cluster = cg::this_cluster();
     pdl_trigger();
     pdl_wait_primary();
-    const int h = blockIdx.x, s = blockIdx.y;
+    const int h = blockIdx.x / kGdnSplit, s = blockIdx.y;
+    const int rank = int(cluster.block_rank());
     const int slot = seq_slot[s];
-    if (slot < 0 || slot >= n_slots) return;
-    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int j = t & (kHD - 1), half = t >> 7;
-    const int i0 = half * kGdnKHalf;
-    float * Sg = S + (size_t(slot) * kNH + h) * kHD * kHD;
     const int r0 = row_offsets[s], r1 = row_offsets[s + 1];
-    if (r1 <= r0) return;
-    float Sr[kGdnKHalf];  // S[i0 + i][j]
+    // every CTA of the cluster takes the same early exit, so no cluster barrier is left waiting
+    if (slot < 0 || slot >= n_slots || r1 <= r0) return;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int jj = t & (kGdnCols - 1), kp = t >> 5;   // column in the slice, k slice
+    const int j = rank * kGdnCols + jj;               // column in the head
+    const int i0 = kp * kGdnKRows;
+    float * Sg = S + (size_t(slot) * kNH + h) * kHD * kHD;
+    float Sr[kGdnKRows];  // S[i0 + i][j]
 #pragma unroll
-    for (int i = 0; i < kGdnKHalf; ++i) Sr[i] = Sg[(i0 + i) * kHD + j];
+    for (int i = 0; i < kGdnKRows; ++i) Sr[i] = Sg[(i0 + i) * kHD + j];
     constexpr int QKVZ = 4 * kNH * kHD;
     constexpr int CH = 3 * kNH * kHD;  // convolved channels (q, k, v)
     constexpr int C3 = 3 * kHD;
@@ -387,9 +402,10 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const __ha
     const float A = -expf(A_log[h]);
     const float dtb = dt_bias[h];
     const float qscale = rsqrtf(float(kHD));
-    int rb = 0;  // reduction buffer of the current row
+    int rb = 0;    // reduction buffer of the current row
+    int tpar = 0;  // psum buffer of the current tile
     __syncthreads();
-    for (int tr0 = r0; tr0 < r1; tr0 += kGdnTile) {
+    for (int tr0 = r0; tr0 < r1; tr0 += kGdnTile, tpar ^= 1) {
         const int nt = min(kGdnTile, r1 - tr0);
         // ---- A: stage the conv inputs x[tr0-3 .. tr0+nt-1] of the head's 384 channels ----
         // (rows before the sequence's first come from the conv state)
@@ -468,34 +484,38 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const __ha
             if (lane == 0) gate[rr * 4 + 2] = kq;
         }
         __syncthreads();
-        // ---- B: the recurrence, row by row (state in registers) ----
+        // ---- B: the recurrence, row by row (state slice in registers) ----
         for (int rr = 0; rr < nt; ++rr) {
             const float4 * kv4 = reinterpret_cast<const float4 *>(tk + rr * kHD + i0);
             const float4 * qv4 = reinterpret_cast<const float4 *>(tq + rr * kHD + i0);
-            float ak = 0.f, cqs = 0.f;
+            float a4[2] = {0.f, 0.f}, c4[2] = {0.f, 0.f};
 #pragma unroll
-            for (int i = 0; i < kGdnKHalf / 4; ++i) {
+            for (int i = 0; i < kGdnKRows / 4; ++i) {
                 const float4 kk = kv4[i], qq = qv4[i];
-                ak = fmaf(Sr[4 * i], kk.x, ak);
-                ak = fmaf(Sr[4 * i + 1], kk.y, ak);
-                ak = fmaf(Sr[4 * i + 2], kk.z, ak);
-                ak = fmaf(Sr[4 * i + 3], kk.w, ak);
-                cqs = fmaf(Sr[4 * i], qq.x, cqs);
-                cqs = fmaf(Sr[4 * i + 1], qq.y, cqs);
-                cqs = fmaf(Sr[4 * i + 2], qq.z, cqs);
-                cqs = fmaf(Sr[4 * i + 3], qq.w, cqs);
+                a4[0] = fmaf(Sr[4 * i], kk.x, a4[0]);
+                a4[1] = fmaf(Sr[4 * i + 1], kk.y, a4[1]);
+                a4[0] = fmaf(Sr[4 * i + 2], kk.z, a4[0]);
+                a4[1] = fmaf(Sr[4 * i + 3], kk.w, a4[1]);
+                c4[0] = fmaf(Sr[4 * i], qq.x, c4[0]);
+                c4[1] = fmaf(Sr[4 * i + 1], qq.y, c4[1]);
+                c4[0] = fmaf(Sr[4 * i + 2], qq.z, c4[0]);
+                c4[1] = fmaf(Sr[4 * i + 3], qq.w, c4[1]);
             }
-            float * rd = red + rb * 4 * kHD;
-            rd[half * kHD + j] = ak;
-            rd[2 * kHD + half * kHD + j] = cqs;
+            float * rd = red + rb * 2 * kGdnKParts * kGdnCols;
+            rd[kp * kGdnCols + jj] = a4[0] + a4[1];
+            rd[kGdnKParts * kGdnCols + kp * kGdnCols + jj] = c4[0] + c4[1];
             __syncthreads();
-            const float alpha = gate[rr * 4 + 0], beta = gate[rr * 4 + 1], kq = gate[rr * 4 + 2];
-            const float a_j = rd[j] + rd[kHD + j];
-            const float c_j = rd[2 * kHD + j] + rd[3 * kHD + j];
-            const float u_j = beta * (tv[rr * kHD + j] - alpha * a_j);
-            if (half == 0) to[rr * kHD + j] = fmaf(kq, u_j, alpha * c_j);
+            float a_j = 0.f, c_j = 0.f;
 #pragma unroll
-            for (int i = 0; i < kGdnKHalf / 4; ++i) {
+            for (int p = 0; p < kGdnKParts; ++p) {  // fixed order: every thread of column j agrees
+                a_j += rd[p * kGdnCols + jj];
+                c_j += rd[kGdnKParts * kGdnCols + p * kGdnCols + jj];
+            }
+            const float alpha = gate[rr * 4 + 0], beta = gate[rr * 4 + 1], kq = gate[rr * 4 + 2];
+            const float u_j = beta * (tv[rr * kHD + j] - alpha * a_j);
+            if (kp == 0) to[rr * kGdnCols + jj] = fmaf(kq, u_j, alpha * c_j);
+#pragma unroll
+            for (int i = 0; i < kGdnKRows / 4; ++i) {
                 const float4 kk = kv4[i];
                 Sr[4 * i] = fmaf(kk.x, u_j, alpha * Sr[4 * i]);
                 Sr[4 * i + 1] = fmaf(kk.y, u_j, alpha * Sr[4 * i + 1]);
@@ -504,37 +524,46 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const __ha
             }
             rb ^= 1;  // the next row writes the other buffer: no second barrier needed
         }
-        __syncthreads();  // every row's o is in `to`
-        // ---- C: gated RMSNorm of o, warp per row ----
+        __syncthreads();  // every row's o slice is in `to`
+        // ---- C: this rank's sum(o^2) per row, exchanged across the cluster ----
+        float * ps = psum + tpar * kGdnTile;
         for (int rr = warp; rr < nt; rr += kGdnThreads / 32) {
-            const float * ov = to + rr * kHD;
+            const float o = to[rr * kGdnCols + lane];
+            const float ss = warp_sum(o * o);
+            if (lane == 0) ps[rr] = ss;
+        }
+        cluster.sync();  // every rank's partial sums are visible
+        for (int rr = warp; rr < nt; rr += kGdnThreads / 32) {
             float ss = 0.f;
-            for (int d = lane; d < kHD; d += 32) ss = fmaf(ov[d], ov[d], ss);
-            const float inv = rsqrtf(warp_sum(ss) / float(kHD) + eps);
+#pragma unroll
+            for (int q = 0; q < kGdnSplit; ++q) ss += cluster.map_shared_rank(ps, q)[rr];  // rank order
+            const float inv = rsqrtf(ss / float(kHD) + eps);
             const size_t r = size_t(tr0 + rr);
-            for (int d = lane; d < kHD; d += 32) {
-                const float z = qkvz[r * QKVZ + 3 * kNH * kHD + h * kHD + d];
-                out[r * kNH * kHD + h * kHD + d] = ov[d] * inv * norm_w[d] * silu(z);
+            const int d = rank * kGdnCols + lane;
+            const float z = qkvz[r * QKVZ + 3 * kNH * kHD + h * kHD + d];
+            out[r * kNH * kHD + h * kHD + d] = to[rr * kGdnCols + lane] * inv * norm_w[d] * silu(z);
+        }
+        __syncthreads();  // the next tile overwrites tq, tk, tv, to, gate, cx (psum is double-buffered)
+    }
+    cluster.sync();  // peers are done reading this rank's psum, and with the conv state
+    // the conv state: the last three inputs of the sequence so far (rank 0)
+    if (rank == 0) {
+        const int n = r1 - r0;
+        for (int c = t; c < C3; c += kGdnThreads) {
+            const int ch = (c / kHD) * kNH * kHD + h * kHD + c % kHD;
+            float * st = conv_state + (size_t(slot) * CH + ch) * (kConvW - 1);
+            float nv[kConvW - 1];
+#pragma unroll
+            for (int w = 0; w < kConvW - 1; ++w) {
+                const int ri = r1 - (kConvW - 1) + w;  // input index for new slot w
+                nv[w] = ri >= r0 ? qkvz[size_t(ri) * QKVZ + ch] : st[w + n];
             }
-        }
-        __syncthreads();  // the next tile overwrites tq, tk, tv, to, gate, cx
-    }
-    // the conv state: the last three inputs of the sequence so far
-    const int n = r1 - r0;
-    for (int c = t; c < C3; c += kGdnThreads) {
-        const int ch = (c / kHD) * kNH * kHD + h * kHD + c % kHD;
-        float * st = conv_state + (size_t(slot) * CH + ch) * (kConvW - 1);
-        float nv[kConvW - 1];
 #pragma unroll
-        for (int w = 0; w < kConvW - 1; ++w) {
-            const int ri = r1 - (kConvW - 1) + w;  // input index for new slot w
-            nv[w] = ri >= r0 ? qkvz[size_t(ri) * QKVZ + ch] : st[w + n];
+            for (int w = 0; w < kConvW - 1; ++w) st[w] = nv[w];
         }
-#pragma unroll
-        for (int w = 0; w < kConvW - 1; ++w) st[w] = nv[w];
     }
 #pragma unroll
-    for (int i = 0; i < kGdnKHalf; ++i) Sg[(i0 + i) * kHD + j] = Sr[i];
+    for (int i = 0; i < kGdnKRows; ++i) Sg[(i0 + i) * kHD + j] = Sr[i];
 }
 
 // Order-preserving key of a float (larger float, larger key).
@@ -661,6 +690,27 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, voi
     return status_of(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
 }
 
+// The same with a cluster of `cluster_x` CTAs along x.
+template <typename... KArgs, typename... Args>
+int launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, int cluster_x, void * stream,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = unsigned(cluster_x);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return status_of(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
 // Per-device one-time kernel attributes.
 bool set_smem_attr_once(const void * fn, int bytes, std::atomic<unsigned long long> & done_mask) {
     int dev = 0;
@@ -759,7 +809,8 @@ int exl3cu_hyb_gdn(const float * d_qkvz, const float * d_xn, const uint16_t * d_
     const size_t smem = exl3cu_hyb_gdn_smem_bytes_for(hidden);
     if (!set_smem_attr_once(reinterpret_cast<const void *>(k_gdn), int(exl3cu_hyb_gdn_smem_bytes()), g_gdn_attr))
         return status_of(cudaGetLastError());
-    return launch_pdl(k_gdn, dim3(kNH, unsigned(n_seq)), dim3(kGdnThreads), smem, stream, d_qkvz, d_xn,
+    return launch_pdl_cluster(k_gdn, dim3(kNH * kGdnSplit, unsigned(n_seq)), dim3(kGdnThreads), smem, kGdnSplit,
+                      stream, d_qkvz, d_xn,
                       reinterpret_cast<const __half *>(d_wab), hidden,
                       d_conv_w, d_conv_state, d_A_log, d_dt_bias, d_norm_w, eps, d_state, d_row_offsets, d_seq_slot,
                       n_slots, d_out);
