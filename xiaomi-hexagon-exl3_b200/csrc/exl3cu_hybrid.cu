@@ -596,43 +596,87 @@ k_head(const float * __restrict__ xn, const int32_t * __restrict__ rows, int nou
 #pragma unroll
     for (int o = 0; o < kHeadMaxRows; ++o) mine[o] = 0ull;
     const int nwarps = gridDim.x * (kHeadThreads / 32);
-    for (int v = blockIdx.x * (kHeadThreads / 32) + warp; v < V; v += nwarps) {
-        const __half * er = E + size_t(v) * H + lane * 8;
-        uint4 raw[ITER];
+    // one activation row: all of a vocab row's 16-byte loads in flight together
+    if (nout == 1) {
+        for (int v = blockIdx.x * (kHeadThreads / 32) + warp; v < V; v += nwarps) {
+            const __half * er = E + size_t(v) * H + lane * 8;
+            uint4 raw[ITER];
 #pragma unroll
-        for (int it = 0; it < ITER; ++it) raw[it] = __ldcs(reinterpret_cast<const uint4 *>(er + it * 256));
-        float acc[kHeadMaxRows];
+            for (int it = 0; it < ITER; ++it) raw[it] = __ldcs(reinterpret_cast<const uint4 *>(er + it * 256));
+            float acc = 0.f;
 #pragma unroll
-        for (int o = 0; o < kHeadMaxRows; ++o) acc[o] = 0.f;
-#pragma unroll
-        for (int it = 0; it < ITER; ++it) {
-            const __half2 * e2 = reinterpret_cast<const __half2 *>(&raw[it]);
-            float2 ef[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) ef[q] = __half22float2(e2[q]);
-#pragma unroll
-            for (int o = 0; o < kHeadMaxRows; ++o) {
-                if (o >= nout) break;
-                const float4 * xr = reinterpret_cast<const float4 *>(xs + o * H + it * 256 + lane * 8);
+            for (int it = 0; it < ITER; ++it) {
+                const __half2 * e2 = reinterpret_cast<const __half2 *>(&raw[it]);
+                const float4 * xr = reinterpret_cast<const float4 *>(xs + it * 256 + lane * 8);
                 const float4 x0 = xr[0], x1 = xr[1];
-                acc[o] = fmaf(x0.x, ef[0].x, acc[o]);
-                acc[o] = fmaf(x0.y, ef[0].y, acc[o]);
-                acc[o] = fmaf(x0.z, ef[1].x, acc[o]);
-                acc[o] = fmaf(x0.w, ef[1].y, acc[o]);
-                acc[o] = fmaf(x1.x, ef[2].x, acc[o]);
-                acc[o] = fmaf(x1.y, ef[2].y, acc[o]);
-                acc[o] = fmaf(x1.z, ef[3].x, acc[o]);
-                acc[o] = fmaf(x1.w, ef[3].y, acc[o]);
+                const float2 e0 = __half22float2(e2[0]), e1 = __half22float2(e2[1]);
+                const float2 e2v = __half22float2(e2[2]), e3 = __half22float2(e2[3]);
+                acc = fmaf(x0.x, e0.x, acc);
+                acc = fmaf(x0.y, e0.y, acc);
+                acc = fmaf(x0.z, e1.x, acc);
+                acc = fmaf(x0.w, e1.y, acc);
+                acc = fmaf(x1.x, e2v.x, acc);
+                acc = fmaf(x1.y, e2v.y, acc);
+                acc = fmaf(x1.z, e3.x, acc);
+                acc = fmaf(x1.w, e3.y, acc);
+            }
+            const float s = warp_sum(acc);
+            if (lane == 0) {
+                if (logits) logits[v] = s;
+                const unsigned long long key = (uint64_t(float_key(s)) << 32) | uint32_t(~uint32_t(v));
+                mine[0] = key > mine[0] ? key : mine[0];
             }
         }
+    } else {
+        // several activation rows: four vocab rows per pass, so that each activation value read from
+        // shared memory serves four vocab rows
+        constexpr int VB = 4;
+        for (int v0 = (blockIdx.x * (kHeadThreads / 32) + warp) * VB; v0 < V; v0 += nwarps * VB) {
+            float acc[VB][kHeadMaxRows];
 #pragma unroll
-        for (int o = 0; o < kHeadMaxRows; ++o) {
-            if (o >= nout) break;
-            const float s = warp_sum(acc[o]);
-            if (lane == 0) {
-                if (logits) logits[size_t(o) * V + v] = s;
-                const unsigned long long key = (uint64_t(float_key(s)) << 32) | uint32_t(~uint32_t(v));
-                mine[o] = key > mine[o] ? key : mine[o];
+            for (int b = 0; b < VB; ++b)
+#pragma unroll
+                for (int o = 0; o < kHeadMaxRows; ++o) acc[b][o] = 0.f;
+#pragma unroll 2
+            for (int it = 0; it < ITER; ++it) {
+                float ef[VB][8];
+#pragma unroll
+                for (int b = 0; b < VB; ++b) {
+                    uint4 raw = make_uint4(0, 0, 0, 0);
+                    if (v0 + b < V) raw = __ldcs(reinterpret_cast<const uint4 *>(E + size_t(v0 + b) * H + it * 256 + lane * 8));
+                    const __half2 * e2 = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float2 f = __half22float2(e2[q]);
+                        ef[b][2 * q] = f.x;
+                        ef[b][2 * q + 1] = f.y;
+                    }
+                }
+#pragma unroll
+                for (int o = 0; o < kHeadMaxRows; ++o) {
+                    if (o >= nout) break;
+                    const float4 * xr = reinterpret_cast<const float4 *>(xs + o * H + it * 256 + lane * 8);
+                    const float4 x0 = xr[0], x1 = xr[1];
+                    const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                    for (int b = 0; b < VB; ++b)
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) acc[b][o] = fmaf(xv[q], ef[b][q], acc[b][o]);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < VB; ++b) {
+                const int v = v0 + b;
+#pragma unroll
+                for (int o = 0; o < kHeadMaxRows; ++o) {
+                    if (o >= nout) break;
+                    const float s = warp_sum(acc[b][o]);
+                    if (lane == 0 && v < V) {
+                        if (logits) logits[size_t(o) * V + v] = s;
+                        const unsigned long long key = (uint64_t(float_key(s)) << 32) | uint32_t(~uint32_t(v));
+                        mine[o] = key > mine[o] ? key : mine[o];
+                    }
+                }
             }
         }
     }

@@ -262,6 +262,8 @@ class HybridEngine:
         self._batch_args = {}
         # L2 prefetch of layer i+1's weights while layer i runs (side stream, joined per step)
         self.prefetch = os.environ.get("EXL3_HYB_PREFETCH", "0") != "0"  # measured: no gain (see DESIGN)
+        if os.environ.get("EXL3_GEMM_MIN_ROWS"):  # tuning: rows at which the operator switches to the GEMM
+            check(L.exl3cu_gemm_config(int(os.environ["EXL3_GEMM_MIN_ROWS"]), 0, 0))
         self._pf_args = []
         for d in self.layers:
             ws = list(d["mats"].values())
@@ -276,20 +278,33 @@ class HybridEngine:
 
     # -- one step ---------------------------------------------------------------------------------
     def _mm_batch(self, names, mats, x, out_cols, rows, st):
-        """Projections sharing input x into column ranges of self.proj / self.gu."""
-        key = (tuple(names), id(mats), out_cols[0].data_ptr(), rows)
+        """Projections sharing input x into column ranges of self.proj / self.gu (or self.o, self.down).
+
+        Steps of 5..8 rows (batched decode) go to the operator as two problems of <= 4 rows per
+        matrix in one grouped call: the grouped integer-tensor-core GEMV then decodes the weights of
+        every matrix in one launch, which measured faster for these grouped decode shapes than one
+        tensor-core GEMM launch per matrix."""
+        key = (tuple(mats[nm].handle.value for nm in names), x.data_ptr(), tuple(o.data_ptr() for o in out_cols),
+               rows)
         args = self._batch_args.get(key)
         if args is None:
-            n = len(names)
+            pieces = [(0, rows)] if not 5 <= rows <= 8 else [(0, 4), (4, rows - 4)]
+            ws, xs, rs, ys, yst = [], [], [], [], []
+            for nm, o in zip(names, out_cols):
+                for r0, nr in pieces:
+                    ws.append(mats[nm].handle.value)
+                    xs.append(x.data_ptr() + r0 * x.stride(0) * x.element_size())
+                    rs.append(nr)
+                    ys.append(o.data_ptr() + r0 * o.stride(0) * o.element_size())
+                    yst.append(o.stride(0))
+            n = len(ws)
             VP, SZ, IN = ctypes.c_void_p * n, ctypes.c_size_t * n, ctypes.c_int * n
-            args = (n, VP(*[mats[nm].handle.value for nm in names]), VP(*[x.data_ptr()] * n), IN(*[0] * n),
-                    SZ(*[rows] * n), SZ(*[x.stride(0)] * n), VP(*[o.data_ptr() for o in out_cols]),
-                    SZ(*[o.stride(0) for o in out_cols]))
+            args = (n, VP(*ws), VP(*xs), IN(*[0] * n), SZ(*rs), SZ(*[x.stride(0)] * n), VP(*ys), SZ(*yst))
             self._batch_args[key] = args
         check(self.L.exl3cu_mul_mat_batch(*args, st))
 
     def _mm(self, w, x, out, rows, st):
-        check(self.L.exl3cu_mul_mat(w.handle, _vp(x), 0, rows, x.stride(0), _vp(out), out.stride(0), st))
+        self._mm_batch(("_one",), {"_one": w}, x, [out], rows, st)
 
     def forward(self, rows: int, n_seq: int, nout: int, stream=None):
         """Run the step whose metadata is in self.meta.dev; next tokens land in self.out_tokens[:nout]."""
