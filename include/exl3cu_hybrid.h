@@ -64,12 +64,15 @@ size_t exl3cu_hyb_gdn_smem_bytes(void);
 
 /* Gated delta rule over each step sequence's rows in order, per head:
  *   qkvz rows [q | k | v | z] (4 x 16 x 128, f32, the projections' outputs);
- *   xn: the layer's normed input rows, f32 (for the gate projections);
+ *   xn: the layer's normed input rows, f32 (for the gate projections); or,
+ *       with xn_norm_w, the residual-stream rows h, normalised here with
+ *       weights xn_norm_w [hidden] and eps (RMSNorm folded into the gates);
  *   wab: fp16 [32][hidden], rows 0..15 W_a, 16..31 W_b;
  *   conv_w f32 [3*2048][4], conv_state f32 [n_slots][3*2048][3] (last three inputs);
  *   A_log, dt_bias f32 [16]; norm_w f32 [128]; state f32 [n_slots][16][128 (k)][128 (v)].
  * Writes f32 [rows][16*128] = RMSNorm(o_head) * norm_w * silu(z_head). */
-int exl3cu_hyb_gdn(const float * d_qkvz, const float * d_xn, const uint16_t * d_wab, int hidden,
+int exl3cu_hyb_gdn(const float * d_qkvz, const float * d_xn, const float * d_xn_norm_w, const uint16_t * d_wab,
+                   int hidden,
                    const float * d_conv_w, float * d_conv_state, const float * d_A_log, const float * d_dt_bias,
                    const float * d_norm_w, float eps, float * d_state, const int32_t * d_row_offsets,
                    const int32_t * d_seq_slot, int n_seq, int n_slots, float * d_out, void * stream);

@@ -276,3 +276,47 @@ def test_global_workspace_variant_matches(ops):
     rel, _ = errs(a.cpu().numpy(), b.cpu().numpy())
     assert rel < TOL_MAX_ABS_REL
     w.free()
+
+
+def test_fused_input_forms_and_accumulate(ops):
+    """exl3cu_mul_mat_batch_ex: SwiGLU-on-load and RMSNorm-on-load inputs and the accumulating
+    epilogue against the plain operator on inputs formed in fp32 on the host (same values up to
+    the order of the RMS sum)."""
+    import ctypes
+
+    from exl3_b200 import _lib, synthetic
+
+    L = _lib.lib()
+    k, n, bits = 1024, 512, 4
+    m = synthetic.matrix(k, n, bits, seed=61)
+    w = ops.Exl3Weight.from_records(m.records(), k, n, bits)
+    rng = np.random.default_rng(7)
+    for rows in (1, 3, 4):
+        gu = torch.from_numpy(rng.standard_normal((rows, 2 * k)).astype(np.float32)).cuda()
+        h = torch.from_numpy((rng.standard_normal((rows, k)) * 3).astype(np.float32)).cuda()
+        nw = torch.from_numpy((1 + 0.1 * rng.standard_normal(k)).astype(np.float32)).cuda()
+        base = torch.from_numpy(rng.standard_normal((rows, n)).astype(np.float32)).cuda()
+        g, u = gu[:, :k], gu[:, k:]
+        x_glu = (g / (1 + torch.exp(-g)) * u).contiguous()
+        x_rms = (h * torch.rsqrt((h * h).mean(dim=1, keepdim=True) + 1e-6) * nw).contiguous()
+        y_glu = base.clone()
+        y_rms = torch.empty((rows, n), dtype=torch.float32, device="cuda")
+        VP, SZ, IN = ctypes.c_void_p * 2, ctypes.c_size_t * 2, ctypes.c_int * 2
+        rc = L.exl3cu_mul_mat_batch_ex(
+            2, VP(w.handle.value, w.handle.value), VP(gu.data_ptr(), h.data_ptr()), IN(_lib.X_GLU, _lib.X_RMSNORM),
+            SZ(rows, rows), SZ(2 * k, k), VP(0, nw.data_ptr()), ctypes.c_float(1e-6),
+            VP(y_glu.data_ptr(), y_rms.data_ptr()), SZ(n, n), IN(1, 0), None)
+        assert rc == 0, L.exl3cu_last_error()
+        ref_glu = base + w.mul_mat(x_glu)
+        ref_rms = w.mul_mat(x_rms)
+        torch.cuda.synchronize()
+        assert_close(y_glu.cpu().numpy(), ref_glu.cpu().numpy(), f"glu rows={rows}")
+        assert_close(y_rms.cpu().numpy(), ref_rms.cpu().numpy(), f"rmsnorm rows={rows}")
+    # the fused forms are GEMV-only: an 8-row item goes to the GEMM and is refused
+    h8 = torch.zeros((8, k), dtype=torch.float32, device="cuda")
+    y8 = torch.zeros((8, n), dtype=torch.float32, device="cuda")
+    VP1, SZ1, IN1 = ctypes.c_void_p * 1, ctypes.c_size_t * 1, ctypes.c_int * 1
+    rc = L.exl3cu_mul_mat_batch_ex(1, VP1(w.handle.value), VP1(h8.data_ptr()), IN1(_lib.X_RMSNORM), SZ1(8), SZ1(k),
+                                   VP1(nw.data_ptr()), ctypes.c_float(1e-6), VP1(y8.data_ptr()), SZ1(n), None, None)
+    assert rc == _lib.NO_SUPPORT
+    w.free()

@@ -239,6 +239,10 @@ struct MmItem {
     size_t x_stride;
     float * y;
     size_t y_stride;
+    int x_mode = kXPlain;       // kXGlu / kXRmsNorm: fused input forms (mul1 GEMV only)
+    const float * nw = nullptr;  // kXRmsNorm weights [k]
+    float eps = 0.f;
+    int y_accum = 0;
 };
 
 bool pdl_enabled() {
@@ -362,6 +366,9 @@ int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
     gemv_items.reserve(count);
     for (size_t i = 0; i < count; ++i) {
         if (items[i].rows >= gemm_min_rows()) {
+            if (items[i].x_mode != kXPlain || items[i].y_accum)
+                return fail(EXL3CU_NO_SUPPORT, "fused input forms and accumulation run on the GEMV (rows < %zu)",
+                            gemm_min_rows());
             int rc = run_gemm(items[i], st);
             if (rc) return rc;
         } else {
@@ -376,6 +383,9 @@ int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
         float * y;
         size_t x_stride, y_stride;
         int rows, x_f16;
+        int x_mode, y_accum;
+        const float * nw;
+        float eps;
     };
     std::vector<Sub> subs;
     for (size_t i = 0; i < count; ++i) {
@@ -392,6 +402,10 @@ int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
             s.y_stride = it.y_stride;
             s.rows = int(it.rows - r0 < per ? it.rows - r0 : per);
             s.x_f16 = it.x_dtype == EXL3CU_F16;
+            s.x_mode = it.x_mode;
+            s.y_accum = it.y_accum;
+            s.nw = it.nw;
+            s.eps = it.eps;
             subs.push_back(s);
         }
     }
@@ -421,6 +435,10 @@ int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
             P.nchunks = int(s.w->k / 16);
             P.rows = s.rows;
             P.x_f16 = s.x_f16;
+            P.x_mode = s.x_mode;
+            P.nw = s.nw;
+            P.eps = s.eps;
+            P.y_accum = s.y_accum;
             P.unit_base = units;
             units += int(s.w->nblocks);
             min_nchunks = P.nchunks < min_nchunks ? P.nchunks : min_nchunks;
@@ -433,6 +451,9 @@ int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
             if (e != cudaSuccess) return cuda_fail(e, "launching the EXL3 mul1 GEMV");
             continue;
         }
+        for (size_t gi = 0; gi < group.size(); ++gi)
+            if (subs[group[gi]].x_mode != kXPlain || subs[group[gi]].y_accum)
+                return fail(EXL3CU_NO_SUPPORT, "fused input forms and accumulation need mul1 weights of 2..8 bits");
         b.splits = choose_cluster_splits(subs[i].w->sms, units, min_nchunks);
         int max_cps = 1;
         for (int gi = 0; gi < b.count; ++gi) {
@@ -673,6 +694,44 @@ int exl3cu_mul_mat_batch(size_t count, const exl3cu_weight * const * weights, co
             return fail(rc, "batch item %zu: %s", i, why.c_str());
         }
         items[i] = MmItem{weights[i], d_x[i], x_dtype[i], rows[i], x_row_stride[i], d_y[i], y_row_stride[i]};
+    }
+    return run_cluster(items.data(), count, static_cast<cudaStream_t>(stream));
+}
+
+int exl3cu_mul_mat_batch_ex(size_t count, const exl3cu_weight * const * weights, const void * const * d_x,
+                            const int * x_form, const size_t * rows, const size_t * x_row_stride,
+                            const float * const * d_norm_w, float eps, float * const * d_y,
+                            const size_t * y_row_stride, const int * y_accumulate, void * stream) {
+    if (!count) return EXL3CU_OK;
+    if (!weights || !d_x || !x_form || !rows || !x_row_stride || !d_y || !y_row_stride)
+        return fail(EXL3CU_INVALID_ARGUMENT, "batch arrays must not be NULL");
+    std::vector<MmItem> items(count);
+    for (size_t i = 0; i < count; ++i) {
+        const int form = x_form[i];
+        if (form < EXL3CU_F32 || form > EXL3CU_X_RMSNORM)
+            return fail(EXL3CU_INVALID_ARGUMENT, "batch item %zu: unknown input form %d", i, form);
+        const int dtype = form == EXL3CU_F16 ? EXL3CU_F16 : EXL3CU_F32;
+        int rc = validate_mm(weights[i], d_x[i], dtype, rows[i], x_row_stride[i], d_y[i], y_row_stride[i]);
+        if (!rc) rc = check_device_ptr(d_x[i], weights[i]->device, "x");
+        if (!rc) rc = check_device_ptr(d_y[i], weights[i]->device, "y");
+        if (!rc && form == EXL3CU_X_GLU && x_row_stride[i] < 2 * weights[i]->k)
+            rc = fail(EXL3CU_INVALID_ARGUMENT, "GLU rows hold gate and up: stride at least 2k");
+        if (!rc && form == EXL3CU_X_RMSNORM) {
+            if (!d_norm_w || !d_norm_w[i]) rc = fail(EXL3CU_INVALID_ARGUMENT, "RMSNorm input needs norm weights");
+            else if (reinterpret_cast<uintptr_t>(d_norm_w[i]) % 16)
+                rc = fail(EXL3CU_INVALID_ARGUMENT, "norm weights must be 16-byte aligned");
+            else rc = check_device_ptr(d_norm_w[i], weights[i]->device, "norm weights");
+        }
+        if (rc) {
+            std::string why = g_last_error;
+            return fail(rc, "batch item %zu: %s", i, why.c_str());
+        }
+        MmItem it{weights[i], d_x[i], dtype, rows[i], x_row_stride[i], d_y[i], y_row_stride[i]};
+        it.x_mode = form == EXL3CU_X_GLU ? kXGlu : form == EXL3CU_X_RMSNORM ? kXRmsNorm : kXPlain;
+        it.nw = form == EXL3CU_X_RMSNORM ? d_norm_w[i] : nullptr;
+        it.eps = eps;
+        it.y_accum = y_accumulate ? (y_accumulate[i] != 0) : 0;
+        items[i] = it;
     }
     return run_cluster(items.data(), count, static_cast<cudaStream_t>(stream));
 }

@@ -74,7 +74,7 @@ __host__ __device__ inline Mul1Layout mul1_layout(int bits, int cps, int rows, i
     L.slot_off = int(L.part_off + part);
     L.gmax_off = int(L.slot_off + slot);
     L.bar_off = int((L.gmax_off + gmax + 15) & ~size_t(15));
-    L.bytes = L.bar_off + 2 * stages * 8 + 2 * 4 * kMRows;
+    L.bytes = L.bar_off + 2 * stages * 8 + 3 * 4 * kMRows;  // + per-row scale, digit sum, inverse norm
     return L;
 }
 
@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
     uint64_t * empty = full + NS;
     float * scale_s = reinterpret_cast<float *>(empty + NS);
     int * xsum_s = reinterpret_cast<int *>(scale_s + kMRows);
+    float * invn_s = reinterpret_cast<float *>(xsum_s + kMRows);  // kXRmsNorm: 1/rms of each row
     const int nacc = rows * 256;
 
     if (threadIdx.x == 0) {
@@ -167,7 +168,54 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             if (item < nitems) su_pre[ii] = *reinterpret_cast<const uint2 *>(P.su + (g0 + item / rows) * 128 + lane * 4);
         }
         pdl_wait_primary();  // activations may be written by the previous kernel
+        const int ktot = P.nchunks * 16;
+        if (P.x_mode == kXRmsNorm) {
+            // every CTA takes the whole row's mean square (from L2) before normalising its K range
+            float * red = part;  // scratch until the epilogue: [kMW][rows]
+            for (int r = 0; r < rows; ++r) {
+                const float * hr = static_cast<const float *>(P.x) + size_t(r) * P.x_stride;
+                float ss = 0.f;
+                for (int i = threadIdx.x * 4; i < ktot; i += kMW * 32 * 4) {
+                    const float4 v = *reinterpret_cast<const float4 *>(hr + i);
+                    ss = fmaf(v.x, v.x, ss);
+                    ss = fmaf(v.y, v.y, ss);
+                    ss = fmaf(v.z, v.z, ss);
+                    ss = fmaf(v.w, v.w, ss);
+                }
+#pragma unroll
+                for (int sh = 16; sh; sh >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sh);
+                if (lane == 0) red[warp * rows + r] = ss;
+            }
+            consumer_sync();
+            if (threadIdx.x < rows) {
+                float ss = 0.f;
+                for (int w = 0; w < kMW; ++w) ss += red[w * rows + threadIdx.x];
+                invn_s[threadIdx.x] = rsqrtf(ss / float(ktot) + P.eps);
+            }
+            consumer_sync();
+        }
         auto load_x = [&](int r, int kcol, float (&o)[4]) {
+            if (P.x_mode == kXGlu) {
+                const float * xr = static_cast<const float *>(P.x) + size_t(r) * P.x_stride;
+                const float4 g = *reinterpret_cast<const float4 *>(xr + kcol);
+                const float4 u = *reinterpret_cast<const float4 *>(xr + ktot + kcol);
+                o[0] = g.x / (1.0f + expf(-g.x)) * u.x;
+                o[1] = g.y / (1.0f + expf(-g.y)) * u.y;
+                o[2] = g.z / (1.0f + expf(-g.z)) * u.z;
+                o[3] = g.w / (1.0f + expf(-g.w)) * u.w;
+                return;
+            }
+            if (P.x_mode == kXRmsNorm) {
+                const float4 hv = *reinterpret_cast<const float4 *>(static_cast<const float *>(P.x) +
+                                                                    size_t(r) * P.x_stride + kcol);
+                const float4 wv = *reinterpret_cast<const float4 *>(P.nw + kcol);
+                const float inv = invn_s[r];
+                o[0] = hv.x * inv * wv.x;
+                o[1] = hv.y * inv * wv.y;
+                o[2] = hv.z * inv * wv.z;
+                o[3] = hv.w * inv * wv.w;
+                return;
+            }
             if (P.x_f16) {
                 const uint2 raw = *reinterpret_cast<const uint2 *>(static_cast<const __half *>(P.x) +
                                                                    size_t(r) * P.x_stride + kcol);
@@ -187,22 +235,8 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             o[3] = __fmul_rn(o[3], __high2float(s23));
         };
         auto load_xsu = [&](int r, int kcol, float (&o)[4]) {
-            if (P.x_f16) {
-                const uint2 raw = *reinterpret_cast<const uint2 *>(static_cast<const __half *>(P.x) +
-                                                                   size_t(r) * P.x_stride + kcol);
-                const __half2 lo = bits_half2(raw.x), hi = bits_half2(raw.y);
-                o[0] = __low2float(lo); o[1] = __high2float(lo); o[2] = __low2float(hi); o[3] = __high2float(hi);
-            } else {
-                const float4 f = *reinterpret_cast<const float4 *>(static_cast<const float *>(P.x) +
-                                                                   size_t(r) * P.x_stride + kcol);
-                o[0] = f.x; o[1] = f.y; o[2] = f.z; o[3] = f.w;
-            }
-            const uint2 sraw = *reinterpret_cast<const uint2 *>(P.su + kcol);
-            const __half2 s01 = bits_half2(sraw.x), s23 = bits_half2(sraw.y);
-            o[0] = __fmul_rn(o[0], __low2float(s01));
-            o[1] = __fmul_rn(o[1], __high2float(s01));
-            o[2] = __fmul_rn(o[2], __low2float(s23));
-            o[3] = __fmul_rn(o[3], __high2float(s23));
+            load_x(r, kcol, o);
+            apply_su(*reinterpret_cast<const uint2 *>(P.su + kcol), o);
         };
         // (1) the CTA's (group, row) items round robin over warps: xh = H128(x * su), the
         //     first kItems kept in registers, each group's max |xh| published
@@ -388,7 +422,15 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             o.y = __fmul_rn(v[1], __high2float(s01));
             o.z = __fmul_rn(v[2], __low2float(s23));
             o.w = __fmul_rn(v[3], __high2float(s23));
-            *reinterpret_cast<float4 *>(P.y + size_t(r) * P.y_stride + nb * 128 + lane * 4) = o;
+            float4 * yp = reinterpret_cast<float4 *>(P.y + size_t(r) * P.y_stride + nb * 128 + lane * 4);
+            if (P.y_accum) {
+                const float4 prev = *yp;
+                o.x += prev.x;
+                o.y += prev.y;
+                o.z += prev.z;
+                o.w += prev.w;
+            }
+            *yp = o;
         }
     }
 }

@@ -353,11 +353,11 @@ struct GdnSmem {
 };
 
 __global__ void __launch_bounds__(kGdnThreads, 1)
-k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const __half * __restrict__ wab, int H,
-      const float * __restrict__ conv_w, float * __restrict__ conv_state, const float * __restrict__ A_log,
-      const float * __restrict__ dt_bias, const float * __restrict__ norm_w, float eps, float * __restrict__ S,
-      const int32_t * __restrict__ row_offsets, const int32_t * __restrict__ seq_slot, int n_slots,
-      float * __restrict__ out) {
+k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const float * __restrict__ xn_norm_w,
+      const __half * __restrict__ wab, int H, const float * __restrict__ conv_w, float * __restrict__ conv_state,
+      const float * __restrict__ A_log, const float * __restrict__ dt_bias, const float * __restrict__ norm_w,
+      float eps, float * __restrict__ S, const int32_t * __restrict__ row_offsets,
+      const int32_t * __restrict__ seq_slot, int n_slots, float * __restrict__ out) {
     extern __shared__ __align__(128) float sm[];
     float * tq = sm + GdnSmem::Q;
     float * tk = sm + GdnSmem::K;
@@ -433,10 +433,12 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const __ha
             const int part = c / kHD, d = c % kHD;
             (part == 0 ? tq : part == 1 ? tk : tv)[rr * kHD + d] = silu(acc);
         }
-        // gate projections: warp per row, 16-byte loads of the row in flight together
+        // gate projections: warp per row, 16-byte loads of the row in flight together.  With
+        // xn_norm_w the rows are the residual stream h and the layer's RMSNorm is folded in:
+        // x . W = rsqrt(mean(h^2) + eps) * sum h * w * W.
         for (int rr = warp; rr < nt; rr += kGdnThreads / 32) {
             const float * xr = xn + size_t(tr0 + rr) * H;
-            float pa = 0.f, pb = 0.f;
+            float pa = 0.f, pb = 0.f, ss = 0.f;
             for (int ib0 = lane * 4; ib0 < H; ib0 += 32 * 4 * 4) {
                 float4 raw[4];
 #pragma unroll
@@ -447,7 +449,16 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const __ha
                 for (int u = 0; u < 4; ++u) {
                     const int ib = ib0 + u * 128;
                     if (ib >= H) break;
-                    const float xv[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+                    float xv[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+                    if (xn_norm_w) {
+                        const float4 wv = *reinterpret_cast<const float4 *>(xn_norm_w + ib);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) ss = fmaf(xv[q], xv[q], ss);
+                        xv[0] *= wv.x;
+                        xv[1] *= wv.y;
+                        xv[2] *= wv.z;
+                        xv[3] *= wv.w;
+                    }
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         pa = fmaf(xv[q], __half2float(wab_s[ib + q]), pa);
@@ -457,6 +468,11 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const __ha
             }
             pa = warp_sum(pa);
             pb = warp_sum(pb);
+            if (xn_norm_w) {
+                const float inv = rsqrtf(warp_sum(ss) / float(H) + eps);
+                pa *= inv;
+                pb *= inv;
+            }
             if (lane == 0) {
                 gate[rr * 4 + 0] = expf(A * softplus(pa + dtb));  // alpha
                 gate[rr * 4 + 1] = 1.0f / (1.0f + expf(-pb));     // beta
@@ -839,7 +855,8 @@ size_t exl3cu_hyb_gdn_smem_bytes_for(int hidden) {
 
 size_t exl3cu_hyb_gdn_smem_bytes(void) { return exl3cu_hyb_gdn_smem_bytes_for(8192); }
 
-int exl3cu_hyb_gdn(const float * d_qkvz, const float * d_xn, const uint16_t * d_wab, int hidden,
+int exl3cu_hyb_gdn(const float * d_qkvz, const float * d_xn, const float * d_xn_norm_w, const uint16_t * d_wab,
+                   int hidden,
                    const float * d_conv_w, float * d_conv_state, const float * d_A_log, const float * d_dt_bias,
                    const float * d_norm_w, float eps, float * d_state, const int32_t * d_row_offsets,
                    const int32_t * d_seq_slot, int n_seq, int n_slots, float * d_out, void * stream) {
@@ -854,7 +871,7 @@ int exl3cu_hyb_gdn(const float * d_qkvz, const float * d_xn, const uint16_t * d_
     if (!set_smem_attr_once(reinterpret_cast<const void *>(k_gdn), int(exl3cu_hyb_gdn_smem_bytes()), g_gdn_attr))
         return status_of(cudaGetLastError());
     return launch_pdl_cluster(k_gdn, dim3(kNH * kGdnSplit, unsigned(n_seq)), dim3(kGdnThreads), smem, kGdnSplit,
-                      stream, d_qkvz, d_xn,
+                      stream, d_qkvz, d_xn, d_xn_norm_w,
                       reinterpret_cast<const __half *>(d_wab), hidden,
                       d_conv_w, d_conv_state, d_A_log, d_dt_bias, d_norm_w, eps, d_state, d_row_offsets, d_seq_slot,
                       n_slots, d_out);

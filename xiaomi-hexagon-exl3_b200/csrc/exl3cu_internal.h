@@ -44,8 +44,14 @@ struct GemvProblem {
     int rows;       // 1..8
     int x_f16;
     int unit_base;  // first unit (column block) of this problem in the launch
-    int pad;
+    int x_mode;     // kXPlain; kXGlu: rows [gate (k) | up (k)], input silu(gate) up;
+                    // kXRmsNorm: rows h, input h rsqrt(mean(h^2) + eps) nw (mul1 kernel only)
+    const float * nw;
+    float eps;
+    int y_accum;    // 1: y += x . W (one writer per element) instead of y = x . W
 };
+
+constexpr int kXPlain = 0, kXGlu = 1, kXRmsNorm = 2;
 
 constexpr int kMaxBatch = 8;  // problems per launch, passed by value in the kernel parameters
 

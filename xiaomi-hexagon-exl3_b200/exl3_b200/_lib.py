@@ -14,6 +14,7 @@ GGML_LIB_PATH = PKG_DIR / "libexl3cu_ggml.so"
 
 OK, INVALID_ARGUMENT, NO_SUPPORT, OUT_OF_MEMORY, CUDA_ERROR = range(5)
 F32, F16 = 0, 1
+X_GLU, X_RMSNORM = 2, 3
 CB_3INST, CB_MCG, CB_MUL1 = 0, 1, 2
 ST_F16, ST_BF16, ST_I16, ST_F32, ST_I32 = range(5)
 MODEL_VALIDATE_ONLY = 1
@@ -27,6 +28,7 @@ EXPORTS = (
     "exl3cu_mul_mat_host", "exl3cu_mul_mat_noalloc", "exl3cu_mul_mat_batch",
     "exl3cu_device_status", "exl3cu_gemm_config", "exl3cu_pack_ragged", "exl3cu_mul_mat_ragged",
     "exl3cu_mul_mat_sequence", "exl3cu_get_rows", "exl3cu_get_rows_host", "exl3cu_prefetch_l2",
+    "exl3cu_mul_mat_batch_ex",
     "exl3cu_model_open", "exl3cu_model_free", "exl3cu_model_info", "exl3cu_model_matrix_count",
     "exl3cu_model_matrix", "exl3cu_model_find_matrix", "exl3cu_model_head", "exl3cu_model_tensor",
     "exl3cu_model_find_tensor", "exl3cu_model_embedding", "exl3cu_model_embed",
@@ -86,6 +88,9 @@ def _declare(L):
                                           _c.POINTER(_c.c_int), _c.c_int, _vp]
     L.exl3cu_mul_mat_batch.argtypes = [_sz, _c.POINTER(_vp), _c.POINTER(_vp), _c.POINTER(_c.c_int),
                                        _c.POINTER(_sz), _c.POINTER(_sz), _c.POINTER(_vp), _c.POINTER(_sz), _vp]
+    L.exl3cu_mul_mat_batch_ex.argtypes = [_sz, _c.POINTER(_vp), _c.POINTER(_vp), _c.POINTER(_c.c_int),
+                                          _c.POINTER(_sz), _c.POINTER(_sz), _c.POINTER(_vp), _c.c_float,
+                                          _c.POINTER(_vp), _c.POINTER(_sz), _c.POINTER(_c.c_int), _vp]
     _P = _c.POINTER
     L.exl3cu_model_open.argtypes = [_c.c_char_p, _c.c_int, _c.c_uint, _P(_vp)]
     L.exl3cu_model_free.argtypes = [_vp]

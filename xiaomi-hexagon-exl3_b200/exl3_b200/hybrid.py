@@ -149,7 +149,7 @@ def _declare(L):
     L.exl3cu_hyb_attn_scratch_bytes.argtypes = [I, I]
     L.exl3cu_hyb_status.argtypes = [I, ctypes.POINTER(ctypes.c_uint)]
     L.exl3cu_hyb_gdn_smem_bytes.restype = S
-    L.exl3cu_hyb_gdn.argtypes = [P, P, P, I, P, P, P, P, P, F, P, P, P, I, I, P, P]
+    L.exl3cu_hyb_gdn.argtypes = [P, P, P, P, I, P, P, P, P, P, F, P, P, P, I, I, P, P]
     L.exl3cu_hyb_head.argtypes = [P, P, I, I, P, I, P, P, P, P]
     for n in ("exl3cu_hyb_embed", "exl3cu_hyb_rmsnorm", "exl3cu_hyb_swiglu", "exl3cu_hyb_attn_prep",
               "exl3cu_hyb_attn", "exl3cu_hyb_gdn", "exl3cu_hyb_head", "exl3cu_hyb_status"):
@@ -262,6 +262,7 @@ class HybridEngine:
         self._batch_args = {}
         # L2 prefetch of layer i+1's weights while layer i runs (side stream, joined per step)
         self.prefetch = os.environ.get("EXL3_HYB_PREFETCH", "0") != "0"  # measured: no gain (see DESIGN)
+        self.fused = os.environ.get("EXL3_HYB_FUSED", "1") != "0"  # layer glue folded into the operator
         if os.environ.get("EXL3_GEMM_MIN_ROWS"):  # tuning: rows at which the operator switches to the GEMM
             check(L.exl3cu_gemm_config(int(os.environ["EXL3_GEMM_MIN_ROWS"]), 0, 0))
         self._pf_args = []
@@ -277,15 +278,17 @@ class HybridEngine:
         self.conv[:, slot].zero_()
 
     # -- one step ---------------------------------------------------------------------------------
-    def _mm_batch(self, names, mats, x, out_cols, rows, st):
-        """Projections sharing input x into column ranges of self.proj / self.gu (or self.o, self.down).
+    def _mm_batch(self, names, mats, x, out_cols, rows, st, form: int = 0, nw=None, accum: bool = False):
+        """Projections sharing input x (form 0: f32 rows; 2: [gate | up] rows, SwiGLU on load; 3: residual
+        rows, RMSNorm with weights nw on load) into column ranges of the given outputs, stored or (accum)
+        added.
 
         Steps of 5..8 rows (batched decode) go to the operator as two problems of <= 4 rows per
         matrix in one grouped call: the grouped integer-tensor-core GEMV then decodes the weights of
         every matrix in one launch, which measured faster for these grouped decode shapes than one
         tensor-core GEMM launch per matrix."""
         key = (tuple(mats[nm].handle.value for nm in names), x.data_ptr(), tuple(o.data_ptr() for o in out_cols),
-               rows)
+               rows, form, nw.data_ptr() if nw is not None else 0, accum)
         args = self._batch_args.get(key)
         if args is None:
             pieces = [(0, rows)] if not 5 <= rows <= 8 else [(0, 4), (4, rows - 4)]
@@ -299,12 +302,14 @@ class HybridEngine:
                     yst.append(o.stride(0))
             n = len(ws)
             VP, SZ, IN = ctypes.c_void_p * n, ctypes.c_size_t * n, ctypes.c_int * n
-            args = (n, VP(*ws), VP(*xs), IN(*[0] * n), SZ(*rs), SZ(*[x.stride(0)] * n), VP(*ys), SZ(*yst))
+            nws = VP(*[nw.data_ptr() if nw is not None else 0] * n)
+            args = (n, VP(*ws), VP(*xs), IN(*[form] * n), SZ(*rs), SZ(*[x.stride(0)] * n), nws,
+                    ctypes.c_float(self.cfg.eps), VP(*ys), SZ(*yst), IN(*[1 if accum else 0] * n))
             self._batch_args[key] = args
-        check(self.L.exl3cu_mul_mat_batch(*args, st))
+        check(self.L.exl3cu_mul_mat_batch_ex(*args, st))
 
-    def _mm(self, w, x, out, rows, st):
-        self._mm_batch(("_one",), {"_one": w}, x, [out], rows, st)
+    def _mm(self, w, x, out, rows, st, form: int = 0, nw=None, accum: bool = False):
+        self._mm_batch(("_one",), {"_one": w}, x, [out], rows, st, form, nw, accum)
 
     def forward(self, rows: int, n_seq: int, nout: int, stream=None):
         """Run the step whose metadata is in self.meta.dev; next tokens land in self.out_tokens[:nout]."""
@@ -322,8 +327,12 @@ class HybridEngine:
             self._pf_stream.wait_event(self._pf_events[0])
             check(L.exl3cu_prefetch_l2(n0, a0, ctypes.c_void_p(self._pf_stream.cuda_stream)))
         check(L.exl3cu_hyb_embed(_vp(self.embed), cfg.vocab, _vp(tokens), rows, H, _vp(self.h), st))
-        delta = None
         scale = 1.0 / float(np.sqrt(cfg.head_dim))
+        if rows <= 8 and self.fused:
+            self._forward_fused(rows, n_seq, nout, st, scale, row_seq, row_pos, row_offsets, seq_slot, logit_rows,
+                                pf, main)
+            return
+        delta = None
         for li, d in enumerate(self.layers):
             mats = d["mats"]
             if pf and li + 1 < len(self.layers):
@@ -353,7 +362,7 @@ class HybridEngine:
                 outs = [p[:, 0:D], p[:, D:2 * D], p[:, 2 * D:3 * D], p[:, 3 * D:4 * D]]
                 self._mm_batch(("q", "k", "v", "z"), mats, self.xn, outs, rows, st)
                 c = d["cache"]
-                check(L.exl3cu_hyb_gdn(_vp(p), _vp(self.xn), _vp(d["wab"]), H, _vp(d["conv_w"]), _vp(self.conv[c]),
+                check(L.exl3cu_hyb_gdn(_vp(p), _vp(self.xn), None, _vp(d["wab"]), H, _vp(d["conv_w"]), _vp(self.conv[c]),
                                        _vp(d["A_log"]), _vp(d["dt_bias"]), _vp(d["gnorm"]), cfg.eps,
                                        _vp(self.state[c]), _vp(row_offsets), _vp(seq_slot), n_seq, self.slots,
                                        _vp(self.mix), st))
@@ -369,6 +378,55 @@ class HybridEngine:
         check(L.exl3cu_hyb_head(_vp(self.xn), _vp(logit_rows), nout, H, _vp(self.embed), cfg.vocab, None,
                                 _vp(self.best), _vp(self.out_tokens), st))
         if pf:  # join the prefetch stream (required inside a capture; cheap otherwise)
+            ev = self._pf_events[-1]
+            ev.record(self._pf_stream)
+            main.wait_event(ev)
+
+    def _forward_fused(self, rows, n_seq, nout, st, scale, row_seq, row_pos, row_offsets, seq_slot, logit_rows, pf,
+                       main):
+        """Steps of <= 8 rows: the layer glue folded into the packed operator -- RMSNorm on load for the
+        projections (and inside the delta-rule gates), SwiGLU on load for the down projection, the o and
+        down products added into the residual stream h -- so a layer is 4 operator launches plus its
+        mixer (attention or delta rule)."""
+        cfg, L = self.cfg, self.L
+        H, F, D, KV = cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim, self.KV
+        for li, d in enumerate(self.layers):
+            mats = d["mats"]
+            if pf and li + 1 < len(self.layers):
+                n1, a1 = self._pf_args[li + 1]
+                self._pf_events[li + 1].record(main)
+                self._pf_stream.wait_event(self._pf_events[li + 1])
+                check(L.exl3cu_prefetch_l2(n1, a1, ctypes.c_void_p(self._pf_stream.cuda_stream)))
+            if d["kind"] == "full":
+                qkv = self.proj.view(-1)[: self.max_rows * (D + 2 * KV)].view(self.max_rows, D + 2 * KV)
+                outs = [qkv[:, 0:D], qkv[:, D:D + KV], qkv[:, D + KV:D + 2 * KV]]
+                self._mm_batch(("q", "k", "v"), mats, self.h, outs, rows, st, 3, d["in_norm"])
+                c = d["cache"]
+                kc, vc = self.kc[c], self.vc[c]
+                check(L.exl3cu_hyb_attn_prep(_vp(qkv), rows, _vp(row_seq), _vp(row_pos), _vp(seq_slot),
+                                             _vp(d["q_norm"]), _vp(d["k_norm"]), _vp(self.inv_freq), cfg.eps,
+                                             _vp(kc), _vp(vc), self.max_len, self.slots, _vp(self.q), st))
+                sp = attn_splits(rows)
+                check(L.exl3cu_hyb_attn(_vp(self.q), rows, _vp(row_seq), _vp(row_pos), _vp(seq_slot), _vp(kc),
+                                        _vp(vc), self.max_len, self.slots, scale, sp, _vp(self.attn_part),
+                                        self.attn_part.numel() * 4, _vp(self.attn_tickets), _vp(self.mix), st))
+            else:
+                p = self.proj
+                outs = [p[:, 0:D], p[:, D:2 * D], p[:, 2 * D:3 * D], p[:, 3 * D:4 * D]]
+                self._mm_batch(("q", "k", "v", "z"), mats, self.h, outs, rows, st, 3, d["in_norm"])
+                c = d["cache"]
+                check(L.exl3cu_hyb_gdn(_vp(p), _vp(self.h), _vp(d["in_norm"]), _vp(d["wab"]), H, _vp(d["conv_w"]),
+                                       _vp(self.conv[c]), _vp(d["A_log"]), _vp(d["dt_bias"]), _vp(d["gnorm"]),
+                                       cfg.eps, _vp(self.state[c]), _vp(row_offsets), _vp(seq_slot), n_seq,
+                                       self.slots, _vp(self.mix), st))
+            self._mm(mats["o"], self.mix, self.h, rows, st, 0, None, True)                 # h += o
+            self._mm_batch(("gate", "up"), mats, self.h, [self.gu[:, 0:F], self.gu[:, F:2 * F]], rows, st, 3,
+                           d["post_norm"])
+            self._mm(mats["down"], self.gu, self.h, rows, st, 2, None, True)               # h += down(swiglu)
+        check(L.exl3cu_hyb_rmsnorm(_vp(self.h), None, H, _vp(self.final_norm), cfg.eps, rows, H, _vp(self.xn), st))
+        check(L.exl3cu_hyb_head(_vp(self.xn), _vp(logit_rows), nout, H, _vp(self.embed), cfg.vocab, None,
+                                _vp(self.best), _vp(self.out_tokens), st))
+        if pf:
             ev = self._pf_events[-1]
             ev.record(self._pf_stream)
             main.wait_event(ev)
