@@ -169,7 +169,19 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
         }
         pdl_wait_primary();  // activations may be written by the previous kernel
         const int ktot = P.nchunks * 16;
+        float v[kItems][4];
         if (P.x_mode == kXRmsNorm) {
+            // the register-cached items' raw h goes out with the full-row loads below (one round trip)
+#pragma unroll
+            for (int ii = 0; ii < kItems; ++ii) {
+                const int item = warp + ii * kMW;
+                if (item < nitems) {
+                    const int gi = item / rows;
+                    const float4 hv = *reinterpret_cast<const float4 *>(
+                        static_cast<const float *>(P.x) + size_t(item - gi * rows) * P.x_stride + (g0 + gi) * 128 + lane * 4);
+                    v[ii][0] = hv.x; v[ii][1] = hv.y; v[ii][2] = hv.z; v[ii][3] = hv.w;
+                }
+            }
             // every CTA takes the whole row's mean square (from L2) before normalising its K range
             float * red = part;  // scratch until the epilogue: [kMW][rows]
             for (int r = 0; r < rows; ++r) {
@@ -240,7 +252,6 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
         };
         // (1) the CTA's (group, row) items round robin over warps: xh = H128(x * su), the
         //     first kItems kept in registers, each group's max |xh| published
-        float v[kItems][4];
         auto rotate_from = [&](int item, float (&o)[4]) {  // o already holds x * su
             const int gi = item / rows;
             const int r = item - gi * rows;
@@ -261,7 +272,17 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             const int item = warp + ii * kMW;
             if (item < nitems) {
                 const int gi = item / rows;
-                load_x(item - gi * rows, (g0 + gi) * 128 + lane * 4, v[ii]);
+                const int kcol = (g0 + gi) * 128 + lane * 4;
+                if (P.x_mode == kXRmsNorm) {  // raw h already loaded: normalise
+                    const float4 wv = *reinterpret_cast<const float4 *>(P.nw + kcol);
+                    const float inv = invn_s[item - gi * rows];
+                    v[ii][0] = v[ii][0] * inv * wv.x;
+                    v[ii][1] = v[ii][1] * inv * wv.y;
+                    v[ii][2] = v[ii][2] * inv * wv.z;
+                    v[ii][3] = v[ii][3] * inv * wv.w;
+                } else {
+                    load_x(item - gi * rows, kcol, v[ii]);
+                }
             }
         }
 #pragma unroll

@@ -25,8 +25,10 @@
 //
 // Every kernel is launched with programmatic dependent launch: it lets the
 // next kernel be scheduled at once (griddepcontrol.launch_dependents) and
-// reads or writes nothing before its own griddepcontrol.wait, which returns
-// when the preceding grid has completed and flushed -- so a chain of these
+// reads nothing that a kernel of the step writes, and writes nothing, before
+// its own griddepcontrol.wait (layer constants such as the delta rule's conv
+// weights may load earlier), which returns when the preceding grid has
+// completed and flushed -- so a chain of these
 // kernels and the EXL3 operator keeps stream order while each launch's
 // latency overlaps the tail of the one before.
 #include "exl3cu.h"
@@ -371,25 +373,14 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const floa
     __half * wab_s = reinterpret_cast<__half *>(sm + GdnSmem::WAB);
     cg::cluster_group cluster = cg::this_cluster();
     pdl_trigger();
-    pdl_wait_primary();
     const int h = blockIdx.x / kGdnSplit, s = blockIdx.y;
     const int rank = int(cluster.block_rank());
-    const int slot = seq_slot[s];
-    const int r0 = row_offsets[s], r1 = row_offsets[s + 1];
-    // every CTA of the cluster takes the same early exit, so no cluster barrier is left waiting
-    if (slot < 0 || slot >= n_slots || r1 <= r0) return;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int jj = t & (kGdnCols - 1), kp = t >> 5;   // column in the slice, k slice
-    const int j = rank * kGdnCols + jj;               // column in the head
-    const int i0 = kp * kGdnKRows;
-    float * Sg = S + (size_t(slot) * kNH + h) * kHD * kHD;
-    float Sr[kGdnKRows];  // S[i0 + i][j]
-#pragma unroll
-    for (int i = 0; i < kGdnKRows; ++i) Sr[i] = Sg[(i0 + i) * kHD + j];
     constexpr int QKVZ = 4 * kNH * kHD;
     constexpr int CH = 3 * kNH * kHD;  // convolved channels (q, k, v)
     constexpr int C3 = 3 * kHD;
-    // the head's conv weights and gate rows, once
+    // the head's conv weights, gate rows and scalars are layer constants that no kernel
+    // writes: they load while the previous kernel is still running
     for (int c = t; c < C3; c += kGdnThreads) {
         const int ch = (c / kHD) * kNH * kHD + h * kHD + c % kHD;
 #pragma unroll
@@ -402,52 +393,43 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const floa
     const float A = -expf(A_log[h]);
     const float dtb = dt_bias[h];
     const float qscale = rsqrtf(float(kHD));
+    pdl_wait_primary();
+    const int slot = seq_slot[s];
+    const int r0 = row_offsets[s], r1 = row_offsets[s + 1];
+    // every CTA of the cluster takes the same early exit, so no cluster barrier is left waiting
+    if (slot < 0 || slot >= n_slots || r1 <= r0) return;
+    const int jj = t & (kGdnCols - 1), kp = t >> 5;   // column in the slice, k slice
+    const int j = rank * kGdnCols + jj;               // column in the head
+    const int i0 = kp * kGdnKRows;
+    float * Sg = S + (size_t(slot) * kNH + h) * kHD * kHD;
+    float Sr[kGdnKRows];  // S[i0 + i][j]
+#pragma unroll
+    for (int i = 0; i < kGdnKRows; ++i) Sr[i] = Sg[(i0 + i) * kHD + j];
     int rb = 0;    // reduction buffer of the current row
     int tpar = 0;  // psum buffer of the current tile
     __syncthreads();
     for (int tr0 = r0; tr0 < r1; tr0 += kGdnTile, tpar ^= 1) {
         const int nt = min(kGdnTile, r1 - tr0);
-        // ---- A: stage the conv inputs x[tr0-3 .. tr0+nt-1] of the head's 384 channels ----
-        // (rows before the sequence's first come from the conv state)
-        for (int e = t; e < (nt + kConvW - 1) * (C3 / 4); e += kGdnThreads) {
-            const int rr = e / (C3 / 4), c4 = (e % (C3 / 4)) * 4;  // row tr0 - 3 + rr, channels c4..c4+3
-            const int ri = tr0 - (kConvW - 1) + rr;
-            const int part = c4 / kHD, d = c4 % kHD;
-            const int ch = part * kNH * kHD + h * kHD + d;
-            float4 x;
-            if (ri >= r0) {
-                x = *reinterpret_cast<const float4 *>(qkvz + size_t(ri) * QKVZ + ch);
-            } else {
-                const float * st = conv_state + (size_t(slot) * CH + ch) * (kConvW - 1) + (ri - r0 + kConvW - 1);
-                x = make_float4(st[0], st[kConvW - 1], st[2 * (kConvW - 1)], st[3 * (kConvW - 1)]);
-            }
-            *reinterpret_cast<float4 *>(cx + rr * C3 + c4) = x;
-        }
-        __syncthreads();
-        // conv + SiLU for every (row, channel) of the tile, from shared memory
-        for (int e = t; e < nt * C3; e += kGdnThreads) {
-            const int rr = e / C3, c = e % C3;
-            float acc = 0.f;
-#pragma unroll
-            for (int w = 0; w < kConvW; ++w) acc = fmaf(cx[(rr + w) * C3 + c], cw[c * kConvW + w], acc);
-            const int part = c / kHD, d = c % kHD;
-            (part == 0 ? tq : part == 1 ? tk : tv)[rr * kHD + d] = silu(acc);
-        }
-        // gate projections: warp per row, 16-byte loads of the row in flight together.  With
-        // xn_norm_w the rows are the residual stream h and the layer's RMSNorm is folded in:
+        // gate projections: every warp takes the 128-element blocks warp, warp + 8, ... of each
+        // row (a decode row is one round trip of 16-byte loads, not one per block), and the
+        // eight partial sums of a row meet in shared memory in warp order.  With xn_norm_w the
+        // rows are the residual stream h and the layer's RMSNorm is folded in:
         // x . W = rsqrt(mean(h^2) + eps) * sum h * w * W.
-        for (int rr = warp; rr < nt; rr += kGdnThreads / 32) {
+        constexpr int kGW = kGdnThreads / 32;
+        float * gpart = red;  // [T][kGW][3]: free until the recurrence
+#pragma unroll 2
+        for (int rr = 0; rr < nt; ++rr) {
             const float * xr = xn + size_t(tr0 + rr) * H;
             float pa = 0.f, pb = 0.f, ss = 0.f;
-            for (int ib0 = lane * 4; ib0 < H; ib0 += 32 * 4 * 4) {
-                float4 raw[4];
+            for (int ib0 = warp * 128 + lane * 4; ib0 < H; ib0 += kGW * 128 * 2) {
+                float4 raw[2];
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    raw[u] = ib0 + u * 128 < H ? *reinterpret_cast<const float4 *>(xr + ib0 + u * 128)
-                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int u = 0; u < 2; ++u)
+                    raw[u] = ib0 + u * kGW * 128 < H ? *reinterpret_cast<const float4 *>(xr + ib0 + u * kGW * 128)
+                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int ib = ib0 + u * 128;
+                for (int u = 0; u < 2; ++u) {
+                    const int ib = ib0 + u * kGW * 128;
                     if (ib >= H) break;
                     float xv[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
                     if (xn_norm_w) {
@@ -468,15 +450,57 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const floa
             }
             pa = warp_sum(pa);
             pb = warp_sum(pb);
+            ss = warp_sum(ss);
+            if (lane == 0) {
+                float * gp = gpart + (rr * kGW + warp) * 3;
+                gp[0] = pa;
+                gp[1] = pb;
+                gp[2] = ss;
+            }
+        }
+        // ---- stage the conv inputs x[tr0-3 .. tr0+nt-1] of the head's 384 channels ----
+        // (rows before the sequence's first come from the conv state); these loads are
+        // independent of the gate rows' and go out before the barrier
+        for (int e = t; e < (nt + kConvW - 1) * (C3 / 4); e += kGdnThreads) {
+            const int rr = e / (C3 / 4), c4 = (e % (C3 / 4)) * 4;  // row tr0 - 3 + rr, channels c4..c4+3
+            const int ri = tr0 - (kConvW - 1) + rr;
+            const int part = c4 / kHD, d = c4 % kHD;
+            const int ch = part * kNH * kHD + h * kHD + d;
+            float4 x;
+            if (ri >= r0) {
+                x = *reinterpret_cast<const float4 *>(qkvz + size_t(ri) * QKVZ + ch);
+            } else {
+                const float * st = conv_state + (size_t(slot) * CH + ch) * (kConvW - 1) + (ri - r0 + kConvW - 1);
+                x = make_float4(st[0], st[kConvW - 1], st[2 * (kConvW - 1)], st[3 * (kConvW - 1)]);
+            }
+            *reinterpret_cast<float4 *>(cx + rr * C3 + c4) = x;
+        }
+        __syncthreads();
+        if (t < nt) {
+            float pa = 0.f, pb = 0.f, ss = 0.f;
+#pragma unroll
+            for (int w = 0; w < kGW; ++w) {  // warp order
+                const float * gp = gpart + (t * kGW + w) * 3;
+                pa += gp[0];
+                pb += gp[1];
+                ss += gp[2];
+            }
             if (xn_norm_w) {
-                const float inv = rsqrtf(warp_sum(ss) / float(H) + eps);
+                const float inv = rsqrtf(ss / float(H) + eps);
                 pa *= inv;
                 pb *= inv;
             }
-            if (lane == 0) {
-                gate[rr * 4 + 0] = expf(A * softplus(pa + dtb));  // alpha
-                gate[rr * 4 + 1] = 1.0f / (1.0f + expf(-pb));     // beta
-            }
+            gate[t * 4 + 0] = expf(A * softplus(pa + dtb));  // alpha
+            gate[t * 4 + 1] = 1.0f / (1.0f + expf(-pb));     // beta
+        }
+        // conv + SiLU for every (row, channel) of the tile, from shared memory
+        for (int e = t; e < nt * C3; e += kGdnThreads) {
+            const int rr = e / C3, c = e % C3;
+            float acc = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConvW; ++w) acc = fmaf(cx[(rr + w) * C3 + c], cw[c * kConvW + w], acc);
+            const int part = c / kHD, d = c % kHD;
+            (part == 0 ? tq : part == 1 ? tk : tv)[rr * kHD + d] = silu(acc);
         }
         __syncthreads();
         // L2 norms and k.q: warp per row
@@ -543,39 +567,45 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const floa
         __syncthreads();  // every row's o slice is in `to`
         // ---- C: this rank's sum(o^2) per row, exchanged across the cluster ----
         float * ps = psum + tpar * kGdnTile;
+        constexpr int kZRows = kGdnTile / (kGdnThreads / 32);  // rows per warp
+        const int d = rank * kGdnCols + lane;
+        float zr[kZRows];  // the gate inputs z, loaded ahead of the exchange
+#pragma unroll
+        for (int q = 0; q < kZRows; ++q) {
+            const int rr = warp + q * (kGdnThreads / 32);
+            zr[q] = rr < nt ? qkvz[size_t(tr0 + rr) * QKVZ + 3 * kNH * kHD + h * kHD + d] : 0.f;
+        }
         for (int rr = warp; rr < nt; rr += kGdnThreads / 32) {
             const float o = to[rr * kGdnCols + lane];
             const float ss = warp_sum(o * o);
             if (lane == 0) ps[rr] = ss;
         }
         cluster.sync();  // every rank's partial sums are visible
-        for (int rr = warp; rr < nt; rr += kGdnThreads / 32) {
+#pragma unroll
+        for (int q = 0; q < kZRows; ++q) {
+            const int rr = warp + q * (kGdnThreads / 32);
+            if (rr >= nt) break;
             float ss = 0.f;
 #pragma unroll
-            for (int q = 0; q < kGdnSplit; ++q) ss += cluster.map_shared_rank(ps, q)[rr];  // rank order
+            for (int p = 0; p < kGdnSplit; ++p) ss += cluster.map_shared_rank(ps, p)[rr];  // rank order
             const float inv = rsqrtf(ss / float(kHD) + eps);
             const size_t r = size_t(tr0 + rr);
-            const int d = rank * kGdnCols + lane;
-            const float z = qkvz[r * QKVZ + 3 * kNH * kHD + h * kHD + d];
-            out[r * kNH * kHD + h * kHD + d] = to[rr * kGdnCols + lane] * inv * norm_w[d] * silu(z);
+            out[r * kNH * kHD + h * kHD + d] = to[rr * kGdnCols + lane] * inv * norm_w[d] * silu(zr[q]);
         }
+        if (tr0 + kGdnTile >= r1) break;  // the last tile's cx stays for the conv state below
         __syncthreads();  // the next tile overwrites tq, tk, tv, to, gate, cx (psum is double-buffered)
     }
     cluster.sync();  // peers are done reading this rank's psum, and with the conv state
-    // the conv state: the last three inputs of the sequence so far (rank 0)
+    // the conv state: the last three inputs of the sequence so far (rank 0), which are
+    // rows nt .. nt+2 of the last tile's staged inputs (those before the sequence's first
+    // row were staged from the old conv state)
     if (rank == 0) {
-        const int n = r1 - r0;
+        const int nt_last = (r1 - r0 - 1) % kGdnTile + 1;
         for (int c = t; c < C3; c += kGdnThreads) {
             const int ch = (c / kHD) * kNH * kHD + h * kHD + c % kHD;
             float * st = conv_state + (size_t(slot) * CH + ch) * (kConvW - 1);
-            float nv[kConvW - 1];
 #pragma unroll
-            for (int w = 0; w < kConvW - 1; ++w) {
-                const int ri = r1 - (kConvW - 1) + w;  // input index for new slot w
-                nv[w] = ri >= r0 ? qkvz[size_t(ri) * QKVZ + ch] : st[w + n];
-            }
-#pragma unroll
-            for (int w = 0; w < kConvW - 1; ++w) st[w] = nv[w];
+            for (int w = 0; w < kConvW - 1; ++w) st[w] = cx[(nt_last + w) * C3 + c];
         }
     }
 #pragma unroll
