@@ -144,6 +144,22 @@ int exl3cu_mul_mat_sequence(size_t count, const exl3cu_weight * const * weights,
                             float * const * d_y, const size_t * y_row_stride, const int * group, int depend,
                             void * stream);
 
+/* No counterpart in the reference.  exl3cu_mul_mat_batch with the layer glue of a
+ * decoder folded into the operator: per item an input form (EXL3CU_F32,
+ * EXL3CU_F16, EXL3CU_X_GLU: SwiGLU of a [gate | up] row computed on load,
+ * EXL3CU_X_RMSNORM: RMSNorm of a residual-stream row with d_norm_w[i] and eps
+ * computed on load), and y_accumulate[i] != 0 to add the product into y (the
+ * residual add) instead of storing it.  The fused forms and accumulation run on
+ * the integer-tensor-core GEMV only: mul1 weights of 2..8 bits and rows below
+ * the GEMM threshold (5 by default); other items return EXL3CU_NO_SUPPORT.
+ * d_norm_w / y_accumulate may be NULL when no item uses them.  As in
+ * exl3cu_mul_mat_batch, an output must not alias any item's input, its own
+ * included. */
+int exl3cu_mul_mat_batch_ex(size_t count, const exl3cu_weight * const * weights, const void * const * d_x,
+                            const int * x_form, const size_t * rows, const size_t * x_row_stride,
+                            const float * const * d_norm_w, float eps, float * const * d_y,
+                            const size_t * y_row_stride, const int * y_accumulate, void * stream);
+
 /* ---- ragged continuous-admission batches ----------------------------------------- */
 
 /* GPU-side batch packer.  Sequence i asks for d_want[i] rows this step (1 for a
@@ -155,20 +171,6 @@ int exl3cu_mul_mat_sequence(size_t count, const exl3cu_weight * const * weights,
  * (-1 past the packed rows).  Device int32 arrays of the current device.  No
  * counterpart in the reference (the upstream llama-server slots do this on the
  * host). */
-/* No counterpart in the reference.  exl3cu_mul_mat_batch with the layer glue of a
- * decoder folded into the operator: per item an input form (EXL3CU_F32,
- * EXL3CU_F16, EXL3CU_X_GLU: SwiGLU of a [gate | up] row computed on load,
- * EXL3CU_X_RMSNORM: RMSNorm of a residual-stream row with d_norm_w[i] and eps
- * computed on load), and y_accumulate[i] != 0 to add the product into y (the
- * residual add) instead of storing it.  The fused forms and accumulation run on
- * the integer-tensor-core GEMV only: mul1 weights of 2..8 bits and rows below
- * the GEMM threshold (5 by default); other items return EXL3CU_NO_SUPPORT.
- * d_norm_w / y_accumulate may be NULL when no item uses them. */
-int exl3cu_mul_mat_batch_ex(size_t count, const exl3cu_weight * const * weights, const void * const * d_x,
-                            const int * x_form, const size_t * rows, const size_t * x_row_stride,
-                            const float * const * d_norm_w, float eps, float * const * d_y,
-                            const size_t * y_row_stride, const int * y_accumulate, void * stream);
-
 int exl3cu_pack_ragged(size_t n_seq, const int32_t * d_want, const int32_t * d_pos, int32_t max_rows,
                        int32_t * d_row_offsets, int32_t * d_row_seq, int32_t * d_row_pos, void * stream);
 

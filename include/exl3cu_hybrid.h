@@ -59,6 +59,18 @@ int exl3cu_hyb_attn(const float * d_q, int rows, const int32_t * d_row_seq, cons
                     int n_slots, float scale, int splits, float * d_part, size_t part_bytes, unsigned * d_tickets,
                     float * d_out, void * stream);
 
+/* exl3cu_hyb_attn_prep and exl3cu_hyb_attn in one launch, for a step in which
+ * every sequence has exactly one row (decode): d_qkv holds the packed
+ * [q | k | v] rows of exl3cu_hyb_attn_prep, the new k and v are appended to
+ * the caches at row_pos and used from on-chip memory, and the result equals the
+ * two calls' bit for bit.  With two rows of one sequence in the step, a row
+ * would miss the other's new position: use the two calls. */
+int exl3cu_hyb_attn_decode(const float * d_qkv, int rows, const int32_t * d_row_seq, const int32_t * d_row_pos,
+                           const int32_t * d_seq_slot, const float * d_qn_w, const float * d_kn_w,
+                           const float * d_inv_freq, float eps, uint16_t * d_kcache, uint16_t * d_vcache, int max_len,
+                           int n_slots, float scale, int splits, float * d_part, size_t part_bytes,
+                           unsigned * d_tickets, float * d_out, void * stream);
+
 /* Dynamic shared memory one exl3cu_hyb_gdn CTA uses (the 128x128 state and scratch). */
 size_t exl3cu_hyb_gdn_smem_bytes(void);
 
@@ -77,12 +89,17 @@ int exl3cu_hyb_gdn(const float * d_qkvz, const float * d_xn, const float * d_xn_
                    const float * d_norm_w, float eps, float * d_state, const int32_t * d_row_offsets,
                    const int32_t * d_seq_slot, int n_seq, int n_slots, float * d_out, void * stream);
 
-/* Tied fp16 head with greedy choice: for o < nout (<= 8), logits[o][v] =
- * sum_i xn[rows[o]][i] * embed[v][i] (f32 xn, fp32 sums; written when d_logits is not
- * NULL), tokens[o] = argmax_v (lowest index on ties).  d_best: nout 64-bit
- * scratch words.  hidden is 1024, 2048, 4096 or 8192. */
-int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hidden, const uint16_t * d_embed,
-                    int vocab, float * d_logits, unsigned long long * d_best, int32_t * d_tokens, void * stream);
+/* Tied fp16 head with greedy choice, one launch: for o < nout (<= 8),
+ * logits[o][v] = sum_i x[rows[o]][i] * embed[v][i] (f32 x, fp32 sums; written
+ * when d_logits is not NULL), tokens[o] = argmax_v (lowest index on ties).
+ * x = d_xn, or with d_norm_w the final RMSNorm of d_xn's rows (weights
+ * d_norm_w, eps) computed on load, equal bit for bit to exl3cu_hyb_rmsnorm
+ * followed by this call.  d_best: 9 64-bit scratch words, zero before the
+ * first call; every call leaves them zero.  hidden is 1024, 2048, 4096 or
+ * 8192. */
+int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hidden, const float * d_norm_w,
+                    float eps, const uint16_t * d_embed, int vocab, float * d_logits, unsigned long long * d_best,
+                    int32_t * d_tokens, void * stream);
 
 /* Sticky error bits of these kernels on the current device (reserved: the
  * current kernels wait on nothing and raise none).  Synchronises the device. */

@@ -99,15 +99,18 @@ def test_ragged_continuous_admission_matches_per_sequence_oracle(model):
 
 
 def test_head_argmax_and_embedding(model):
-    """The fused head: argmax over fp32 logits of the tied fp16 embedding, lowest index on ties."""
+    """The fused head: the final RMSNorm of the residual rows on load, then argmax over fp32 logits of
+    the tied fp16 embedding, lowest index on ties."""
     eng, _ = model
     E = eng.embed.float().cpu().numpy()
     x = (np.random.default_rng(5).standard_normal((3, eng.cfg.hidden)) * 0.5).astype(np.float32)
-    eng.xn[:3].copy_(torch.from_numpy(x).cuda())
+    eng.h[:3].copy_(torch.from_numpy(x).cuda())
     eng.meta.fill([0], [0], [0], [0, 1], [0], [0, 1, 2])
     eng.meta.upload(None)
     lg = eng.head_logits(3).cpu().numpy()
-    ref = x.astype(np.float64) @ E.T.astype(np.float64)
+    x64 = x.astype(np.float64)
+    xn = x64 / np.sqrt(np.mean(x64 * x64, axis=1, keepdims=True) + eng.cfg.eps) * eng.final_norm.cpu().numpy()
+    ref = xn @ E.T.astype(np.float64)
     assert np.max(np.abs(lg - ref)) / np.max(np.abs(ref)) < 1e-5
     assert list(eng.out_tokens[:3].cpu().numpy()) == list(np.argmax(lg, axis=1))
 
@@ -158,3 +161,53 @@ def test_attention_splits_agree(model):
     assert int(eng.attn_tickets.abs().sum()) == 0
     st = ctypes.c_uint(0)
     assert L.exl3cu_hyb_status(1, ctypes.byref(st)) == 0 and st.value == 0
+
+
+def test_fused_decode_attention_matches_prep_plus_attention(model):
+    """exl3cu_hyb_attn_decode (q/k norm, RoPE, KV append and attention in one launch, one row per
+    sequence) against exl3cu_hyb_attn_prep + exl3cu_hyb_attn on the same inputs: outputs and both
+    caches bit for bit, at positions 0, inside and at the end of the cache, for 1, 2 and 8 splits."""
+    import ctypes
+
+    from exl3_b200.hybrid import _vp
+
+    eng, _ = model
+    L = eng.L
+    c = 0
+    full = next(d for d in eng.layers if d["kind"] == "full")
+    g = torch.Generator(device="cuda").manual_seed(12)
+    k0 = torch.randn(eng.kc[c].shape, generator=g, device="cuda").half()
+    v0 = torch.randn(eng.vc[c].shape, generator=g, device="cuda").half()
+    rows = 3
+    qkv = torch.randn((rows, (16 + 2 * 4) * 128), generator=g, device="cuda")
+    pos = [0, 57, eng.max_len - 1]
+    eng.meta.fill([0] * rows, [0, 1, 2], pos, [0, 1, 2, 3], [2, 0, 1], [0])
+    eng.meta.upload(None)
+    assert eng.meta.one_row_each
+    m = eng.meta
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    args_meta = (_vp(m.view("row_seq")), _vp(m.view("row_pos")), _vp(m.view("seq_slot")))
+    norms = (_vp(full["q_norm"]), _vp(full["k_norm"]), _vp(eng.inv_freq), eng.cfg.eps)
+    for sp in (1, 2, 8):
+        eng.kc[c].copy_(k0)
+        eng.vc[c].copy_(v0)
+        q = torch.zeros((rows, 16 * 128), dtype=torch.float32, device="cuda")
+        oa = torch.zeros((rows, 16 * 128), dtype=torch.float32, device="cuda")
+        assert L.exl3cu_hyb_attn_prep(_vp(qkv), rows, *args_meta, *norms, _vp(eng.kc[c]), _vp(eng.vc[c]),
+                                      eng.max_len, eng.slots, _vp(q), st) == 0
+        assert L.exl3cu_hyb_attn(_vp(q), rows, *args_meta, _vp(eng.kc[c]), _vp(eng.vc[c]), eng.max_len, eng.slots,
+                                 0.088388, sp, _vp(eng.attn_part), eng.attn_part.numel() * 4,
+                                 _vp(eng.attn_tickets), _vp(oa), st) == 0
+        ka, va = eng.kc[c].clone(), eng.vc[c].clone()
+        eng.kc[c].copy_(k0)
+        eng.vc[c].copy_(v0)
+        ob = torch.zeros((rows, 16 * 128), dtype=torch.float32, device="cuda")
+        assert L.exl3cu_hyb_attn_decode(_vp(qkv), rows, *args_meta, *norms, _vp(eng.kc[c]), _vp(eng.vc[c]),
+                                        eng.max_len, eng.slots, 0.088388, sp, _vp(eng.attn_part),
+                                        eng.attn_part.numel() * 4, _vp(eng.attn_tickets), _vp(ob), st) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(oa, ob), sp
+        assert torch.equal(ka.view(torch.int16), eng.kc[c].view(torch.int16)), sp
+        assert torch.equal(va.view(torch.int16), eng.vc[c].view(torch.int16)), sp
+        assert not torch.equal(ka.view(torch.int16), k0.view(torch.int16))  # the append happened
+    assert int(eng.attn_tickets.abs().sum()) == 0

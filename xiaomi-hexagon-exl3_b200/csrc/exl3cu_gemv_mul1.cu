@@ -46,7 +46,8 @@ namespace cg = cooperative_groups;
 
 namespace exl3cu {
 
-static __device__ unsigned g_mul1_status;  // kStatus* bits raised by k_gemv_mul1
+static __device__ unsigned g_mul1_status;
+static_assert(kMRows <= kMW, "the epilogue gives each row its own consumer warp");  // kStatus* bits raised by k_gemv_mul1
 
 struct Mul1Layout {
     int ring_off, xq_off, acc_off, part_off, slot_off, gmax_off, bar_off;
@@ -131,6 +132,8 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
     }
     __syncthreads();
 
+    uint2 sv_pre = make_uint2(0, 0);                    // rank 0: output signs of this lane's columns
+    float4 y_prev = make_float4(0.f, 0.f, 0.f, 0.f);    // rank 0, y_accum: y of row `warp` before this launch
     if (warp == kMW) {
         // ---- producer: the CTA's chunks [c0, c1) are contiguous in the device layout ----
         if (lane == 0 && nch > 0) {
@@ -167,6 +170,7 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             su_pre[ii] = make_uint2(0, 0);
             if (item < nitems) su_pre[ii] = *reinterpret_cast<const uint2 *>(P.su + (g0 + item / rows) * 128 + lane * 4);
         }
+        if (split == 0) sv_pre = *reinterpret_cast<const uint2 *>(P.sv + nb * 128 + lane * 4);
         pdl_wait_primary();  // activations may be written by the previous kernel
         const int ktot = P.nchunks * 16;
         float v[kItems][4];
@@ -416,6 +420,9 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             const float sq = fmaf(float(acc[2 * e]), 128.f, float(acc[2 * e + 1]));
             dst[e] = scale_s[r] * fmaf(kCodeA, sq, kCodeC * float(xsum_s[r]));
         }
+        // the accumulated y goes out before the barrier (nothing else writes it during this launch)
+        if (split == 0 && P.y_accum && warp < rows)
+            y_prev = *reinterpret_cast<const float4 *>(P.y + size_t(warp) * P.y_stride + nb * 128 + lane * 4);
     }
 
     // ---- one cluster barrier; rank 0 sums the partials in rank order ----
@@ -431,8 +438,7 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             }
             consumer_sync();
         }
-        const uint2 sraw = *reinterpret_cast<const uint2 *>(P.sv + nb * 128 + lane * 4);
-        const __half2 s01 = bits_half2(sraw.x), s23 = bits_half2(sraw.y);
+        const __half2 s01 = bits_half2(sv_pre.x), s23 = bits_half2(sv_pre.y);
         for (int r = warp; r < rows; r += kMW) {
             float v[4];
 #pragma unroll
@@ -444,12 +450,11 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             o.z = __fmul_rn(v[2], __low2float(s23));
             o.w = __fmul_rn(v[3], __high2float(s23));
             float4 * yp = reinterpret_cast<float4 *>(P.y + size_t(r) * P.y_stride + nb * 128 + lane * 4);
-            if (P.y_accum) {
-                const float4 prev = *yp;
-                o.x += prev.x;
-                o.y += prev.y;
-                o.z += prev.z;
-                o.w += prev.w;
+            if (P.y_accum) {  // rows <= kMRows <= kMW: warp r prefetched row r
+                o.x += y_prev.x;
+                o.y += y_prev.y;
+                o.z += y_prev.z;
+                o.w += y_prev.w;
             }
             *yp = o;
         }

@@ -145,6 +145,32 @@ __global__ void k_swiglu(const float * __restrict__ gu, int F, float * __restric
     out[size_t(r) * F + i] = silu(g) * u;
 }
 
+// One head of 128 values x[d] (lane holds d = lane + 32 q, q < 4): RMSNorm
+// with weights wn, then the rotary embedding of the pairs (i, i + 64) by
+// pos * inv_freq[i].  Shared by k_attn_prep and k_attn_decode, which must
+// agree bit for bit.
+__device__ __forceinline__ void head_norm_rope(const float * __restrict__ x, const float * __restrict__ wn,
+                                               const float * __restrict__ inv_freq, int pos, float eps, int lane,
+                                               float (&o)[4]) {
+    float v[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] = x[lane + 32 * q];
+    float ss = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) ss = fmaf(v[q], v[q], ss);
+    const float inv = rsqrtf(warp_sum(ss) / float(kHD) + eps);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] = v[q] * inv * wn[lane + 32 * q];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int i = lane + 32 * q;  // first-half index; partner i + 64
+        float sn, cs;
+        sincosf(float(pos) * inv_freq[i], &sn, &cs);
+        o[q] = v[q] * cs - v[q + 2] * sn;
+        o[q + 2] = v[q + 2] * cs + v[q] * sn;
+    }
+}
+
 // Per row: RMSNorm of each q and k head (weights qn_w / kn_w), rotary
 // embedding (pairs i, i+64 rotated by pos * inv_freq[i]), k and v appended to
 // the fp16 cache at the row's position, q written out (f32).  One CTA of
@@ -166,25 +192,8 @@ __global__ void k_attn_prep(const float * __restrict__ qkv, const int32_t * __re
     const bool is_q = warp < kNH;
     const int head = is_q ? warp : warp - kNH;
     const float * x = src + (is_q ? head * kHD : kNH * kHD + head * kHD);
-    const float * wn = is_q ? qn_w : kn_w;
-    float v[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = x[lane + 32 * q];  // dims lane, lane+32, lane+64, lane+96
-    float ss = 0.f;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) ss = fmaf(v[q], v[q], ss);
-    const float inv = rsqrtf(warp_sum(ss) / float(kHD) + eps);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = v[q] * inv * wn[lane + 32 * q];
     float o[4];
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-        const int i = lane + 32 * q;  // first-half index; partner i + 64
-        float sn, cs;
-        sincosf(float(pos) * inv_freq[i], &sn, &cs);
-        o[q] = v[q] * cs - v[q + 2] * sn;
-        o[q + 2] = v[q + 2] * cs + v[q] * sn;
-    }
+    head_norm_rope(x, is_q ? qn_w : kn_w, inv_freq, pos, eps, lane, o);
     if (is_q) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) q_out[size_t(r) * kNH * kHD + head * kHD + lane + 32 * q] = o[q];
@@ -208,12 +217,21 @@ __global__ void k_attn_prep(const float * __restrict__ qkv, const int32_t * __re
 // order and resets the ticket.
 constexpr int kAttnPart = kHD + 2;
 
+// PREP (k_attn_decode): a step in which every sequence has exactly one row,
+// so a row attends to cached positions plus its own new one.  q points at the
+// packed [q | k | v] rows; the CTA computes its q head and the row's new k, v
+// (k_attn_prep's math, same rounding) into shared memory and uses them for
+// position pos, and one CTA per (row, kv head) appends k, v to the cache.  No
+// CTA of the launch reads the cache at pos, so the append needs no ordering.
+template <bool PREP>
 __global__ void __launch_bounds__(128)
 k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const int32_t * __restrict__ row_pos,
-       const int32_t * __restrict__ seq_slot, const __half * __restrict__ kc, const __half * __restrict__ vc,
+       const int32_t * __restrict__ seq_slot, __half * __restrict__ kc, __half * __restrict__ vc,
        int max_len, int n_slots, float scale, float * __restrict__ part, unsigned * __restrict__ tickets,
-       float * __restrict__ out) {
+       float * __restrict__ out, const float * __restrict__ qn_w, const float * __restrict__ kn_w,
+       const float * __restrict__ inv_freq, float eps) {
     __shared__ float sm_m[4], sm_l[4], sm_acc[4][kHD];
+    __shared__ __align__(16) float sm_q[PREP ? kHD : 1], sm_k[PREP ? kHD : 1], sm_v[PREP ? kHD : 1];
     __shared__ unsigned sm_last;
     pdl_trigger();
     pdl_wait_primary();
@@ -221,19 +239,66 @@ k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int slot = seq_slot[row_seq[r]];
     if (slot < 0 || slot >= n_slots) return;
-    const int npos = min(row_pos[r], max_len - 1) + 1;
+    const int pos = row_pos[r];
+    const int npos = min(pos, max_len - 1) + 1;
     const int chunk = (npos + S - 1) / S;
     const int p0 = z * chunk, p1 = min(npos, p0 + chunk);
     const int kvh = head / (kNH / kNKV);
-    const float4 qv = *reinterpret_cast<const float4 *>(q + size_t(r) * kNH * kHD + head * kHD + lane * 4);
+    float4 qv;
+    if constexpr (PREP) {
+        constexpr int QKV = (kNH + 2 * kNKV) * kHD;
+        const float * src = q + size_t(r) * QKV;
+        // the CTA of the kv group's first q head and split 0 appends (a position outside the cache: none)
+        const bool writer = pos >= 0 && pos < max_len && head % (kNH / kNKV) == 0 && z == 0;
+        const size_t base = ((size_t(slot) * kNKV + kvh) * max_len + (writer ? pos : 0)) * kHD;
+        if (warp == 0) {
+            float o[4];
+            head_norm_rope(src + head * kHD, qn_w, inv_freq, pos, eps, lane, o);
+#pragma unroll
+            for (int q2 = 0; q2 < 4; ++q2) sm_q[lane + 32 * q2] = o[q2];
+        } else if (warp == 1) {
+            float o[4];
+            head_norm_rope(src + kNH * kHD + kvh * kHD, kn_w, inv_freq, pos, eps, lane, o);
+#pragma unroll
+            for (int q2 = 0; q2 < 4; ++q2) {
+                const __half hk = __float2half_rn(o[q2]);
+                sm_k[lane + 32 * q2] = __half2float(hk);
+                if (writer) kc[base + lane + 32 * q2] = hk;
+            }
+        } else if (warp == 2) {
+            const float * vs = src + kNH * kHD + kNKV * kHD + kvh * kHD;
+#pragma unroll
+            for (int q2 = 0; q2 < 4; ++q2) {
+                const __half hv = __float2half_rn(vs[lane + 32 * q2]);
+                sm_v[lane + 32 * q2] = __half2float(hv);
+                if (writer) vc[base + lane + 32 * q2] = hv;
+            }
+        }
+        __syncthreads();
+        qv = *reinterpret_cast<const float4 *>(sm_q + lane * 4);
+    } else {
+        qv = *reinterpret_cast<const float4 *>(q + size_t(r) * kNH * kHD + head * kHD + lane * 4);
+    }
     const __half * kb = kc + (size_t(slot) * kNKV + kvh) * max_len * kHD;
     const __half * vb = vc + (size_t(slot) * kNKV + kvh) * max_len * kHD;
     float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int p = p0 + warp; p < p1; p += 4) {
-        const uint2 kr = *reinterpret_cast<const uint2 *>(kb + size_t(p) * kHD + lane * 4);
-        const uint2 vr = *reinterpret_cast<const uint2 *>(vb + size_t(p) * kHD + lane * 4);
-        const float2 k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.x));
-        const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.y));
+        float2 k01, k23, v01, v23;
+        if (PREP && p == pos) {  // this step's own position: from shared memory
+            const float4 kk = *reinterpret_cast<const float4 *>(sm_k + lane * 4);
+            const float4 vv = *reinterpret_cast<const float4 *>(sm_v + lane * 4);
+            k01 = make_float2(kk.x, kk.y);
+            k23 = make_float2(kk.z, kk.w);
+            v01 = make_float2(vv.x, vv.y);
+            v23 = make_float2(vv.z, vv.w);
+        } else {
+            const uint2 kr = *reinterpret_cast<const uint2 *>(kb + size_t(p) * kHD + lane * 4);
+            const uint2 vr = *reinterpret_cast<const uint2 *>(vb + size_t(p) * kHD + lane * 4);
+            k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.x));
+            k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.y));
+            v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.x));
+            v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
+        }
         float s = qv.x * k01.x;
         s = fmaf(qv.y, k01.y, s);
         s = fmaf(qv.z, k23.x, s);
@@ -241,8 +306,6 @@ k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const
         s = warp_sum(s) * scale;
         const float mn = fmaxf(m, s);
         const float corr = expf(m - mn), e = expf(s - mn);
-        const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.x));
-        const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
         l = l * corr + e;
         acc[0] = fmaf(e, v01.x, acc[0] * corr);
         acc[1] = fmaf(e, v01.y, acc[1] * corr);
@@ -622,20 +685,69 @@ __device__ __forceinline__ uint32_t float_key(float f) {
 // nout <= 8 rows; best[o] = max over v of (key(logit) << 32 | ~v) (the first
 // index wins ties).  Warp per vocab row, activations staged in shared memory;
 // ITER = H / 256 16-byte loads per lane per vocab row, issued together.
+// With norm_w the rows are the residual stream h and the final RMSNorm is
+// applied while staging, with k_rmsnorm's arithmetic (thread t sums the
+// squares of float4s t, t + 256, ... in order; warps add in order), so the
+// logits equal those of k_rmsnorm + this kernel bit for bit.  The last CTA to
+// finish (a ticket in best[kHeadMaxRows]) turns best[] into tokens[] and
+// leaves best[] zero for the next launch.
 constexpr int kHeadMaxRows = 8;
 constexpr int kHeadThreads = 256;
 
 template <int ITER>
 __global__ void __launch_bounds__(kHeadThreads)
 k_head(const float * __restrict__ xn, const int32_t * __restrict__ rows, int nout, int H,
-       const __half * __restrict__ E, int V, float * __restrict__ logits, unsigned long long * __restrict__ best) {
+       const __half * __restrict__ E, int V, float * __restrict__ logits, unsigned long long * __restrict__ best,
+       const float * __restrict__ norm_w, float eps, int32_t * __restrict__ tokens) {
     extern __shared__ __align__(16) float xs[];  // [nout][H]
+    __shared__ float red[kHeadThreads / 32][kHeadMaxRows];
+    __shared__ float inv_s[kHeadMaxRows];
+    __shared__ unsigned last_s;
     pdl_trigger();
     pdl_wait_primary();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int e = threadIdx.x; e < nout * H / 4; e += kHeadThreads) {
-        const int o = (e * 4) / H, i = (e * 4) % H;
-        reinterpret_cast<float4 *>(xs)[e] = *reinterpret_cast<const float4 *>(xn + size_t(rows[o]) * H + i);
+    if (norm_w) {
+        const int nv = H / 4;
+        float ss[kHeadMaxRows];
+#pragma unroll
+        for (int o = 0; o < kHeadMaxRows; ++o) {
+            ss[o] = 0.f;
+            if (o >= nout) continue;
+            const float4 * hr = reinterpret_cast<const float4 *>(xn + size_t(rows[o]) * H);
+            for (int e = threadIdx.x; e < nv; e += kHeadThreads) {
+                const float4 x = hr[e];
+                reinterpret_cast<float4 *>(xs)[o * nv + e] = x;
+                ss[o] = fmaf(x.x, x.x, ss[o]);
+                ss[o] = fmaf(x.y, x.y, ss[o]);
+                ss[o] = fmaf(x.z, x.z, ss[o]);
+                ss[o] = fmaf(x.w, x.w, ss[o]);
+            }
+        }
+#pragma unroll
+        for (int o = 0; o < kHeadMaxRows; ++o) {
+            const float w = warp_sum(ss[o]);
+            if (lane == 0) red[warp][o] = w;
+        }
+        __syncthreads();
+        if (threadIdx.x < nout) {
+            float t = 0.f;
+            for (int w = 0; w < kHeadThreads / 32; ++w) t += red[w][threadIdx.x];  // warp order
+            inv_s[threadIdx.x] = rsqrtf(t / float(H) + eps);
+        }
+        __syncthreads();
+        const float4 * w4 = reinterpret_cast<const float4 *>(norm_w);
+        for (int e = threadIdx.x; e < nout * nv; e += kHeadThreads) {
+            const int o = e / nv;
+            const float inv = inv_s[o];
+            const float4 x = reinterpret_cast<float4 *>(xs)[e], wv = w4[e - o * nv];
+            reinterpret_cast<float4 *>(xs)[e] = make_float4(x.x * inv * wv.x, x.y * inv * wv.y, x.z * inv * wv.z,
+                                                            x.w * inv * wv.w);
+        }
+    } else {
+        for (int e = threadIdx.x; e < nout * H / 4; e += kHeadThreads) {
+            const int o = (e * 4) / H, i = (e * 4) % H;
+            reinterpret_cast<float4 *>(xs)[e] = *reinterpret_cast<const float4 *>(xn + size_t(rows[o]) * H + i);
+        }
     }
     __syncthreads();
     unsigned long long mine[kHeadMaxRows];
@@ -730,21 +842,19 @@ k_head(const float * __restrict__ xn, const int32_t * __restrict__ rows, int nou
 #pragma unroll
         for (int o = 0; o < kHeadMaxRows; ++o)
             if (o < nout) atomicMax(best + o, mine[o]);
+        __threadfence();
     }
-}
-
-// The head's memset of best[] folded in: one launch before the head clears it.
-__global__ void k_head_clear(unsigned long long * __restrict__ best, int nout) {
-    pdl_trigger();
-    pdl_wait_primary();
-    if (threadIdx.x < nout) best[threadIdx.x] = 0ull;
-}
-
-__global__ void k_head_tokens(const unsigned long long * __restrict__ best, int nout, int32_t * __restrict__ tokens) {
-    pdl_trigger();
-    pdl_wait_primary();
-    const int o = threadIdx.x;
-    if (o < nout) tokens[o] = int32_t(~uint32_t(best[o] & 0xffffffffull));
+    __syncthreads();
+    if (threadIdx.x == 0) last_s = atomicAdd(best + kHeadMaxRows, 1ull) == gridDim.x - 1;
+    __syncthreads();
+    if (!last_s) return;
+    // the last CTA: every other CTA's maxima are in; read and clear them atomically
+    __threadfence();
+    if (threadIdx.x < nout) {
+        const unsigned long long b = atomicExch(best + threadIdx.x, 0ull);
+        tokens[threadIdx.x] = int32_t(~uint32_t(b & 0xffffffffull));
+    }
+    if (threadIdx.x == 0) atomicExch(best + kHeadMaxRows, 0ull);
 }
 
 }  // namespace
@@ -873,9 +983,31 @@ int exl3cu_hyb_attn(const float * d_q, int rows, const int32_t * d_row_seq, cons
     if (rows > 65535) return bad("attn: at most 65535 rows");
     if (splits > 1 && (!d_part || !d_tickets || part_bytes < exl3cu_hyb_attn_scratch_bytes(rows, splits)))
         return bad("attn: split scratch missing or too small (exl3cu_hyb_attn_scratch_bytes; tickets rows*16, zeroed)");
-    return launch_pdl(k_attn, dim3(kNH, unsigned(rows), unsigned(splits)), dim3(128), 0, stream, d_q, d_row_seq,
-                      d_row_pos, d_seq_slot, reinterpret_cast<const __half *>(d_kcache),
-                      reinterpret_cast<const __half *>(d_vcache), max_len, n_slots, scale, d_part, d_tickets, d_out);
+    // the plain kernel only reads the caches
+    __half * kc = reinterpret_cast<__half *>(const_cast<uint16_t *>(d_kcache));
+    __half * vc = reinterpret_cast<__half *>(const_cast<uint16_t *>(d_vcache));
+    return launch_pdl(k_attn<false>, dim3(kNH, unsigned(rows), unsigned(splits)), dim3(128), 0, stream, d_q,
+                      d_row_seq, d_row_pos, d_seq_slot, kc, vc, max_len, n_slots, scale, d_part, d_tickets, d_out,
+                      static_cast<const float *>(nullptr), static_cast<const float *>(nullptr),
+                      static_cast<const float *>(nullptr), 0.f);
+}
+
+int exl3cu_hyb_attn_decode(const float * d_qkv, int rows, const int32_t * d_row_seq, const int32_t * d_row_pos,
+                           const int32_t * d_seq_slot, const float * d_qn_w, const float * d_kn_w,
+                           const float * d_inv_freq, float eps, uint16_t * d_kcache, uint16_t * d_vcache, int max_len,
+                           int n_slots, float scale, int splits, float * d_part, size_t part_bytes,
+                           unsigned * d_tickets, float * d_out, void * stream) {
+    if (!d_qkv || !d_row_seq || !d_row_pos || !d_seq_slot || !d_qn_w || !d_kn_w || !d_inv_freq || !d_kcache ||
+        !d_vcache || !d_out || rows < 0 || max_len <= 0 || n_slots <= 0 || splits < 1 || splits > 64)
+        return bad("attn_decode: bad arguments");
+    if (!rows) return EXL3CU_OK;
+    if (rows > 65535) return bad("attn_decode: at most 65535 rows");
+    if (splits > 1 && (!d_part || !d_tickets || part_bytes < exl3cu_hyb_attn_scratch_bytes(rows, splits)))
+        return bad("attn_decode: split scratch missing or too small (exl3cu_hyb_attn_scratch_bytes; tickets rows*16, zeroed)");
+    return launch_pdl(k_attn<true>, dim3(kNH, unsigned(rows), unsigned(splits)), dim3(128), 0, stream, d_qkv,
+                      d_row_seq, d_row_pos, d_seq_slot, reinterpret_cast<__half *>(d_kcache),
+                      reinterpret_cast<__half *>(d_vcache), max_len, n_slots, scale, d_part, d_tickets, d_out, d_qn_w,
+                      d_kn_w, d_inv_freq, eps);
 }
 
 size_t exl3cu_hyb_gdn_smem_bytes_for(int hidden) {
@@ -907,19 +1039,20 @@ int exl3cu_hyb_gdn(const float * d_qkvz, const float * d_xn, const float * d_xn_
                       n_slots, d_out);
 }
 
-int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hidden, const uint16_t * d_embed,
-                    int vocab, float * d_logits, unsigned long long * d_best, int32_t * d_tokens, void * stream) {
+int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hidden, const float * d_norm_w,
+                    float eps, const uint16_t * d_embed, int vocab, float * d_logits, unsigned long long * d_best,
+                    int32_t * d_tokens, void * stream) {
     if (!d_xn || !d_rows || !d_embed || !d_best || !d_tokens || nout < 0 || nout > kHeadMaxRows || hidden <= 0 ||
         hidden % 256 || hidden > 8192 || vocab <= 0)
         return bad("head: bad arguments (nout <= 8, hidden a multiple of 256 up to 8192)");
+    if (d_norm_w && reinterpret_cast<uintptr_t>(d_norm_w) % 16) return bad("head: norm weights must be 16-byte aligned");
     if (!nout) return EXL3CU_OK;
     const size_t smem = size_t(nout) * hidden * sizeof(float);
     if (smem > size_t(kHeadSmemMax)) return bad("head: activations exceed shared memory");
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int rc = launch_pdl(k_head_clear, dim3(1), dim3(32), 0, stream, d_best, nout);
-    if (rc) return rc;
+    int rc = 0;
     const dim3 grid(unsigned(sms * 4)), block(kHeadThreads);
     const float * xn = d_xn;
     const auto * E = reinterpret_cast<const __half *>(d_embed);
@@ -928,7 +1061,8 @@ int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hi
     case N:                                                                                                        \
         if (!set_smem_attr_once(reinterpret_cast<const void *>(k_head<N>), kHeadSmemMax, g_head_attr_##N))        \
             return status_of(cudaGetLastError());                                                                  \
-        rc = launch_pdl(k_head<N>, grid, block, smem, stream, xn, d_rows, nout, hidden, E, vocab, d_logits, d_best); \
+        rc = launch_pdl(k_head<N>, grid, block, smem, stream, xn, d_rows, nout, hidden, E, vocab, d_logits, d_best, \
+                        d_norm_w, eps, d_tokens);                                                                  \
         break;
         EXL3CU_HEAD_CASE(4)
         EXL3CU_HEAD_CASE(8)
@@ -938,9 +1072,7 @@ int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hi
         default:
             return bad("head: hidden must be 1024, 2048, 4096 or 8192");
     }
-    if (rc) return rc;
-    return launch_pdl(k_head_tokens, dim3(1), dim3(32), 0, stream, static_cast<const unsigned long long *>(d_best),
-                      nout, d_tokens);
+    return rc;
 }
 
 int exl3cu_hyb_status(int clear, unsigned * status) {

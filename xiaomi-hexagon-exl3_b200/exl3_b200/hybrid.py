@@ -10,12 +10,18 @@ tokens and prefill chunks of several sequences together):
         full attention:  [q|k|v] = xn . W_{q,k,v}         exl3cu_mul_mat_batch (EXL3)
                          q/k norm, RoPE, KV append        exl3cu_hyb_attn_prep
                          a = attn(q, K, V)                exl3cu_hyb_attn
+                         (decode steps: both in one launch, exl3cu_hyb_attn_decode)
         delta rule:      [q|k|v|z] = xn . W_{q,k,v,z}     exl3cu_mul_mat_batch (EXL3)
                          a = gdn(...)                     exl3cu_hyb_gdn (conv, gates, state update, gated norm)
         o = a . W_o                                       exl3cu_mul_mat (EXL3)
         xn = rmsnorm(h += o)
         [g|u] = xn . W_{gate,up}; d = swiglu . W_down     exl3cu_mul_mat_batch, exl3cu_hyb_swiglu, exl3cu_mul_mat
     xn = rmsnorm(h += d); token = argmax(xn . E^T)        exl3cu_hyb_head (tied fp16 embedding)
+
+Steps of <= 8 rows fold the glue into the operator (exl3cu_mul_mat_batch_ex:
+RMSNorm and SwiGLU on load, residual adds in the epilogue) and the final
+RMSNorm into the head, which then is one launch; a layer is 4 operator
+launches plus its mixer.
 
 The model is synthetic (no checkpoints offline): random-init parameters with
 the stated shapes; each linear layer is an EXL3 matrix with a seeded random
@@ -145,14 +151,16 @@ def _declare(L):
     L.exl3cu_hyb_swiglu.argtypes = [P, I, I, P, P]
     L.exl3cu_hyb_attn_prep.argtypes = [P, I, P, P, P, P, P, P, F, P, P, I, I, P, P]
     L.exl3cu_hyb_attn.argtypes = [P, I, P, P, P, P, P, I, I, F, I, P, S, P, P, P]
+    L.exl3cu_hyb_attn_decode.argtypes = [P, I, P, P, P, P, P, P, F, P, P, I, I, F, I, P, S, P, P, P]
     L.exl3cu_hyb_attn_scratch_bytes.restype = S
     L.exl3cu_hyb_attn_scratch_bytes.argtypes = [I, I]
     L.exl3cu_hyb_status.argtypes = [I, ctypes.POINTER(ctypes.c_uint)]
     L.exl3cu_hyb_gdn_smem_bytes.restype = S
     L.exl3cu_hyb_gdn.argtypes = [P, P, P, P, I, P, P, P, P, P, F, P, P, P, I, I, P, P]
-    L.exl3cu_hyb_head.argtypes = [P, P, I, I, P, I, P, P, P, P]
+    L.exl3cu_hyb_head.argtypes = [P, P, I, I, P, F, P, I, P, P, P, P]
     for n in ("exl3cu_hyb_embed", "exl3cu_hyb_rmsnorm", "exl3cu_hyb_swiglu", "exl3cu_hyb_attn_prep",
-              "exl3cu_hyb_attn", "exl3cu_hyb_gdn", "exl3cu_hyb_head", "exl3cu_hyb_status"):
+              "exl3cu_hyb_attn", "exl3cu_hyb_attn_decode", "exl3cu_hyb_gdn", "exl3cu_hyb_head",
+              "exl3cu_hyb_status"):
         getattr(L, n).restype = ctypes.c_int
     L._hyb_declared = True
 
@@ -176,6 +184,7 @@ class StepMeta:
         self.off = {"tokens": 0, "row_seq": R, "row_pos": 2 * R, "row_offsets": 3 * R, "seq_slot": 3 * R + Q + 1,
                     "logit_rows": 3 * R + 2 * Q + 1}
         self.len = {"tokens": R, "row_seq": R, "row_pos": R, "row_offsets": Q + 1, "seq_slot": Q, "logit_rows": O}
+        self.one_row_each = False  # every sequence of the filled step has exactly one row (a decode step)
 
     def view(self, name):
         o = self.off[name]
@@ -189,6 +198,8 @@ class StepMeta:
             if a.size > self.len[name]:
                 raise ValueError(f"{name}: {a.size} entries, capacity {self.len[name]}")
             h[self.off[name]:self.off[name] + a.size] = a
+        offs = np.asarray(row_offsets, np.int64)
+        self.one_row_each = offs.size > 1 and bool(np.all(np.diff(offs) == 1))
 
     def upload(self, stream):
         self.dev.copy_(self.host, non_blocking=True)
@@ -256,7 +267,7 @@ class HybridEngine:
         cap = max(r * attn_splits(r) for r in range(1, R + 1))
         self.attn_part = torch.zeros(cap * cfg.heads * (cfg.head_dim + 2), dtype=f32, device=dev)
         self.attn_tickets = torch.zeros(R * cfg.heads, dtype=torch.int32, device=dev)
-        self.best = torch.zeros(8, dtype=torch.int64, device=dev)
+        self.best = torch.zeros(9, dtype=torch.int64, device=dev)  # head scratch: 8 maxima + a ticket, left zero
         self.out_tokens = torch.zeros(8, dtype=torch.int32, device=dev)
         self.KV = KV
         self._batch_args = {}
@@ -375,8 +386,8 @@ class HybridEngine:
             delta = self.down
         check(L.exl3cu_hyb_rmsnorm(_vp(self.h), _vp(delta), H, _vp(self.final_norm), cfg.eps, rows, H, _vp(self.xn),
                                    st))
-        check(L.exl3cu_hyb_head(_vp(self.xn), _vp(logit_rows), nout, H, _vp(self.embed), cfg.vocab, None,
-                                _vp(self.best), _vp(self.out_tokens), st))
+        check(L.exl3cu_hyb_head(_vp(self.xn), _vp(logit_rows), nout, H, None, cfg.eps, _vp(self.embed), cfg.vocab,
+                                None, _vp(self.best), _vp(self.out_tokens), st))
         if pf:  # join the prefetch stream (required inside a capture; cheap otherwise)
             ev = self._pf_events[-1]
             ev.record(self._pf_stream)
@@ -403,13 +414,20 @@ class HybridEngine:
                 self._mm_batch(("q", "k", "v"), mats, self.h, outs, rows, st, 3, d["in_norm"])
                 c = d["cache"]
                 kc, vc = self.kc[c], self.vc[c]
-                check(L.exl3cu_hyb_attn_prep(_vp(qkv), rows, _vp(row_seq), _vp(row_pos), _vp(seq_slot),
-                                             _vp(d["q_norm"]), _vp(d["k_norm"]), _vp(self.inv_freq), cfg.eps,
-                                             _vp(kc), _vp(vc), self.max_len, self.slots, _vp(self.q), st))
                 sp = attn_splits(rows)
-                check(L.exl3cu_hyb_attn(_vp(self.q), rows, _vp(row_seq), _vp(row_pos), _vp(seq_slot), _vp(kc),
-                                        _vp(vc), self.max_len, self.slots, scale, sp, _vp(self.attn_part),
-                                        self.attn_part.numel() * 4, _vp(self.attn_tickets), _vp(self.mix), st))
+                if rows == n_seq and self.meta.one_row_each:  # decode: prep + attention in one launch
+                    check(L.exl3cu_hyb_attn_decode(_vp(qkv), rows, _vp(row_seq), _vp(row_pos), _vp(seq_slot),
+                                                   _vp(d["q_norm"]), _vp(d["k_norm"]), _vp(self.inv_freq), cfg.eps,
+                                                   _vp(kc), _vp(vc), self.max_len, self.slots, scale, sp,
+                                                   _vp(self.attn_part), self.attn_part.numel() * 4,
+                                                   _vp(self.attn_tickets), _vp(self.mix), st))
+                else:
+                    check(L.exl3cu_hyb_attn_prep(_vp(qkv), rows, _vp(row_seq), _vp(row_pos), _vp(seq_slot),
+                                                 _vp(d["q_norm"]), _vp(d["k_norm"]), _vp(self.inv_freq), cfg.eps,
+                                                 _vp(kc), _vp(vc), self.max_len, self.slots, _vp(self.q), st))
+                    check(L.exl3cu_hyb_attn(_vp(self.q), rows, _vp(row_seq), _vp(row_pos), _vp(seq_slot), _vp(kc),
+                                            _vp(vc), self.max_len, self.slots, scale, sp, _vp(self.attn_part),
+                                            self.attn_part.numel() * 4, _vp(self.attn_tickets), _vp(self.mix), st))
             else:
                 p = self.proj
                 outs = [p[:, 0:D], p[:, D:2 * D], p[:, 2 * D:3 * D], p[:, 3 * D:4 * D]]
@@ -423,9 +441,9 @@ class HybridEngine:
             self._mm_batch(("gate", "up"), mats, self.h, [self.gu[:, 0:F], self.gu[:, F:2 * F]], rows, st, 3,
                            d["post_norm"])
             self._mm(mats["down"], self.gu, self.h, rows, st, 2, None, True)               # h += down(swiglu)
-        check(L.exl3cu_hyb_rmsnorm(_vp(self.h), None, H, _vp(self.final_norm), cfg.eps, rows, H, _vp(self.xn), st))
-        check(L.exl3cu_hyb_head(_vp(self.xn), _vp(logit_rows), nout, H, _vp(self.embed), cfg.vocab, None,
-                                _vp(self.best), _vp(self.out_tokens), st))
+        # the final RMSNorm is applied by the head as it loads h
+        check(L.exl3cu_hyb_head(_vp(self.h), _vp(logit_rows), nout, H, _vp(self.final_norm), cfg.eps,
+                                _vp(self.embed), cfg.vocab, None, _vp(self.best), _vp(self.out_tokens), st))
         if pf:
             ev = self._pf_events[-1]
             ev.record(self._pf_stream)
@@ -436,8 +454,10 @@ class HybridEngine:
         torch, cfg = self.torch, self.cfg
         st = ctypes.c_void_p((stream or torch.cuda.current_stream()).cuda_stream)
         out = torch.empty((nout, cfg.vocab), dtype=torch.float32, device=self.dev)
-        check(self.L.exl3cu_hyb_head(_vp(self.xn), _vp(self.meta.view("logit_rows")), nout, cfg.hidden,
-                                     _vp(self.embed), cfg.vocab, _vp(out), _vp(self.best), _vp(self.out_tokens), st))
+        # h holds the last step's final residual stream on both forward paths
+        check(self.L.exl3cu_hyb_head(_vp(self.h), _vp(self.meta.view("logit_rows")), nout, cfg.hidden,
+                                     _vp(self.final_norm), cfg.eps, _vp(self.embed), cfg.vocab, _vp(out),
+                                     _vp(self.best), _vp(self.out_tokens), st))
         return out
 
     def free(self):
