@@ -282,36 +282,55 @@ k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const
     const __half * kb = kc + (size_t(slot) * kNKV + kvh) * max_len * kHD;
     const __half * vb = vc + (size_t(slot) * kNKV + kvh) * max_len * kHD;
     float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int p = p0 + warp; p < p1; p += 4) {
-        float2 k01, k23, v01, v23;
-        if (PREP && p == pos) {  // this step's own position: from shared memory
-            const float4 kk = *reinterpret_cast<const float4 *>(sm_k + lane * 4);
-            const float4 vv = *reinterpret_cast<const float4 *>(sm_v + lane * 4);
-            k01 = make_float2(kk.x, kk.y);
-            k23 = make_float2(kk.z, kk.w);
-            v01 = make_float2(vv.x, vv.y);
-            v23 = make_float2(vv.z, vv.w);
-        } else {
-            const uint2 kr = *reinterpret_cast<const uint2 *>(kb + size_t(p) * kHD + lane * 4);
-            const uint2 vr = *reinterpret_cast<const uint2 *>(vb + size_t(p) * kHD + lane * 4);
-            k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.x));
-            k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kr.y));
-            v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.x));
-            v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
+    // warp w takes positions w, w+4, w+8, ... of the range, kU at a time: their k/v loads go out
+    // together, then the online-softmax updates run in position order
+    constexpr int kU = 4;
+    for (int pb = p0 + warp; pb < p1; pb += 4 * kU) {
+        float2 k01[kU], k23[kU], v01[kU], v23[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int p = pb + 4 * u;
+            if (PREP && p == pos) {  // this step's own position: from shared memory
+                const float4 kk = *reinterpret_cast<const float4 *>(sm_k + lane * 4);
+                const float4 vv = *reinterpret_cast<const float4 *>(sm_v + lane * 4);
+                k01[u] = make_float2(kk.x, kk.y);
+                k23[u] = make_float2(kk.z, kk.w);
+                v01[u] = make_float2(vv.x, vv.y);
+                v23[u] = make_float2(vv.z, vv.w);
+            } else {
+                uint2 kr = make_uint2(0, 0), vr = make_uint2(0, 0);
+                if (p < p1) {
+                    kr = *reinterpret_cast<const uint2 *>(kb + size_t(p) * kHD + lane * 4);
+                    vr = *reinterpret_cast<const uint2 *>(vb + size_t(p) * kHD + lane * 4);
+                }
+                k01[u] = __half22float2(*reinterpret_cast<const __half2 *>(&kr.x));
+                k23[u] = __half22float2(*reinterpret_cast<const __half2 *>(&kr.y));
+                v01[u] = __half22float2(*reinterpret_cast<const __half2 *>(&vr.x));
+                v23[u] = __half22float2(*reinterpret_cast<const __half2 *>(&vr.y));
+            }
         }
-        float s = qv.x * k01.x;
-        s = fmaf(qv.y, k01.y, s);
-        s = fmaf(qv.z, k23.x, s);
-        s = fmaf(qv.w, k23.y, s);
-        s = warp_sum(s) * scale;
-        const float mn = fmaxf(m, s);
-        const float corr = expf(m - mn), e = expf(s - mn);
-        l = l * corr + e;
-        acc[0] = fmaf(e, v01.x, acc[0] * corr);
-        acc[1] = fmaf(e, v01.y, acc[1] * corr);
-        acc[2] = fmaf(e, v23.x, acc[2] * corr);
-        acc[3] = fmaf(e, v23.y, acc[3] * corr);
-        m = mn;
+        float sc[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            float s = qv.x * k01[u].x;
+            s = fmaf(qv.y, k01[u].y, s);
+            s = fmaf(qv.z, k23[u].x, s);
+            s = fmaf(qv.w, k23[u].y, s);
+            sc[u] = warp_sum(s) * scale;
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            if (pb + 4 * u >= p1) break;
+            const float s = sc[u];
+            const float mn = fmaxf(m, s);
+            const float corr = expf(m - mn), e = expf(s - mn);
+            l = l * corr + e;
+            acc[0] = fmaf(e, v01[u].x, acc[0] * corr);
+            acc[1] = fmaf(e, v01[u].y, acc[1] * corr);
+            acc[2] = fmaf(e, v23[u].x, acc[2] * corr);
+            acc[3] = fmaf(e, v23[u].y, acc[3] * corr);
+            m = mn;
+        }
     }
     if (lane == 0) {
         sm_m[warp] = m;
