@@ -152,13 +152,19 @@ int exl3cu_mul_mat_sequence(size_t count, const exl3cu_weight * const * weights,
  * residual add) instead of storing it.  The fused forms and accumulation run on
  * the integer-tensor-core GEMV only: mul1 weights of 2..8 bits and rows below
  * the GEMM threshold (5 by default); other items return EXL3CU_NO_SUPPORT.
- * d_norm_w / y_accumulate may be NULL when no item uses them.  As in
- * exl3cu_mul_mat_batch, an output must not alias any item's input, its own
- * included. */
+ * d_norm_w / y_accumulate may be NULL when no item uses them.
+ * Sums of squares for the RMSNorm, per 128-column block (f32 [rows][width/128],
+ * dense): with d_y_sumsq[i] the operator also writes those of item i's final y
+ * rows (after the accumulation), and an RMSNorm item given d_x_sumsq[i] takes
+ * its rows' mean square from them instead of reading every row in full -- so
+ * the kernel that updates the residual stream hands its norm to the next.
+ * Either array, or entries of it, may be NULL.  As in exl3cu_mul_mat_batch, an
+ * output must not alias any item's input, its own included. */
 int exl3cu_mul_mat_batch_ex(size_t count, const exl3cu_weight * const * weights, const void * const * d_x,
                             const int * x_form, const size_t * rows, const size_t * x_row_stride,
                             const float * const * d_norm_w, float eps, float * const * d_y,
-                            const size_t * y_row_stride, const int * y_accumulate, void * stream);
+                            const size_t * y_row_stride, const int * y_accumulate,
+                            const float * const * d_x_sumsq, float * const * d_y_sumsq, void * stream);
 
 /* ---- ragged continuous-admission batches ----------------------------------------- */
 

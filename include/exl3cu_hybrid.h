@@ -24,9 +24,12 @@
 extern "C" {
 #endif
 
-/* h[r] = fp32(table[ids[r]]) for an fp16 [vocab, hidden] table (ids outside give zeros). */
+/* h[r] = fp32(table[ids[r]]) for an fp16 [vocab, hidden] table (ids outside give zeros).
+ * With d_h_sumsq (hidden a multiple of 128) also each row's sums of squares per
+ * 128-block, f32 [rows][hidden/128], the form exl3cu_mul_mat_batch_ex's
+ * RMSNorm input takes. */
 int exl3cu_hyb_embed(const uint16_t * d_table, int vocab, const int32_t * d_ids, int rows, int hidden, float * d_h,
-                     void * stream);
+                     float * d_h_sumsq, void * stream);
 
 /* h += delta (when d_delta is not NULL, row stride delta_stride), then
  * out = h * rsqrt(mean(h^2) + eps) * w, per row of `hidden` values (f32). */

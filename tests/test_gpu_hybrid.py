@@ -135,7 +135,7 @@ def test_attention_splits_agree(model):
     eng.meta.upload(None)
     m = eng.meta
     outs = []
-    for sp in (1, 2, 8):
+    for sp in (1, 2, 8, 16):
         o = torch.zeros((rows, 16 * 128), dtype=torch.float32, device="cuda")
         st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         rc = L.exl3cu_hyb_attn(_vp(q), rows, _vp(m.view("row_seq")), _vp(m.view("row_pos")), _vp(m.view("seq_slot")),
@@ -188,7 +188,7 @@ def test_fused_decode_attention_matches_prep_plus_attention(model):
     st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     args_meta = (_vp(m.view("row_seq")), _vp(m.view("row_pos")), _vp(m.view("seq_slot")))
     norms = (_vp(full["q_norm"]), _vp(full["k_norm"]), _vp(eng.inv_freq), eng.cfg.eps)
-    for sp in (1, 2, 8):
+    for sp in (1, 2, 8, 32):
         eng.kc[c].copy_(k0)
         eng.vc[c].copy_(v0)
         q = torch.zeros((rows, 16 * 128), dtype=torch.float32, device="cuda")

@@ -302,21 +302,36 @@ def test_fused_input_forms_and_accumulate(ops):
         y_glu = base.clone()
         y_rms = torch.empty((rows, n), dtype=torch.float32, device="cuda")
         VP, SZ, IN = ctypes.c_void_p * 2, ctypes.c_size_t * 2, ctypes.c_int * 2
+        y_ss = torch.full((rows, n // 128), -1.0, dtype=torch.float32, device="cuda")
         rc = L.exl3cu_mul_mat_batch_ex(
             2, VP(w.handle.value, w.handle.value), VP(gu.data_ptr(), h.data_ptr()), IN(_lib.X_GLU, _lib.X_RMSNORM),
             SZ(rows, rows), SZ(2 * k, k), VP(0, nw.data_ptr()), ctypes.c_float(1e-6),
-            VP(y_glu.data_ptr(), y_rms.data_ptr()), SZ(n, n), IN(1, 0), None)
+            VP(y_glu.data_ptr(), y_rms.data_ptr()), SZ(n, n), IN(1, 0), None, VP(y_ss.data_ptr(), 0), None)
         assert rc == 0, L.exl3cu_last_error()
         ref_glu = base + w.mul_mat(x_glu)
         ref_rms = w.mul_mat(x_rms)
         torch.cuda.synchronize()
         assert_close(y_glu.cpu().numpy(), ref_glu.cpu().numpy(), f"glu rows={rows}")
         assert_close(y_rms.cpu().numpy(), ref_rms.cpu().numpy(), f"rmsnorm rows={rows}")
+        # the accumulated output's sums of squares per 128-block
+        ss_ref = (y_glu.double() ** 2).view(rows, n // 128, 128).sum(dim=2)
+        assert torch.allclose(y_ss.double(), ss_ref, rtol=1e-5, atol=0), f"y sums of squares rows={rows}"
+        # RMSNorm input with the mean square taken from block sums of squares: same result as from the rows
+        h_ss = (h.double() ** 2).view(rows, k // 128, 128).sum(dim=2).float().contiguous()
+        y_rms2 = torch.empty((rows, n), dtype=torch.float32, device="cuda")
+        VP1, SZ1, IN1 = ctypes.c_void_p * 1, ctypes.c_size_t * 1, ctypes.c_int * 1
+        rc = L.exl3cu_mul_mat_batch_ex(1, VP1(w.handle.value), VP1(h.data_ptr()), IN1(_lib.X_RMSNORM), SZ1(rows),
+                                       SZ1(k), VP1(nw.data_ptr()), ctypes.c_float(1e-6), VP1(y_rms2.data_ptr()),
+                                       SZ1(n), None, VP1(h_ss.data_ptr()), None, None)
+        assert rc == 0, L.exl3cu_last_error()
+        torch.cuda.synchronize()
+        assert_close(y_rms2.cpu().numpy(), ref_rms.cpu().numpy(), f"rmsnorm from block sums rows={rows}")
     # the fused forms are GEMV-only: an 8-row item goes to the GEMM and is refused
     h8 = torch.zeros((8, k), dtype=torch.float32, device="cuda")
     y8 = torch.zeros((8, n), dtype=torch.float32, device="cuda")
     VP1, SZ1, IN1 = ctypes.c_void_p * 1, ctypes.c_size_t * 1, ctypes.c_int * 1
     rc = L.exl3cu_mul_mat_batch_ex(1, VP1(w.handle.value), VP1(h8.data_ptr()), IN1(_lib.X_RMSNORM), SZ1(8), SZ1(k),
-                                   VP1(nw.data_ptr()), ctypes.c_float(1e-6), VP1(y8.data_ptr()), SZ1(n), None, None)
+                                   VP1(nw.data_ptr()), ctypes.c_float(1e-6), VP1(y8.data_ptr()), SZ1(n), None, None,
+                                   None, None)
     assert rc == _lib.NO_SUPPORT
     w.free()

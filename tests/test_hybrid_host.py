@@ -60,4 +60,5 @@ def test_hybrid_c_abi_exports_every_declared_symbol():
 def test_attention_split_policy():
     from exl3_b200.hybrid import attn_splits
 
-    assert attn_splits(1) == 8 and attn_splits(8) == 8 and attn_splits(9) == 2 and attn_splits(512) == 1
+    assert attn_splits(1) == 32 and attn_splits(2) == 16 and attn_splits(8) == 8 and attn_splits(9) == 2
+    assert attn_splits(512) == 1

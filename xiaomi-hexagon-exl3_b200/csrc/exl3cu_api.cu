@@ -243,6 +243,8 @@ struct MmItem {
     const float * nw = nullptr;  // kXRmsNorm weights [k]
     float eps = 0.f;
     int y_accum = 0;
+    const float * x_ss = nullptr;  // kXRmsNorm: the rows' per-128-block sums of squares [rows][k/128]
+    float * y_ss = nullptr;        // per-128-block sums of squares of the final y [rows][n_local/128]
 };
 
 bool pdl_enabled() {
@@ -366,7 +368,7 @@ int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
     gemv_items.reserve(count);
     for (size_t i = 0; i < count; ++i) {
         if (items[i].rows >= gemm_min_rows()) {
-            if (items[i].x_mode != kXPlain || items[i].y_accum)
+            if (items[i].x_mode != kXPlain || items[i].y_accum || items[i].y_ss)
                 return fail(EXL3CU_NO_SUPPORT, "fused input forms and accumulation run on the GEMV (rows < %zu)",
                             gemm_min_rows());
             int rc = run_gemm(items[i], st);
@@ -386,6 +388,8 @@ int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
         int x_mode, y_accum;
         const float * nw;
         float eps;
+        const float * x_ss;
+        float * y_ss;
     };
     std::vector<Sub> subs;
     for (size_t i = 0; i < count; ++i) {
@@ -406,6 +410,8 @@ int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
             s.y_accum = it.y_accum;
             s.nw = it.nw;
             s.eps = it.eps;
+            s.x_ss = it.x_ss ? it.x_ss + r0 * (it.w->k / 128) : nullptr;
+            s.y_ss = it.y_ss ? it.y_ss + r0 * it.w->nblocks : nullptr;
             subs.push_back(s);
         }
     }
@@ -439,6 +445,9 @@ int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
             P.nw = s.nw;
             P.eps = s.eps;
             P.y_accum = s.y_accum;
+            P.x_ss = s.x_ss;
+            P.y_ss = s.y_ss;
+            P.y_ss_stride = int(s.w->nblocks);
             P.unit_base = units;
             units += int(s.w->nblocks);
             min_nchunks = P.nchunks < min_nchunks ? P.nchunks : min_nchunks;
@@ -452,7 +461,7 @@ int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
             continue;
         }
         for (size_t gi = 0; gi < group.size(); ++gi)
-            if (subs[group[gi]].x_mode != kXPlain || subs[group[gi]].y_accum)
+            if (subs[group[gi]].x_mode != kXPlain || subs[group[gi]].y_accum || subs[group[gi]].y_ss)
                 return fail(EXL3CU_NO_SUPPORT, "fused input forms and accumulation need mul1 weights of 2..8 bits");
         b.splits = choose_cluster_splits(subs[i].w->sms, units, min_nchunks);
         int max_cps = 1;
@@ -701,7 +710,8 @@ int exl3cu_mul_mat_batch(size_t count, const exl3cu_weight * const * weights, co
 int exl3cu_mul_mat_batch_ex(size_t count, const exl3cu_weight * const * weights, const void * const * d_x,
                             const int * x_form, const size_t * rows, const size_t * x_row_stride,
                             const float * const * d_norm_w, float eps, float * const * d_y,
-                            const size_t * y_row_stride, const int * y_accumulate, void * stream) {
+                            const size_t * y_row_stride, const int * y_accumulate,
+                            const float * const * d_x_sumsq, float * const * d_y_sumsq, void * stream) {
     if (!count) return EXL3CU_OK;
     if (!weights || !d_x || !x_form || !rows || !x_row_stride || !d_y || !y_row_stride)
         return fail(EXL3CU_INVALID_ARGUMENT, "batch arrays must not be NULL");
@@ -722,6 +732,11 @@ int exl3cu_mul_mat_batch_ex(size_t count, const exl3cu_weight * const * weights,
                 rc = fail(EXL3CU_INVALID_ARGUMENT, "norm weights must be 16-byte aligned");
             else rc = check_device_ptr(d_norm_w[i], weights[i]->device, "norm weights");
         }
+        if (!rc && d_x_sumsq && d_x_sumsq[i]) {
+            if (form != EXL3CU_X_RMSNORM) rc = fail(EXL3CU_INVALID_ARGUMENT, "x sums of squares need the RMSNorm form");
+            else rc = check_device_ptr(d_x_sumsq[i], weights[i]->device, "x sums of squares");
+        }
+        if (!rc && d_y_sumsq && d_y_sumsq[i]) rc = check_device_ptr(d_y_sumsq[i], weights[i]->device, "y sums of squares");
         if (rc) {
             std::string why = g_last_error;
             return fail(rc, "batch item %zu: %s", i, why.c_str());
@@ -731,6 +746,8 @@ int exl3cu_mul_mat_batch_ex(size_t count, const exl3cu_weight * const * weights,
         it.nw = form == EXL3CU_X_RMSNORM ? d_norm_w[i] : nullptr;
         it.eps = eps;
         it.y_accum = y_accumulate ? (y_accumulate[i] != 0) : 0;
+        it.x_ss = d_x_sumsq ? d_x_sumsq[i] : nullptr;
+        it.y_ss = d_y_sumsq ? d_y_sumsq[i] : nullptr;
         items[i] = it;
     }
     return run_cluster(items.data(), count, static_cast<cudaStream_t>(stream));

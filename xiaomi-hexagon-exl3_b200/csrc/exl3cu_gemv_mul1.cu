@@ -186,29 +186,42 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
                     v[ii][0] = hv.x; v[ii][1] = hv.y; v[ii][2] = hv.z; v[ii][3] = hv.w;
                 }
             }
-            // every CTA takes the whole row's mean square (from L2) before normalising its K range
-            float * red = part;  // scratch until the epilogue: [kMW][rows]
-            for (int r = 0; r < rows; ++r) {
-                const float * hr = static_cast<const float *>(P.x) + size_t(r) * P.x_stride;
-                float ss = 0.f;
-                for (int i = threadIdx.x * 4; i < ktot; i += kMW * 32 * 4) {
-                    const float4 v = *reinterpret_cast<const float4 *>(hr + i);
-                    ss = fmaf(v.x, v.x, ss);
-                    ss = fmaf(v.y, v.y, ss);
-                    ss = fmaf(v.z, v.z, ss);
-                    ss = fmaf(v.w, v.w, ss);
-                }
+            if (P.x_ss) {
+                // the producer's sums of squares per 128-block: warp r adds row r's (fixed tree)
+                const int nbk = ktot / 128;
+                if (warp < rows) {
+                    float ss = 0.f;
+                    for (int bk = lane; bk < nbk; bk += 32) ss += P.x_ss[size_t(warp) * nbk + bk];
 #pragma unroll
-                for (int sh = 16; sh; sh >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sh);
-                if (lane == 0) red[warp * rows + r] = ss;
+                    for (int sh = 16; sh; sh >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sh);
+                    if (lane == 0) invn_s[warp] = rsqrtf(ss / float(ktot) + P.eps);
+                }
+                consumer_sync();
+            } else {
+                // every CTA takes the whole row's mean square (from L2) before normalising its K range
+                float * red = part;  // scratch until the epilogue: [kMW][rows]
+                for (int r = 0; r < rows; ++r) {
+                    const float * hr = static_cast<const float *>(P.x) + size_t(r) * P.x_stride;
+                    float ss = 0.f;
+                    for (int i = threadIdx.x * 4; i < ktot; i += kMW * 32 * 4) {
+                        const float4 v = *reinterpret_cast<const float4 *>(hr + i);
+                        ss = fmaf(v.x, v.x, ss);
+                        ss = fmaf(v.y, v.y, ss);
+                        ss = fmaf(v.z, v.z, ss);
+                        ss = fmaf(v.w, v.w, ss);
+                    }
+#pragma unroll
+                    for (int sh = 16; sh; sh >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sh);
+                    if (lane == 0) red[warp * rows + r] = ss;
+                }
+                consumer_sync();
+                if (threadIdx.x < rows) {
+                    float ss = 0.f;
+                    for (int w = 0; w < kMW; ++w) ss += red[w * rows + threadIdx.x];
+                    invn_s[threadIdx.x] = rsqrtf(ss / float(ktot) + P.eps);
+                }
+                consumer_sync();
             }
-            consumer_sync();
-            if (threadIdx.x < rows) {
-                float ss = 0.f;
-                for (int w = 0; w < kMW; ++w) ss += red[w * rows + threadIdx.x];
-                invn_s[threadIdx.x] = rsqrtf(ss / float(ktot) + P.eps);
-            }
-            consumer_sync();
         }
         auto load_x = [&](int r, int kcol, float (&o)[4]) {
             if (P.x_mode == kXGlu) {
@@ -457,6 +470,15 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
                 o.w += y_prev.w;
             }
             *yp = o;
+            if (P.y_ss) {  // this block's sum of squares of the final y, for a later RMSNorm of the row
+                float ss = o.x * o.x;
+                ss = fmaf(o.y, o.y, ss);
+                ss = fmaf(o.z, o.z, ss);
+                ss = fmaf(o.w, o.w, ss);
+#pragma unroll
+                for (int sh = 16; sh; sh >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sh);
+                if (lane == 0) P.y_ss[size_t(r) * P.y_ss_stride + nb] = ss;
+            }
         }
     }
 }

@@ -75,15 +75,38 @@ __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1p
 
 // ---------------------------------------------------------------------------
 
+// With h_ss (H a multiple of 128): also the row's sum of squares per 128-block,
+// [rows][H/128] (warp w takes blocks w, w + 8, ...; lane 4 values of a block).
 __global__ void k_embed(const __half * __restrict__ table, const int32_t * __restrict__ ids, int vocab, int H,
-                        float * __restrict__ h) {
+                        float * __restrict__ h, float * __restrict__ h_ss) {
     pdl_trigger();
     pdl_wait_primary();
     const int r = blockIdx.x;
     const int32_t id = ids[r];
     const bool ok = id >= 0 && id < vocab;  // an id outside the table gives a zero row
-    for (int i = threadIdx.x; i < H; i += blockDim.x)
-        h[size_t(r) * H + i] = ok ? __half2float(table[size_t(id) * H + i]) : 0.f;
+    if (!h_ss) {
+        for (int i = threadIdx.x; i < H; i += blockDim.x)
+            h[size_t(r) * H + i] = ok ? __half2float(table[size_t(id) * H + i]) : 0.f;
+        return;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int b = warp; b < H / 128; b += nw) {
+        const int i = b * 128 + lane * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ok) {
+            const uint2 raw = *reinterpret_cast<const uint2 *>(table + size_t(id) * H + i);
+            const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+            const float2 c = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+            v = make_float4(a.x, a.y, c.x, c.y);
+        }
+        *reinterpret_cast<float4 *>(h + size_t(r) * H + i) = v;
+        float ss = v.x * v.x;
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+        ss = warp_sum(ss);
+        if (lane == 0) h_ss[size_t(r) * (H / 128) + b] = ss;
+    }
 }
 
 // h += delta (when given), then out = h / sqrt(mean(h^2) + eps) * w.
@@ -215,7 +238,7 @@ __global__ void k_attn_prep(const float * __restrict__ qkv, const int32_t * __re
 // more than one split each CTA stores (max, sum, acc[128]) to `part`, and the
 // last CTA of the (row, head) to arrive (ticket) merges the splits in split
 // order and resets the ticket.
-constexpr int kAttnPart = kHD + 2;
+constexpr int kAttnPart = kHD + 4;  // per split: max, sum, 2 pad, acc[128] (16-byte aligned records)
 
 // PREP (k_attn_decode): a step in which every sequence has exactly one row,
 // so a row attends to cached positions plus its own new one.  q points at the
@@ -284,7 +307,7 @@ k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const
     float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
     // warp w takes positions w, w+4, w+8, ... of the range, kU at a time: their k/v loads go out
     // together, then the online-softmax updates run in position order
-    constexpr int kU = 4;
+    constexpr int kU = 8;
     for (int pb = p0 + warp; pb < p1; pb += 4 * kU) {
         float2 k01[kU], k23[kU], v01[kU], v23[kU];
 #pragma unroll
@@ -366,8 +389,7 @@ k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const
             mine[0] = M;
             mine[1] = L;
         }
-#pragma unroll
-        for (int q2 = 0; q2 < 4; ++q2) mine[2 + lane * 4 + q2] = A[q2];
+        reinterpret_cast<float4 *>(mine + 4)[lane] = make_float4(A[0], A[1], A[2], A[3]);
         __threadfence();
     }
     __syncthreads();
@@ -375,17 +397,32 @@ k_attn(const float * __restrict__ q, const int32_t * __restrict__ row_seq, const
     __syncthreads();
     if (!sm_last || warp != 0) return;
     __threadfence();
+    // merge the splits (S <= 64): lane j holds the (max, sum) of splits j and j + 32, loaded together;
+    // the weights exp(m_z - M) go to every lane by shuffles; the sums run in a fixed order
     const float * all = part + (size_t(r) * kNH + head) * S * kAttnPart;
-    float GM = -INFINITY;
-    for (int zz = 0; zz < S; ++zz) GM = fmaxf(GM, __ldcg(all + zz * kAttnPart));
-    float GL = 0.f, G[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int zz = 0; zz < S; ++zz) {
-        const float mz = __ldcg(all + zz * kAttnPart);
-        if (mz == -INFINITY) continue;
-        const float c = expf(mz - GM);
-        GL = fmaf(__ldcg(all + zz * kAttnPart + 1), c, GL);
+    float mz[2], lz[2];
 #pragma unroll
-        for (int q2 = 0; q2 < 4; ++q2) G[q2] = fmaf(__ldcg(all + zz * kAttnPart + 2 + lane * 4 + q2), c, G[q2]);
+    for (int i = 0; i < 2; ++i) {
+        const int zz = lane + 32 * i;
+        mz[i] = zz < S ? __ldcg(all + zz * kAttnPart) : -INFINITY;
+        lz[i] = zz < S ? __ldcg(all + zz * kAttnPart + 1) : 0.f;
+    }
+    float GM = fmaxf(mz[0], mz[1]);
+#pragma unroll
+    for (int sh = 16; sh; sh >>= 1) GM = fmaxf(GM, __shfl_xor_sync(0xffffffffu, GM, sh));
+    float cz[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) cz[i] = mz[i] == -INFINITY ? 0.f : expf(mz[i] - GM);  // a split that saw nothing: 0
+    const float GL = warp_sum(fmaf(lz[1], cz[1], lz[0] * cz[0]));
+    float G[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+    for (int zz = 0; zz < S; ++zz) {
+        const float c = __shfl_sync(0xffffffffu, zz < 32 ? cz[0] : cz[1], zz & 31);
+        const float4 a = __ldcg(reinterpret_cast<const float4 *>(all + zz * kAttnPart + 4) + lane);
+        G[0] = fmaf(a.x, c, G[0]);
+        G[1] = fmaf(a.y, c, G[1]);
+        G[2] = fmaf(a.z, c, G[2]);
+        G[3] = fmaf(a.w, c, G[3]);
     }
     const float invL = 1.0f / GL;
 #pragma unroll
@@ -950,11 +987,13 @@ constexpr int kHeadSmemMax = 200 * 1024;
 extern "C" {
 
 int exl3cu_hyb_embed(const uint16_t * d_table, int vocab, const int32_t * d_ids, int rows, int hidden, float * d_h,
-                     void * stream) {
+                     float * d_h_sumsq, void * stream) {
     if (!d_table || !d_ids || !d_h || rows < 0 || hidden <= 0 || vocab <= 0) return bad("embed: bad arguments");
+    if (d_h_sumsq && (hidden % 128 || reinterpret_cast<uintptr_t>(d_h) % 16 || reinterpret_cast<uintptr_t>(d_table) % 8))
+        return bad("embed: sums of squares need hidden a multiple of 128 and aligned rows");
     if (!rows) return EXL3CU_OK;
     return launch_pdl(k_embed, dim3(unsigned(rows)), dim3(256), 0, stream,
-                      reinterpret_cast<const __half *>(d_table), d_ids, vocab, hidden, d_h);
+                      reinterpret_cast<const __half *>(d_table), d_ids, vocab, hidden, d_h, d_h_sumsq);
 }
 
 int exl3cu_hyb_rmsnorm(float * d_h, const float * d_delta, int delta_stride, const float * d_w, float eps, int rows,
@@ -1002,6 +1041,7 @@ int exl3cu_hyb_attn(const float * d_q, int rows, const int32_t * d_row_seq, cons
     if (rows > 65535) return bad("attn: at most 65535 rows");
     if (splits > 1 && (!d_part || !d_tickets || part_bytes < exl3cu_hyb_attn_scratch_bytes(rows, splits)))
         return bad("attn: split scratch missing or too small (exl3cu_hyb_attn_scratch_bytes; tickets rows*16, zeroed)");
+    if (reinterpret_cast<uintptr_t>(d_part) % 16) return bad("attn: split scratch must be 16-byte aligned");
     // the plain kernel only reads the caches
     __half * kc = reinterpret_cast<__half *>(const_cast<uint16_t *>(d_kcache));
     __half * vc = reinterpret_cast<__half *>(const_cast<uint16_t *>(d_vcache));
@@ -1023,6 +1063,7 @@ int exl3cu_hyb_attn_decode(const float * d_qkv, int rows, const int32_t * d_row_
     if (rows > 65535) return bad("attn_decode: at most 65535 rows");
     if (splits > 1 && (!d_part || !d_tickets || part_bytes < exl3cu_hyb_attn_scratch_bytes(rows, splits)))
         return bad("attn_decode: split scratch missing or too small (exl3cu_hyb_attn_scratch_bytes; tickets rows*16, zeroed)");
+    if (reinterpret_cast<uintptr_t>(d_part) % 16) return bad("attn_decode: split scratch must be 16-byte aligned");
     return launch_pdl(k_attn<true>, dim3(kNH, unsigned(rows), unsigned(splits)), dim3(128), 0, stream, d_qkv,
                       d_row_seq, d_row_pos, d_seq_slot, reinterpret_cast<__half *>(d_kcache),
                       reinterpret_cast<__half *>(d_vcache), max_len, n_slots, scale, d_part, d_tickets, d_out, d_qn_w,

@@ -49,6 +49,9 @@ struct GemvProblem {
     const float * nw;
     float eps;
     int y_accum;    // 1: y += x . W (one writer per element) instead of y = x . W
+    const float * x_ss;  // kXRmsNorm, optional: [rows][k/128] sums of squares of the rows' 128-blocks
+    float * y_ss;        // optional: [rows][y_ss_stride] sums of squares of the final y, per column block
+    int y_ss_stride;     // column blocks of the item's y row
 };
 
 constexpr int kXPlain = 0, kXGlu = 1, kXRmsNorm = 2;

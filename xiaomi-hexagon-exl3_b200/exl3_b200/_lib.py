@@ -90,7 +90,8 @@ def _declare(L):
                                        _c.POINTER(_sz), _c.POINTER(_sz), _c.POINTER(_vp), _c.POINTER(_sz), _vp]
     L.exl3cu_mul_mat_batch_ex.argtypes = [_sz, _c.POINTER(_vp), _c.POINTER(_vp), _c.POINTER(_c.c_int),
                                           _c.POINTER(_sz), _c.POINTER(_sz), _c.POINTER(_vp), _c.c_float,
-                                          _c.POINTER(_vp), _c.POINTER(_sz), _c.POINTER(_c.c_int), _vp]
+                                          _c.POINTER(_vp), _c.POINTER(_sz), _c.POINTER(_c.c_int), _c.POINTER(_vp),
+                                          _c.POINTER(_vp), _vp]
     _P = _c.POINTER
     L.exl3cu_model_open.argtypes = [_c.c_char_p, _c.c_int, _c.c_uint, _P(_vp)]
     L.exl3cu_model_free.argtypes = [_vp]

@@ -146,7 +146,7 @@ def _declare(L):
     if getattr(L, "_hyb_declared", False):
         return
     I, F, S, P = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
-    L.exl3cu_hyb_embed.argtypes = [P, I, P, I, I, P, P]
+    L.exl3cu_hyb_embed.argtypes = [P, I, P, I, I, P, P, P]
     L.exl3cu_hyb_rmsnorm.argtypes = [P, P, I, P, F, I, I, P, P]
     L.exl3cu_hyb_swiglu.argtypes = [P, I, I, P, P]
     L.exl3cu_hyb_attn_prep.argtypes = [P, I, P, P, P, P, P, P, F, P, P, I, I, P, P]
@@ -168,7 +168,7 @@ def _declare(L):
 def attn_splits(rows: int) -> int:
     """Position splits per (row, head) of the attention kernel: many for decode steps (few rows, long
     contexts), one when the rows alone fill the GPU."""
-    return 8 if rows <= 8 else (2 if rows <= 64 else 1)
+    return 32 if rows <= 1 else (16 if rows <= 2 else (8 if rows <= 8 else (2 if rows <= 64 else 1)))
 
 
 class StepMeta:
@@ -240,6 +240,7 @@ class HybridEngine:
         R = max_rows
         f32, f16 = torch.float32, torch.float16
         self.h = torch.zeros((R, H), dtype=f32, device=dev)
+        self.h_ss = torch.zeros((R, H // 128), dtype=f32, device=dev)  # h's sums of squares per 128-block
         self.xn = torch.zeros((R, H), dtype=f32, device=dev)
         self.proj = torch.zeros((R, 4 * D), dtype=f32, device=dev)      # [q|k|v|z] or [q|k|v]
         self.q = torch.zeros((R, D), dtype=f32, device=dev)
@@ -264,8 +265,8 @@ class HybridEngine:
                 d["cache"] = gi
                 gi += 1
         self.meta = StepMeta(torch, dev, R, slots, 8)
-        cap = max(r * attn_splits(r) for r in range(1, R + 1))
-        self.attn_part = torch.zeros(cap * cfg.heads * (cfg.head_dim + 2), dtype=f32, device=dev)
+        part_bytes = max(L.exl3cu_hyb_attn_scratch_bytes(r, attn_splits(r)) for r in range(1, R + 1))
+        self.attn_part = torch.zeros(max(1, part_bytes // 4), dtype=f32, device=dev)
         self.attn_tickets = torch.zeros(R * cfg.heads, dtype=torch.int32, device=dev)
         self.best = torch.zeros(9, dtype=torch.int64, device=dev)  # head scratch: 8 maxima + a ticket, left zero
         self.out_tokens = torch.zeros(8, dtype=torch.int32, device=dev)
@@ -289,21 +290,24 @@ class HybridEngine:
         self.conv[:, slot].zero_()
 
     # -- one step ---------------------------------------------------------------------------------
-    def _mm_batch(self, names, mats, x, out_cols, rows, st, form: int = 0, nw=None, accum: bool = False):
+    def _mm_batch(self, names, mats, x, out_cols, rows, st, form: int = 0, nw=None, accum: bool = False,
+                  x_ss=None, y_ss=None):
         """Projections sharing input x (form 0: f32 rows; 2: [gate | up] rows, SwiGLU on load; 3: residual
-        rows, RMSNorm with weights nw on load) into column ranges of the given outputs, stored or (accum)
-        added.
+        rows, RMSNorm with weights nw on load, the rows' mean squares from the block sums x_ss) into
+        column ranges of the given outputs, stored or (accum) added; y_ss receives the block sums of
+        squares of a full-row output.
 
         Steps of 5..8 rows (batched decode) go to the operator as two problems of <= 4 rows per
         matrix in one grouped call: the grouped integer-tensor-core GEMV then decodes the weights of
         every matrix in one launch, which measured faster for these grouped decode shapes than one
         tensor-core GEMM launch per matrix."""
         key = (tuple(mats[nm].handle.value for nm in names), x.data_ptr(), tuple(o.data_ptr() for o in out_cols),
-               rows, form, nw.data_ptr() if nw is not None else 0, accum)
+               rows, form, nw.data_ptr() if nw is not None else 0, accum,
+               x_ss.data_ptr() if x_ss is not None else 0, y_ss.data_ptr() if y_ss is not None else 0)
         args = self._batch_args.get(key)
         if args is None:
             pieces = [(0, rows)] if not 5 <= rows <= 8 else [(0, 4), (4, rows - 4)]
-            ws, xs, rs, ys, yst = [], [], [], [], []
+            ws, xs, rs, ys, yst, xss, yss = [], [], [], [], [], [], []
             for nm, o in zip(names, out_cols):
                 for r0, nr in pieces:
                     ws.append(mats[nm].handle.value)
@@ -311,16 +315,19 @@ class HybridEngine:
                     rs.append(nr)
                     ys.append(o.data_ptr() + r0 * o.stride(0) * o.element_size())
                     yst.append(o.stride(0))
+                    xss.append(x_ss[r0:].data_ptr() if x_ss is not None else 0)
+                    yss.append(y_ss[r0:].data_ptr() if y_ss is not None else 0)
             n = len(ws)
             VP, SZ, IN = ctypes.c_void_p * n, ctypes.c_size_t * n, ctypes.c_int * n
             nws = VP(*[nw.data_ptr() if nw is not None else 0] * n)
             args = (n, VP(*ws), VP(*xs), IN(*[form] * n), SZ(*rs), SZ(*[x.stride(0)] * n), nws,
-                    ctypes.c_float(self.cfg.eps), VP(*ys), SZ(*yst), IN(*[1 if accum else 0] * n))
+                    ctypes.c_float(self.cfg.eps), VP(*ys), SZ(*yst), IN(*[1 if accum else 0] * n),
+                    VP(*xss), VP(*yss))
             self._batch_args[key] = args
         check(self.L.exl3cu_mul_mat_batch_ex(*args, st))
 
-    def _mm(self, w, x, out, rows, st, form: int = 0, nw=None, accum: bool = False):
-        self._mm_batch(("_one",), {"_one": w}, x, [out], rows, st, form, nw, accum)
+    def _mm(self, w, x, out, rows, st, form: int = 0, nw=None, accum: bool = False, x_ss=None, y_ss=None):
+        self._mm_batch(("_one",), {"_one": w}, x, [out], rows, st, form, nw, accum, x_ss, y_ss)
 
     def forward(self, rows: int, n_seq: int, nout: int, stream=None):
         """Run the step whose metadata is in self.meta.dev; next tokens land in self.out_tokens[:nout]."""
@@ -337,9 +344,11 @@ class HybridEngine:
             self._pf_events[0].record(main)
             self._pf_stream.wait_event(self._pf_events[0])
             check(L.exl3cu_prefetch_l2(n0, a0, ctypes.c_void_p(self._pf_stream.cuda_stream)))
-        check(L.exl3cu_hyb_embed(_vp(self.embed), cfg.vocab, _vp(tokens), rows, H, _vp(self.h), st))
+        fused = rows <= 8 and self.fused
+        check(L.exl3cu_hyb_embed(_vp(self.embed), cfg.vocab, _vp(tokens), rows, H, _vp(self.h),
+                                 _vp(self.h_ss) if fused else None, st))
         scale = 1.0 / float(np.sqrt(cfg.head_dim))
-        if rows <= 8 and self.fused:
+        if fused:
             self._forward_fused(rows, n_seq, nout, st, scale, row_seq, row_pos, row_offsets, seq_slot, logit_rows,
                                 pf, main)
             return
@@ -398,7 +407,9 @@ class HybridEngine:
         """Steps of <= 8 rows: the layer glue folded into the packed operator -- RMSNorm on load for the
         projections (and inside the delta-rule gates), SwiGLU on load for the down projection, the o and
         down products added into the residual stream h -- so a layer is 4 operator launches plus its
-        mixer (attention or delta rule)."""
+        mixer (attention or delta rule).  The kernels that write h (the embedding, the o and down
+        products) also write its sums of squares per 128-block (h_ss), from which the RMSNorm-on-load
+        projections take the rows' mean squares without reading h in full."""
         cfg, L = self.cfg, self.L
         H, F, D, KV = cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim, self.KV
         for li, d in enumerate(self.layers):
@@ -411,7 +422,7 @@ class HybridEngine:
             if d["kind"] == "full":
                 qkv = self.proj.view(-1)[: self.max_rows * (D + 2 * KV)].view(self.max_rows, D + 2 * KV)
                 outs = [qkv[:, 0:D], qkv[:, D:D + KV], qkv[:, D + KV:D + 2 * KV]]
-                self._mm_batch(("q", "k", "v"), mats, self.h, outs, rows, st, 3, d["in_norm"])
+                self._mm_batch(("q", "k", "v"), mats, self.h, outs, rows, st, 3, d["in_norm"], x_ss=self.h_ss)
                 c = d["cache"]
                 kc, vc = self.kc[c], self.vc[c]
                 sp = attn_splits(rows)
@@ -431,16 +442,17 @@ class HybridEngine:
             else:
                 p = self.proj
                 outs = [p[:, 0:D], p[:, D:2 * D], p[:, 2 * D:3 * D], p[:, 3 * D:4 * D]]
-                self._mm_batch(("q", "k", "v", "z"), mats, self.h, outs, rows, st, 3, d["in_norm"])
+                self._mm_batch(("q", "k", "v", "z"), mats, self.h, outs, rows, st, 3, d["in_norm"],
+                               x_ss=self.h_ss)
                 c = d["cache"]
                 check(L.exl3cu_hyb_gdn(_vp(p), _vp(self.h), _vp(d["in_norm"]), _vp(d["wab"]), H, _vp(d["conv_w"]),
                                        _vp(self.conv[c]), _vp(d["A_log"]), _vp(d["dt_bias"]), _vp(d["gnorm"]),
                                        cfg.eps, _vp(self.state[c]), _vp(row_offsets), _vp(seq_slot), n_seq,
                                        self.slots, _vp(self.mix), st))
-            self._mm(mats["o"], self.mix, self.h, rows, st, 0, None, True)                 # h += o
+            self._mm(mats["o"], self.mix, self.h, rows, st, 0, None, True, y_ss=self.h_ss)    # h += o
             self._mm_batch(("gate", "up"), mats, self.h, [self.gu[:, 0:F], self.gu[:, F:2 * F]], rows, st, 3,
-                           d["post_norm"])
-            self._mm(mats["down"], self.gu, self.h, rows, st, 2, None, True)               # h += down(swiglu)
+                           d["post_norm"], x_ss=self.h_ss)
+            self._mm(mats["down"], self.gu, self.h, rows, st, 2, None, True, y_ss=self.h_ss)  # h += down(swiglu)
         # the final RMSNorm is applied by the head as it loads h
         check(L.exl3cu_hyb_head(_vp(self.h), _vp(logit_rows), nout, H, _vp(self.final_norm), cfg.eps,
                                 _vp(self.embed), cfg.vocab, None, _vp(self.best), _vp(self.out_tokens), st))
