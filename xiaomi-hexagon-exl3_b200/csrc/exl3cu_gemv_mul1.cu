@@ -50,16 +50,18 @@ static __device__ unsigned g_mul1_status;
 static_assert(kMRows <= kMW, "the epilogue gives each row its own consumer warp");  // kStatus* bits raised by k_gemv_mul1
 
 struct Mul1Layout {
-    int ring_off, xq_off, acc_off, part_off, slot_off, gmax_off, bar_off;
+    int ring_off, xq_off, acc_off, part_off, slot_off, gmax_off, nw_off, bar_off;
     size_t bytes;
 };
 
 // ring: kMStages stages of kMW chunks; xq: activation digits of the CTA's K
 // range; acc: the CTA's integer sums [rows][128][hi, lo]; part: its fp32
 // partial; slot: the other cluster ranks' partials (written remotely, read by
-// rank 0); gmax: max |xh| per (row, own group); then the mbarriers and per-row
-// scale / digit sum.
-__host__ __device__ inline Mul1Layout mul1_layout(int bits, int cps, int rows, int splits, int stages) {
+// rank 0); gmax: max |xh| per (row, own group); nw (RMSNorm form, when staged):
+// the norm weights of the CTA's groups; then the mbarriers and per-row scale /
+// digit sum.
+__host__ __device__ inline Mul1Layout mul1_layout(int bits, int cps, int rows, int splits, int stages,
+                                                  bool nw_smem) {
     Mul1Layout L;
     const int ng = (cps + 7) / 8 + 1;
     const size_t ring = size_t(stages) * kMW * 256 * bits;
@@ -74,7 +76,8 @@ __host__ __device__ inline Mul1Layout mul1_layout(int bits, int cps, int rows, i
     L.part_off = int(L.acc_off + acc);
     L.slot_off = int(L.part_off + part);
     L.gmax_off = int(L.slot_off + slot);
-    L.bar_off = int((L.gmax_off + gmax + 15) & ~size_t(15));
+    L.nw_off = int((L.gmax_off + gmax + 15) & ~size_t(15));
+    L.bar_off = L.nw_off + (nw_smem ? ng * 128 * 4 : 0);
     L.bytes = L.bar_off + 2 * stages * 8 + 3 * 4 * kMRows;  // + per-row scale, digit sum, inverse norm
     return L;
 }
@@ -104,13 +107,14 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
     const int lane = threadIdx.x & 31;
 
     const int NS = b.stages;
-    const Mul1Layout L = mul1_layout(BITS, P.cps, rows, S, NS);
+    const Mul1Layout L = mul1_layout(BITS, P.cps, rows, S, NS, b.nw_smem != 0);
     unsigned char * ring = smem + L.ring_off;
     unsigned char * xq = smem + L.xq_off;
     int * acc = reinterpret_cast<int *>(smem + L.acc_off);          // [rows][128][2]
     float * part = reinterpret_cast<float *>(smem + L.part_off);    // [rows][128]
     float * slots = reinterpret_cast<float *>(smem + L.slot_off);   // [S-1][rows][128]
     float * gmax = reinterpret_cast<float *>(smem + L.gmax_off);    // [rows][ng]
+    float * nws = reinterpret_cast<float *>(smem + L.nw_off);       // [ng][128] (staged RMSNorm weights)
     uint64_t * full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
     uint64_t * empty = full + NS;
     float * scale_s = reinterpret_cast<float *>(empty + NS);
@@ -171,8 +175,20 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             if (item < nitems) su_pre[ii] = *reinterpret_cast<const uint2 *>(P.su + (g0 + item / rows) * 128 + lane * 4);
         }
         if (split == 0) sv_pre = *reinterpret_cast<const uint2 *>(P.sv + nb * 128 + lane * 4);
-        pdl_wait_primary();  // activations may be written by the previous kernel
         const int ktot = P.nchunks * 16;
+        // RMSNorm weights of the CTA's groups (a layer constant): staged in shared memory before the
+        // wait when the launch has room for them (read after a barrier below), else read from L2
+        const bool staged = P.x_mode == kXRmsNorm && b.nw_smem;
+        if (staged)
+            for (int e = threadIdx.x * 4; e < ng * 128; e += kMW * 32 * 4)
+                *reinterpret_cast<float4 *>(nws + e) = g0 * 128 + e < ktot
+                                                           ? *reinterpret_cast<const float4 *>(P.nw + g0 * 128 + e)
+                                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        auto norm_w4 = [&](int kcol) {  // RMSNorm weights k .. k+3
+            return staged ? *reinterpret_cast<const float4 *>(nws + (kcol - g0 * 128))
+                          : *reinterpret_cast<const float4 *>(P.nw + kcol);
+        };
+        pdl_wait_primary();  // activations may be written by the previous kernel
         float v[kItems][4];
         if (P.x_mode == kXRmsNorm) {
             // the register-cached items' raw h goes out with the full-row loads below (one round trip)
@@ -237,7 +253,7 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             if (P.x_mode == kXRmsNorm) {
                 const float4 hv = *reinterpret_cast<const float4 *>(static_cast<const float *>(P.x) +
                                                                     size_t(r) * P.x_stride + kcol);
-                const float4 wv = *reinterpret_cast<const float4 *>(P.nw + kcol);
+                const float4 wv = norm_w4(kcol);
                 const float inv = invn_s[r];
                 o[0] = hv.x * inv * wv.x;
                 o[1] = hv.y * inv * wv.y;
@@ -291,7 +307,7 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
                 const int gi = item / rows;
                 const int kcol = (g0 + gi) * 128 + lane * 4;
                 if (P.x_mode == kXRmsNorm) {  // raw h already loaded: normalise
-                    const float4 wv = *reinterpret_cast<const float4 *>(P.nw + kcol);
+                    const float4 wv = norm_w4(kcol);
                     const float inv = invn_s[item - gi * rows];
                     v[ii][0] = v[ii][0] * inv * wv.x;
                     v[ii][1] = v[ii][1] * inv * wv.y;
@@ -576,7 +592,9 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
                              cudaStream_t st) {
     if (!mul1_prepare(device, bits)) return cudaErrorInvalidValue;
     int min_nchunks = 1 << 30, max_nchunks = 0, max_rows = 1;
+    bool nw_smem = false;
     for (int i = 0; i < b.count; ++i) {
+        nw_smem = nw_smem || b.prob[i].x_mode == kXRmsNorm;
         min_nchunks = std::min(min_nchunks, b.prob[i].nchunks);
         max_nchunks = std::max(max_nchunks, b.prob[i].nchunks);
         max_rows = std::max(max_rows, b.prob[i].rows);
@@ -586,27 +604,38 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
     int S = 0;
     if (env && std::atoi(env) > 0) {
         S = std::min(16, std::atoi(env));
+        nw_smem = false;
     } else {
         // largest cluster size whose grid is one wave; else the largest that can run at all.
         // EXL3CU_MUL1_CTAS_PER_SM (tuning experiments) caps the grid at that many CTAs per SM, leaving
         // room for the next launch's CTAs to start under programmatic dependent launch.
         const char * cap_env = std::getenv("EXL3CU_MUL1_CTAS_PER_SM");
         const int cap = cap_env && std::atoi(cap_env) > 0 ? std::atoi(cap_env) * sms : 1 << 30;
-        int feasible = 0;
-        for (int cand = 16; cand >= 1; --cand) {
-            if (cand > 1 && min_nchunks / cand < kMW) continue;
-            const int cps = (max_nchunks + cand - 1) / cand;
-            const Mul1Layout L = mul1_layout(int(bits), cps, max_rows, cand, NS);
-            if (L.bytes > kMul1MaxSmem) break;  // fewer splits only grow the per-CTA range
-            const int fit = std::min(mul1_active_clusters(device, bits, cand, L.bytes), cap / cand);
-            if (fit <= 0) continue;
-            if (!feasible) feasible = cand;
-            if (nunits <= fit) {
-                S = cand;
-                break;
+        auto choose = [&](bool staged, int & fit_out) {
+            int feasible = 0, feasible_fit = 0;
+            for (int cand = 16; cand >= 1; --cand) {
+                if (cand > 1 && min_nchunks / cand < kMW) continue;
+                const int cps = (max_nchunks + cand - 1) / cand;
+                const Mul1Layout L = mul1_layout(int(bits), cps, max_rows, cand, NS, staged);
+                if (L.bytes > kMul1MaxSmem) break;  // fewer splits only grow the per-CTA range
+                const int fit = std::min(mul1_active_clusters(device, bits, cand, L.bytes), cap / cand);
+                if (fit <= 0) continue;
+                if (!feasible) {
+                    feasible = cand;
+                    feasible_fit = fit;
+                }
+                if (nunits <= fit) {
+                    fit_out = fit;
+                    return cand;
+                }
             }
-        }
-        if (!S) S = feasible;
+            fit_out = feasible_fit;
+            return feasible;
+        };
+        int fit0 = 0, fit1 = 0;
+        S = choose(false, fit0);
+        // stage the RMSNorm weights only where that costs no occupancy: same split, same wave
+        if (nw_smem) nw_smem = choose(true, fit1) == S && (fit1 >= nunits || fit1 == fit0);
     }
     if (S <= 0) return cudaErrorInvalidConfiguration;
     b.splits = S;
@@ -615,9 +644,10 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
         b.prob[i].cps = (b.prob[i].nchunks + S - 1) / S;
         max_cps = std::max(max_cps, b.prob[i].cps);
     }
-    const Mul1Layout L = mul1_layout(int(bits), max_cps, max_rows, S, NS);
+    const Mul1Layout L = mul1_layout(int(bits), max_cps, max_rows, S, NS, nw_smem);
     if (L.bytes > kMul1MaxSmem) return cudaErrorInvalidConfiguration;
     b.stages = NS;
+    b.nw_smem = nw_smem ? 1 : 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(nunits * S), 1, 1);
     cfg.blockDim = dim3(kMThreads, 1, 1);

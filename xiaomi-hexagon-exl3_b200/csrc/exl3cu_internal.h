@@ -63,6 +63,7 @@ struct GemvBatch {
     int count;
     int splits;     // cluster size: CTAs per unit along K
     int stages;     // mul1 kernel: weight ring depth (stages of kMW chunks)
+    int nw_smem;    // mul1 kernel: RMSNorm weights staged in shared memory before the dependency wait
 };
 
 int choose_cluster_splits(int sms, int nunits, int min_nchunks);
