@@ -192,7 +192,7 @@ int exl3cu_mul_mat_ragged(const exl3cu_weight * w, const void * d_x, int x_dtype
 
 /* Plan overrides of the batched path, process-wide (for tuning).  Operands of
  * at least `min_rows` rows run on the tensor-core GEMM (tcgen05, decoded
- * weights and accumulators in TMEM; default 9), smaller ones on the decode
+ * weights and accumulators in TMEM; default 5), smaller ones on the decode
  * GEMV.  `tokens_per_cta` (a multiple of 32 up to 256: the MMA's N) and
  * `splits` (1, 2, 4, 8 or 16 CTAs of a cluster along K) replace the automatic
  * plan; 0 leaves a value automatic, min_rows 0 leaves it unchanged.  No

@@ -39,6 +39,7 @@
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <atomic>
 
 namespace cg = cooperative_groups;
@@ -473,7 +474,11 @@ struct GdnSmem {
     static constexpr int floats_without_wab = WAB;
 };
 
-__global__ void __launch_bounds__(kGdnThreads, 1)
+// MINB CTAs per SM: 1 (no register cap) for steps of one or two sequences, whose
+// few CTAs fit the GPU anyway; 2 (at most 128 registers) for more, so that the
+// clusters of a many-sequence step run in half the waves.
+template <int MINB>
+__global__ void __launch_bounds__(kGdnThreads, MINB)
 k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const float * __restrict__ xn_norm_w,
       const __half * __restrict__ wab, int H, const float * __restrict__ conv_w, float * __restrict__ conv_state,
       const float * __restrict__ A_log, const float * __restrict__ dt_bias, const float * __restrict__ norm_w,
@@ -731,6 +736,17 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const floa
     for (int i = 0; i < kGdnKRows; ++i) Sg[(i0 + i) * kHD + j] = Sr[i];
 }
 
+// D += A B for one m16n8k16 tile (f16 x f16 -> f32): A row-major fragments a0..a3, B column
+// fragments b0, b1 (the PTX ISA's layout for mma.m16n8k16).
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              __half2 b0, __half2 b1) {
+    const uint32_t rb0 = *reinterpret_cast<const uint32_t *>(&b0), rb1 = *reinterpret_cast<const uint32_t *>(&b1);
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(rb0), "r"(rb1));
+}
+
 // Order-preserving key of a float (larger float, larger key).
 __device__ __forceinline__ uint32_t float_key(float f) {
     const uint32_t b = __float_as_uint(f);
@@ -739,8 +755,10 @@ __device__ __forceinline__ uint32_t float_key(float f) {
 
 // logits[o][v] = sum_i xn[rows[o]][i] * E[v][i] (f32 x, fp16 E, fp32 sums) for
 // nout <= 8 rows; best[o] = max over v of (key(logit) << 32 | ~v) (the first
-// index wins ties).  Warp per vocab row, activations staged in shared memory;
-// ITER = H / 256 16-byte loads per lane per vocab row, issued together.
+// index wins ties).  Activations staged in shared memory.  One row: warp per
+// vocab row, ITER = H / 256 16-byte loads per lane per vocab row issued
+// together.  2..8 rows: 16 vocab rows per warp on the tensor cores (fp16 MMA
+// with the activations split into fp16 hi + lo).
 // With norm_w the rows are the residual stream h and the final RMSNorm is
 // applied while staging, with k_rmsnorm's arithmetic (thread t sums the
 // squares of float4s t, t + 256, ... in order; warps add in order), so the
@@ -842,56 +860,62 @@ k_head(const float * __restrict__ xn, const int32_t * __restrict__ rows, int nou
             }
         }
     } else {
-        // several activation rows: four vocab rows per pass, so that each activation value read from
-        // shared memory serves four vocab rows
-        constexpr int VB = 4;
-        for (int v0 = (blockIdx.x * (kHeadThreads / 32) + warp) * VB; v0 < V; v0 += nwarps * VB) {
-            float acc[VB][kHeadMaxRows];
-#pragma unroll
-            for (int b = 0; b < VB; ++b)
-#pragma unroll
-                for (int o = 0; o < kHeadMaxRows; ++o) acc[b][o] = 0.f;
+        // 2..8 activation rows on the tensor cores: mma.m16n8k16, A = 16 vocab rows of E (fp16),
+        // B = the activation rows as fp16 hi + lo (x - hi - lo is about 2^-22 x), fp32 sums.  A warp
+        // takes 16 vocab rows at a time; per 64-wide k-block lane (g, t) loads k [8t, 8t + 8) and
+        // [32 + 8t, 32 + 8t + 8) of vocab rows g and g + 8 (each load instruction reads whole 64-byte
+        // row pieces), and k-step s pairs registers 2s, 2s+1 of those with activation row g at the
+        // same k: the MMA sums over a permutation of the real k order, the same for A and B.  Lanes
+        // of activation rows >= nout supply zeros.
+        const int g = lane >> 2, t = lane & 3;
+        unsigned long long cand[2] = {0ull, 0ull};  // best (key, ~v) of activation rows 2t, 2t + 1
+        const int ngroups = (V + 15) / 16;
+        for (int grp = blockIdx.x * (kHeadThreads / 32) + warp; grp < ngroups; grp += nwarps) {
+            const int va = grp * 16 + g, vb = va + 8;
+            const __half * ea = E + size_t(min(va, V - 1)) * H + 8 * t;
+            const __half * eb = E + size_t(min(vb, V - 1)) * H + 8 * t;
+            const float * xr = xs + size_t(g < nout ? g : 0) * H + 8 * t;
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 2
-            for (int it = 0; it < ITER; ++it) {
-                float ef[VB][8];
+            for (int kb = 0; kb < H / 64; ++kb) {
+                const uint4 a0 = __ldcs(reinterpret_cast<const uint4 *>(ea + kb * 64));
+                const uint4 a1 = __ldcs(reinterpret_cast<const uint4 *>(ea + kb * 64 + 32));
+                const uint4 b0 = __ldcs(reinterpret_cast<const uint4 *>(eb + kb * 64));
+                const uint4 b1 = __ldcs(reinterpret_cast<const uint4 *>(eb + kb * 64 + 32));
+                const uint32_t ra[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const uint32_t rb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-                for (int b = 0; b < VB; ++b) {
-                    uint4 raw = make_uint4(0, 0, 0, 0);
-                    if (v0 + b < V) raw = __ldcs(reinterpret_cast<const uint4 *>(E + size_t(v0 + b) * H + it * 256 + lane * 8));
-                    const __half2 * e2 = reinterpret_cast<const __half2 *>(&raw);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const float2 f = __half22float2(e2[q]);
-                        ef[b][2 * q] = f.x;
-                        ef[b][2 * q + 1] = f.y;
-                    }
-                }
-#pragma unroll
-                for (int o = 0; o < kHeadMaxRows; ++o) {
-                    if (o >= nout) break;
-                    const float4 * xr = reinterpret_cast<const float4 *>(xs + o * H + it * 256 + lane * 8);
-                    const float4 x0 = xr[0], x1 = xr[1];
-                    const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-                    for (int b = 0; b < VB; ++b)
-#pragma unroll
-                        for (int q = 0; q < 8; ++q) acc[b][o] = fmaf(xv[q], ef[b][q], acc[b][o]);
+                for (int st = 0; st < 4; ++st) {
+                    float4 x = *reinterpret_cast<const float4 *>(xr + kb * 64 + 32 * (st >> 1) + 4 * (st & 1));
+                    if (g >= nout) x = make_float4(0.f, 0.f, 0.f, 0.f);
+                    const __half2 h01 = __floats2half2_rn(x.x, x.y), h23 = __floats2half2_rn(x.z, x.w);
+                    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                    const __half2 l01 = __floats2half2_rn(x.x - f01.x, x.y - f01.y);
+                    const __half2 l23 = __floats2half2_rn(x.z - f23.x, x.w - f23.y);
+                    mma_f16_16816(d, ra[2 * st], rb[2 * st], ra[2 * st + 1], rb[2 * st + 1], h01, h23);
+                    mma_f16_16816(d, ra[2 * st], rb[2 * st], ra[2 * st + 1], rb[2 * st + 1], l01, l23);
                 }
             }
+            // d: (va, row 2t), (va, 2t + 1), (vb, 2t), (vb, 2t + 1)
 #pragma unroll
-            for (int b = 0; b < VB; ++b) {
-                const int v = v0 + b;
-#pragma unroll
-                for (int o = 0; o < kHeadMaxRows; ++o) {
-                    if (o >= nout) break;
-                    const float s = warp_sum(acc[b][o]);
-                    if (lane == 0 && v < V) {
-                        if (logits) logits[size_t(o) * V + v] = s;
-                        const unsigned long long key = (uint64_t(float_key(s)) << 32) | uint32_t(~uint32_t(v));
-                        mine[o] = key > mine[o] ? key : mine[o];
-                    }
-                }
+            for (int j = 0; j < 4; ++j) {
+                const int v = j < 2 ? va : vb, o = 2 * t + (j & 1);
+                if (v >= V || o >= nout) continue;
+                if (logits) logits[size_t(o) * V + v] = d[j];
+                const unsigned long long key = (uint64_t(float_key(d[j])) << 32) | uint32_t(~uint32_t(v));
+                cand[j & 1] = key > cand[j & 1] ? key : cand[j & 1];
             }
+        }
+        // the warp's best per activation row, into lane 0's mine[]
+#pragma unroll
+        for (int o = 0; o < kHeadMaxRows; ++o) {
+            unsigned long long k = (o >> 1) == t ? cand[o & 1] : 0ull;
+#pragma unroll
+            for (int sh = 16; sh; sh >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, k, sh);
+                k = other > k ? other : k;
+            }
+            if (lane == 0) mine[o] = k;
         }
     }
     if (lane == 0) {
@@ -978,7 +1002,7 @@ bool set_smem_attr_once(const void * fn, int bytes, std::atomic<unsigned long lo
     return true;
 }
 
-std::atomic<unsigned long long> g_gdn_attr{0}, g_head_attr_4{0}, g_head_attr_8{0}, g_head_attr_16{0},
+std::atomic<unsigned long long> g_gdn_attr{0}, g_gdn2_attr{0}, g_head_attr_4{0}, g_head_attr_8{0}, g_head_attr_16{0},
     g_head_attr_32{0};
 constexpr int kHeadSmemMax = 200 * 1024;
 
@@ -1090,10 +1114,12 @@ int exl3cu_hyb_gdn(const float * d_qkvz, const float * d_xn, const float * d_xn_
     if (hidden > 8192 || hidden % 8) return bad("gdn: hidden must be a multiple of 8 up to 8192");
     if (!n_seq) return EXL3CU_OK;
     const size_t smem = exl3cu_hyb_gdn_smem_bytes_for(hidden);
-    if (!set_smem_attr_once(reinterpret_cast<const void *>(k_gdn), int(exl3cu_hyb_gdn_smem_bytes()), g_gdn_attr))
+    const bool few = n_seq <= 2;
+    const void * kfn = few ? reinterpret_cast<const void *>(k_gdn<1>) : reinterpret_cast<const void *>(k_gdn<2>);
+    if (!set_smem_attr_once(kfn, int(exl3cu_hyb_gdn_smem_bytes()), few ? g_gdn_attr : g_gdn2_attr))
         return status_of(cudaGetLastError());
-    return launch_pdl_cluster(k_gdn, dim3(kNH * kGdnSplit, unsigned(n_seq)), dim3(kGdnThreads), smem, kGdnSplit,
-                      stream, d_qkvz, d_xn, d_xn_norm_w,
+    return launch_pdl_cluster(few ? k_gdn<1> : k_gdn<2>, dim3(kNH * kGdnSplit, unsigned(n_seq)), dim3(kGdnThreads),
+                      smem, kGdnSplit, stream, d_qkvz, d_xn, d_xn_norm_w,
                       reinterpret_cast<const __half *>(d_wab), hidden,
                       d_conv_w, d_conv_state, d_A_log, d_dt_bias, d_norm_w, eps, d_state, d_row_offsets, d_seq_slot,
                       n_slots, d_out);
@@ -1113,7 +1139,9 @@ int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hi
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     int rc = 0;
-    const dim3 grid(unsigned(sms * 4)), block(kHeadThreads);
+    // CTAs that are resident together: four per SM, fewer when the staged rows fill shared memory
+    const int per_sm = std::max(1, std::min(4, int((200 * 1024) / std::max<size_t>(smem, 1))));
+    const dim3 grid(unsigned(sms * per_sm)), block(kHeadThreads);
     const float * xn = d_xn;
     const auto * E = reinterpret_cast<const __half *>(d_embed);
     switch (hidden / 256) {

@@ -692,3 +692,56 @@ class DecodeGraph:
 
     def replay(self):
         self.graph.replay()
+
+
+def main(argv=None) -> int:
+    """Run the synthetic decoder for a few eager steps: `requests` sequences prefilled with seeded
+    random prompts of `prompt` tokens, then `steps` greedy decode steps of one row per sequence.
+    Prints the tokens and the host-timed milliseconds per decode step.  Eager launches (no CUDA
+    graph) keep every kernel visible to a profiler's launch list."""
+    import argparse
+    import time
+
+    import torch
+
+    ap = argparse.ArgumentParser(prog="python -m exl3_b200.hybrid")
+    ap.add_argument("--layers", type=int, default=28)
+    ap.add_argument("--requests", type=int, default=1)
+    ap.add_argument("--prompt", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=4)
+    ap.add_argument("--seed", type=int, default=7)
+    args = ap.parse_args(argv)
+    if not 1 <= args.requests <= 8:
+        ap.error("--requests must be 1..8 (one step's logit rows)")
+    cfg = HybridConfig(layers=args.layers)
+    eng = HybridEngine(synthetic_weights(cfg, seed=args.seed), device=0, slots=args.requests,
+                       max_len=args.prompt + args.steps + 1, max_rows=max(64, args.requests))
+    rng = np.random.default_rng(args.seed)
+    tok = []
+    for sq in range(args.requests):
+        eng.reset_slot(sq)
+        prompt = rng.integers(0, cfg.vocab, args.prompt).astype(np.int32)
+        for c0 in range(0, args.prompt, 64):
+            c = min(64, args.prompt - c0)
+            eng.meta.fill(prompt[c0:c0 + c], np.zeros(c), np.arange(c0, c0 + c), [0, c], [sq], [c - 1])
+            eng.meta.upload(None)
+            eng.forward(c, 1, 1)
+        tok.append(int(eng.out_tokens[0]))
+    n, pos, out = args.requests, args.prompt, []
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.meta.fill(tok, np.arange(n), [pos] * n, np.arange(n + 1), np.arange(n), np.arange(n))
+        eng.meta.upload(None)
+        eng.forward(n, n, n)
+        tok = [int(v) for v in eng.out_tokens[:n].cpu().numpy()]
+        out.append(tok)
+        pos += 1
+    ms = (time.perf_counter() - t0) * 1000 / max(1, args.steps)
+    print(f"tokens {out}\n{ms:.3f} ms per eager decode step ({n} rows, {args.layers} layers)")
+    eng.free()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
