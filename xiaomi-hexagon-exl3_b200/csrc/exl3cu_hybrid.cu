@@ -768,8 +768,10 @@ __device__ __forceinline__ uint32_t float_key(float f) {
 constexpr int kHeadMaxRows = 8;
 constexpr int kHeadThreads = 256;
 
+// At most 64 registers: four CTAs per SM, the occupancy the one-row form is
+// tuned for (a build at 40 registers measured slower within the decode step).
 template <int ITER>
-__global__ void __launch_bounds__(kHeadThreads)
+__global__ void __launch_bounds__(kHeadThreads, 4)
 k_head(const float * __restrict__ xn, const int32_t * __restrict__ rows, int nout, int H,
        const __half * __restrict__ E, int V, float * __restrict__ logits, unsigned long long * __restrict__ best,
        const float * __restrict__ norm_w, float eps, int32_t * __restrict__ tokens) {
@@ -876,12 +878,20 @@ k_head(const float * __restrict__ xn, const int32_t * __restrict__ rows, int nou
             const __half * eb = E + size_t(min(vb, V - 1)) * H + 8 * t;
             const float * xr = xs + size_t(g < nout ? g : 0) * H + 8 * t;
             float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
-            for (int kb = 0; kb < H / 64; ++kb) {
-                const uint4 a0 = __ldcs(reinterpret_cast<const uint4 *>(ea + kb * 64));
-                const uint4 a1 = __ldcs(reinterpret_cast<const uint4 *>(ea + kb * 64 + 32));
-                const uint4 b0 = __ldcs(reinterpret_cast<const uint4 *>(eb + kb * 64));
-                const uint4 b1 = __ldcs(reinterpret_cast<const uint4 *>(eb + kb * 64 + 32));
+            // double-buffered: the next k-block's table rows are in flight while this one's MMAs run
+            auto load_kb = [&](int kb, uint4 (&r)[4]) {
+                r[0] = __ldcs(reinterpret_cast<const uint4 *>(ea + kb * 64));
+                r[1] = __ldcs(reinterpret_cast<const uint4 *>(ea + kb * 64 + 32));
+                r[2] = __ldcs(reinterpret_cast<const uint4 *>(eb + kb * 64));
+                r[3] = __ldcs(reinterpret_cast<const uint4 *>(eb + kb * 64 + 32));
+            };
+            const int nkb = H / 64;
+            uint4 cur[4], nxt[4];
+            load_kb(0, cur);
+#pragma unroll 1
+            for (int kb = 0; kb < nkb; ++kb) {
+                if (kb + 1 < nkb) load_kb(kb + 1, nxt);
+                const uint4 a0 = cur[0], a1 = cur[1], b0 = cur[2], b1 = cur[3];
                 const uint32_t ra[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
                 const uint32_t rb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
@@ -895,6 +905,8 @@ k_head(const float * __restrict__ xn, const int32_t * __restrict__ rows, int nou
                     mma_f16_16816(d, ra[2 * st], rb[2 * st], ra[2 * st + 1], rb[2 * st + 1], h01, h23);
                     mma_f16_16816(d, ra[2 * st], rb[2 * st], ra[2 * st + 1], rb[2 * st + 1], l01, l23);
                 }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) cur[i] = nxt[i];
             }
             // d: (va, row 2t), (va, 2t + 1), (vb, 2t), (vb, 2t + 1)
 #pragma unroll
