@@ -62,3 +62,15 @@ def test_attention_split_policy():
 
     assert attn_splits(1) == 32 and attn_splits(2) == 16 and attn_splits(8) == 8 and attn_splits(9) == 2
     assert attn_splits(512) == 1
+
+
+def test_decode_step_detection():
+    """The fused attention runs only when every sequence of the step has exactly one row."""
+    from exl3_b200.hybrid import one_row_each
+
+    assert one_row_each([0, 1, 2, 3])
+    assert one_row_each([0, 1])
+    assert not one_row_each([0, 2])           # a 2-row chunk: its rows attend to each other
+    assert not one_row_each([0, 1, 1, 2])     # a sequence granted no row
+    assert not one_row_each([0, 1, 5])        # a decode row beside a prefill chunk
+    assert not one_row_each([0])              # no sequence

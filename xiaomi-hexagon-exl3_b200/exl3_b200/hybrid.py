@@ -171,6 +171,13 @@ def attn_splits(rows: int) -> int:
     return 32 if rows <= 1 else (16 if rows <= 2 else (8 if rows <= 8 else (2 if rows <= 64 else 1)))
 
 
+def one_row_each(row_offsets) -> bool:
+    """True when every sequence of a step has exactly one row (a decode step): then a row attends only
+    to cached positions and its own, and the fused attention (exl3cu_hyb_attn_decode) is valid."""
+    offs = np.asarray(row_offsets, np.int64)
+    return offs.size > 1 and bool(np.all(np.diff(offs) == 1))
+
+
 class StepMeta:
     """Device int32 row metadata of one step, filled from one pinned host buffer by one copy:
     [tokens R | row_seq R | row_pos R | row_offsets n_seq+1 | seq_slot n_seq | logit_rows nout]."""
@@ -198,8 +205,7 @@ class StepMeta:
             if a.size > self.len[name]:
                 raise ValueError(f"{name}: {a.size} entries, capacity {self.len[name]}")
             h[self.off[name]:self.off[name] + a.size] = a
-        offs = np.asarray(row_offsets, np.int64)
-        self.one_row_each = offs.size > 1 and bool(np.all(np.diff(offs) == 1))
+        self.one_row_each = one_row_each(row_offsets)
 
     def upload(self, stream):
         self.dev.copy_(self.host, non_blocking=True)
