@@ -104,6 +104,16 @@ int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hi
                     float eps, const uint16_t * d_embed, int vocab, float * d_logits, unsigned long long * d_best,
                     int32_t * d_tokens, void * stream);
 
+/* exl3cu_hyb_head for replayed decode steps with the token feedback on the
+ * device, one launch: besides d_tokens, the last CTA writes row o's token into
+ * d_next_tokens[o] (the next step's token ids), adds 1 to d_next_pos[o] (its
+ * positions), stores it at d_log[*d_counter * nout + o] (clamped to
+ * log_capacity - 1) and adds 1 to *d_counter.  No logits are written. */
+int exl3cu_hyb_head_feedback(const float * d_xn, const int32_t * d_rows, int nout, int hidden, const float * d_norm_w,
+                             float eps, const uint16_t * d_embed, int vocab, unsigned long long * d_best,
+                             int32_t * d_tokens, int32_t * d_next_tokens, int32_t * d_next_pos, int32_t * d_log,
+                             int64_t * d_counter, size_t log_capacity, void * stream);
+
 /* Sticky error bits of these kernels on the current device (reserved: the
  * current kernels wait on nothing and raise none).  Synchronises the device. */
 int exl3cu_hyb_status(int clear, unsigned * status);

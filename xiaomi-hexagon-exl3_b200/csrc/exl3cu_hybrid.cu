@@ -768,13 +768,24 @@ __device__ __forceinline__ uint32_t float_key(float f) {
 constexpr int kHeadMaxRows = 8;
 constexpr int kHeadThreads = 256;
 
+// Optional device-side token feedback for replayed decode steps (tokens NULL: none): the last CTA
+// also writes row o's token into next_tokens[o], increments next_pos[o], appends it to
+// log[counter * nout + o] (clamped to log_cap - 1) and increments counter.
+struct HeadFeedback {
+    int32_t * next_tokens;
+    int32_t * next_pos;
+    int32_t * log;
+    long long * counter;
+    long long log_cap;
+};
+
 // At most 64 registers: four CTAs per SM, the occupancy the one-row form is
 // tuned for (a build at 40 registers measured slower within the decode step).
 template <int ITER>
 __global__ void __launch_bounds__(kHeadThreads, 4)
 k_head(const float * __restrict__ xn, const int32_t * __restrict__ rows, int nout, int H,
        const __half * __restrict__ E, int V, float * __restrict__ logits, unsigned long long * __restrict__ best,
-       const float * __restrict__ norm_w, float eps, int32_t * __restrict__ tokens) {
+       const float * __restrict__ norm_w, float eps, int32_t * __restrict__ tokens, const HeadFeedback fb) {
     extern __shared__ __align__(16) float xs[];  // [nout][H]
     __shared__ float red[kHeadThreads / 32][kHeadMaxRows];
     __shared__ float inv_s[kHeadMaxRows];
@@ -944,9 +955,19 @@ k_head(const float * __restrict__ xn, const int32_t * __restrict__ rows, int nou
     __threadfence();
     if (threadIdx.x < nout) {
         const unsigned long long b = atomicExch(best + threadIdx.x, 0ull);
-        tokens[threadIdx.x] = int32_t(~uint32_t(b & 0xffffffffull));
+        const int32_t tok = int32_t(~uint32_t(b & 0xffffffffull));
+        tokens[threadIdx.x] = tok;
+        if (fb.next_tokens) {
+            fb.next_tokens[threadIdx.x] = tok;
+            fb.next_pos[threadIdx.x] += 1;
+            fb.log[min(*fb.counter * nout + threadIdx.x, fb.log_cap - 1)] = tok;
+        }
     }
     if (threadIdx.x == 0) atomicExch(best + kHeadMaxRows, 0ull);
+    if (fb.next_tokens) {
+        __syncthreads();  // every row has read the counter
+        if (threadIdx.x == 0) *fb.counter += 1;
+    }
 }
 
 }  // namespace
@@ -1137,9 +1158,13 @@ int exl3cu_hyb_gdn(const float * d_qkvz, const float * d_xn, const float * d_xn_
                       n_slots, d_out);
 }
 
-int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hidden, const float * d_norm_w,
-                    float eps, const uint16_t * d_embed, int vocab, float * d_logits, unsigned long long * d_best,
-                    int32_t * d_tokens, void * stream) {
+}  // extern "C"
+
+namespace {
+
+int head_launch(const float * d_xn, const int32_t * d_rows, int nout, int hidden, const float * d_norm_w, float eps,
+                const uint16_t * d_embed, int vocab, float * d_logits, unsigned long long * d_best, int32_t * d_tokens,
+                const HeadFeedback & fb, void * stream) {
     if (!d_xn || !d_rows || !d_embed || !d_best || !d_tokens || nout < 0 || nout > kHeadMaxRows || hidden <= 0 ||
         hidden % 256 || hidden > 8192 || vocab <= 0)
         return bad("head: bad arguments (nout <= 8, hidden a multiple of 256 up to 8192)");
@@ -1162,7 +1187,7 @@ int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hi
         if (!set_smem_attr_once(reinterpret_cast<const void *>(k_head<N>), kHeadSmemMax, g_head_attr_##N))        \
             return status_of(cudaGetLastError());                                                                  \
         rc = launch_pdl(k_head<N>, grid, block, smem, stream, xn, d_rows, nout, hidden, E, vocab, d_logits, d_best, \
-                        d_norm_w, eps, d_tokens);                                                                  \
+                        d_norm_w, eps, d_tokens, fb);                                                              \
         break;
         EXL3CU_HEAD_CASE(4)
         EXL3CU_HEAD_CASE(8)
@@ -1173,6 +1198,29 @@ int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hi
             return bad("head: hidden must be 1024, 2048, 4096 or 8192");
     }
     return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+int exl3cu_hyb_head(const float * d_xn, const int32_t * d_rows, int nout, int hidden, const float * d_norm_w,
+                    float eps, const uint16_t * d_embed, int vocab, float * d_logits, unsigned long long * d_best,
+                    int32_t * d_tokens, void * stream) {
+    return head_launch(d_xn, d_rows, nout, hidden, d_norm_w, eps, d_embed, vocab, d_logits, d_best, d_tokens,
+                       HeadFeedback{nullptr, nullptr, nullptr, nullptr, 0}, stream);
+}
+
+int exl3cu_hyb_head_feedback(const float * d_xn, const int32_t * d_rows, int nout, int hidden, const float * d_norm_w,
+                             float eps, const uint16_t * d_embed, int vocab, unsigned long long * d_best,
+                             int32_t * d_tokens, int32_t * d_next_tokens, int32_t * d_next_pos, int32_t * d_log,
+                             int64_t * d_counter, size_t log_capacity, void * stream) {
+    if (!d_next_tokens || !d_next_pos || !d_log || !d_counter || log_capacity == 0)
+        return bad("head_feedback: the feedback buffers must be given (log_capacity >= 1)");
+    return head_launch(d_xn, d_rows, nout, hidden, d_norm_w, eps, d_embed, vocab, nullptr, d_best, d_tokens,
+                       HeadFeedback{d_next_tokens, d_next_pos, d_log, reinterpret_cast<long long *>(d_counter),
+                                    static_cast<long long>(log_capacity)},
+                       stream);
 }
 
 int exl3cu_hyb_status(int clear, unsigned * status) {

@@ -158,9 +158,10 @@ def _declare(L):
     L.exl3cu_hyb_gdn_smem_bytes.restype = S
     L.exl3cu_hyb_gdn.argtypes = [P, P, P, P, I, P, P, P, P, P, F, P, P, P, I, I, P, P]
     L.exl3cu_hyb_head.argtypes = [P, P, I, I, P, F, P, I, P, P, P, P]
+    L.exl3cu_hyb_head_feedback.argtypes = [P, P, I, I, P, F, P, I, P, P, P, P, P, P, S, P]
     for n in ("exl3cu_hyb_embed", "exl3cu_hyb_rmsnorm", "exl3cu_hyb_swiglu", "exl3cu_hyb_attn_prep",
               "exl3cu_hyb_attn", "exl3cu_hyb_attn_decode", "exl3cu_hyb_gdn", "exl3cu_hyb_head",
-              "exl3cu_hyb_status"):
+              "exl3cu_hyb_head_feedback", "exl3cu_hyb_status"):
         getattr(L, n).restype = ctypes.c_int
     L._hyb_declared = True
 
@@ -335,8 +336,10 @@ class HybridEngine:
     def _mm(self, w, x, out, rows, st, form: int = 0, nw=None, accum: bool = False, x_ss=None, y_ss=None):
         self._mm_batch(("_one",), {"_one": w}, x, [out], rows, st, form, nw, accum, x_ss, y_ss)
 
-    def forward(self, rows: int, n_seq: int, nout: int, stream=None):
-        """Run the step whose metadata is in self.meta.dev; next tokens land in self.out_tokens[:nout]."""
+    def forward(self, rows: int, n_seq: int, nout: int, stream=None, feedback=None) -> bool:
+        """Run the step whose metadata is in self.meta.dev; next tokens land in self.out_tokens[:nout].
+        feedback = (next_tokens, next_pos, log, counter) asks the head to feed the tokens back on the
+        device (exl3cu_hyb_head_feedback); returns whether it did (steps of <= 8 rows only)."""
         torch, cfg, L = self.torch, self.cfg, self.L
         st = ctypes.c_void_p((stream or torch.cuda.current_stream()).cuda_stream)
         H, F, D, KV = cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim, self.KV
@@ -356,8 +359,8 @@ class HybridEngine:
         scale = 1.0 / float(np.sqrt(cfg.head_dim))
         if fused:
             self._forward_fused(rows, n_seq, nout, st, scale, row_seq, row_pos, row_offsets, seq_slot, logit_rows,
-                                pf, main)
-            return
+                                pf, main, feedback)
+            return feedback is not None
         delta = None
         for li, d in enumerate(self.layers):
             mats = d["mats"]
@@ -409,7 +412,7 @@ class HybridEngine:
             main.wait_event(ev)
 
     def _forward_fused(self, rows, n_seq, nout, st, scale, row_seq, row_pos, row_offsets, seq_slot, logit_rows, pf,
-                       main):
+                       main, feedback=None):
         """Steps of <= 8 rows: the layer glue folded into the packed operator -- RMSNorm on load for the
         projections (and inside the delta-rule gates), SwiGLU on load for the down projection, the o and
         down products added into the residual stream h -- so a layer is 4 operator launches plus its
@@ -460,8 +463,14 @@ class HybridEngine:
                            d["post_norm"], x_ss=self.h_ss)
             self._mm(mats["down"], self.gu, self.h, rows, st, 2, None, True, y_ss=self.h_ss)  # h += down(swiglu)
         # the final RMSNorm is applied by the head as it loads h
-        check(L.exl3cu_hyb_head(_vp(self.h), _vp(logit_rows), nout, H, _vp(self.final_norm), cfg.eps,
-                                _vp(self.embed), cfg.vocab, None, _vp(self.best), _vp(self.out_tokens), st))
+        if feedback is not None:
+            nt, npos, log, counter = feedback
+            check(L.exl3cu_hyb_head_feedback(_vp(self.h), _vp(logit_rows), nout, H, _vp(self.final_norm), cfg.eps,
+                                             _vp(self.embed), cfg.vocab, _vp(self.best), _vp(self.out_tokens),
+                                             _vp(nt), _vp(npos), _vp(log), _vp(counter), log.numel(), st))
+        else:
+            check(L.exl3cu_hyb_head(_vp(self.h), _vp(logit_rows), nout, H, _vp(self.final_norm), cfg.eps,
+                                    _vp(self.embed), cfg.vocab, None, _vp(self.best), _vp(self.out_tokens), st))
         if pf:
             ev = self._pf_events[-1]
             ev.record(self._pf_stream)
@@ -686,7 +695,8 @@ class DecodeGraph:
 
     def _body(self):
         e, n = self.engine, self.n
-        e.forward(n, n, n, self.stream)
+        if e.forward(n, n, n, self.stream, feedback=(self._tok, self._pos, self.log, self.counter)):
+            return  # the head kernel fed the tokens back (same effect as the steps below)
         self._tok.copy_(e.out_tokens[:n])
         self._pos.add_(1)
         idx = (self.counter * n + self.ar).clamp_(max=self.log.numel() - 1)
