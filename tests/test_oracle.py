@@ -135,7 +135,7 @@ def test_golden_mul_mat(oracle, golden, bits):
         assert _max_abs_rel(y, data[f"mm_y_b{bits}_r{rows}"]) < 1e-6
     y16 = oracle.mul_mat(records, bits, k, n, kat.kat_input(1).astype(np.float16))
     assert _max_abs_rel(y16, data[f"mm_y16_b{bits}_r1"]) < 1e-6
-    for nth in (2, 3):  # thread-count invariance (survey: identical across 1 and 8 threads)
+    for nth in (2, 3):  # thread-count invariance: the reference gives the same y for any ith/nth split
         assert np.array_equal(oracle.mul_mat(records, bits, k, n, kat.kat_input(1), nth=nth),
                               oracle.mul_mat(records, bits, k, n, kat.kat_input(1), nth=1))
 
