@@ -466,8 +466,8 @@ struct GdnSmem {
     static constexpr int V = K + kGdnTile * kHD;              // [T][128] v
     static constexpr int O = V + kGdnTile * kHD;              // [T][32] o of this rank's columns
     static constexpr int RED = O + kGdnTile * kGdnCols;       // [2 buffers][2][8][32]
-    static constexpr int PSUM = RED + 2 * 2 * kGdnKParts * kGdnCols;  // [2 tiles][T] sum(o^2) of this rank
-    static constexpr int CW = PSUM + 2 * kGdnTile;            // [384][4] conv weights of the head
+    static constexpr int PSUM = RED + 2 * 2 * kGdnKParts * kGdnCols;  // [2 tiles][rank][T] sum(o^2) of every rank
+    static constexpr int CW = PSUM + 2 * kGdnSplit * kGdnTile;  // [384][4] conv weights of the head
     static constexpr int GATE = CW + 3 * kHD * kConvW;        // [T][4]: alpha, beta, k.q
     static constexpr int CX = GATE + kGdnTile * 4;            // [T+3][384] conv inputs of the tile
     static constexpr int WAB = CX + (kGdnTile + kConvW - 1) * 3 * kHD;  // fp16 [2][H] gate rows (H <= 8192)
@@ -690,7 +690,7 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const floa
         }
         __syncthreads();  // every row's o slice is in `to`
         // ---- C: this rank's sum(o^2) per row, exchanged across the cluster ----
-        float * ps = psum + tpar * kGdnTile;
+        float * ps = psum + tpar * kGdnSplit * kGdnTile;  // [rank][T]
         constexpr int kZRows = kGdnTile / (kGdnThreads / 32);  // rows per warp
         const int d = rank * kGdnCols + lane;
         float zr[kZRows];  // the gate inputs z, loaded ahead of the exchange
@@ -699,19 +699,22 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const floa
             const int rr = warp + q * (kGdnThreads / 32);
             zr[q] = rr < nt ? qkvz[size_t(tr0 + rr) * QKVZ + 3 * kNH * kHD + h * kHD + d] : 0.f;
         }
+        // this rank's partial goes into every rank's shared memory (its own included), so that after
+        // the barrier each rank reads only its own: no remote access follows the last barrier, and a
+        // CTA may exit without waiting for its peers
         for (int rr = warp; rr < nt; rr += kGdnThreads / 32) {
             const float o = to[rr * kGdnCols + lane];
             const float ss = warp_sum(o * o);
-            if (lane == 0) ps[rr] = ss;
+            if (lane < kGdnSplit) cluster.map_shared_rank(ps, lane)[rank * kGdnTile + rr] = ss;
         }
-        cluster.sync();  // every rank's partial sums are visible
+        cluster.sync();  // every rank's partial sums are in place
 #pragma unroll
         for (int q = 0; q < kZRows; ++q) {
             const int rr = warp + q * (kGdnThreads / 32);
             if (rr >= nt) break;
             float ss = 0.f;
 #pragma unroll
-            for (int p = 0; p < kGdnSplit; ++p) ss += cluster.map_shared_rank(ps, p)[rr];  // rank order
+            for (int p = 0; p < kGdnSplit; ++p) ss += ps[p * kGdnTile + rr];  // rank order
             const float inv = rsqrtf(ss / float(kHD) + eps);
             const size_t r = size_t(tr0 + rr);
             out[r * kNH * kHD + h * kHD + d] = to[rr * kGdnCols + lane] * inv * norm_w[d] * silu(zr[q]);
@@ -719,8 +722,9 @@ k_gdn(const float * __restrict__ qkvz, const float * __restrict__ xn, const floa
         if (tr0 + kGdnTile >= r1) break;  // the last tile's cx stays for the conv state below
         __syncthreads();  // the next tile overwrites tq, tk, tv, to, gate, cx (psum is double-buffered)
     }
-    cluster.sync();  // peers are done reading this rank's psum, and with the conv state
-    // the conv state: the last three inputs of the sequence so far (rank 0), which are
+    // No closing cluster barrier: peers only ever wrote into this CTA's shared memory before the
+    // last tile's barrier, and every rank staged (read) the old conv state before arriving there.
+    // The conv state: the last three inputs of the sequence so far (rank 0), which are
     // rows nt .. nt+2 of the last tile's staged inputs (those before the sequence's first
     // row were staged from the old conv state)
     if (rank == 0) {
