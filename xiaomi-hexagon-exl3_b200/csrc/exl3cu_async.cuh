@@ -85,37 +85,6 @@ __device__ __forceinline__ void bulk_g2s(void * dst_smem, const void * src_gmem,
         : "memory");
 }
 
-// Split cluster barrier (every thread of every CTA in the cluster executes both).
-__device__ __forceinline__ void cluster_arrive_release() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
-
-// Arrive (release, cluster scope) on the mbarrier at the same shared-memory
-// offset as `bar` in cluster rank `rank`.
-__device__ __forceinline__ void mbar_arrive_remote_release(uint64_t * bar, unsigned rank) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(bar)), "r"(rank));
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
-}
-
-// Wait (acquire, cluster scope) for the phase with the given parity; false after kWaitSpins rounds.
-__device__ __forceinline__ bool mbar_wait_cluster_acquire(uint64_t * bar, uint32_t parity) {
-    const uint32_t addr = smem_addr(bar);
-    for (unsigned i = 0; i < kWaitSpins; ++i) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (done) return true;
-    }
-    return false;
-}
-
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
