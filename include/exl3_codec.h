@@ -21,16 +21,20 @@ float half_to_float(uint16_t value);
 uint16_t float_to_half(float value);
 uint16_t decode_codebook(uint16_t state, Codebook codebook);
 
-// Packed tiles use upstream CUDA lane order and little-endian uint16 storage.
+// `packed` is the upstream trellis tensor [k/16][n/16][16*bits] as little-endian
+// uint16 words, tiles in the order the upstream CUDA kernels use; outputs are
+// row-major fp16 bit patterns.
 void decode_tile(const uint16_t * packed, unsigned bits, Codebook codebook, uint16_t * row_major);
 void decode_inner(const uint16_t * packed, size_t k, size_t n, unsigned bits, Codebook codebook, uint16_t * output);
 void decode_inner_slice(const uint16_t * packed, size_t k, size_t n, size_t first_column, size_t column_count,
                         unsigned bits, Codebook codebook, uint16_t * output);
 
-// In-place orthonormal H128 on each consecutive group of 128 values.
+// Rotates every run of 128 consecutive floats by the normalised 128-point
+// Walsh-Hadamard transform, in place; `count` is a multiple of 128.
 void hadamard128(float * values, size_t count);
 
-// Original-basis matrix: diag(suh) H128 W_hat H128 diag(svh), laid out as [k,n].
+// The weight matrix in its unrotated basis, [k][n] row-major fp16:
+// rows scaled by suh, H128 on both sides of the decoded matrix, columns by svh.
 void reconstruct(const uint16_t * packed, const uint16_t * suh, const uint16_t * svh, size_t k, size_t n,
                  unsigned bits, Codebook codebook, uint16_t * output);
 void reconstruct_slice(const uint16_t * packed, const uint16_t * suh, const uint16_t * svh, size_t k, size_t n,

@@ -2,16 +2,27 @@
 //
 // Same signatures, layouts and std::invalid_argument contract as the
 // reference's src/exl3_codec.cpp; the work runs on the current CUDA device.
-// Each call stages its host buffers in device memory, launches, and copies
-// the result back on a private stream it synchronises before returning.
+// A call stages its host buffers in a per-thread, per-device device buffer
+// that only grows, runs on a per-thread stream, copies the result back and
+// synchronises before returning, so nothing is allocated per call once the
+// buffer has reached the working size.  decode_codebook() reads a 65536-entry
+// table per (device, codebook) that the GPU codebook kernel fills on first use
+// -- the reference likewise builds its state tables lazily
+// (src/exl3_codec.cpp:94-100).
 #include "exl3_codec.h"
 
 #include <cuda_runtime.h>
 
+#include <array>
 #include <cstring>
 #include <limits>
+#include <map>
+#include <memory>
+#include <mutex>
 #include <stdexcept>
 #include <string>
+#include <utility>
+#include <vector>
 
 #include "exl3cu.h"
 
@@ -37,29 +48,60 @@ void check_status(int rc) {
     if (rc) throw std::runtime_error(std::string("exl3cu: ") + exl3cu_last_error());
 }
 
-// Device buffer owned for the duration of one call.
-struct DeviceBuffer {
-    void * p = nullptr;
-    explicit DeviceBuffer(size_t bytes) { check_cuda(cudaMalloc(&p, bytes ? bytes : 16), "cudaMalloc"); }
-    ~DeviceBuffer() { cudaFree(p); }
-    DeviceBuffer(const DeviceBuffer &) = delete;
-    DeviceBuffer & operator=(const DeviceBuffer &) = delete;
-    template <class T> T * as() const { return static_cast<T *>(p); }
-};
-
-struct Stream {
-    cudaStream_t s = nullptr;
-    Stream() { check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate"); }
-    ~Stream() { cudaStreamDestroy(s); }
-    void sync() const { check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize"); }
-};
-
-void upload(void * dst, const void * src, size_t bytes, const Stream & st) {
-    check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, st.s), "copy to device");
+int current_device() {
+    int d = 0;
+    check_cuda(cudaGetDevice(&d), "cudaGetDevice");
+    return d;
 }
 
-void download(void * dst, const void * src, size_t bytes, const Stream & st) {
-    check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, st.s), "copy to host");
+// This thread's stream and staging buffer on one device.  The buffer grows to
+// the largest call seen and is reused; a call synchronises its stream before
+// returning, so no copy or kernel of an earlier call still uses it.
+struct Staging {
+    cudaStream_t stream = nullptr;
+    char * buf = nullptr;
+    size_t cap = 0;
+    Staging() { check_cuda(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate"); }
+    ~Staging() {
+        if (buf) cudaFree(buf);
+        if (stream) cudaStreamDestroy(stream);
+    }
+    Staging(const Staging &) = delete;
+    Staging & operator=(const Staging &) = delete;
+    // `parts` byte counts, each region 256-byte aligned; returns their device addresses.
+    template <size_t N>
+    std::array<char *, N> carve(const std::array<size_t, N> & parts) {
+        size_t total = 0;
+        for (size_t b : parts) total += (b + 255) & ~size_t(255);
+        if (total > cap) {
+            if (buf) check_cuda(cudaFree(buf), "cudaFree");
+            buf = nullptr;
+            cap = 0;
+            check_cuda(cudaMalloc(&buf, total), "cudaMalloc");
+            cap = total;
+        }
+        std::array<char *, N> out{};
+        size_t off = 0;
+        for (size_t i = 0; i < N; ++i) {
+            out[i] = buf + off;
+            off += (parts[i] + 255) & ~size_t(255);
+        }
+        return out;
+    }
+    void upload(void * dst, const void * src, size_t bytes) {
+        check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream), "copy to device");
+    }
+    void download(void * dst, const void * src, size_t bytes) {
+        check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, stream), "copy to host");
+    }
+    void sync() { check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize"); }
+};
+
+Staging & staging() {
+    thread_local std::map<int, std::unique_ptr<Staging>> per_device;
+    auto & slot = per_device[current_device()];
+    if (!slot) slot.reset(new Staging());
+    return *slot;
 }
 
 }  // namespace
@@ -107,15 +149,26 @@ uint16_t float_to_half(float value) {
 
 uint16_t decode_codebook(uint16_t state, Codebook codebook) {
     if (static_cast<uint32_t>(codebook) > 2) throw std::invalid_argument("Unknown EXL3 codebook");
-    Stream st;
-    DeviceBuffer in(2), out(2);
-    upload(in.p, &state, 2, st);
-    check_status(exl3cu_decode_codebook(in.as<uint16_t>(), 1, static_cast<unsigned>(codebook), out.as<uint16_t>(),
-                                        st.s));
-    uint16_t r = 0;
-    download(&r, out.p, 2, st);
-    st.sync();
-    return r;
+    static std::mutex mu;
+    static std::map<std::pair<int, uint32_t>, std::vector<uint16_t>> tables;
+    const auto key = std::make_pair(current_device(), static_cast<uint32_t>(codebook));
+    std::lock_guard<std::mutex> g(mu);
+    auto it = tables.find(key);
+    if (it == tables.end()) {
+        // every state once through the device codebook kernel
+        std::vector<uint16_t> states(65536), table(65536);
+        for (size_t i = 0; i < states.size(); ++i) states[i] = uint16_t(i);
+        Staging & st = staging();
+        const auto d = st.carve(std::array<size_t, 2>{65536 * 2, 65536 * 2});
+        st.upload(d[0], states.data(), 65536 * 2);
+        check_status(exl3cu_decode_codebook(reinterpret_cast<const uint16_t *>(d[0]), 65536,
+                                            static_cast<unsigned>(codebook), reinterpret_cast<uint16_t *>(d[1]),
+                                            st.stream));
+        st.download(table.data(), d[1], 65536 * 2);
+        st.sync();
+        it = tables.emplace(key, std::move(table)).first;
+    }
+    return it->second[state];
 }
 
 void decode_tile(const uint16_t * packed, unsigned bits, Codebook codebook, uint16_t * row_major) {
@@ -136,23 +189,23 @@ void decode_inner_slice(const uint16_t * packed, size_t k, size_t n, size_t firs
         throw std::invalid_argument("Invalid EXL3 column slice");
     const size_t packed_bytes = k * n * bits / 8;
     const size_t out_bytes = k * column_count * 2;
-    Stream st;
-    DeviceBuffer dp(packed_bytes), dout(out_bytes);
-    upload(dp.p, packed, packed_bytes, st);
-    check_status(exl3cu_decode_inner(dp.as<uint16_t>(), k, n, first_column, column_count, bits,
-                                     static_cast<unsigned>(codebook), dout.as<uint16_t>(), st.s));
-    download(output, dout.p, out_bytes, st);
+    Staging & st = staging();
+    const auto d = st.carve(std::array<size_t, 2>{packed_bytes, out_bytes});
+    st.upload(d[0], packed, packed_bytes);
+    check_status(exl3cu_decode_inner(reinterpret_cast<const uint16_t *>(d[0]), k, n, first_column, column_count, bits,
+                                     static_cast<unsigned>(codebook), reinterpret_cast<uint16_t *>(d[1]), st.stream));
+    st.download(output, d[1], out_bytes);
     st.sync();
 }
 
 void hadamard128(float * values, size_t count) {
     if (count % 128) throw std::invalid_argument("H128 length must be a multiple of 128");
     if (!count) return;
-    Stream st;
-    DeviceBuffer dv(count * 4);
-    upload(dv.p, values, count * 4, st);
-    check_status(exl3cu_hadamard128(dv.as<float>(), count, st.s));
-    download(values, dv.p, count * 4, st);
+    Staging & st = staging();
+    const auto d = st.carve(std::array<size_t, 1>{count * 4});
+    st.upload(d[0], values, count * 4);
+    check_status(exl3cu_hadamard128(reinterpret_cast<float *>(d[0]), count, st.stream));
+    st.download(values, d[0], count * 4);
     st.sync();
 }
 
@@ -171,14 +224,15 @@ void reconstruct_slice(const uint16_t * packed, const uint16_t * suh, const uint
         throw std::invalid_argument("Invalid EXL3 column slice");
     const size_t packed_bytes = k * n * bits / 8;
     const size_t out_bytes = k * column_count * 2;
-    Stream st;
-    DeviceBuffer dp(packed_bytes), dsu(k * 2), dsv(n * 2), dout(out_bytes);
-    upload(dp.p, packed, packed_bytes, st);
-    upload(dsu.p, suh, k * 2, st);
-    upload(dsv.p, svh, n * 2, st);
-    check_status(exl3cu_reconstruct(dp.as<uint16_t>(), dsu.as<uint16_t>(), dsv.as<uint16_t>(), k, n, first_column,
-                                    column_count, bits, static_cast<unsigned>(codebook), dout.as<uint16_t>(), st.s));
-    download(output, dout.p, out_bytes, st);
+    Staging & st = staging();
+    const auto d = st.carve(std::array<size_t, 4>{packed_bytes, k * 2, n * 2, out_bytes});
+    st.upload(d[0], packed, packed_bytes);
+    st.upload(d[1], suh, k * 2);
+    st.upload(d[2], svh, n * 2);
+    check_status(exl3cu_reconstruct(reinterpret_cast<const uint16_t *>(d[0]), reinterpret_cast<const uint16_t *>(d[1]),
+                                    reinterpret_cast<const uint16_t *>(d[2]), k, n, first_column, column_count, bits,
+                                    static_cast<unsigned>(codebook), reinterpret_cast<uint16_t *>(d[3]), st.stream));
+    st.download(output, d[3], out_bytes);
     st.sync();
 }
 
