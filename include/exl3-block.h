@@ -39,6 +39,10 @@ extern "C" {
 #endif
 void ggml_exl3_mul_mat(const struct ggml_compute_params * params, struct ggml_tensor * dst);
 void ggml_exl3_get_rows(const struct ggml_compute_params * params, struct ggml_tensor * dst);
+/* No counterpart in the reference (whose CPU operator keeps no device state):
+ * frees every weight the two operators above uploaded to the GPU.  Call it
+ * when a model is unloaded; later calls upload again on first sight. */
+void ggml_exl3_release_weights(void);
 #ifdef __cplusplus
 }
 #endif

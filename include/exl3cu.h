@@ -258,6 +258,8 @@ int exl3cu_get_rows_host(exl3cu_weight * w, const int32_t * h_ids, size_t count,
  * first call on a device resolves that array's address (make it before any
  * stream capture); every call clears the part it needs first; calls that
  * overlap on the GPU share the array and race, so order them on one stream.
+ * The resolved address is cached per device for the life of the process: do
+ * not use this entry across a cudaDeviceReset of that device.
  * Returns EXL3CU_NO_SUPPORT when the weight's split-K plan needs more than the
  * array holds. */
 int exl3cu_mul_mat_noalloc(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,

@@ -87,3 +87,27 @@ def test_ggml_mul_mat_live_reference(ggml_lib, reference):
     y = ggml_mul_mat(ggml_lib, rec, bits, k, n, x)
     ref = reference.mul_mat(rec, bits, k, n, x, nth=8)
     assert np.max(np.abs(y - ref)) / np.max(np.abs(ref)) <= 2e-3
+
+
+def test_ggml_weight_cache_follows_buffer_contents(ggml_lib, oracle):
+    """A model reloaded into the same host buffer (same address, type and shape) must be served its
+    own weights, not the device copy of the previous ones; ggml_exl3_release_weights drops every
+    cached upload and the next call uploads again."""
+    from exl3_b200 import synthetic
+
+    k, n, bits = 1024, 512, 4
+    a = synthetic.matrix(k, n, bits, seed=91).records()
+    b = synthetic.matrix(k, n, bits, seed=92).records()
+    buf = a.copy()
+    x = synthetic.activations(2, k, seed=93)
+    ya = ggml_mul_mat(ggml_lib, buf, bits, k, n, x)
+    buf[:] = b  # a second model at the same address
+    yb = ggml_mul_mat(ggml_lib, buf, bits, k, n, x)
+    ref_a = oracle.mul_mat(a, bits, k, n, x)
+    ref_b = oracle.mul_mat(b, bits, k, n, x)
+    assert np.max(np.abs(ya - ref_a)) / np.max(np.abs(ref_a)) <= 2e-3
+    assert np.max(np.abs(yb - ref_b)) / np.max(np.abs(ref_b)) <= 2e-3
+    ggml_lib.ggml_exl3_release_weights.restype = None
+    ggml_lib.ggml_exl3_release_weights()
+    yb2 = ggml_mul_mat(ggml_lib, buf, bits, k, n, x)
+    assert np.array_equal(yb2, yb)

@@ -2,9 +2,11 @@
 
 Tolerance (north star): max|y - y_ref| / max|y_ref| <= 2e-3 with fp32
 accumulation, plus the reference graph test's NMSE < 1e-5
-(tests/test-exl3-graph.cpp:100).  The CUDA path rotates activations in fp32
-and feeds them to the tensor cores as fp16 (as the reference's HMX path does),
-which sets its error floor around 3e-4 max-abs-rel.
+(tests/test-exl3-graph.cpp:100).  The GEMV path rotates activations in fp32
+and holds them as fixed point with one scale per warp (22 bits for one or two
+rows, 15 bits for three or four); the GEMM path feeds them to the tensor cores
+as fp16.  Heavy-tailed inputs (outlier channels, one loud 128-group) are
+checked separately because they stress exactly that scaling.
 """
 import numpy as np
 import pytest
@@ -261,20 +263,24 @@ def test_grouped_batch_matches_single_calls(ops, oracle):
         w.free()
 
 
-def test_global_workspace_variant_matches(ops):
-    """exl3cu_mul_mat_ws (split-K through a global workspace) agrees with the cluster path."""
+def test_global_workspace_variant_matches(ops, oracle):
+    """exl3cu_mul_mat_ws (split-K through a caller's workspace, the k_gemv kernel) agrees with the
+    default operator and, directly, with the CPU restatement of the reference operator."""
     from exl3_b200 import synthetic
 
     k, n, bits = 6144, 2048, 4
     m = synthetic.matrix(k, n, bits, seed=13)
-    w = ops.Exl3Weight.from_records(m.records(), k, n, bits)
-    x = torch.from_numpy(synthetic.activations(3, k, seed=14)).cuda()
+    rec = m.records()
+    w = ops.Exl3Weight.from_records(rec, k, n, bits)
+    xh = synthetic.activations(3, k, seed=14)
+    x = torch.from_numpy(xh).cuda()
     ws = torch.zeros(w.workspace_bytes // 4 + 4, dtype=torch.float32, device="cuda")
     a = w.mul_mat(x)
     b = w.mul_mat(x, workspace=ws)
     torch.cuda.synchronize()
     rel, _ = errs(a.cpu().numpy(), b.cpu().numpy())
     assert rel < TOL_MAX_ABS_REL
+    assert_close(b.cpu().numpy(), oracle.mul_mat(rec, bits, k, n, xh), "workspace kernel vs oracle")
     w.free()
 
 
@@ -335,3 +341,38 @@ def test_fused_input_forms_and_accumulate(ops):
                                    None, None)
     assert rc == _lib.NO_SUPPORT
     w.free()
+
+
+def _heavy_tail(rows, k, seed, mode):
+    """N(0,1) activations with 1% of the channels scaled x300 ('channels'), or one whole 128-group
+    scaled x1000 ('group'); fp16 like the other operator inputs."""
+    from exl3_b200 import synthetic
+
+    x = synthetic.activations(rows, k, seed=seed).astype(np.float32)
+    rng = np.random.default_rng(seed + 1)
+    if mode == "channels":
+        hot = rng.choice(k, size=max(1, k // 100), replace=False)
+        x[:, hot] *= 300.0
+    else:
+        g = int(rng.integers(0, k // 128))
+        x[:, g * 128:(g + 1) * 128] *= 1000.0
+    return x.astype(np.float16)
+
+
+@pytest.mark.parametrize("mode", ["channels", "group"])
+@pytest.mark.parametrize("rows", [1, 4])
+@pytest.mark.parametrize("name", ["q", "gate", "down"])
+def test_heavy_tailed_activations(ops, oracle, name, rows, mode):
+    """configs[1] shapes with outlier channels or a loud 128-group: the per-warp fixed-point scale
+    must keep the ordinary channels' resolution within the operator bars (2e-3, NMSE 1e-5)."""
+    from exl3_b200 import synthetic
+
+    k, n = synthetic.LAYER_SHAPES[name]
+    m = synthetic.matrix(k, n, 4, seed=k + 3 * n + rows)
+    rec = m.records()
+    w = ops.Exl3Weight.from_records(rec, k, n, 4)
+    x = _heavy_tail(rows, k, seed=100 + rows, mode=mode)
+    y = _mm(ops, w, x)
+    assert_close(y, oracle.mul_mat(rec, 4, k, n, x, nth=8), f"{name} rows={rows} {mode}")
+    w.free()
+

@@ -11,11 +11,16 @@
 //
 // ggml calls an op from nth threads with ith = 0..nth-1 and joins them on a
 // barrier before the next op.  Thread 0 alone drives the GPU -- it uploads the
-// weight on first sight (cached by data pointer, shape and type for the life
-// of the process, as ggml treats weights as immutable once loaded), stages
-// the activations, runs the operator and copies y back before returning (on
-// the legacy default stream, synchronised); the other threads return at once
-// and wait on ggml's barrier.
+// weight on first sight, stages the activations, runs the operator and copies
+// y back before returning (on the legacy default stream, synchronised); the
+// other threads return at once and wait on ggml's barrier.
+//
+// Uploaded weights are cached by data pointer, type and shape plus a digest of
+// the records (the first and last record in full and a strided sample of the
+// rest), checked on every call: a model reloaded at the same address, or a
+// second model reusing a freed buffer, gets its own upload and the stale one is
+// freed.  ggml_exl3_release_weights() frees every cached upload (call it when a
+// model is unloaded).
 //
 // Device: EXL3CU_DEVICE (default 0).  Built in a llama.cpp tree this file
 // compiles against upstream's ggml.h / ggml-cpu-impl.h; the standalone build
@@ -35,8 +40,31 @@
 
 namespace {
 
+struct Cached {
+    exl3cu_weight * handle;
+    uint64_t digest;
+};
 std::mutex g_mu;
-std::map<std::tuple<const void *, int, int64_t, int64_t>, exl3cu_weight *> g_weights;
+std::map<std::tuple<const void *, int, int64_t, int64_t>, Cached> g_weights;
+
+// FNV-1a over the first and last record and 64 words sampled evenly across the
+// records: cheap next to the per-call copies, and it changes when a different
+// model occupies the same buffer.
+uint64_t records_digest(const void * data, size_t bytes, size_t group_bytes) {
+    const unsigned char * p = static_cast<const unsigned char *>(data);
+    uint64_t h = 1469598103934665603ull;
+    auto mix = [&](const unsigned char * q, size_t len) {
+        for (size_t i = 0; i < len; ++i) {
+            h ^= q[i];
+            h *= 1099511628211ull;
+        }
+    };
+    mix(p, group_bytes);
+    mix(p + bytes - group_bytes, group_bytes);
+    const size_t words = bytes / 8;
+    for (size_t i = 0; i < 64 && words; ++i) mix(p + (i * (words - 1) / 63) * 8, 8);
+    return h;
+}
 
 int target_device() {
     const char * env = std::getenv("EXL3CU_DEVICE");
@@ -50,14 +78,19 @@ int target_device() {
 
 exl3cu_weight * weight_for(const ggml_tensor * w, unsigned bits, size_t k, size_t n) {
     const auto key = std::make_tuple(static_cast<const void *>(w->data), int(w->type), int64_t(k), int64_t(n));
+    const size_t bytes = (k / 128) * (n / 128) * exl3_group_bytes(bits);
+    const uint64_t digest = records_digest(w->data, bytes, exl3_group_bytes(bits));
     std::lock_guard<std::mutex> g(g_mu);
     auto it = g_weights.find(key);
-    if (it != g_weights.end()) return it->second;
+    if (it != g_weights.end()) {
+        if (it->second.digest == digest) return it->second.handle;
+        exl3cu_weight_free(it->second.handle);  // other records now live at this address
+        g_weights.erase(it);
+    }
     exl3cu_weight * h = nullptr;
-    const size_t bytes = (k / 128) * (n / 128) * exl3_group_bytes(bits);
     int rc = exl3cu_weight_from_records(w->data, bytes, k, n, bits, EXL3CU_CB_MUL1, 0, 0, target_device(), &h);
     if (rc) die("uploading EXL3 weight", rc);
-    g_weights[key] = h;
+    g_weights[key] = Cached{h, digest};
     return h;
 }
 
@@ -140,4 +173,10 @@ extern "C" void ggml_exl3_mul_mat(const ggml_compute_params * params, ggml_tenso
             if (rc) die("ggml_exl3_mul_mat", rc);
         }
     }
+}
+
+extern "C" void ggml_exl3_release_weights(void) {
+    std::lock_guard<std::mutex> g(g_mu);
+    for (auto & e : g_weights) exl3cu_weight_free(e.second.handle);
+    g_weights.clear();
 }
