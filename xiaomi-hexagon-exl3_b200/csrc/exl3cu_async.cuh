@@ -85,6 +85,24 @@ __device__ __forceinline__ void bulk_g2s(void * dst_smem, const void * src_gmem,
         : "memory");
 }
 
+// L2 policy for data read once per pass (streamed weights): evicted first, so
+// that it does not push the activations and outputs of a chain of kernels out
+// of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// bulk_g2s with an L2 cache policy (l2_evict_first_policy for streamed weights).
+__device__ __forceinline__ void bulk_g2s_hint(void * dst_smem, const void * src_gmem, uint32_t bytes, uint64_t * bar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(smem_addr(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 

@@ -12,13 +12,13 @@
 //
 // evaluated here with the codebook's exact values (the reference's fp16
 // rounding of w moves y by ~1e-4 relative, far inside the 2e-3 bar).  The
-// activations are held as 15-bit fixed point, xh = scale * q with
-// q = 128*hi + lo (hi, lo signed bytes), and sum_k q_k s_k is one integer
-// tensor-core product: mma.m16n8k32 u8 x s8 -> s32 with A = the four bytes
-// of every state's product (so the K dimension sums the bytes: the byte sum
-// costs nothing), B = the digits of q replicated over each product's four
-// bytes.  The batch x digit pairs fill the instruction's N = 8 (4 rows x 2
-// digits).  Per 8 trellis states a lane spends ~10 integer ops extracting
+// activations are held as fixed point, xh = scale * q, q split into signed
+// 7/8-bit digits: three (22 bits) when a problem has one or two rows, two (15
+// bits) for three or four.  sum_k q_k s_k is one integer tensor-core product:
+// mma.m16n8k32 u8 x s8 -> s32 with A = the four bytes of every state's
+// product (so the K dimension sums the bytes: the byte sum costs nothing),
+// B = the digits of q replicated over each product's four bytes.  The row x
+// digit columns fill the instruction's N = 8.  Per 8 trellis states a lane spends ~10 integer ops extracting
 // the 16-bit windows (byte permutes on a nibble-shifted copy at 4 bpw), 8
 // IMADs and 2 IMMAs -- no fp16 conversion, no packing, no HMMA.
 //
@@ -27,8 +27,9 @@
 // multicast) on mbarriers; eight consumer warps decode from shared memory.
 // The K split runs across a thread-block cluster and is reduced through
 // distributed shared memory by cluster rank 0, which applies H128 and sv.
-// Programmatic dependent launch: weights stream before griddepcontrol.wait;
-// only the activation prologue waits for the previous kernel.
+// Programmatic dependent launch: weights stream before griddepcontrol.wait
+// (marked evict-first in L2, so activations stay there); only the activation
+// prologue waits for the previous kernel.  Warp reductions use redux.sync.
 // Every mbarrier wait is bounded (exl3cu_async.cuh).
 #include "exl3cu_async.cuh"
 #include "exl3cu_internal.h"
@@ -49,24 +50,31 @@ namespace exl3cu {
 static __device__ unsigned g_mul1_status;
 static_assert(kMRows <= kMW, "the epilogue gives each row its own consumer warp");  // kStatus* bits raised by k_gemv_mul1
 
+constexpr int kQLim2 = 16000;    // |q| with two digits: hi in [-125,125], lo in [-64,63]
+constexpr int kQLim3 = 2000000;  // |q| with three digits: hi in [-123,123]
+
+__host__ __device__ inline int mul1_digits(int rows) { return rows <= 2 ? 3 : 2; }
+
 struct Mul1Layout {
-    int ring_off, xq_off, acc_off, part_off, slot_off, gmax_off, nw_off, bar_off;
+    int ring_off, xq_off, acc_off, part_off, slot_off, gmax_off, qs_off, nw_off, bar_off;
     size_t bytes;
 };
 
 // ring: kMStages stages of kMW chunks; xq: activation digits of the CTA's K
-// range; acc: the CTA's integer sums [rows][128][hi, lo]; part: its fp32
-// partial; slot: the other cluster ranks' partials (written remotely, read by
-// rank 0); gmax: max |xh| per (row, own group); nw (RMSNorm form, when staged):
-// the norm weights of the CTA's groups; then the mbarriers and per-row scale /
-// digit sum.
+// range (64 bytes per digit column per chunk); acc: the CTA's integer sums
+// [rows][128][digits]; part: its fp32 partial; slot: the other cluster ranks'
+// partials (written remotely, read by rank 0); gmax: max |xh| per (row, own
+// group); qs: the digit sum of every (row, own group); nw (RMSNorm form, when
+// staged): the norm weights of the CTA's groups; then the mbarriers and per-row
+// scale / inverse norm.
 __host__ __device__ inline Mul1Layout mul1_layout(int bits, int cps, int rows, int splits, int stages,
                                                   bool nw_smem) {
     Mul1Layout L;
     const int ng = (cps + 7) / 8 + 1;
+    const int dig = mul1_digits(rows);
     const size_t ring = size_t(stages) * kMW * 256 * bits;
-    const size_t xq = size_t(cps) * 128 * rows;
-    const size_t acc = size_t(rows) * 128 * 2 * 4;
+    const size_t xq = size_t(cps) * 64 * dig * rows;
+    const size_t acc = size_t(rows) * 128 * dig * 4;
     const size_t part = size_t(rows) * 128 * 4;
     const size_t slot = size_t(splits > 1 ? splits - 1 : 0) * rows * 128 * 4;
     const size_t gmax = size_t(rows) * ng * 4;
@@ -76,9 +84,10 @@ __host__ __device__ inline Mul1Layout mul1_layout(int bits, int cps, int rows, i
     L.part_off = int(L.acc_off + acc);
     L.slot_off = int(L.part_off + part);
     L.gmax_off = int(L.slot_off + slot);
-    L.nw_off = int((L.gmax_off + gmax + 15) & ~size_t(15));
+    L.qs_off = int(L.gmax_off + gmax);
+    L.nw_off = int((L.qs_off + gmax + 15) & ~size_t(15));
     L.bar_off = L.nw_off + (nw_smem ? ng * 128 * 4 : 0);
-    L.bytes = L.bar_off + 2 * stages * 8 + 3 * 4 * kMRows;  // + per-row scale, digit sum, inverse norm
+    L.bytes = L.bar_off + 2 * stages * 8 + 2 * 4 * kMRows;  // + per-row scale, inverse norm
     return L;
 }
 
@@ -99,6 +108,9 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
     const GemvProblem & P = b.prob[p];
     const int nb = unit - P.unit_base;
     const int rows = P.rows;
+    const int dig = mul1_digits(rows);
+    const int nd = dig * rows;  // B columns in use
+    const int xqc = 64 * nd;    // digit bytes per chunk
     const int c0 = min(split * P.cps, P.nchunks);
     const int c1 = min(c0 + P.cps, P.nchunks);
     const int nch = c1 - c0;
@@ -114,13 +126,13 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
     float * part = reinterpret_cast<float *>(smem + L.part_off);    // [rows][128]
     float * slots = reinterpret_cast<float *>(smem + L.slot_off);   // [S-1][rows][128]
     float * gmax = reinterpret_cast<float *>(smem + L.gmax_off);    // [rows][ng]
+    int * qs = reinterpret_cast<int *>(smem + L.qs_off);            // [rows][ng] digit sums
     float * nws = reinterpret_cast<float *>(smem + L.nw_off);       // [ng][128] (staged RMSNorm weights)
     uint64_t * full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
     uint64_t * empty = full + NS;
     float * scale_s = reinterpret_cast<float *>(empty + NS);
-    int * xsum_s = reinterpret_cast<int *>(scale_s + kMRows);
-    float * invn_s = reinterpret_cast<float *>(xsum_s + kMRows);  // kXRmsNorm: 1/rms of each row
-    const int nacc = rows * 256;
+    float * invn_s = scale_s + kMRows;  // kXRmsNorm: 1/rms of each row
+    const int nacc = rows * 128 * dig;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -130,10 +142,7 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
         mbar_init_fence();
     }
     for (int e = threadIdx.x; e < nacc; e += kMThreads) acc[e] = 0;
-    if (threadIdx.x < kMRows) {
-        xsum_s[threadIdx.x] = 0;
-        scale_s[threadIdx.x] = 1.0f;  // a CTA without chunks contributes scale * 0
-    }
+    if (threadIdx.x < kMRows) scale_s[threadIdx.x] = 1.0f;  // a CTA without chunks contributes scale * 0
     __syncthreads();
 
     uint2 sv_pre = make_uint2(0, 0);                    // rank 0: output signs of this lane's columns
@@ -141,6 +150,7 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
     if (warp == kMW) {
         // ---- producer: the CTA's chunks [c0, c1) are contiguous in the device layout ----
         if (lane == 0 && nch > 0) {
+            const uint64_t pol = l2_evict_first_policy();  // weights are read once per pass
             const unsigned char * src = reinterpret_cast<const unsigned char *>(P.lsc) +
                                         (size_t(nb) * P.nchunks + c0) * CHUNKB;
             for (int j = 0, s = 0, round = 0; j < nstage; ++j) {
@@ -150,8 +160,8 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
                 }
                 const int nc = min(kMW, nch - j * kMW);
                 mbar_arrive_expect_tx(&full[s], uint32_t(nc * CHUNKB));
-                bulk_g2s(ring + size_t(s) * kMW * CHUNKB, src + size_t(j) * kMW * CHUNKB, uint32_t(nc * CHUNKB),
-                         &full[s]);
+                bulk_g2s_hint(ring + size_t(s) * kMW * CHUNKB, src + size_t(j) * kMW * CHUNKB, uint32_t(nc * CHUNKB),
+                              &full[s], pol);
                 if (++s == NS) {
                     s = 0;
                     ++round;
@@ -289,9 +299,9 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             const int gi = item / rows;
             const int r = item - gi * rows;
             h128_warp4(o);
-            float m = fmaxf(fmaxf(fabsf(o[0]), fabsf(o[1])), fmaxf(fabsf(o[2]), fabsf(o[3])));
-#pragma unroll
-            for (int sh = 16; sh; sh >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, sh));
+            // max over the warp of non-negative floats: their bit patterns order as unsigned integers
+            const float m = __uint_as_float(__reduce_max_sync(
+                0xffffffffu, __float_as_uint(fmaxf(fmaxf(fabsf(o[0]), fabsf(o[1])), fmaxf(fabsf(o[2]), fabsf(o[3]))))));
             if (lane == 0) gmax[r * ng + gi] = m;
         };
         auto rotate = [&](int item, float (&o)[4]) {
@@ -331,14 +341,15 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             rotate(item, o);
         }
         consumer_sync();
-        // (2) per row, scale = max |xh| / kQMax over the CTA's groups; each warp quantizes the
-        //     items it rotated into the digit layout and adds their digit sums (integer)
+        // (2) per row, scale = max |xh| / qlim over the CTA's groups; each warp quantizes the
+        //     items it rotated into the digit layout and records their digit sums (integer)
+        const int qlim = dig == 3 ? kQLim3 : kQLim2;
         auto quantize = [&](int item, const float (&o)[4]) {
             const int gi = item / rows;
             const int r = item - gi * rows;
             float amax = 0.f;
             for (int q = 0; q < ng; ++q) amax = fmaxf(amax, gmax[r * ng + q]);
-            const float scale = amax > 0.f ? amax / kQMax : 1.0f;
+            const float scale = amax > 0.f ? amax / float(qlim) : 1.0f;
             const float inv = 1.0f / scale;
             int qsum = 0;
 #pragma unroll
@@ -346,21 +357,27 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
                 const int k = (g0 + gi) * 128 + lane * 4 + e;
                 if (k < kbeg || k >= kend) continue;
                 int q = __float2int_rn(o[e] * inv);
-                q = max(-16000, min(16000, q));
+                q = max(-qlim, min(qlim, q));
                 qsum += q;
-                const int lo = ((q + 64) & 127) - 64;
-                const int hi = (q - lo) >> 7;
                 const int kl = k - kbeg;
                 const int cl = kl >> 4, kk = kl & 15;
-                unsigned char * base = xq + size_t(cl) * 128 * rows + ((kk & 7) >> 1) * 16 +
-                                       ((kk & 1) + 2 * (kk >> 3)) * 4;
-                *reinterpret_cast<uint32_t *>(base + (2 * r) * 64) = uint32_t(uint8_t(int8_t(hi))) * 0x01010101u;
-                *reinterpret_cast<uint32_t *>(base + (2 * r + 1) * 64) = uint32_t(uint8_t(int8_t(lo))) * 0x01010101u;
+                unsigned char * base = xq + size_t(cl) * xqc + ((kk & 7) >> 1) * 16 + ((kk & 1) + 2 * (kk >> 3)) * 4;
+                const int lo = ((q + 64) & 127) - 64;
+                const int rest = (q - lo) >> 7;
+                if (dig == 3) {
+                    const int mid = ((rest + 64) & 127) - 64;
+                    const int hi = (rest - mid) >> 7;
+                    *reinterpret_cast<uint32_t *>(base + (3 * r) * 64) = uint32_t(uint8_t(int8_t(hi))) * 0x01010101u;
+                    *reinterpret_cast<uint32_t *>(base + (3 * r + 1) * 64) = uint32_t(uint8_t(int8_t(mid))) * 0x01010101u;
+                    *reinterpret_cast<uint32_t *>(base + (3 * r + 2) * 64) = uint32_t(uint8_t(int8_t(lo))) * 0x01010101u;
+                } else {
+                    *reinterpret_cast<uint32_t *>(base + (2 * r) * 64) = uint32_t(uint8_t(int8_t(rest))) * 0x01010101u;
+                    *reinterpret_cast<uint32_t *>(base + (2 * r + 1) * 64) = uint32_t(uint8_t(int8_t(lo))) * 0x01010101u;
+                }
             }
-#pragma unroll
-            for (int sh = 16; sh; sh >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, sh);
+            qsum = __reduce_add_sync(0xffffffffu, qsum);  // |qsum| <= 128 * kQLim3 < 2^31
             if (lane == 0) {
-                atomicAdd(&xsum_s[r], qsum);
+                qs[r * ng + gi] = qsum;
                 if (gi == 0) scale_s[r] = scale;
             }
         };
@@ -378,7 +395,7 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
         consumer_sync();
         // (3) decode + integer tensor-core products
         const int src = (lane + 31) & 31;
-        const bool b_live = lane < 8 * rows;  // B column g = 2*row + digit exists
+        const bool b_live = lane < 4 * nd;  // B column lane/4 = dig*row + digit exists
         constexpr uint32_t C = 0x83dcd12du;
         int D[8][4];
 #pragma unroll
@@ -387,7 +404,7 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             const int cl = warp + j * kMW;
             if (cl >= nch) break;
             uint4 bq = make_uint4(0, 0, 0, 0);
-            if (b_live) bq = *reinterpret_cast<const uint4 *>(xq + size_t(cl) * 128 * rows + lane * 16);
+            if (b_live) bq = *reinterpret_cast<const uint4 *>(xq + size_t(cl) * xqc + lane * 16);
             if (!mbar_wait(&full[s], round & 1)) {
                 atomicOr(&g_mul1_status, kStatusWaitTimeout);
                 break;
@@ -429,15 +446,20 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             }
         }
         // (4) the warps' integer sums meet in shared memory (exact, any order) ...
-        const int g = lane >> 2, t = lane & 3;
-        if (t < rows) {
+        {
+            const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                int * a0 = acc + (t * 128 + c * 16 + g) * 2;
-                atomicAdd(a0, D[c][0]);
-                atomicAdd(a0 + 1, D[c][1]);
-                atomicAdd(a0 + 16, D[c][2]);  // column + 8
-                atomicAdd(a0 + 17, D[c][3]);
+            for (int i = 0; i < 2; ++i) {
+                const int n = 2 * t + i;  // B column: row n / dig, digit n % dig
+                if (n < nd) {
+                    const int rr = n / dig;
+                    int * a0 = acc + (rr * 128 + g) * dig + (n - rr * dig);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        atomicAdd(a0 + c * 16 * dig, D[c][i]);
+                        atomicAdd(a0 + (c * 16 + 8) * dig, D[c][i + 2]);  // column + 8
+                    }
+                }
             }
         }
         consumer_sync();
@@ -446,8 +468,12 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
         float * dst = split == 0 ? part : cluster.map_shared_rank(slots, 0) + size_t(split - 1) * rows * 128;
         for (int e = threadIdx.x; e < rows * 128; e += kMW * 32) {
             const int r = e >> 7;
-            const float sq = fmaf(float(acc[2 * e]), 128.f, float(acc[2 * e + 1]));
-            dst[e] = scale_s[r] * fmaf(kCodeA, sq, kCodeC * float(xsum_s[r]));
+            const int * a = acc + e * dig;
+            const double sq = dig == 3 ? (double(a[0]) * 16384.0 + double(a[1]) * 128.0) + double(a[2])
+                                       : double(a[0]) * 128.0 + double(a[1]);
+            long long qsum = 0;
+            for (int q = 0; q < ng; ++q) qsum += qs[r * ng + q];
+            dst[e] = float(double(scale_s[r]) * (double(kCodeA) * sq + double(kCodeC) * double(qsum)));
         }
         // the accumulated y goes out before the barrier (nothing else writes it during this launch)
         if (split == 0 && P.y_accum && warp < rows)

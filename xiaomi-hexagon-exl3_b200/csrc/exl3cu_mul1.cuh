@@ -27,9 +27,10 @@ __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;
 
 // The 8 trellis states of tile c for this lane (see the LSC layout in
 // exl3cu_decode.cuh), s[e] for positions 8L+e.  The 16 ring bits before the
-// lane's slice are state 7 of lane L-1: one shuffle per tile.
-template <int BITS>
-__device__ __forceinline__ void tile_states(const uint32_t (&w)[2 * BITS], int c, int src, uint32_t (&s)[8]) {
+// lane's slice are state 7 of lane L-1: one shuffle per tile.  w holds the
+// lane's segment words from the first tile of interest on.
+template <int BITS, int NW>
+__device__ __forceinline__ void tile_states(const uint32_t (&w)[NW], int c, int src, uint32_t (&s)[8]) {
     if constexpr (BITS == 4) {
         const uint32_t own = w[c];
         s[7] = own & 0xffffu;
