@@ -69,6 +69,8 @@ def parse_args(argv=None):
                          "ragged: configs[2] packed continuous-admission batches on the tensor-core GEMM")
     ap.add_argument("--no-ragged", action="store_true", help="skip the configs[2] summary in the default run")
     ap.add_argument("--no-model", action="store_true", help="skip the configs[3] hybrid decoder summary")
+    ap.add_argument("--no-large", action="store_true",
+                    help="skip the configs[4] column-split summary (14336x4096, batch 1/8/512)")
     return ap.parse_args(argv)
 
 
@@ -556,13 +558,17 @@ def run_reference_arm(args, rank, world):
 
 # ---------------------------------------------------------------------------------------------
 
-def run_large(args, torch, dist, ops, rank, world, local):
-    """W [k=14336, n=4096] at 4 bpw, x [rows, 14336] fp16, column-split over the
-    ranks with one NCCL all-gather of the fp16 outputs.  Reports per-GPU GB/s of the local
-    EXL3 slice and the whole-operator time including the gather (max over ranks)."""
-    from exl3_b200.parallel import ColumnSplit, gather_columns
+def large_tp_measure(torch, dist, ops, rank, world, local, bits=4, steps=50, warmup=5, rows_list=(1, 8, 512)):
+    """W [k=14336, n=4096] at `bits` bpw, x [rows, 14336] fp16, column-split over the
+    ranks (128-column blocks in contiguous ranges) with one NCCL all-gather of the fp32 slices.
+    Per batch: the local EXL3 slice, the all-gather alone, the whole operator (slice + NCCL
+    gather) and, on 2+ GPUs, the operator with the slices exchanged over NVLink peer memory;
+    each timed as CUDA-graph replays of one pass over the rotated weight copies, CUDA events
+    on the launching stream, max over ranks.  Batch 1 and 8 run the GEMV
+    (HBM-bound: per-GPU GB/s of the slice); batch 512 runs the tcgen05 GEMM (per-GPU TFLOP/s)."""
+    from exl3_b200.parallel import ColumnSplit, PeerColumnParallelExl3, gather_columns
 
-    k, n, bits = 14336, 4096, args.bits
+    k, n = 14336, 4096
     split = ColumnSplit(n, world)
     first, count = split.range(rank)
     dev = f"cuda:{local}"
@@ -573,69 +579,109 @@ def run_large(args, torch, dist, ops, rank, world, local):
     suh = (torch.randint(0, 2, (k,), generator=g, device=dev) * 2 - 1).to(torch.float16)
     svh = ((torch.randint(0, 2, (n,), generator=g, device=dev) * 2 - 1).float() *
            (0.01 + 0.02 * torch.rand(n, generator=g, device=dev))).to(torch.float16)
-    w = ops.Exl3Weight.from_trellis(trellis, suh.view(torch.int16), svh.view(torch.int16), device=local,
-                                    first_block=first, block_count=count)
     # Copies of the rank's slice (same values) rotated through so that consecutive launches read
     # more than the 126 MB L2 holds: every timed launch streams its weights from HBM.
     slice_bytes = k * count * 128 * bits // 8
     ncopies = max(2, -(-300_000_000 // slice_bytes))
-    copies = [w] + [ops.Exl3Weight.from_trellis(trellis, suh.view(torch.int16), svh.view(torch.int16),
-                                                device=local, first_block=first, block_count=count)
-                    for _ in range(ncopies - 1)]
+    copies = [ops.Exl3Weight.from_trellis(trellis, suh.view(torch.int16), svh.view(torch.int16), device=local,
+                                          first_block=first, block_count=count) for _ in range(ncopies)]
     del trellis
     results = {}
     stream = torch.cuda.Stream()
-    for rows in (1, 8):
+    peer = None
+    if world > 1:
+        # the peer path runs on the same rotated copies of the slice (handed over per call)
+        peer = PeerColumnParallelExl3(None, k, n, bits, max_rows=max(rows_list), device=local, weight=copies[0])
+
+    def timed(fn):
+        # one CUDA graph of one pass over the rotated copies, replayed: device time, no host gaps
+        with torch.cuda.stream(stream):
+            for i in range(max(warmup, 2)):
+                fn(i)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream, capture_error_mode="relaxed"):
+            for i in range(ncopies):
+                fn(i)
+        reps = max(1, -(-steps // ncopies))
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                graph.replay()
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            s.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e.record(stream)
+        e.synchronize()
+        ms = s.elapsed_time(e) / (reps * ncopies)
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        del graph
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    for rows in rows_list:
         x = torch.randn((rows, k), generator=g, device=dev).to(torch.float16)
         y_local = torch.empty((rows, count * 128), dtype=torch.float32, device=dev)
         local_bytes = k * count * 128 * bits // 8 + 2 * (k + count * 128) + 2 * k * rows + 4 * count * 128 * rows
-        timings = {}
-        for what in ("local", "operator"):
-            with torch.cuda.stream(stream):
-                for i in range(max(3, args.warmup)):
-                    copies[i % ncopies].mul_mat(x, out=y_local, stream=stream)
-                    if what == "operator":
-                        gather_columns(y_local, split)
-            stream.synchronize()
-            if world > 1:
-                dist.barrier()
-            torch.cuda.synchronize()
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(stream):
-                s.record(stream)
-                for i in range(args.steps):
-                    copies[i % ncopies].mul_mat(x, out=y_local, stream=stream)
-                    if what == "operator":
-                        gather_columns(y_local, split)
-                e.record(stream)
-            e.synchronize()
-            ms = s.elapsed_time(e) / args.steps
-            if world > 1:
-                t = torch.tensor([ms], dtype=torch.float64, device=dev)
-                dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                ms = float(t.item())
-            timings[what] = ms
-        results[str(rows)] = {"local_us": round(timings["local"] * 1e3, 2),
-                              "operator_us": round(timings["operator"] * 1e3, 2),
-                              "local_gbs_per_gpu": round(local_bytes / (timings["local"] * 1e-3) / 1e9, 1),
-                              "gather_bytes_per_rank": 2 * rows * 128 * split.max_blocks * world}
+        local_flops = 2.0 * rows * k * count * 128
+        ms_local = timed(lambda i: copies[i % ncopies].mul_mat(x, out=y_local, stream=stream))
+        ms_gather = timed(lambda i: gather_columns(y_local, split)) if world > 1 else 0.0
+
+        def op(i):
+            copies[i % ncopies].mul_mat(x, out=y_local, stream=stream)
+            gather_columns(y_local, split)
+        ms_op = timed(op)
+        r = {"local_us": round(ms_local * 1e3, 2), "gather_us": round(ms_gather * 1e3, 2),
+             "operator_us": round(ms_op * 1e3, 2),
+             "gather_bytes_per_rank": 4 * rows * 128 * split.max_blocks * world}
+        if peer is not None:
+            # the same slices exchanged over NVLink peer memory instead of the NCCL all-gather
+            def op_peer(i):
+                peer.weight = copies[i % ncopies]
+                peer.forward(x, stream=stream)
+            r["operator_peer_us"] = round(timed(op_peer) * 1e3, 2)
+        if rows <= 8:
+            r["local_gbs_per_gpu"] = round(local_bytes / (ms_local * 1e-3) / 1e9, 1)
+        else:
+            r["local_tflops_per_gpu"] = round(local_flops / (ms_local * 1e-3) / 1e12, 1)
+            r["operator_tflops_total"] = round(2.0 * rows * k * n / (ms_op * 1e-3) / 1e12, 1)
+        results[str(rows)] = r
+    if peer is not None:
+        peer.free()
     for c in copies:
         c.free()
+    return {"n_gpus": world, "blocks_per_rank": split.max_blocks, "copies": ncopies, "by_batch": results}
+
+
+def run_large(args, torch, dist, ops, rank, world, local):
+    """--config large: configs[4] alone (see large_tp_measure), one JSON line."""
+    res = large_tp_measure(torch, dist, ops, rank, world, local, bits=args.bits, steps=args.steps,
+                           warmup=max(3, args.warmup))
     if rank == 0:
         pk, pk_kind = peaks()
         peak = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
-        b1 = results["1"]
+        b1 = res["by_batch"]["1"]
         print(json.dumps({
             "metric": "EXL3 4bpw large-matrix GEMV, column split + NCCL all-gather (configs[4])",
             "value": b1["local_gbs_per_gpu"], "unit": "GB/s per GPU", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "dtype": "fp16",
             "data": "synthetic", "vs_baseline": None,
-            "config": {"workload": "W [4096,14336] (k=14336, n=4096) 4 bpw, x fp16 N(0,1); batch 1 and 8",
-                       "parallelism": f"column split tp{world}", "bits": bits,
-                       "l2": f"{ncopies} copies of the rank's slice rotated: > 126 MB per rotation, weights from HBM"},
+            "config": {"workload": "W [4096,14336] (k=14336, n=4096) 4 bpw, x fp16 N(0,1); batch 1, 8 and 512",
+                       "parallelism": f"column split tp{world}", "bits": args.bits,
+                       "l2": f"{res['copies']} copies of the rank's slice rotated: > 126 MB per rotation"},
             "roofline": {"bound": "hbm", "achieved": b1["local_gbs_per_gpu"], "peak": peak, "unit": "GB/s",
                          "frac": round(b1["local_gbs_per_gpu"] / peak, 4), "peak_source": f"{pk_kind} hbm_gbs"},
-            "by_batch": results}), flush=True)
+            "by_batch": res["by_batch"]}), flush=True)
     return 0
 
 
@@ -900,6 +946,9 @@ def main(argv=None):
     model = None
     if not args.no_model:
         model = run_model_measure(torch, dist, local, rank, world)
+    large_tp = None
+    if not args.no_large:
+        large_tp = large_tp_measure(torch, dist, ops, rank, world, local, bits=args.bits)
 
     traffic = None
     tf = ROOT / "profiles" / "gemv_traffic.json"
@@ -953,6 +1002,7 @@ def main(argv=None):
             "sweep_gbs_by_bits": sweep,
             "ragged_configs2": ragged,
             "decode_configs3": model,
+            "large_tp_configs4": large_tp,
         }
         print(json.dumps(line), flush=True)
     for layer in stack:

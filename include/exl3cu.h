@@ -266,6 +266,42 @@ int exl3cu_mul_mat_noalloc(const exl3cu_weight * w, const void * d_x, int x_dtyp
                            float * d_y, size_t y_row_stride, void * stream);
 
 /* ------------------------------------------------------------------------
+ * Peer-memory exchange for the column-split operator (2..8 GPUs of one node,
+ * one process per GPU).  No counterpart in the reference: its operator splits
+ * output column blocks over CPU threads of one process (src/exl3-ggml.cpp:74);
+ * here each GPU computes a contiguous range of column blocks and the slices
+ * meet over NVLink without a collective library.
+ *
+ * exl3cu_ipc_alloc: zero-filled device memory on `device` that peers can map;
+ *   writes its 64-byte CUDA IPC handle to out_handle.
+ * exl3cu_ipc_open / exl3cu_ipc_close: map / unmap a peer's buffer (from
+ *   another process) on `device`.
+ * exl3cu_store_peers: this call's epoch E is this rank's device counter + 1;
+ *   rows x cols floats of this rank's slice (row stride slice_stride) go into
+ *   half (E & 1) of every rank's y buffer (halves y_half floats apart, row
+ *   stride y_row_stride) at column y_col0; once the whole slice is stored,
+ *   state[rank] = E in every rank's state words (system-scope release) and
+ *   the counter advances.  State words (16 per rank, zero-initialised):
+ *   [0, 8) the ranks' last epochs, [8] an arrival ticket, [9] the counter.
+ * exl3cu_wait_peers: on the stream, until every rank's epoch in d_state has
+ *   reached this rank's counter (modulo 2^32: a rank may be one call ahead);
+ *   then, when d_out is not NULL, copies the finished half of this rank's y
+ *   (rows x cols) into d_out.  Bounded: after about a second it sets bit 0
+ *   of exl3cu_device_status and returns.
+ * Both read the epoch on the device, so a call sequence can be captured in a
+ * CUDA graph and replayed.  Columns, strides and offsets are multiples of 4
+ * floats; npeers <= 8. */
+int exl3cu_ipc_alloc(int device, size_t bytes, void ** out_ptr, void * out_handle);
+int exl3cu_ipc_free(int device, void * ptr);
+int exl3cu_ipc_open(int device, const void * handle, void ** out_ptr);
+int exl3cu_ipc_close(int device, void * ptr);
+int exl3cu_store_peers(const float * d_slice, size_t rows, size_t cols, size_t slice_stride, int npeers,
+                       float * const * d_y_peers, size_t y_row_stride, size_t y_half, size_t y_col0,
+                       unsigned * const * d_state_peers, int rank, void * stream);
+int exl3cu_wait_peers(const unsigned * d_state, int npeers, const float * d_y, size_t y_row_stride, size_t y_half,
+                      float * d_out, size_t out_row_stride, size_t rows, size_t cols, void * stream);
+
+/* ------------------------------------------------------------------------
  * Model loader (replaces exl3::Model's constructor, src/exl3_model.cpp:79-157,
  * and extends it from the tied head to every EXL3 matrix).
  *

@@ -1,8 +1,10 @@
 """Column-split EXL3 operator on 2+ GPUs over NCCL (configs[4] shape), one process per GPU.
 
 Each rank uploads only its column blocks, runs the CUDA operator on its slice and
-all-gathers the fp16 slices; every rank must hold y within the operator
-tolerance of the oracle.  Skipped when fewer than two GPUs are visible."""
+rebuilds y on every rank, once through one NCCL all-gather of the fp32 slices and
+once through peer memory (NVLink stores and epoch flags); every rank must hold the
+same y, within the operator tolerance of the oracle, at batch 1, 8 and 512.  Skipped when fewer than two GPUs are visible."""
+import ctypes
 import os
 import socket
 
@@ -43,9 +45,9 @@ def _worker(rank, world, port, q):
         rec = m.records()
         layer = ColumnParallelExl3(rec, k, n, bits, device=rank)
         out = []
-        for rows in (1, 8):
+        for rows in (1, 8, 512):  # GEMV, grouped GEMV, tcgen05 GEMM
             x = synthetic.activations(rows, k, seed=45 + rows)
-            y = layer.forward(torch.from_numpy(x).cuda(rank))
+            y = layer.forward(torch.from_numpy(x).cuda(rank))  # fp32 gather, as one GPU returns y
             torch.cuda.synchronize(rank)
             y = y.float().cpu().numpy()
             ref = Oracle().mul_mat(rec, bits, k, n, x, nth=8) if rank == 0 else None
@@ -58,6 +60,27 @@ def _worker(rank, world, port, q):
             dist.broadcast(ref0, 0)
             out.append((rows, "same", bool(torch.equal(t, ref0))))
         layer.free()
+        # the same through peer memory (NVLink stores + epoch flags, no collective library); three calls
+        # in a row so that both halves of the double-buffered y are used and reused
+        from exl3_b200.parallel import PeerColumnParallelExl3
+
+        peer = PeerColumnParallelExl3(rec, k, n, bits, max_rows=512, device=rank)
+        for rows in (1, 8, 512, 1):
+            x = synthetic.activations(rows, k, seed=45 + rows)
+            y = peer.forward(torch.from_numpy(x).cuda(rank)).clone()
+            torch.cuda.synchronize(rank)
+            if rank == 0:
+                ref = Oracle().mul_mat(rec, bits, k, n, x, nth=8)
+                yn = y.cpu().numpy()
+                out.append((rows, float(np.max(np.abs(yn - ref)) / np.max(np.abs(ref)))))
+            ref0 = y.clone()
+            dist.broadcast(ref0, 0)
+            out.append((rows, "same", bool(torch.equal(y, ref0))))
+        st = ctypes.c_uint(0)
+        from exl3_b200 import _lib
+        _lib.check(_lib.lib().exl3cu_device_status(rank, ctypes.byref(st), 1))
+        out.append((0, "status", int(st.value)))
+        peer.free()
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
@@ -83,8 +106,9 @@ def test_column_parallel_nccl():
         assert p.exitcode == 0
     for rank, out in results.items():
         for item in out:
-            if item[1] == "same":
+            if item[1] == "status":
+                assert item[2] == 0, f"rank {rank}: device status {item[2]:#x} (a peer wait ran out)"
+            elif item[1] == "same":
                 assert item[2], f"rank {rank} rows {item[0]}: gathered y differs from rank 0"
             else:
-                # the fp16 all-gather adds at most 2^-11 of |y| on top of the operator's error
                 assert item[1] <= 2e-3, f"rows {item[0]}: max_abs_rel {item[1]}"

@@ -60,9 +60,12 @@ def _worker(rank, world, port, k, n, bits, rows, q):
         part = tr[:, first * 8:(first + count) * 8, :]
         rec_local = pack_records(part, su, sv[first * 128:(first + count) * 128], bits)
         y_local = orc.mul_mat(rec_local, bits, k, count * 128, x)
-        y = gather_columns(torch.from_numpy(y_local), split)
         full = orc.mul_mat(rec, bits, k, n, x)
-        q.put((rank, float(np.max(np.abs(y.float().numpy() - full.astype(np.float16).astype(np.float32))))))
+        y32 = gather_columns(torch.from_numpy(y_local), split)  # fp32 by default: exact
+        y16 = gather_columns(torch.from_numpy(y_local), split, dtype=torch.float16)
+        e32 = float(np.max(np.abs(y32.numpy() - full)))
+        e16 = float(np.max(np.abs(y16.float().numpy() - full.astype(np.float16).astype(np.float32))))
+        q.put((rank, max(e32, e16), y32.dtype == torch.float32))
     finally:
         dist.destroy_process_group()
 
@@ -79,6 +82,7 @@ def test_column_split_gather_matches_single_process(world, n):
         p.join(timeout=120)
         assert p.exitcode == 0
     results = sorted(q.get(timeout=10) for _ in range(world))
-    assert [r for r, _ in results] == list(range(world))
-    for _, err in results:
-        assert err == 0.0  # every rank rebuilds the exact fp16 of the single-process output
+    assert [r for r, _, _ in results] == list(range(world))
+    for _, err, is32 in results:
+        assert is32  # the default gather keeps the operator's fp32 output
+        assert err == 0.0  # every rank rebuilds the exact fp32 (and, on request, fp16) single-process output

@@ -668,12 +668,13 @@ int exl3cu_device_status(int device, unsigned * status, int clear) {
     DeviceGuard guard(device);
     if (!guard.ok) return fail(EXL3CU_INVALID_ARGUMENT, "cannot select device %d", device);
     CU_TRY(cudaDeviceSynchronize(), "synchronising before reading the device status");
-    unsigned gemv = 0, gemm = 0, seq = 0, rows = 0;
+    unsigned gemv = 0, gemm = 0, seq = 0, rows = 0, peers = 0;
+    CU_TRY(peer_read_status(&peers, clear != 0), "reading the peer-exchange status word");
     CU_TRY(mul1_read_status(&gemv, clear != 0), "reading the GEMV status word");
     CU_TRY(gemm_read_status(&gemm, clear != 0), "reading the GEMM status word");
     CU_TRY(seq_read_status(&seq, clear != 0), "reading the sequence status word");
     CU_TRY(rows_read_status(&rows, clear != 0), "reading the get_rows status word");
-    *status = gemv | gemm | seq | rows;
+    *status = gemv | gemm | seq | rows | peers;
     return EXL3CU_OK;
 }
 

@@ -182,6 +182,7 @@ cudaError_t launch_get_rows(const uint32_t * lsc, const uint16_t * suh, const ui
                             unsigned bits, unsigned cb, const int32_t * ids, size_t count, void * out,
                             size_t out_stride, bool out_f16, cudaStream_t st);
 cudaError_t rows_read_status(unsigned * out, bool clear);
+cudaError_t peer_read_status(unsigned * out, bool clear);
 cudaError_t launch_reconstruct_blocks(uint16_t * io, size_t k, size_t column_count, size_t first_column,
                                       const uint16_t * suh, const uint16_t * svh, cudaStream_t st);
 

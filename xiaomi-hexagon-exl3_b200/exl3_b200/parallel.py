@@ -7,8 +7,11 @@ Two layouts, both one process per GPU over torch.distributed:
 * **Column split** (the large-matrix configuration): output column blocks of
   128 are dealt to ranks in contiguous ranges; each rank uploads only its
   blocks (``Exl3Weight.from_records(..., first_block, block_count)``) and
-  computes its slice of y; one all-gather of the fp16 slices rebuilds y on
-  every rank.  The epilogue's H128 and sv act inside a 128-column block, so a
+  computes its slice of y.  Two ways rebuild y on every rank:
+  ``ColumnParallelExl3`` runs one NCCL all-gather of the fp32 slices (fp16 on
+  request); ``PeerColumnParallelExl3`` stores every slice straight into every
+  rank's y over NVLink (CUDA IPC mappings, P2P stores, an epoch flag per rank
+  and a bounded wait on the device) -- no collective library on the path.  The epilogue's H128 and sv act inside a 128-column block, so a
   slice needs nothing from the other ranks.
 """
 from __future__ import annotations
@@ -47,24 +50,27 @@ class ColumnSplit:
         return -(-self.blocks // self.world)
 
 
-def gather_columns(y_local: torch.Tensor, split: ColumnSplit, group=None) -> torch.Tensor:
-    """All-gather fp16 column slices [rows, 128*count_r] into y [rows, n] on every rank.
+def gather_columns(y_local: torch.Tensor, split: ColumnSplit, group=None, dtype=torch.float32) -> torch.Tensor:
+    """All-gather column slices [rows, 128*count_r] into y [rows, n] on every rank.
 
-    Uneven shares are padded to the largest so one collective moves them; on NCCL that
-    is a single all_gather_into_tensor of [world, rows, 128*max_blocks].  With one rank
-    (or no process group) the slice already is y."""
+    dtype float32 (the default) keeps the operator's fp32 output bit for bit, as one GPU
+    returns it; float16 halves the bytes on the wire and rounds y to fp16 (at most 2^-11
+    relative, and |y| beyond 65504 overflows).  Uneven shares are padded to the largest so
+    one collective moves them; on NCCL that is a single all_gather_into_tensor of
+    [world, rows, 128*max_blocks].  With one rank (or no process group) the slice already
+    is y."""
     rows = y_local.shape[0]
     if split.world == 1 or not dist.is_initialized():
-        return y_local.to(torch.float16)
+        return y_local.to(dtype)
     width = 128 * split.max_blocks
     even = split.blocks % split.world == 0
     if even:
-        send = y_local.to(torch.float16)
+        send = y_local.to(dtype)
     else:
-        send = torch.zeros((rows, width), dtype=torch.float16, device=y_local.device)
-        send[:, : y_local.shape[1]] = y_local.to(torch.float16)
+        send = torch.zeros((rows, width), dtype=dtype, device=y_local.device)
+        send[:, : y_local.shape[1]] = y_local.to(dtype)
     if dist.get_backend(group) == "nccl":
-        recv = torch.empty((split.world, rows, width), dtype=torch.float16, device=y_local.device)
+        recv = torch.empty((split.world, rows, width), dtype=dtype, device=y_local.device)
         dist.all_gather_into_tensor(recv, send.contiguous(), group=group)
         if even:  # rank-major slices are y's column blocks in order
             return recv.permute(1, 0, 2).reshape(rows, split.n)
@@ -72,7 +78,7 @@ def gather_columns(y_local: torch.Tensor, split: ColumnSplit, group=None) -> tor
     else:
         parts = [torch.empty_like(send) for _ in range(split.world)]
         dist.all_gather(parts, send.contiguous(), group=group)
-    out = torch.empty((rows, split.n), dtype=torch.float16, device=y_local.device)
+    out = torch.empty((rows, split.n), dtype=dtype, device=y_local.device)
     for r, part in enumerate(parts):
         first, count = split.range(r)
         out[:, first * 128:(first + count) * 128] = part[:, : count * 128]
@@ -94,10 +100,103 @@ class ColumnParallelExl3:
                                               block_count=count)
         self.k, self.n = k, n
 
-    def forward(self, x: torch.Tensor, stream=None) -> torch.Tensor:
-        """y = x . W as fp16 [rows, n] on every rank (local EXL3 slice + one all-gather)."""
+    def forward(self, x: torch.Tensor, stream=None, dtype=torch.float32) -> torch.Tensor:
+        """y = x . W as [rows, n] on every rank (local EXL3 slice + one all-gather); fp32 like the
+        single-GPU operator unless dtype=torch.float16 asks for the half-size gather."""
         y_local = self.weight.mul_mat(x, stream=stream)
-        return gather_columns(y_local, self.split, self.group)
+        return gather_columns(y_local, self.split, self.group, dtype=dtype)
 
     def free(self):
         self.weight.free()
+
+
+class PeerColumnParallelExl3:
+    """Column-split EXL3 matrix whose slices meet over NVLink peer memory.
+
+    Every rank holds y twice ([2][max_rows][n] fp32, used by epoch parity: a rank can be one call
+    ahead of another) and 16 state words (every rank's last epoch, an arrival ticket, its epoch
+    counter), in buffers every other rank maps through CUDA IPC.  forward(): the local slice into a
+    staging buffer (the EXL3 operator), then exl3cu_store_peers writes it into every rank's y and
+    publishes the call's epoch in every rank's state, and exl3cu_wait_peers holds the stream until
+    every rank's epoch has arrived and copies the finished y into a fixed output.  The epoch lives
+    on the device, so forward() can be captured in a CUDA graph and replayed.  The returned tensor
+    is a view of the fixed output, valid until the next call."""
+
+    def __init__(self, records, k: int, n: int, bits: int, max_rows: int, group=None, device: int | None = None,
+                 codebook: int = 2, weight=None):
+        import ctypes
+
+        from . import _lib
+        from .ops import Exl3Weight
+
+        self.L = _lib.lib()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the peer exchange serves up to 8 ranks")
+        self.split = ColumnSplit(n, self.world)
+        first, count = self.split.range(self.rank)
+        self.first, self.count = first, count
+        self.dev = torch.cuda.current_device() if device is None else device
+        # `weight`: an existing handle of this rank's column blocks, used as is and not freed here
+        self.owns_weight = weight is None
+        self.weight = weight if weight is not None else Exl3Weight.from_records(
+            records, k, n, bits, codebook=codebook, device=self.dev, first_block=first, block_count=count)
+        self.k, self.n, self.max_rows = k, n, max_rows
+        self.half = max_rows * n  # floats between the two halves of y
+        c = ctypes
+        y_ptr, s_ptr = c.c_void_p(), c.c_void_p()
+        y_h, s_h = (c.c_char * 64)(), (c.c_char * 64)()
+        _lib.check(self.L.exl3cu_ipc_alloc(self.dev, 2 * self.half * 4, c.byref(y_ptr), y_h))
+        _lib.check(self.L.exl3cu_ipc_alloc(self.dev, 64, c.byref(s_ptr), s_h))  # 16 state words
+        self.y_own, self.state_own = y_ptr.value, s_ptr.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, (bytes(y_h), bytes(s_h)), group=group)
+        self.y_peers, self.s_peers, self.opened = [], [], []
+        for r, (yh, sh) in enumerate(handles):
+            if r == self.rank:
+                self.y_peers.append(self.y_own)
+                self.s_peers.append(self.state_own)
+                continue
+            yp, sp = c.c_void_p(), c.c_void_p()
+            _lib.check(self.L.exl3cu_ipc_open(self.dev, c.create_string_buffer(yh, 64), c.byref(yp)))
+            _lib.check(self.L.exl3cu_ipc_open(self.dev, c.create_string_buffer(sh, 64), c.byref(sp)))
+            self.y_peers.append(yp.value)
+            self.s_peers.append(sp.value)
+            self.opened += [yp.value, sp.value]
+        dist.barrier(group=group)  # every rank has mapped every buffer before any store
+        self._yp = (c.c_void_p * self.world)(*self.y_peers)
+        self._sp = (c.c_void_p * self.world)(*self.s_peers)
+        self.slice = torch.empty((max_rows, count * 128), dtype=torch.float32, device=f"cuda:{self.dev}")
+        self.out = torch.empty((max_rows, n), dtype=torch.float32, device=f"cuda:{self.dev}")
+
+    def forward(self, x: torch.Tensor, stream=None) -> torch.Tensor:
+        """y = x . W as fp32 [rows, n] on every rank, the slices exchanged over peer memory."""
+        import ctypes
+
+        from . import _lib
+        from .ops import _stream_handle
+
+        rows = x.shape[0]
+        if rows > self.max_rows:
+            raise ValueError(f"{rows} rows > max_rows {self.max_rows}")
+        self.weight.mul_mat(x, out=self.slice[:rows], stream=stream)
+        sh = _stream_handle(stream)
+        cols = self.count * 128
+        _lib.check(self.L.exl3cu_store_peers(self.slice.data_ptr(), rows, cols, cols, self.world, self._yp, self.n,
+                                             self.half, self.first * 128, self._sp, self.rank, sh))
+        _lib.check(self.L.exl3cu_wait_peers(ctypes.c_void_p(self.state_own), self.world, ctypes.c_void_p(self.y_own),
+                                            self.n, self.half, self.out.data_ptr(), self.n, rows, self.n, sh))
+        return self.out[:rows]
+
+    def free(self):
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)  # no rank still stores into another's buffers
+        for p in self.opened:
+            self.L.exl3cu_ipc_close(self.dev, p)
+        dist.barrier(group=self.group)
+        self.L.exl3cu_ipc_free(self.dev, self.y_own)
+        self.L.exl3cu_ipc_free(self.dev, self.state_own)
+        if self.owns_weight:
+            self.weight.free()
