@@ -299,6 +299,75 @@ def time_e2e(torch, ops, stack, steps):
     return max(start.elapsed_time(end), wall_ms), h2d, d2h
 
 
+def time_ggml_e2e(bits, layers, steps, seed=4242):
+    """The reference-facing plugin call, per matrix, from host memory: ggml_exl3_mul_mat (the
+    libexl3cu_ggml.so drop-in) called as ggml's CPU backend calls the reference's operator -- one
+    GGML_OP_MUL_MAT node per matrix, ggml tensors over host buffers (packed records, f32 x [1, k],
+    f32 y [1, n]), every call copying its x in and its y out and returning when y is in host memory.
+    The records (seeded, same shapes and distribution as the device stack) are uploaded once, on the
+    first step, by the adapter's weight cache; timed: `steps` steps of 7 * layers calls, host wall
+    clock (each call is synchronous).  Returns (ms per step, h2d and d2h bytes per step, calls per step)."""
+    import ctypes
+
+    import numpy as np
+
+    from exl3_b200 import _lib
+    from exl3_b200.format import BITS_GGML_TYPE, pack_records
+
+    class T(ctypes.Structure):
+        _fields_ = [("type", ctypes.c_int), ("ne", ctypes.c_int64 * 4), ("nb", ctypes.c_size_t * 4),
+                    ("src", ctypes.c_void_p * 10), ("data", ctypes.c_void_p)]
+
+    class P(ctypes.Structure):
+        _fields_ = [("ith", ctypes.c_int), ("nth", ctypes.c_int), ("wsize", ctypes.c_size_t),
+                    ("wdata", ctypes.c_void_p)]
+
+    def tensor(typ, ne, nb, data):
+        t = T()
+        t.type = typ
+        for i in range(4):
+            t.ne[i], t.nb[i] = ne[i], nb[i]
+        t.data = data
+        return t
+
+    gl = ctypes.CDLL(str(_lib.GGML_LIB_PATH))
+    fn = gl.ggml_exl3_mul_mat
+    fn.argtypes = [ctypes.POINTER(P), ctypes.POINTER(T)]
+    fn.restype = None
+    rng = np.random.Generator(np.random.PCG64(seed))
+    keep, nodes = [], []
+    h2d = d2h = 0
+    for _ in range(layers):
+        for _, (k, n) in shapes():
+            tr = rng.integers(0, 65536, size=(k // 16, n // 16, 16 * bits), dtype=np.uint16)
+            suh = rng.choice(np.array([-1.0, 1.0], np.float16), size=k).view(np.uint16)
+            svh = (rng.choice(np.array([-1.0, 1.0]), size=n) * rng.uniform(0.01, 0.03, size=n)).astype(
+                np.float16).view(np.uint16)
+            rec = pack_records(tr, suh, svh, bits)
+            x = rng.standard_normal((1, k), dtype=np.float32)
+            y = np.zeros((1, n), np.float32)
+            w = tensor(BITS_GGML_TYPE[bits], (k, n, 1, 1), (1, 1, 1, 1), rec.ctypes.data)
+            xi = tensor(0, (k, 1, 1, 1), (4, 4 * k, 4 * k, 4 * k), x.ctypes.data)
+            dst = tensor(0, (n, 1, 1, 1), (4, 4 * n, 4 * n, 4 * n), y.ctypes.data)
+            dst.src[0], dst.src[1] = ctypes.addressof(w), ctypes.addressof(xi)
+            keep.append((rec, x, y, w, xi, dst))
+            nodes.append(ctypes.byref(dst))
+            h2d += x.nbytes
+            d2h += y.nbytes
+    params = ctypes.byref(P(0, 1, 0, None))
+    for _ in range(2):  # the first step uploads every matrix into the adapter's cache
+        for d in nodes:
+            fn(params, d)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for d in nodes:
+            fn(params, d)
+    ms = (time.perf_counter() - t0) * 1e3 / steps
+    gl.ggml_exl3_release_weights()
+    del keep
+    return ms, h2d, d2h, len(nodes)
+
+
 def per_shape_us(torch, stack, reps=4):
     """Average device time of one exl3cu_mul_mat per shape, back to back over distinct layers."""
     out = {}
@@ -922,6 +991,8 @@ def main(argv=None):
     e2e_ms = max_over_ranks(e2e_ms)
     e2e_value = step_bytes * world / (e2e_ms / args.e2e_steps * 1e-3) / 1e9
     shape_us = per_shape_us(torch, stack)
+    ggml_ms, ggml_h2d, ggml_d2h, ggml_calls = time_ggml_e2e(args.bits, args.layers, max(3, args.e2e_steps // 3))
+    ggml_ms = max_over_ranks(ggml_ms)
 
     sweep = {}
     if not args.no_sweep:
@@ -994,7 +1065,13 @@ def main(argv=None):
                     "d2h_bytes_per_step": d2h,
                     "api": "one pinned H2D of all x, the decoder pattern's exl3cu_mul_mat_batch calls (CUDA graph), "
                            "one D2H of all y into pinned memory, stream synchronise",
-                    "ms_per_step": round(e2e_ms / args.e2e_steps, 4)},
+                    "ms_per_step": round(e2e_ms / args.e2e_steps, 4),
+                    "per_call_ggml": {
+                        "value": round(step_bytes * world / (ggml_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                        "ms_per_step": round(ggml_ms, 4), "calls_per_step": ggml_calls,
+                        "h2d_bytes_per_step": ggml_h2d, "d2h_bytes_per_step": ggml_d2h,
+                        "api": "ggml_exl3_mul_mat per matrix as ggml's CPU backend calls it: host ggml tensors "
+                               "(records, f32 x, f32 y), synchronous per call; host wall clock"}},
             "gpu_launches": launches * args.steps,
             "clocks": clk.summary(),
             "patterns": patterns,

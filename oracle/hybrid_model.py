@@ -156,3 +156,106 @@ class OracleHybrid:
         h = (h + delta).astype(np.float32)
         xn = _rms(h, self.w.final_norm, cfg.eps).astype(np.float32)
         return (self.E @ xn.astype(np.float64)).astype(np.float32)
+
+
+class StreamingOracleHybrid:
+    """The same model for a whole token sequence at once (teacher forcing), layer by layer, with
+    nothing dense kept: every EXL3 product runs through the oracle's restatement of the reference
+    operator (ggml_exl3_mul_mat, src/exl3-ggml.cpp:51-92) on the matrix's runtime records, so the
+    memory stays at one layer's records however large the model.  Mixers advance position by
+    position exactly as OracleHybrid.step does.  Returns every layer's residual stream and the
+    logits of every position (float32)."""
+
+    def __init__(self, weights, oracle, nth: int = 8):
+        self.w = weights
+        self.cfg = weights.cfg
+        self.orc = oracle
+        self.nth = nth
+
+    def _mm(self, x, m):
+        from exl3_b200.format import pack_records
+
+        rec = pack_records(m.trellis, m.suh, m.svh, m.bits)
+        return self.orc.mul_mat(rec, m.bits, m.k, m.n, np.ascontiguousarray(x, np.float32), nth=self.nth)
+
+    def run(self, tokens):
+        cfg = self.cfg
+        H, D, HD = cfg.hidden, cfg.heads * cfg.head_dim, cfg.head_dim
+        T = len(tokens)
+        E = self.w.embed
+        h = E[np.asarray(tokens)].astype(np.float32)
+        residuals = []
+        inv_freq = cfg.inv_freq
+        for lw in self.w.layers:
+            M = lw.mats
+            xn = _rms(h, lw.in_norm, cfg.eps).astype(np.float32)
+            mix = np.empty((T, D), np.float32)
+            if lw.kind == "full":
+                q = self._mm(xn, M["q"]).reshape(T, cfg.heads, HD)
+                k = self._mm(xn, M["k"]).reshape(T, cfg.kv_heads, HD)
+                v = self._mm(xn, M["v"]).reshape(T, cfg.kv_heads, HD)
+                q = _rms(q, lw.extra["q_norm"], cfg.eps)
+                k = _rms(k, lw.extra["k_norm"], cfg.eps)
+                ang = (np.arange(T, dtype=np.float32)[:, None] * inv_freq[None, :]).astype(np.float64)
+                cs, sn = np.cos(ang)[:, None, :], np.sin(ang)[:, None, :]
+
+                def rope(x):
+                    a, b = x[..., :HD // 2], x[..., HD // 2:]
+                    return np.concatenate([a * cs - b * sn, b * cs + a * sn], axis=-1)
+
+                q = rope(q).astype(np.float32).astype(np.float64)
+                K = rope(k).astype(np.float16).astype(np.float64)
+                V = v.astype(np.float16).astype(np.float64)
+                g = cfg.heads // cfg.kv_heads
+                for t in range(T):
+                    out = np.empty((cfg.heads, HD))
+                    for hq in range(cfg.heads):
+                        sc = K[:t + 1, hq // g, :] @ q[t, hq] / np.sqrt(HD)
+                        pr = np.exp(sc - sc.max())
+                        out[hq] = (pr / pr.sum()) @ V[:t + 1, hq // g, :]
+                    mix[t] = out.reshape(D).astype(np.float32)
+            else:
+                ex = lw.extra
+                proj = np.concatenate([self._mm(xn, M[nm]) for nm in ("q", "k", "v", "z")], axis=1)
+                cw = ex["conv_w"].astype(np.float64)
+                cst = np.zeros((3 * D, 3), np.float64)
+                S = np.zeros((cfg.heads, HD, HD), np.float64)
+                ab_all = (ex["wab"].astype(np.float64) @ xn.astype(np.float64).T).T  # [T, 2 heads]
+                for t in range(T):
+                    x_qkv = proj[t, :3 * D].astype(np.float64)
+                    z = proj[t, 3 * D:].astype(np.float64).reshape(cfg.heads, HD)
+                    conv = cst[:, 0] * cw[:, 0] + cst[:, 1] * cw[:, 1] + cst[:, 2] * cw[:, 2] + x_qkv * cw[:, 3]
+                    cst[:, 0], cst[:, 1], cst[:, 2] = cst[:, 1].copy(), cst[:, 2].copy(), x_qkv
+                    c = _silu(conv)
+                    qh = c[:D].reshape(cfg.heads, HD)
+                    kh = c[D:2 * D].reshape(cfg.heads, HD)
+                    vh = c[2 * D:].reshape(cfg.heads, HD)
+                    qh = qh / np.sqrt(np.sum(qh * qh, axis=1, keepdims=True) + 1e-6) / np.sqrt(HD)
+                    kh = kh / np.sqrt(np.sum(kh * kh, axis=1, keepdims=True) + 1e-6)
+                    ab = ab_all[t]
+                    out = np.empty((cfg.heads, HD))
+                    for hh in range(cfg.heads):
+                        alpha = np.exp(-np.exp(float(ex["A_log"][hh])) * _softplus(ab[hh] + float(ex["dt_bias"][hh])))
+                        beta = 1.0 / (1.0 + np.exp(-ab[cfg.heads + hh]))
+                        Sh = S[hh]
+                        a_v = kh[hh] @ Sh
+                        c_v = qh[hh] @ Sh
+                        u = beta * (vh[hh] - alpha * a_v)
+                        o = alpha * c_v + (kh[hh] @ qh[hh]) * u
+                        S[hh] = alpha * Sh + np.outer(kh[hh], u)
+                        on = o / np.sqrt(np.mean(o * o) + cfg.eps)
+                        out[hh] = on * ex["gnorm"] * _silu(z[hh])
+                    mix[t] = out.reshape(D).astype(np.float32)
+            h = (h + self._mm(mix, M["o"])).astype(np.float32)
+            xn = _rms(h, lw.post_norm, cfg.eps).astype(np.float32)
+            gu = np.concatenate([self._mm(xn, M["gate"]), self._mm(xn, M["up"])], axis=1).astype(np.float64)
+            act = (_silu(gu[:, :cfg.ffn]) * gu[:, cfg.ffn:]).astype(np.float32)
+            h = (h + self._mm(act, M["down"])).astype(np.float32)
+            residuals.append(h.copy())
+        xn = _rms(h, self.w.final_norm, cfg.eps).astype(np.float32).astype(np.float64)
+        logits = np.empty((T, cfg.vocab), np.float32)
+        for r0 in range(0, cfg.vocab, 16384):  # bounded temporaries over the tied head
+            r1 = min(cfg.vocab, r0 + 16384)
+            logits[:, r0:r1] = (xn @ E[r0:r1].astype(np.float64).T).astype(np.float32)
+        return residuals, logits
+

@@ -74,3 +74,25 @@ def test_decode_step_detection():
     assert not one_row_each([0, 1, 1, 2])     # a sequence granted no row
     assert not one_row_each([0, 1, 5])        # a decode row beside a prefill chunk
     assert not one_row_each([0])              # no sequence
+
+
+def test_streaming_oracle_agrees_with_token_by_token_oracle(oracle):
+    """The teacher-forced, layer-by-layer oracle (packed products through the restated reference
+    operator, nothing dense kept) against the token-by-token oracle on dense reconstructed weights:
+    the same logits up to the operator's activation rounding (2e-3 of max|l|), on a 4-layer model
+    with both mixers."""
+    import numpy as np
+
+    from exl3_b200.hybrid import HybridConfig, synthetic_weights
+    from oracle.hybrid_model import OracleHybrid, StreamingOracleHybrid
+
+    cfg = HybridConfig(layers=4, hidden=256, ffn=512, vocab=512, heads=2, kv_heads=1)
+    w = synthetic_weights(cfg, seed=7)
+    tokens = np.random.default_rng(8).integers(0, cfg.vocab, 6)
+    dense = OracleHybrid(w, oracle)
+    seq = dense.new_sequence()
+    want = np.stack([dense.step(seq, int(t), p) for p, t in enumerate(tokens)])
+    residuals, got = StreamingOracleHybrid(w, oracle, nth=2).run(tokens)
+    assert len(residuals) == cfg.layers and residuals[-1].shape == (len(tokens), cfg.hidden)
+    assert got.shape == want.shape
+    assert np.max(np.abs(got - want)) / np.max(np.abs(want)) <= 2e-3

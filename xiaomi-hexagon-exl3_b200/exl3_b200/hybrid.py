@@ -336,10 +336,12 @@ class HybridEngine:
     def _mm(self, w, x, out, rows, st, form: int = 0, nw=None, accum: bool = False, x_ss=None, y_ss=None):
         self._mm_batch(("_one",), {"_one": w}, x, [out], rows, st, form, nw, accum, x_ss, y_ss)
 
-    def forward(self, rows: int, n_seq: int, nout: int, stream=None, feedback=None) -> bool:
+    def forward(self, rows: int, n_seq: int, nout: int, stream=None, feedback=None, trace=None) -> bool:
         """Run the step whose metadata is in self.meta.dev; next tokens land in self.out_tokens[:nout].
         feedback = (next_tokens, next_pos, log, counter) asks the head to feed the tokens back on the
-        device (exl3cu_hyb_head_feedback); returns whether it did (steps of <= 8 rows only)."""
+        device (exl3cu_hyb_head_feedback); returns whether it did (steps of <= 8 rows only).
+        trace (a list, steps of more than 8 rows): receives every layer's residual stream [rows, H] as
+        f32 copies, for layer-by-layer comparisons with a reference."""
         torch, cfg, L = self.torch, self.cfg, self.L
         st = ctypes.c_void_p((stream or torch.cuda.current_stream()).cuda_stream)
         H, F, D, KV = cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim, self.KV
@@ -353,7 +355,7 @@ class HybridEngine:
             self._pf_events[0].record(main)
             self._pf_stream.wait_event(self._pf_events[0])
             check(L.exl3cu_prefetch_l2(n0, a0, ctypes.c_void_p(self._pf_stream.cuda_stream)))
-        fused = rows <= 8 and self.fused
+        fused = rows <= 8 and self.fused and trace is None
         check(L.exl3cu_hyb_embed(_vp(self.embed), cfg.vocab, _vp(tokens), rows, H, _vp(self.h),
                                  _vp(self.h_ss) if fused else None, st))
         scale = 1.0 / float(np.sqrt(cfg.head_dim))
@@ -402,6 +404,9 @@ class HybridEngine:
             check(L.exl3cu_hyb_swiglu(_vp(self.gu), rows, F, _vp(self.act), st))
             self._mm(mats["down"], self.act, self.down, rows, st)
             delta = self.down
+            if trace is not None:
+                with torch.cuda.stream(main):
+                    trace.append((self.h[:rows] + self.down[:rows]).float().clone())
         check(L.exl3cu_hyb_rmsnorm(_vp(self.h), _vp(delta), H, _vp(self.final_norm), cfg.eps, rows, H, _vp(self.xn),
                                    st))
         check(L.exl3cu_hyb_head(_vp(self.xn), _vp(logit_rows), nout, H, None, cfg.eps, _vp(self.embed), cfg.vocab,
