@@ -201,20 +201,6 @@ def step_launcher(ops, stack, pattern, stream):
             for w, x, y in calls:
                 w.mul_mat(x, out=y, stream=stream)
         return run, len(calls)
-    if pattern == "sequence":
-        # one persistent launch per step with the decoder pattern's 112 dependent groups
-        ws, xs, ys, gs = [], [], [], []
-        for li, mats in enumerate(stack):
-            for gi, grp in enumerate(DECODER_GROUPS):
-                for name in grp:
-                    ws.append(mats[name]["w"])
-                    xs.append(mats[name]["x"])
-                    ys.append(mats[name]["y"])
-                    gs.append(4 * li + gi)
-
-        def run():
-            ops.mul_mat_sequence(ws, xs, ys, groups=gs, depend=True, stream=stream)
-        return run, 1
     if pattern == "layer":
         groups = [list(mats.values()) for mats in stack]
     else:
@@ -981,7 +967,7 @@ def main(argv=None):
     patterns = {"decoder": {"launches_per_step": launches, "ms_per_step": round(ms_step, 5),
                             "gbs_per_gpu": round(value / world, 1)}}
     side_steps = max(20, args.steps // 4)
-    for pat in ("matrix", "layer", "sequence"):
+    for pat in ("matrix", "layer"):
         pms, pl = time_pattern(torch, dist, ops, stack, pat, side_steps, 5, world)
         pms = max_over_ranks(pms) / side_steps
         patterns[pat] = {"launches_per_step": pl, "ms_per_step": round(pms, 5),

@@ -130,20 +130,6 @@ int exl3cu_mul_mat_batch(size_t count, const exl3cu_weight * const * weights, co
                          const int * x_dtype, const size_t * rows, const size_t * x_row_stride, float * const * d_y,
                          const size_t * y_row_stride, void * stream);
 
-/* A sequence of up to 256 problems in one persistent launch: y_i = x_i . W_i
- * with 1..4 rows each, for mul1 weights of one bit width (2..8) on one device.
- * group[i] (non-decreasing) orders the work: with depend != 0 a problem of a
- * group reads its x only after every problem of the previous group has
- * stored its y, so a later group may consume an earlier group's output (a
- * decode step: q,k,v | o | gate,up | down of each layer, the attention and
- * activation between them done elsewhere).  Weights of later problems stream
- * while earlier groups compute.  Same numerics as exl3cu_mul_mat.  No
- * counterpart in the reference (its graph runs one operator call per matmul). */
-int exl3cu_mul_mat_sequence(size_t count, const exl3cu_weight * const * weights, const void * const * d_x,
-                            const int * x_dtype, const size_t * rows, const size_t * x_row_stride,
-                            float * const * d_y, const size_t * y_row_stride, const int * group, int depend,
-                            void * stream);
-
 /* No counterpart in the reference.  exl3cu_mul_mat_batch with the layer glue of a
  * decoder folded into the operator: per item an input form (EXL3CU_F32,
  * EXL3CU_F16, EXL3CU_X_GLU: SwiGLU of a [gate | up] row computed on load,
@@ -224,15 +210,6 @@ int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, si
  * pinned.  Staging buffers are owned by the handle. */
 int exl3cu_mul_mat_host(exl3cu_weight * w, const void * h_x, int x_dtype, size_t rows, size_t x_row_stride,
                         float * h_y, size_t y_row_stride, int synchronize, void * stream);
-
-/* No counterpart in the reference.  Hint the GPU to bring the packed weights
- * (and scales) of `count` handles (at most 21, one device) into L2, on
- * `stream`: a one-warp kernel issuing bulk L2 prefetches, which waits for
- * nothing and changes no data.  A decoder issues it on a side stream for the
- * next layer's matrices while the current layer runs, so that the next
- * launches read their weights from L2 (126 MB) and the HBM stream overlaps the
- * dependency chain. */
-int exl3cu_prefetch_l2(size_t count, const exl3cu_weight * const * weights, void * stream);
 
 /* EXL3 get_rows (replaces ggml_exl3_get_rows, src/exl3-ggml.cpp:19-49; the
  * reference patch dispatches GET_ROWS on an EXL3 src0 to it,

@@ -25,7 +25,7 @@ GGML_LIB = PKG / "libexl3cu_ggml.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_SOURCES = ["exl3cu_api.cu", "exl3cu_kernels.cu", "exl3cu_gemv.cu", "exl3cu_gemv_cluster.cu", "exl3cu_gemv_mul1.cu",
-                "exl3cu_gemm_tc.cu", "exl3cu_gemv_persist.cu", "exl3cu_model.cu",
+                "exl3cu_gemm_tc.cu", "exl3cu_model.cu",
                 "exl3cu_hybrid.cu", "exl3cu_peers.cu"]
 CXX_SOURCES = ["exl3_codec_host.cpp"]
 HEADERS = ["exl3cu_internal.h", "exl3cu_decode.cuh", "exl3cu_common.cuh", "exl3cu_async.cuh", "exl3cu_mul1.cuh",

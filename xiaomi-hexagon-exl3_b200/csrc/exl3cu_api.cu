@@ -668,13 +668,12 @@ int exl3cu_device_status(int device, unsigned * status, int clear) {
     DeviceGuard guard(device);
     if (!guard.ok) return fail(EXL3CU_INVALID_ARGUMENT, "cannot select device %d", device);
     CU_TRY(cudaDeviceSynchronize(), "synchronising before reading the device status");
-    unsigned gemv = 0, gemm = 0, seq = 0, rows = 0, peers = 0;
+    unsigned gemv = 0, gemm = 0, rows = 0, peers = 0;
     CU_TRY(peer_read_status(&peers, clear != 0), "reading the peer-exchange status word");
     CU_TRY(mul1_read_status(&gemv, clear != 0), "reading the GEMV status word");
     CU_TRY(gemm_read_status(&gemm, clear != 0), "reading the GEMM status word");
-    CU_TRY(seq_read_status(&seq, clear != 0), "reading the sequence status word");
     CU_TRY(rows_read_status(&rows, clear != 0), "reading the get_rows status word");
-    *status = gemv | gemm | seq | rows | peers;
+    *status = gemv | gemm | rows | peers;
     return EXL3CU_OK;
 }
 
@@ -788,138 +787,6 @@ int exl3cu_mul_mat_ragged(const exl3cu_weight * w, const void * d_x, int x_dtype
     return run_gemm(item, static_cast<cudaStream_t>(stream), d_row_offsets + n_seq);
 }
 
-int exl3cu_mul_mat_sequence(size_t count, const exl3cu_weight * const * weights, const void * const * d_x,
-                            const int * x_dtype, const size_t * rows, const size_t * x_row_stride,
-                            float * const * d_y, const size_t * y_row_stride, const int * group, int depend,
-                            void * stream) {
-    if (!count) return EXL3CU_OK;
-    if (count > size_t(kSeqMaxProblems))
-        return fail(EXL3CU_INVALID_ARGUMENT, "at most %d problems per sequence", kSeqMaxProblems);
-    if (!weights || !d_x || !x_dtype || !rows || !x_row_stride || !d_y || !y_row_stride || !group)
-        return fail(EXL3CU_INVALID_ARGUMENT, "sequence arrays must not be NULL");
-    const exl3cu_weight * w0 = weights[0];
-    if (!w0) return fail(EXL3CU_INVALID_ARGUMENT, "weight 0 is NULL");
-    const unsigned bits = w0->bits;
-    static SeqArgs args;  // ~25 KB: kept off the stack; guarded by the mutex below
-    static std::mutex args_mu;
-    std::lock_guard<std::mutex> lock(args_mu);
-    std::memset(&args, 0, sizeof(args));
-    int ngroups = 0, prev_group = 0;
-    for (size_t i = 0; i < count; ++i) {
-        const exl3cu_weight * w = weights[i];
-        int rc = validate_mm(w, d_x[i], x_dtype[i], rows[i], x_row_stride[i], d_y[i], y_row_stride[i]);
-        if (!rc && (w->codebook != EXL3CU_CB_MUL1 || w->bits != bits || bits < 2 || w->device != w0->device))
-            rc = fail(EXL3CU_NO_SUPPORT, "a sequence takes mul1 weights of one bit width (2..8) on one device");
-        if (!rc && rows[i] > 4) rc = fail(EXL3CU_INVALID_ARGUMENT, "a sequence takes 1..4 rows per problem");
-        if (!rc && (i > 0 && group[i] < prev_group))
-            rc = fail(EXL3CU_INVALID_ARGUMENT, "group ids must not decrease along the sequence");
-        if (!rc && (x_row_stride[i] > size_t(INT32_MAX) || y_row_stride[i] > size_t(INT32_MAX)))
-            rc = fail(EXL3CU_NO_SUPPORT, "row strides above 2^31 elements");
-        if (!rc) rc = check_device_ptr(d_x[i], w->device, "x");
-        if (!rc) rc = check_device_ptr(d_y[i], w->device, "y");
-        if (rc) {
-            std::string why = g_last_error;
-            return fail(rc, "sequence item %zu: %s", i, why.c_str());
-        }
-        if (i == 0 || group[i] != prev_group) ++ngroups;
-        if (ngroups > kSeqMaxGroups) return fail(EXL3CU_INVALID_ARGUMENT, "at most %d groups", kSeqMaxGroups);
-        prev_group = group[i];
-        SeqProblem & P = args.prob[i];
-        P.lsc = w->lsc;
-        P.su = w->su;
-        P.sv = w->sv;
-        P.x = d_x[i];
-        P.y = d_y[i];
-        P.x_stride = int(x_row_stride[i]);
-        P.y_stride = int(y_row_stride[i]);
-        P.nchunks = int(w->k / 16);
-        P.nblocks = int(w->nblocks);
-        P.rows = int(rows[i]);
-        P.x_f16 = x_dtype[i] == EXL3CU_F16;
-        P.group = ngroups - 1;
-        args.group_need[ngroups - 1] += P.nblocks;
-    }
-    DeviceGuard guard(w0->device);
-    // K split per group: the split count (1..16, <= 256 chunks per CTA) that minimises the most
-    // work any resident CTA does for the group (units are dealt round robin)
-    auto plan = [&](int grid) {
-        std::vector<int> per_group(ngroups, 1);
-        for (int g = 0; g < ngroups; ++g) {
-            long long best = -1;
-            for (int per = 1; per <= kSeqMaxSplits; ++per) {
-                long long units = 0, worst_chunks = 0;
-                bool ok = true;
-                for (size_t i = 0; i < count; ++i) {
-                    const SeqProblem & P = args.prob[i];
-                    if (P.group != g) continue;
-                    int cps = std::max(8, ((P.nchunks + per - 1) / per + 7) / 8 * 8);
-                    if (cps > 256) ok = false;
-                    units += (long long)P.nblocks * ((P.nchunks + cps - 1) / cps);
-                    worst_chunks = std::max<long long>(worst_chunks, cps);
-                }
-                if (!ok) continue;
-                // a unit's fixed cost (activation prologue, partial hand-off, epilogue) is worth about
-                // 48 chunks of decode; CTAs take ceil(units / grid) units each
-                const long long load = (units + grid - 1) / grid * (worst_chunks + 48);
-                if (best < 0 || load < best) {
-                    best = load;
-                    per_group[g] = per;
-                }
-            }
-        }
-        int units = 0, cus = 0, cps_max = 8;
-        long long slot = 0;
-        for (size_t i = 0; i < count; ++i) {
-            SeqProblem & P = args.prob[i];
-            const int per = per_group[P.group];
-            int cps = std::max(8, ((P.nchunks + per - 1) / per + 7) / 8 * 8);
-            P.cps = cps;
-            P.splits = (P.nchunks + cps - 1) / cps;
-            P.unit_base = units;
-            P.cu_base = cus;
-            P.slot_base = slot;
-            units += P.nblocks * P.splits;
-            cus += P.nblocks;
-            if (P.splits > 1) slot += (long long)P.nblocks * P.splits * P.rows * 128;
-            cps_max = std::max(cps_max, cps);
-        }
-        args.nunits = units;
-        args.cps_max = cps_max;
-        return std::make_tuple(cus, slot);
-    };
-    int grid = w0->sms;
-    auto [cus, slot_floats] = plan(grid);
-    size_t smem = seq_smem_bytes(bits, args.cps_max);
-    const int resident = seq_resident_ctas(w0->device, bits, smem, w0->sms);
-    if (resident <= 0) return fail(EXL3CU_NO_SUPPORT, "sequence plan needs %zu bytes of shared memory per CTA", smem);
-    if (resident != grid) {
-        std::tie(cus, slot_floats) = plan(resident);
-        const size_t smem2 = seq_smem_bytes(bits, args.cps_max);
-        if (seq_resident_ctas(w0->device, bits, smem2, w0->sms) >= resident) {
-            grid = resident;
-            smem = smem2;
-        } else {
-            std::tie(cus, slot_floats) = plan(grid);
-        }
-    }
-    args.nprob = int(count);
-    args.ngroups = ngroups;
-    args.depend = depend ? 1 : 0;
-    const size_t counters = (size_t(cus) + size_t(ngroups) + 1) * sizeof(unsigned);
-    const size_t counters_al = (counters + 255) & ~size_t(255);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    void * ws = nullptr;
-    int rc = gemm_scratch(w0->device, st, counters_al + size_t(slot_floats) * sizeof(float), &ws);
-    if (rc) return rc;
-    args.tickets = static_cast<unsigned *>(ws);
-    args.group_done = args.tickets + cus;
-    args.abort = args.group_done + ngroups;
-    args.slots = reinterpret_cast<float *>(static_cast<char *>(ws) + counters_al);
-    CU_TRY(cudaMemsetAsync(ws, 0, counters, st), "clearing the sequence counters");
-    CU_TRY(launch_gemv_persist(args, bits, grid, smem, st), "launching the persistent EXL3 GEMV");
-    return EXL3CU_OK;
-}
-
 int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
                       float * d_y, size_t y_row_stride, void * d_workspace, size_t workspace_bytes, void * stream) {
     int rc = validate_mm(w, d_x, x_dtype, rows, x_row_stride, d_y, y_row_stride);
@@ -936,30 +803,6 @@ int exl3cu_mul_mat_ws(const exl3cu_weight * w, const void * d_x, int x_dtype, si
     DeviceGuard guard(w->device);
     return run_mm(w, d_x, x_dtype, rows, x_row_stride, d_y, y_row_stride, d_workspace,
                   static_cast<cudaStream_t>(stream));
-}
-
-int exl3cu_prefetch_l2(size_t count, const exl3cu_weight * const * weights, void * stream) {
-    if (!count) return EXL3CU_OK;
-    if (!weights) return fail(EXL3CU_INVALID_ARGUMENT, "weights is NULL");
-    if (count * 3 > size_t(kPrefetchMax))
-        return fail(EXL3CU_INVALID_ARGUMENT, "at most %d weights per prefetch", kPrefetchMax / 3);
-    PrefetchList list{};
-    int dev = -1;
-    for (size_t i = 0; i < count; ++i) {
-        const exl3cu_weight * w = weights[i];
-        if (!w) return fail(EXL3CU_INVALID_ARGUMENT, "weight %zu is NULL", i);
-        if (dev >= 0 && w->device != dev) return fail(EXL3CU_INVALID_ARGUMENT, "weights on different devices");
-        dev = w->device;
-        list.ptr[list.count] = w->lsc;
-        list.bytes[list.count++] = w->nblocks * (w->k / 16) * 256u * w->bits;
-        list.ptr[list.count] = w->su;
-        list.bytes[list.count++] = (w->k * 2) & ~size_t(15);
-        list.ptr[list.count] = w->sv;
-        list.bytes[list.count++] = (w->nblocks * 256) & ~size_t(15);
-    }
-    DeviceGuard guard(dev);
-    CU_TRY(launch_prefetch_l2(list, static_cast<cudaStream_t>(stream)), "launching the L2 prefetch");
-    return EXL3CU_OK;
 }
 
 int exl3cu_get_rows(const exl3cu_weight * w, const int32_t * d_ids, size_t count, float * d_out,

@@ -101,53 +101,6 @@ cudaError_t launch_pack_ragged(int n_seq, const int32_t * want, const int32_t * 
                                int32_t * row_offsets, int32_t * row_seq, int32_t * row_pos, cudaStream_t st);
 cudaError_t gemm_read_status(unsigned * out, bool clear);
 
-// Persistent GEMV over a sequence of problems in dependency groups (exl3cu_gemv_persist.cu).
-constexpr int kSeqMaxProblems = 256;
-constexpr int kSeqMaxGroups = 256;
-constexpr int kSeqMaxSplits = 16;  // K splits per problem in a sequence
-
-struct SeqProblem {
-    const uint32_t * lsc;
-    const __half * su;
-    const __half * sv;
-    const void * x;
-    float * y;
-    long long slot_base;  // floats: this problem's partial slots [nblocks][splits][rows][128]
-    int x_stride;         // elements
-    int y_stride;
-    int nchunks;          // k / 16
-    int nblocks;
-    int cps;              // chunks per split, a multiple of 8
-    int splits;
-    int rows;             // 1..4
-    int x_f16;
-    int group;            // dense group index, non-decreasing over problems
-    int cu_base;          // first column unit (ticket index) of this problem
-    int unit_base;        // first work unit
-    int pad;
-};
-
-struct SeqArgs {
-    SeqProblem prob[kSeqMaxProblems];
-    int group_need[kSeqMaxGroups];  // column blocks per group
-    float * slots;
-    unsigned * tickets;             // [column units], zero at launch
-    unsigned * group_done;          // [groups], zero at launch
-    unsigned * abort;               // one word, zero at launch
-    int nprob;
-    int ngroups;
-    int nunits;
-    int depend;                     // group g waits for group g-1
-    int cps_max;
-    int pad;
-};
-static_assert(sizeof(SeqArgs) <= 32000, "kernel parameter space");
-
-size_t seq_smem_bytes(unsigned bits, int cps_max);
-int seq_resident_ctas(int device, unsigned bits, size_t smem, int sms);
-cudaError_t launch_gemv_persist(const SeqArgs & a, unsigned bits, int grid, size_t smem, cudaStream_t st);
-cudaError_t seq_read_status(unsigned * out, bool clear);
-
 struct GemvPlan {
     int cps;
     int splits;
@@ -168,15 +121,6 @@ cudaError_t launch_trellis_to_lsc(const uint16_t * trellis, size_t k, size_t n, 
 cudaError_t launch_lsc_decode(const uint32_t * lsc, size_t k, size_t nbc, unsigned bits, unsigned cb, uint16_t * out,
                               cudaStream_t st);
 cudaError_t launch_hadamard128(float * v, size_t count, cudaStream_t st);
-// Ranges (16-byte aligned start) to prefetch into L2.
-constexpr int kPrefetchMax = 64;
-struct PrefetchList {
-    const void * ptr[kPrefetchMax];
-    size_t bytes[kPrefetchMax];
-    int count;
-};
-cudaError_t launch_prefetch_l2(const PrefetchList & list, cudaStream_t st);
-
 // out: f32 rows, or fp16 rows (the bits exl3::reconstruct produces) with out_f16.
 cudaError_t launch_get_rows(const uint32_t * lsc, const uint16_t * suh, const uint16_t * svh, size_t k, size_t ncols,
                             unsigned bits, unsigned cb, const int32_t * ids, size_t count, void * out,

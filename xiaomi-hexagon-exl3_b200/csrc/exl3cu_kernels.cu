@@ -225,42 +225,6 @@ __global__ void k_reconstruct_blocks(uint16_t * __restrict__ io, size_t ld, size
 }
 
 // ---------------------------------------------------------------------------
-// L2 prefetch of weight ranges: the ranges are cut into 256 KB pieces and
-// CTA b (thread 0) issues cp.async.bulk.prefetch.L2 for pieces b, b + grid,
-// ... (a hint: no data moves to the SM, nothing is waited on).  One SM's bulk
-// unit alone prefetches at a few hundred GB/s, so the pieces are spread over
-// the grid.  Lets a later launch read its weights from L2 while this stream's
-// HBM traffic overlaps whatever runs in the meantime.
-constexpr size_t kPrefetchPiece = size_t(256) << 10;
-
-__global__ void k_prefetch_l2(const PrefetchList list) {
-    if (threadIdx.x != 0) return;
-    size_t piece = 0;
-    for (int i = 0; i < list.count; ++i) {
-        const size_t n_pieces = (list.bytes[i] + kPrefetchPiece - 1) / kPrefetchPiece;
-        for (size_t q = 0; q < n_pieces; ++q, ++piece) {
-            if (piece % gridDim.x != blockIdx.x) continue;
-            const size_t off = q * kPrefetchPiece;
-            const size_t left = list.bytes[i] - off;
-            const uint32_t n = uint32_t((left > kPrefetchPiece ? kPrefetchPiece : left) & ~size_t(15));
-            if (n) {
-                const char * p = static_cast<const char *>(list.ptr[i]) + off;
-                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(n) : "memory");
-            }
-        }
-    }
-}
-
-cudaError_t launch_prefetch_l2(const PrefetchList & list, cudaStream_t st) {
-    if (list.count <= 0) return cudaSuccess;
-    size_t pieces = 0;
-    for (int i = 0; i < list.count; ++i) pieces += (list.bytes[i] + kPrefetchPiece - 1) / kPrefetchPiece;
-    const unsigned grid = unsigned(pieces < 148 ? (pieces ? pieces : 1) : 148);
-    k_prefetch_l2<<<grid, 32, 0, st>>>(list);
-    return cudaGetLastError();
-}
-
-// ---------------------------------------------------------------------------
 // get_rows (src/exl3-ggml.cpp:19-49): for token id, the original-basis column
 // W[:, id] over all k rows as f32.  One CTA per (id, 128-row group kb), as the
 // reference reconstructs one 128x128 group per (id, kb): the group is decoded

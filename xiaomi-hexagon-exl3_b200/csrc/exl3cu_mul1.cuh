@@ -1,6 +1,6 @@
-// Device helpers shared by the mul1 GEMV kernels (exl3cu_gemv_mul1.cu and
-// exl3cu_gemv_persist.cu): launch constants, the integer tensor-core product
-// and the per-tile trellis state extraction from a lane's LSC segment.
+// Device helpers of the mul1 GEMV (exl3cu_gemv_mul1.cu): launch constants,
+// the integer tensor-core product and the per-tile trellis state extraction
+// from a lane's LSC segment.
 #pragma once
 #include "exl3cu_internal.h"
 

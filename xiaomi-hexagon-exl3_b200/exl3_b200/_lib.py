@@ -27,7 +27,7 @@ EXPORTS = (
     "exl3cu_weight_decode_inner", "exl3cu_mul_mat", "exl3cu_mul_mat_workspace_bytes", "exl3cu_mul_mat_ws",
     "exl3cu_mul_mat_host", "exl3cu_mul_mat_noalloc", "exl3cu_mul_mat_batch",
     "exl3cu_device_status", "exl3cu_gemm_config", "exl3cu_pack_ragged", "exl3cu_mul_mat_ragged",
-    "exl3cu_mul_mat_sequence", "exl3cu_get_rows", "exl3cu_get_rows_host", "exl3cu_prefetch_l2",
+    "exl3cu_get_rows", "exl3cu_get_rows_host",
     "exl3cu_mul_mat_batch_ex",
     "exl3cu_ipc_alloc", "exl3cu_ipc_free", "exl3cu_ipc_open", "exl3cu_ipc_close", "exl3cu_store_peers",
     "exl3cu_wait_peers",
@@ -78,16 +78,12 @@ def _declare(L):
     L.exl3cu_mul_mat_ws.argtypes = [_vp, _vp, _c.c_int, _sz, _sz, _vp, _sz, _vp, _sz, _vp]
     L.exl3cu_mul_mat_host.argtypes = [_vp, _vp, _c.c_int, _sz, _sz, _vp, _sz, _c.c_int, _vp]
     L.exl3cu_get_rows.argtypes = [_vp, _vp, _sz, _vp, _sz, _vp]
-    L.exl3cu_prefetch_l2.argtypes = [_sz, _c.POINTER(_vp), _vp]
     L.exl3cu_get_rows_host.argtypes = [_vp, _vp, _sz, _vp, _sz, _c.c_int, _vp]
     L.exl3cu_mul_mat_noalloc.argtypes = [_vp, _vp, _c.c_int, _sz, _sz, _vp, _sz, _vp]
     L.exl3cu_device_status.argtypes = [_c.c_int, _c.POINTER(_c.c_uint), _c.c_int]
     L.exl3cu_gemm_config.argtypes = [_sz, _c.c_int, _c.c_int]
     L.exl3cu_pack_ragged.argtypes = [_sz, _vp, _vp, _c.c_int32, _vp, _vp, _vp, _vp]
     L.exl3cu_mul_mat_ragged.argtypes = [_vp, _vp, _c.c_int, _sz, _vp, _sz, _sz, _vp, _sz, _vp]
-    L.exl3cu_mul_mat_sequence.argtypes = [_sz, _c.POINTER(_vp), _c.POINTER(_vp), _c.POINTER(_c.c_int),
-                                          _c.POINTER(_sz), _c.POINTER(_sz), _c.POINTER(_vp), _c.POINTER(_sz),
-                                          _c.POINTER(_c.c_int), _c.c_int, _vp]
     L.exl3cu_mul_mat_batch.argtypes = [_sz, _c.POINTER(_vp), _c.POINTER(_vp), _c.POINTER(_c.c_int),
                                        _c.POINTER(_sz), _c.POINTER(_sz), _c.POINTER(_vp), _c.POINTER(_sz), _vp]
     L.exl3cu_mul_mat_batch_ex.argtypes = [_sz, _c.POINTER(_vp), _c.POINTER(_vp), _c.POINTER(_c.c_int),

@@ -279,17 +279,9 @@ class HybridEngine:
         self.out_tokens = torch.zeros(8, dtype=torch.int32, device=dev)
         self.KV = KV
         self._batch_args = {}
-        # L2 prefetch of layer i+1's weights while layer i runs (side stream, joined per step)
-        self.prefetch = os.environ.get("EXL3_HYB_PREFETCH", "0") != "0"  # measured: no gain (see DESIGN)
         self.fused = os.environ.get("EXL3_HYB_FUSED", "1") != "0"  # layer glue folded into the operator
         if os.environ.get("EXL3_GEMM_MIN_ROWS"):  # tuning: rows at which the operator switches to the GEMM
             check(L.exl3cu_gemm_config(int(os.environ["EXL3_GEMM_MIN_ROWS"]), 0, 0))
-        self._pf_args = []
-        for d in self.layers:
-            ws = list(d["mats"].values())
-            self._pf_args.append((len(ws), (ctypes.c_void_p * len(ws))(*[w.handle.value for w in ws])))
-        self._pf_stream = torch.cuda.Stream(device=dev)
-        self._pf_events = [torch.cuda.Event() for _ in range(len(self.layers) + 1)]
 
     # -- slot management --------------------------------------------------------------------------
     def reset_slot(self, slot: int):
@@ -349,28 +341,17 @@ class HybridEngine:
         tokens, row_seq, row_pos = m.view("tokens"), m.view("row_seq"), m.view("row_pos")
         row_offsets, seq_slot, logit_rows = m.view("row_offsets"), m.view("seq_slot"), m.view("logit_rows")
         main = stream or torch.cuda.current_stream()
-        pf = self.prefetch and rows <= 4  # weight-streaming steps only; larger steps are compute-bound
-        if pf:
-            n0, a0 = self._pf_args[0]
-            self._pf_events[0].record(main)
-            self._pf_stream.wait_event(self._pf_events[0])
-            check(L.exl3cu_prefetch_l2(n0, a0, ctypes.c_void_p(self._pf_stream.cuda_stream)))
         fused = rows <= 8 and self.fused and trace is None
         check(L.exl3cu_hyb_embed(_vp(self.embed), cfg.vocab, _vp(tokens), rows, H, _vp(self.h),
                                  _vp(self.h_ss) if fused else None, st))
         scale = 1.0 / float(np.sqrt(cfg.head_dim))
         if fused:
             self._forward_fused(rows, n_seq, nout, st, scale, row_seq, row_pos, row_offsets, seq_slot, logit_rows,
-                                pf, main, feedback)
+                                feedback)
             return feedback is not None
         delta = None
         for li, d in enumerate(self.layers):
             mats = d["mats"]
-            if pf and li + 1 < len(self.layers):
-                n1, a1 = self._pf_args[li + 1]
-                self._pf_events[li + 1].record(main)
-                self._pf_stream.wait_event(self._pf_events[li + 1])
-                check(L.exl3cu_prefetch_l2(n1, a1, ctypes.c_void_p(self._pf_stream.cuda_stream)))
             check(L.exl3cu_hyb_rmsnorm(_vp(self.h), _vp(delta) if delta is not None else None, H, _vp(d["in_norm"]),
                                        cfg.eps, rows, H, _vp(self.xn), st))
             if d["kind"] == "full":
@@ -411,13 +392,9 @@ class HybridEngine:
                                    st))
         check(L.exl3cu_hyb_head(_vp(self.xn), _vp(logit_rows), nout, H, None, cfg.eps, _vp(self.embed), cfg.vocab,
                                 None, _vp(self.best), _vp(self.out_tokens), st))
-        if pf:  # join the prefetch stream (required inside a capture; cheap otherwise)
-            ev = self._pf_events[-1]
-            ev.record(self._pf_stream)
-            main.wait_event(ev)
 
-    def _forward_fused(self, rows, n_seq, nout, st, scale, row_seq, row_pos, row_offsets, seq_slot, logit_rows, pf,
-                       main, feedback=None):
+    def _forward_fused(self, rows, n_seq, nout, st, scale, row_seq, row_pos, row_offsets, seq_slot, logit_rows,
+                       feedback=None):
         """Steps of <= 8 rows: the layer glue folded into the packed operator -- RMSNorm on load for the
         projections (and inside the delta-rule gates), SwiGLU on load for the down projection, the o and
         down products added into the residual stream h -- so a layer is 4 operator launches plus its
@@ -428,11 +405,6 @@ class HybridEngine:
         H, F, D, KV = cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim, self.KV
         for li, d in enumerate(self.layers):
             mats = d["mats"]
-            if pf and li + 1 < len(self.layers):
-                n1, a1 = self._pf_args[li + 1]
-                self._pf_events[li + 1].record(main)
-                self._pf_stream.wait_event(self._pf_events[li + 1])
-                check(L.exl3cu_prefetch_l2(n1, a1, ctypes.c_void_p(self._pf_stream.cuda_stream)))
             if d["kind"] == "full":
                 qkv = self.proj.view(-1)[: self.max_rows * (D + 2 * KV)].view(self.max_rows, D + 2 * KV)
                 outs = [qkv[:, 0:D], qkv[:, D:D + KV], qkv[:, D + KV:D + 2 * KV]]
@@ -476,10 +448,6 @@ class HybridEngine:
         else:
             check(L.exl3cu_hyb_head(_vp(self.h), _vp(logit_rows), nout, H, _vp(self.final_norm), cfg.eps,
                                     _vp(self.embed), cfg.vocab, None, _vp(self.best), _vp(self.out_tokens), st))
-        if pf:
-            ev = self._pf_events[-1]
-            ev.record(self._pf_stream)
-            main.wait_event(ev)
 
     def head_logits(self, nout: int, stream=None):
         """Logits of the last step's logit rows (f32 [nout, vocab]); recomputes the head only."""

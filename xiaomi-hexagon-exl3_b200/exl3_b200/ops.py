@@ -263,38 +263,6 @@ def reconstruct(packed, suh, svh, k: int, n: int, bits: int, codebook: int = CB_
 __all__ = ["Exl3Weight", "mul_mat_batch", "decode_codebook", "decode_inner", "hadamard128", "reconstruct", "_lib"]
 
 
-def mul_mat_sequence(weights, xs, outs=None, groups=None, depend: bool = True, stream=None):
-    """y_i = x_i . W_i for up to 256 problems (1..4 rows each, mul1 weights of one bit width) in one
-    persistent launch (exl3cu_mul_mat_sequence).  groups[i] (non-decreasing) orders the work: with
-    `depend`, a group reads its inputs only after the previous group stored its outputs."""
-    n = len(weights)
-    if len(xs) != n:
-        raise ValueError("one activation tensor per weight")
-    if groups is None:
-        groups = list(range(n))
-    xs2 = []
-    for x in xs:
-        if x.dtype not in (torch.float32, torch.float16):
-            raise TypeError("x must be float32 or float16")
-        x2 = x.reshape(-1, x.shape[-1])
-        if x2.stride(-1) != 1:
-            raise ValueError("x rows must be contiguous")
-        xs2.append(x2)
-    if outs is None:
-        outs = [torch.empty((x.shape[0], w.n), dtype=torch.float32, device=x.device) for w, x in zip(weights, xs2)]
-    VP = ctypes.c_void_p * n
-    SZ = ctypes.c_size_t * n
-    IN = ctypes.c_int * n
-    check(lib().exl3cu_mul_mat_sequence(
-        n, VP(*[w.handle.value for w in weights]), VP(*[x.data_ptr() for x in xs2]),
-        IN(*[F32 if x.dtype == torch.float32 else F16 for x in xs2]), SZ(*[x.shape[0] for x in xs2]),
-        SZ(*[x.stride(0) for x in xs2]), VP(*[o.data_ptr() for o in outs]), SZ(*[o.stride(0) for o in outs]),
-        IN(*[int(g) for g in groups]), int(bool(depend)), _stream_handle(stream)))
-    return outs
-
-
-# -- ragged batches -----------------------------------------------------------------------------
-
 def pack_ragged(want: torch.Tensor, pos: torch.Tensor, max_rows: int, stream=None,
                 out: tuple | None = None):
     """GPU-side packer (exl3cu_pack_ragged): sequence i is granted min(want[i], rows left of
