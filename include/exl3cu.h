@@ -265,9 +265,15 @@ int exl3cu_mul_mat_noalloc(const exl3cu_weight * w, const void * d_x, int x_dtyp
  *   then, when d_out is not NULL, copies the finished half of this rank's y
  *   (rows x cols) into d_out.  Bounded: after about a second it sets bit 0
  *   of exl3cu_device_status and returns.
- * Both read the epoch on the device, so a call sequence can be captured in a
- * CUDA graph and replayed.  Columns, strides and offsets are multiples of 4
- * floats; npeers <= 8. */
+ * exl3cu_mul_mat_peers: the operator of this rank's slice (handle w) with the
+ *   store above: y = x . W_local goes into every rank's buffer and the epoch
+ *   is published.  For 1..4 rows of mul1 weights this is one launch: the
+ *   GEMV's epilogue stores its output blocks to the peers over NVLink and its
+ *   last block publishes the epoch.  Other operands run the operator into
+ *   d_slice (row stride slice_stride) and then exl3cu_store_peers.
+ * All of them read the epoch on the device, so a call sequence can be
+ * captured in a CUDA graph and replayed.  Columns, strides and offsets are
+ * multiples of 4 floats; npeers <= 8. */
 int exl3cu_ipc_alloc(int device, size_t bytes, void ** out_ptr, void * out_handle);
 int exl3cu_ipc_free(int device, void * ptr);
 int exl3cu_ipc_open(int device, const void * handle, void ** out_ptr);
@@ -277,6 +283,10 @@ int exl3cu_store_peers(const float * d_slice, size_t rows, size_t cols, size_t s
                        unsigned * const * d_state_peers, int rank, void * stream);
 int exl3cu_wait_peers(const unsigned * d_state, int npeers, const float * d_y, size_t y_row_stride, size_t y_half,
                       float * d_out, size_t out_row_stride, size_t rows, size_t cols, void * stream);
+int exl3cu_mul_mat_peers(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
+                         float * d_slice, size_t slice_stride, int npeers, float * const * d_y_peers,
+                         size_t y_row_stride, size_t y_half, size_t y_col0, unsigned * const * d_state_peers, int rank,
+                         void * stream);
 
 /* ------------------------------------------------------------------------
  * Model loader (replaces exl3::Model's constructor, src/exl3_model.cpp:79-157,

@@ -363,7 +363,7 @@ int run_gemm(const MmItem & it, cudaStream_t st, const int32_t * m_dev = nullptr
 // together, at most kMaxBatch per launch, in the order given.  Operands with
 // gemm_min_rows() rows or more run on the tensor-core GEMM instead, one
 // launch pair each.
-int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
+int run_cluster(const MmItem * items, size_t count, cudaStream_t st, const PeerOut * peer = nullptr) {
     std::vector<MmItem> gemv_items;
     gemv_items.reserve(count);
     for (size_t i = 0; i < count; ++i) {
@@ -454,6 +454,10 @@ int run_cluster(const MmItem * items, size_t count, cudaStream_t st) {
             max_rows = s.rows > max_rows ? s.rows : max_rows;
         }
         b.count = int(group.size());
+        if (peer) {  // one 1..4-row mul1 problem (checked by the caller)
+            b.peer_on = 1;
+            b.peer = *peer;
+        }
         if (cb == EXL3CU_CB_MUL1 && mul1_supported(bits, max_rows)) {
             DeviceGuard guard(device);
             cudaError_t e = launch_gemv_mul1(b, units, subs[i].w->sms, device, bits, pdl_enabled(), st);
@@ -961,8 +965,55 @@ extern "C" int exl3cu_mul_mat_noalloc(const exl3cu_weight * w, const void * d_x,
 }
 
 // ---------------------------------------------------------------------------
+// The operator of one rank of a column split, with its all-gather: y = x . W_local stored into
+// every rank's y buffer over NVLink (half (E & 1) for this rank's E-th call), then the epoch
+// published to every rank.  1..4 rows of mul1 weights: one launch, the GEMV's epilogue storing to
+// the peers.  Otherwise the operator writes d_slice and exl3cu_store_peers sends it.
+extern "C" int exl3cu_mul_mat_peers(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows,
+                                    size_t x_row_stride, float * d_slice, size_t slice_stride, int npeers,
+                                    float * const * d_y_peers, size_t y_row_stride, size_t y_half, size_t y_col0,
+                                    unsigned * const * d_state_peers, int rank, void * stream) {
+    if (npeers < 1 || npeers > kMaxPeers || rank < 0 || rank >= npeers)
+        return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: 1..%d ranks and 0 <= rank < npeers", kMaxPeers);
+    if (!d_y_peers || !d_state_peers) return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: NULL peer arrays");
+    if (y_row_stride % 4 || y_half % 4 || y_col0 % 4)
+        return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: y strides and offsets must be multiples of 4 floats");
+    if (!w) return fail(EXL3CU_INVALID_ARGUMENT, "weight handle is NULL");
+    const size_t n_local = w->nblocks * 128;
+    if (y_row_stride < y_col0 + n_local || y_half < rows * y_row_stride)
+        return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: the slice does not fit the peers' y buffers");
+    PeerOut po{};
+    for (int p = 0; p < npeers; ++p) {
+        if (!d_y_peers[p] || !d_state_peers[p]) return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: NULL peer");
+        po.y[p] = d_y_peers[p];
+        po.state[p] = d_state_peers[p];
+    }
+    po.y_stride = (long long)y_row_stride;
+    po.y_half = (long long)y_half;
+    po.y_col0 = (long long)y_col0;
+    po.npeers = npeers;
+    po.rank = rank;
+    const bool fused = w->codebook == EXL3CU_CB_MUL1 && rows >= 1 && rows < gemm_min_rows() &&
+                       mul1_supported(w->bits, int(rows < 64 ? rows : 64));
+    if (fused) {
+        int rc = validate_mm(w, d_x, x_dtype, rows, x_row_stride, d_y_peers[rank] + y_col0, y_row_stride);
+        if (rc) return rc;
+        if ((rc = check_device_ptr(d_x, w->device, "x"))) return rc;
+        const MmItem item{w, d_x, x_dtype, rows, x_row_stride, d_y_peers[rank] + y_col0, y_row_stride};
+        return run_cluster(&item, 1, static_cast<cudaStream_t>(stream), &po);
+    }
+    if (!d_slice) return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: this operand needs d_slice");
+    int rc = exl3cu_mul_mat(w, d_x, x_dtype, rows, x_row_stride, d_slice, slice_stride, stream);
+    if (rc) return rc;
+    return exl3cu_store_peers(d_slice, rows, n_local, slice_stride, npeers, d_y_peers, y_row_stride, y_half, y_col0,
+                              d_state_peers, rank, stream);
+}
+
+// ---------------------------------------------------------------------------
 // Internal hooks for the other C-ABI translation units (the model loader).
 namespace exl3cu {
+
+bool pdl_launch_enabled() { return pdl_enabled(); }
 
 int api_fail(int status, const char * message) { return fail(status, "%s", message); }
 

@@ -27,6 +27,10 @@
 // multicast) on mbarriers; eight consumer warps decode from shared memory.
 // The K split runs across a thread-block cluster and is reduced through
 // distributed shared memory by cluster rank 0, which applies H128 and sv.
+// With a peer output (a column split over GPUs) rank 0 of every column block
+// stores its y block into every rank's buffer over NVLink, and the last block
+// to finish publishes the call's epoch to every rank: the GEMV and its
+// all-gather are one kernel.
 // Programmatic dependent launch: weights stream before griddepcontrol.wait
 // (marked evict-first in L2, so activations stay there); only the activation
 // prologue waits for the previous kernel.  Warp reductions use redux.sync.
@@ -91,7 +95,7 @@ __host__ __device__ inline Mul1Layout mul1_layout(int bits, int cps, int rows, i
     return L;
 }
 
-template <int BITS>
+template <int BITS, bool PEER>
 __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int CHUNKB = 256 * BITS;
@@ -494,6 +498,10 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             consumer_sync();
         }
         const __half2 s01 = bits_half2(sv_pre.x), s23 = bits_half2(sv_pre.y);
+        // column split over GPUs: this call's epoch picks the half of every rank's y buffer
+        constexpr bool to_peers = PEER;  // a separate build, so the plain kernel carries none of this
+        const unsigned epoch =
+            to_peers ? *reinterpret_cast<const volatile unsigned *>(b.peer.state[b.peer.rank] + kPeerEpochWord) + 1u : 0u;
         for (int r = warp; r < rows; r += kMW) {
             float v[4];
 #pragma unroll
@@ -511,7 +519,13 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
                 o.z += y_prev.z;
                 o.w += y_prev.w;
             }
-            *yp = o;
+            if constexpr (to_peers) {  // NVLink stores into every rank's y (this rank's own buffer included)
+                const long long off = ((epoch & 1u) ? b.peer.y_half : 0) + r * b.peer.y_stride + b.peer.y_col0 +
+                                      nb * 128 + lane * 4;
+                for (int pi = 0; pi < b.peer.npeers; ++pi) *reinterpret_cast<float4 *>(b.peer.y[pi] + off) = o;
+            } else {
+                *yp = o;
+            }
             if (P.y_ss) {  // this block's sum of squares of the final y, for a later RMSNorm of the row
                 float ss = o.x * o.x;
                 ss = fmaf(o.y, o.y, ss);
@@ -522,6 +536,24 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
                 if (lane == 0) P.y_ss[size_t(r) * P.y_ss_stride + nb] = ss;
             }
         }
+        if constexpr (to_peers) {
+            // the last column block to finish (ticket) publishes the epoch to every rank; the peers'
+            // wait (exl3cu_wait_peers) then finds this rank's whole slice in place
+            consumer_sync();
+            if (threadIdx.x == 0) {
+                unsigned * own = b.peer.state[b.peer.rank];
+                __threadfence_system();  // this block's stores reach every GPU before its ticket
+                if (atomicAdd(own + kPeerTicketWord, 1u) == gridDim.x / unsigned(S) - 1u) {
+                    own[kPeerTicketWord] = 0u;  // every block has arrived (and read the counter)
+                    own[kPeerEpochWord] = epoch;
+                    __threadfence_system();
+                    for (int pi = 0; pi < b.peer.npeers; ++pi)
+                        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(b.peer.state[pi] + b.peer.rank),
+                                     "r"(epoch)
+                                     : "memory");
+                }
+            }
+        }
     }
 }
 
@@ -530,19 +562,19 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
 namespace {
 
 template <int BITS>
-void * mul1_kernel() {
-    return reinterpret_cast<void *>(k_gemv_mul1<BITS>);
+void * mul1_kernel(bool peer) {
+    return peer ? reinterpret_cast<void *>(k_gemv_mul1<BITS, true>) : reinterpret_cast<void *>(k_gemv_mul1<BITS, false>);
 }
 
-void * mul1_kernel_for(unsigned bits) {
+void * mul1_kernel_for(unsigned bits, bool peer = false) {
     switch (bits) {
-        case 2: return mul1_kernel<2>();
-        case 3: return mul1_kernel<3>();
-        case 4: return mul1_kernel<4>();
-        case 5: return mul1_kernel<5>();
-        case 6: return mul1_kernel<6>();
-        case 7: return mul1_kernel<7>();
-        case 8: return mul1_kernel<8>();
+        case 2: return mul1_kernel<2>(peer);
+        case 3: return mul1_kernel<3>(peer);
+        case 4: return mul1_kernel<4>(peer);
+        case 5: return mul1_kernel<5>(peer);
+        case 6: return mul1_kernel<6>(peer);
+        case 7: return mul1_kernel<7>(peer);
+        case 8: return mul1_kernel<8>(peer);
         default: return nullptr;
     }
 }
@@ -556,21 +588,23 @@ bool mul1_prepare(int device, unsigned bits) {
     if (device < 0 || device >= 64 || bits > 8) return false;
     std::lock_guard<std::mutex> g(mu);
     if (done[device][bits]) return true;
-    const void * k = mul1_kernel_for(bits);
-    if (!k) return false;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMul1MaxSmem)) != cudaSuccess)
-        return false;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) return false;
+    for (const bool peer : {false, true}) {
+        const void * k = mul1_kernel_for(bits, peer);
+        if (!k) return false;
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMul1MaxSmem)) != cudaSuccess)
+            return false;
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) return false;
+    }
     done[device][bits] = true;
     return true;
 }
 
 // Clusters of `cs` CTAs with `smem` bytes each that the device holds at once
 // (0 when such a cluster cannot be scheduled at all); cached per key.
-int mul1_active_clusters(int device, unsigned bits, int cs, size_t smem) {
+int mul1_active_clusters(int device, unsigned bits, int cs, size_t smem, bool peer) {
     static std::mutex mu;
-    static std::map<std::tuple<int, unsigned, int, size_t>, int> cache;
-    const auto key = std::make_tuple(device, bits, cs, (smem + 1023) / 1024);
+    static std::map<std::tuple<int, unsigned, int, size_t, bool>, int> cache;
+    const auto key = std::make_tuple(device, bits, cs, (smem + 1023) / 1024, peer);
     {
         std::lock_guard<std::mutex> g(mu);
         auto it = cache.find(key);
@@ -588,7 +622,7 @@ int mul1_active_clusters(int device, unsigned bits, int cs, size_t smem) {
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, mul1_kernel_for(bits), &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, mul1_kernel_for(bits, peer), &cfg) != cudaSuccess) {
         (void)cudaGetLastError();
         n = 0;
     }
@@ -644,7 +678,7 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
                 const int cps = (max_nchunks + cand - 1) / cand;
                 const Mul1Layout L = mul1_layout(int(bits), cps, max_rows, cand, NS, staged);
                 if (L.bytes > kMul1MaxSmem) break;  // fewer splits only grow the per-CTA range
-                const int fit = std::min(mul1_active_clusters(device, bits, cand, L.bytes), cap / cand);
+                const int fit = std::min(mul1_active_clusters(device, bits, cand, L.bytes, b.peer_on != 0), cap / cand);
                 if (fit <= 0) continue;
                 if (!feasible) {
                     feasible = cand;
@@ -689,7 +723,7 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
     cfg.attrs = attrs;
     cfg.numAttrs = pdl ? 2 : 1;
     void * args[] = {&b};
-    return cudaLaunchKernelExC(&cfg, mul1_kernel_for(bits), args);
+    return cudaLaunchKernelExC(&cfg, mul1_kernel_for(bits, b.peer_on != 0), args);
 }
 
 cudaError_t mul1_read_status(unsigned * out, bool clear) {

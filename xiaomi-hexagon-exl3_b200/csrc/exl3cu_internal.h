@@ -58,12 +58,33 @@ constexpr int kXPlain = 0, kXGlu = 1, kXRmsNorm = 2;
 
 constexpr int kMaxBatch = 8;  // problems per launch, passed by value in the kernel parameters
 
+// Peer-memory exchange of a column split (exl3cu_peers.cu, and the mul1 GEMV's epilogue): every
+// rank's state words are [0, kMaxPeers) the last epoch each rank published into this rank,
+// [kPeerTicketWord] an arrival ticket of the kernel that stores this rank's slice (reset by its
+// last CTA), [kPeerEpochWord] this rank's epoch counter.
+constexpr int kMaxPeers = 8;
+constexpr int kPeerTicketWord = kMaxPeers;
+constexpr int kPeerEpochWord = kMaxPeers + 1;
+
+// Where a launch's output also goes: the E-th call stores its y rows into half (E & 1) of every
+// rank's y buffer, then its last CTA publishes E into every rank's state (st.release.sys).
+struct PeerOut {
+    float * y[kMaxPeers];         // every rank's y buffer [2][rows_cap][y_stride] (this rank's included)
+    unsigned * state[kMaxPeers];  // every rank's state words
+    long long y_stride;           // floats between rows of a y buffer
+    long long y_half;             // floats between the two halves
+    long long y_col0;             // this rank's first column in the full row
+    int npeers, rank;
+};
+
 struct GemvBatch {
     GemvProblem prob[kMaxBatch];
     int count;
     int splits;     // cluster size: CTAs per unit along K
     int stages;     // mul1 kernel: weight ring depth (stages of kMW chunks)
     int nw_smem;    // mul1 kernel: RMSNorm weights staged in shared memory before the dependency wait
+    int peer_on;    // mul1 kernel, one problem: y goes to the peers' buffers (`peer`) instead of prob[0].y
+    PeerOut peer;
 };
 
 int choose_cluster_splits(int sms, int nunits, int min_nchunks);
@@ -72,6 +93,7 @@ cudaError_t launch_gemv_cluster(const GemvBatch & b, int nunits, size_t smem, un
                                 cudaStream_t st);
 
 bool mul1_supported(unsigned bits, int rows);
+bool pdl_launch_enabled();  // programmatic dependent launch on (EXL3CU_PDL unset or not "0")
 cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, unsigned bits, bool pdl,
                              cudaStream_t st);
 cudaError_t mul1_read_status(unsigned * out, bool clear);

@@ -25,13 +25,12 @@ namespace exl3cu {
 
 static __device__ unsigned g_peer_status;
 
-constexpr int kMaxPeers = 8;
 constexpr unsigned kPeerWaitRounds = 1u << 20;  // polls of >= ~1 us: about a second
 
 // A rank's state words (its IPC-shared flag buffer): [0, 8) every rank's last
-// epoch, [8] the store kernel's arrival ticket, [9] this rank's epoch counter.
-constexpr int kTicketWord = kMaxPeers;
-constexpr int kEpochWord = kMaxPeers + 1;
+// epoch, [8] the storing kernel's arrival ticket, [9] this rank's epoch counter.
+constexpr int kTicketWord = kPeerTicketWord;
+constexpr int kEpochWord = kPeerEpochWord;
 
 struct PeerArgs {
     float * y[kMaxPeers];         // every rank's y buffer [2][rows_cap][...] (this rank's included)
@@ -50,6 +49,8 @@ struct PeerArgs {
 // (ticket) publishes E in every rank's state and advances the counter.
 __global__ void __launch_bounds__(256) k_store_peers(const PeerArgs a) {
     __shared__ int last;
+    pdl_trigger();
+    pdl_wait_primary();  // the slice is written by the previous kernel
     unsigned * own = a.state[a.rank];
     const unsigned E = *reinterpret_cast<volatile unsigned *>(own + kEpochWord) + 1u;
     const long long half = (E & 1u) ? a.y_half : 0;
@@ -84,6 +85,8 @@ __global__ void __launch_bounds__(256) k_wait_peers(const unsigned * state, int 
                                                     long long y_half, long long y_stride, float * out,
                                                     long long out_stride, int rows, int cols) {
     __shared__ unsigned epoch_s;
+    pdl_trigger();
+    pdl_wait_primary();  // this rank's own storing kernel has finished: only other GPUs are waited for
     if (threadIdx.x == 0) {
         const unsigned E = *reinterpret_cast<const volatile unsigned *>(state + kEpochWord);
         epoch_s = E;
@@ -112,6 +115,21 @@ __global__ void __launch_bounds__(256) k_wait_peers(const unsigned * state, int 
         const int c = int(i - (long long)r * c4) * 4;
         *reinterpret_cast<float4 *>(out + r * out_stride + c) = *reinterpret_cast<const float4 *>(src + r * y_stride + c);
     }
+}
+
+// 256-thread launch, with programmatic dependent launch when it is enabled.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = pdl_launch_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 cudaError_t peer_read_status(unsigned * out, bool clear) {
@@ -216,8 +234,7 @@ int exl3cu_store_peers(const float * d_slice, size_t rows, size_t cols, size_t s
     a.rank = rank;
     const size_t f4 = rows * cols / 4;
     const unsigned grid = unsigned(f4 < 256 ? 1 : (f4 + 255) / 256 < 296 ? (f4 + 255) / 256 : 296);
-    k_store_peers<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch_pdl(k_store_peers, grid, static_cast<cudaStream_t>(stream), a);
     return e == cudaSuccess ? EXL3CU_OK : api_cuda_fail(e, "launching the peer stores");
 }
 
@@ -228,10 +245,9 @@ int exl3cu_wait_peers(const unsigned * d_state, int npeers, const float * d_y, s
         return api_fail(EXL3CU_INVALID_ARGUMENT, "wait_peers: y, strides and columns must be multiples of 4 floats");
     const size_t f4 = d_out ? rows * cols / 4 : 0;
     const unsigned grid = unsigned(f4 < 256 ? 1 : (f4 + 255) / 256 < 148 ? (f4 + 255) / 256 : 148);
-    k_wait_peers<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        d_state, npeers, d_y, (long long)y_half, (long long)y_row_stride, d_out, (long long)out_row_stride, int(rows),
-        int(cols));
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch_pdl(k_wait_peers, grid, static_cast<cudaStream_t>(stream), d_state, npeers, d_y,
+                                     (long long)y_half, (long long)y_row_stride, d_out, (long long)out_row_stride,
+                                     int(rows), int(cols));
     return e == cudaSuccess ? EXL3CU_OK : api_cuda_fail(e, "launching the peer wait");
 }
 

@@ -30,7 +30,7 @@ EXPORTS = (
     "exl3cu_get_rows", "exl3cu_get_rows_host",
     "exl3cu_mul_mat_batch_ex",
     "exl3cu_ipc_alloc", "exl3cu_ipc_free", "exl3cu_ipc_open", "exl3cu_ipc_close", "exl3cu_store_peers",
-    "exl3cu_wait_peers",
+    "exl3cu_wait_peers", "exl3cu_mul_mat_peers",
     "exl3cu_model_open", "exl3cu_model_free", "exl3cu_model_info", "exl3cu_model_matrix_count",
     "exl3cu_model_matrix", "exl3cu_model_find_matrix", "exl3cu_model_head", "exl3cu_model_tensor",
     "exl3cu_model_find_tensor", "exl3cu_model_embedding", "exl3cu_model_embed",
@@ -97,6 +97,8 @@ def _declare(L):
     L.exl3cu_ipc_close.argtypes = [_c.c_int, _vp]
     L.exl3cu_store_peers.argtypes = [_vp, _sz, _sz, _sz, _c.c_int, _vp, _sz, _sz, _sz, _vp, _c.c_int, _vp]
     L.exl3cu_wait_peers.argtypes = [_vp, _c.c_int, _vp, _sz, _sz, _vp, _sz, _sz, _sz, _vp]
+    L.exl3cu_mul_mat_peers.argtypes = [_vp, _vp, _c.c_int, _sz, _sz, _vp, _sz, _c.c_int, _vp, _sz, _sz, _sz, _vp,
+                                       _c.c_int, _vp]
     L.exl3cu_model_open.argtypes = [_c.c_char_p, _c.c_int, _c.c_uint, _P(_vp)]
     L.exl3cu_model_free.argtypes = [_vp]
     L.exl3cu_model_info.argtypes = [_vp, _P(_sz), _P(_sz), _P(_sz), _P(_sz), _P(_sz), _P(_c.c_double)]

@@ -181,11 +181,17 @@ class PeerColumnParallelExl3:
         rows = x.shape[0]
         if rows > self.max_rows:
             raise ValueError(f"{rows} rows > max_rows {self.max_rows}")
-        self.weight.mul_mat(x, out=self.slice[:rows], stream=stream)
+        if x.dtype not in (torch.float32, torch.float16):
+            raise TypeError("x must be float32 or float16")
+        x = x if x.stride(-1) == 1 else x.contiguous()
         sh = _stream_handle(stream)
         cols = self.count * 128
-        _lib.check(self.L.exl3cu_store_peers(self.slice.data_ptr(), rows, cols, cols, self.world, self._yp, self.n,
-                                             self.half, self.first * 128, self._sp, self.rank, sh))
+        # the slice's operator and its all-gather: one launch for 1..4 rows (the GEMV stores its output
+        # blocks into every rank's buffer), else the operator into self.slice plus the peer stores
+        _lib.check(self.L.exl3cu_mul_mat_peers(self.weight.handle, x.data_ptr(), _lib.F32 if x.dtype == torch.float32
+                                               else _lib.F16, rows, x.stride(0), self.slice.data_ptr(), cols,
+                                               self.world, self._yp, self.n, self.half, self.first * 128, self._sp,
+                                               self.rank, sh))
         _lib.check(self.L.exl3cu_wait_peers(ctypes.c_void_p(self.state_own), self.world, ctypes.c_void_p(self.y_own),
                                             self.n, self.half, self.out.data_ptr(), self.n, rows, self.n, sh))
         return self.out[:rows]
