@@ -162,13 +162,19 @@ __global__ void k_tile_x(const void * __restrict__ x, int x_f16, long long x_str
     }
     h128_warp4(v);
     const int tg = tok / ntok, tr = tok - tg * ntok;
-    const int kk = kcol & 15;  // 0, 4, 8 or 12: values go to p, p+1 and p+4, p+5
-    const int p = kperm16(kk);
-    const size_t base = size_t(tg) * ntok * k + size_t(kcol >> 4) * ntok * 16 + (tr >> 3) * 128 + (tr & 7) * 8;
-    __half * dst0 = xt + base + (p >> 3) * 64 + (p & 7);
-    __half * dst1 = xt + base + ((p + 4) >> 3) * 64 + ((p + 4) & 7);
-    *reinterpret_cast<uint32_t *>(dst0) = half2_bits(__floats2half2_rn(v[0], v[1]));
-    *reinterpret_cast<uint32_t *>(dst1) = half2_bits(__floats2half2_rn(v[2], v[3]));
+    // Lane L holds k = 4L..4L+3 of its 16-wide chunk, kk = 4t..4t+3 (t = L & 3), which kperm16 sends
+    // to p = {0,1,4,5} (t = 0), {8,9,12,13} (t = 1), {2,3,6,7} (t = 2), {10,11,14,15} (t = 3).  So lanes
+    // t and t + 2 together hold one 8-half row (p>>3 = t) of the token's core matrix: the t < 2 lane
+    // takes its partner's two half2 and stores the whole row as one 16-byte write.
+    const int t = lane & 3;
+    const uint32_t h01 = half2_bits(__floats2half2_rn(v[0], v[1]));
+    const uint32_t h23 = half2_bits(__floats2half2_rn(v[2], v[3]));
+    const uint32_t q01 = __shfl_xor_sync(0xffffffffu, h01, 2);
+    const uint32_t q23 = __shfl_xor_sync(0xffffffffu, h23, 2);
+    if (t < 2) {
+        const size_t base = size_t(tg) * ntok * k + size_t(kcol >> 4) * ntok * 16 + (tr >> 3) * 128 + (tr & 7) * 8;
+        *reinterpret_cast<uint4 *>(xt + base + t * 64) = make_uint4(h01, q01, h23, q23);
+    }
 }
 
 __device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
