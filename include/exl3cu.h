@@ -253,40 +253,42 @@ int exl3cu_mul_mat_noalloc(const exl3cu_weight * w, const void * d_x, int x_dtyp
  *   writes its 64-byte CUDA IPC handle to out_handle.
  * exl3cu_ipc_open / exl3cu_ipc_close: map / unmap a peer's buffer (from
  *   another process) on `device`.
- * exl3cu_store_peers: this call's epoch E is this rank's device counter + 1;
- *   rows x cols floats of this rank's slice (row stride slice_stride) go into
- *   half (E & 1) of every rank's y buffer (halves y_half floats apart, row
- *   stride y_row_stride) at column y_col0; once the whole slice is stored,
- *   state[rank] = E in every rank's state words (system-scope release) and
- *   the counter advances.  State words (16 per rank, zero-initialised):
- *   [0, 8) the ranks' last epochs, [8] an arrival ticket, [9] the counter.
- * exl3cu_wait_peers: on the stream, until every rank's epoch in d_state has
- *   reached this rank's counter (modulo 2^32: a rank may be one call ahead);
- *   then, when d_out is not NULL, copies the finished half of this rank's y
- *   (rows x cols) into d_out.  Bounded: after about a second it sets bit 0
- *   of exl3cu_device_status and returns.
+ * Exchange protocol: a rank's y buffer holds 8-byte words (epoch << 32 |
+ *   float bits), two halves of rows_cap x y_row_stride words each (y_half
+ *   words apart); its state words (16, zero-initialised) hold an arrival
+ *   ticket [8] and the rank's epoch counter [9].  The E-th call (E = counter
+ *   + 1, read on the device) writes half (E & 1).  Every word is stored with
+ *   one single-copy-atomic 8-byte store, so no fence or flag is needed: a
+ *   reader waits until each word carries this call's epoch.
+ * exl3cu_store_peers: rows x cols floats of this rank's slice (row stride
+ *   slice_stride) go as (E, value) words into half (E & 1) of every rank's y
+ *   buffer at column y_col0 (row stride y_row_stride).
  * exl3cu_mul_mat_peers: the operator of this rank's slice (handle w) with the
- *   store above: y = x . W_local goes into every rank's buffer and the epoch
- *   is published.  For 1..4 rows of mul1 weights this is one launch: the
- *   GEMV's epilogue stores its output blocks to the peers over NVLink and its
- *   last block publishes the epoch.  Other operands run the operator into
- *   d_slice (row stride slice_stride) and then exl3cu_store_peers.
- * All of them read the epoch on the device, so a call sequence can be
- * captured in a CUDA graph and replayed.  Columns, strides and offsets are
- * multiples of 4 floats; npeers <= 8. */
+ *   store above.  For 1..4 rows of mul1 weights this is one launch: the
+ *   GEMV's epilogue stores its output blocks to the peers over NVLink.
+ *   Other operands run the operator into d_slice (row stride slice_stride)
+ *   and then exl3cu_store_peers.
+ * exl3cu_wait_peers: on the stream, waits until every word of rows x cols in
+ *   half (E & 1) of this rank's y carries epoch E, copies the values into
+ *   d_out (row stride out_row_stride; NULL: wait only) and advances the
+ *   counter.  Bounded: after about a second it sets bit 0 of
+ *   exl3cu_device_status, copies what is there and returns.
+ * A rank can be at most one call ahead of another, since its next store
+ * follows its wait for this call.  All of them read the epoch on the device,
+ * so a call sequence can be captured in a CUDA graph and replayed.  Columns,
+ * strides and offsets are multiples of 4; npeers <= 8. */
 int exl3cu_ipc_alloc(int device, size_t bytes, void ** out_ptr, void * out_handle);
 int exl3cu_ipc_free(int device, void * ptr);
 int exl3cu_ipc_open(int device, const void * handle, void ** out_ptr);
 int exl3cu_ipc_close(int device, void * ptr);
 int exl3cu_store_peers(const float * d_slice, size_t rows, size_t cols, size_t slice_stride, int npeers,
-                       float * const * d_y_peers, size_t y_row_stride, size_t y_half, size_t y_col0,
-                       unsigned * const * d_state_peers, int rank, void * stream);
-int exl3cu_wait_peers(const unsigned * d_state, int npeers, const float * d_y, size_t y_row_stride, size_t y_half,
-                      float * d_out, size_t out_row_stride, size_t rows, size_t cols, void * stream);
+                       void * const * d_y_peers, size_t y_row_stride, size_t y_half, size_t y_col0,
+                       const unsigned * d_state, void * stream);
+int exl3cu_wait_peers(unsigned * d_state, const void * d_y, size_t y_row_stride, size_t y_half, float * d_out,
+                      size_t out_row_stride, size_t rows, size_t cols, void * stream);
 int exl3cu_mul_mat_peers(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows, size_t x_row_stride,
-                         float * d_slice, size_t slice_stride, int npeers, float * const * d_y_peers,
-                         size_t y_row_stride, size_t y_half, size_t y_col0, unsigned * const * d_state_peers, int rank,
-                         void * stream);
+                         float * d_slice, size_t slice_stride, int npeers, void * const * d_y_peers,
+                         size_t y_row_stride, size_t y_half, size_t y_col0, const unsigned * d_state, void * stream);
 
 /* ------------------------------------------------------------------------
  * Model loader (replaces exl3::Model's constructor, src/exl3_model.cpp:79-157,

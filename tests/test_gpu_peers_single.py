@@ -5,13 +5,13 @@ rank's y buffer (two halves) and state words are plain device buffers, and
 every rank's "peer pointers" are the same local buffers.  Per call, rank 0's
 and then rank 1's exl3cu_mul_mat_peers run in stream order (each stores its
 slice into both ranks' buffers and publishes its epoch), and only then do the
-two exl3cu_wait_peers run.  Every flag they wait for was set by a kernel that
-already finished, so no kernel waits on another kernel running at the same
-time.  1 and 4 rows take the fused path (the GEMV's epilogue stores to the
+two exl3cu_wait_peers run.  Every word they wait for was stored by a kernel
+that already finished, so no kernel waits on another kernel running at the
+same time.  1 and 4 rows take the fused path (the GEMV's epilogue stores to the
 peers); 8 rows take the operator plus exl3cu_store_peers.  Three calls in a
 row use both halves of the double-buffered y.  Each rank's output is checked
-bit for bit against the 1-GPU operator on the same slice, and the state words
-are checked after the calls.
+bit for bit against the 1-GPU operator on the same slice, and the epoch
+counters and tickets are checked after the calls.
 """
 import ctypes
 
@@ -34,10 +34,9 @@ def test_two_ranks_on_one_gpu_fused_and_fallback(cuda_lib, oracle):
     ws = [Exl3Weight.from_trellis(trellis, suh, svh, device=0, first_block=r * count, block_count=count)
           for r in range(world)]
     half = max_rows * n
-    ys = [torch.zeros(2 * half, dtype=torch.float32, device="cuda") for _ in range(world)]
+    ys = [torch.zeros(2 * half, dtype=torch.int64, device="cuda") for _ in range(world)]  # (epoch, value) words
     states = [torch.zeros(16, dtype=torch.int32, device="cuda") for _ in range(world)]
     yp = (ctypes.c_void_p * world)(*[y.data_ptr() for y in ys])
-    sp = (ctypes.c_void_p * world)(*[s.data_ptr() for s in states])
     slices = [torch.empty((max_rows, count * 128), dtype=torch.float32, device="cuda") for _ in range(world)]
     outs = [torch.empty((max_rows, n), dtype=torch.float32, device="cuda") for _ in range(world)]
     st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
@@ -46,12 +45,12 @@ def test_two_ranks_on_one_gpu_fused_and_fallback(cuda_lib, oracle):
         x = torch.from_numpy(synthetic.activations(rows, k, seed=72 + rows)).cuda()
         for r in range(world):
             _lib.check(L.exl3cu_mul_mat_peers(ws[r].handle, x.data_ptr(), _lib.F16, rows, k, slices[r].data_ptr(),
-                                              count * 128, world, yp, n, half, r * count * 128, sp, r, st))
+                                              count * 128, world, yp, n, half, r * count * 128,
+                                              states[r].data_ptr(), st))
         for r in range(world):
             outs[r].fill_(float("nan"))
-            _lib.check(L.exl3cu_wait_peers(ctypes.c_void_p(states[r].data_ptr()), world,
-                                           ctypes.c_void_p(ys[r].data_ptr()), n, half, outs[r].data_ptr(), n, rows,
-                                           n, st))
+            _lib.check(L.exl3cu_wait_peers(states[r].data_ptr(), ys[r].data_ptr(), n, half, outs[r].data_ptr(), n,
+                                           rows, n, st))
         calls += 1
         torch.cuda.synchronize()
         want = torch.cat([w.mul_mat(x) for w in ws], dim=1)
@@ -62,9 +61,8 @@ def test_two_ranks_on_one_gpu_fused_and_fallback(cuda_lib, oracle):
         assert np.max(np.abs(got - ref)) / np.max(np.abs(ref)) <= 2e-3
     st_words = [s.cpu().numpy() for s in states]
     for r in range(world):
-        assert list(st_words[r][:world]) == [calls] * world  # every rank's epoch reached every rank
-        assert st_words[r][8] == 0                           # the arrival ticket reset itself
-        assert st_words[r][9] == calls                       # this rank's epoch counter
+        assert st_words[r][8] == 0      # the wait kernel's arrival ticket reset itself
+        assert st_words[r][9] == calls  # this rank's epoch counter
     status = ctypes.c_uint(0)
     _lib.check(L.exl3cu_device_status(0, ctypes.byref(status), 1))
     assert status.value == 0

@@ -971,42 +971,43 @@ extern "C" int exl3cu_mul_mat_noalloc(const exl3cu_weight * w, const void * d_x,
 // the peers.  Otherwise the operator writes d_slice and exl3cu_store_peers sends it.
 extern "C" int exl3cu_mul_mat_peers(const exl3cu_weight * w, const void * d_x, int x_dtype, size_t rows,
                                     size_t x_row_stride, float * d_slice, size_t slice_stride, int npeers,
-                                    float * const * d_y_peers, size_t y_row_stride, size_t y_half, size_t y_col0,
-                                    unsigned * const * d_state_peers, int rank, void * stream) {
-    if (npeers < 1 || npeers > kMaxPeers || rank < 0 || rank >= npeers)
-        return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: 1..%d ranks and 0 <= rank < npeers", kMaxPeers);
-    if (!d_y_peers || !d_state_peers) return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: NULL peer arrays");
+                                    void * const * d_y_peers, size_t y_row_stride, size_t y_half, size_t y_col0,
+                                    const unsigned * d_state, void * stream) {
+    if (npeers < 1 || npeers > kMaxPeers) return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: 1..%d ranks", kMaxPeers);
+    if (!d_y_peers || !d_state) return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: NULL peer arrays or state");
     if (y_row_stride % 4 || y_half % 4 || y_col0 % 4)
-        return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: y strides and offsets must be multiples of 4 floats");
+        return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: y strides and offsets must be multiples of 4 words");
     if (!w) return fail(EXL3CU_INVALID_ARGUMENT, "weight handle is NULL");
     const size_t n_local = w->nblocks * 128;
     if (y_row_stride < y_col0 + n_local || y_half < rows * y_row_stride)
         return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: the slice does not fit the peers' y buffers");
     PeerOut po{};
     for (int p = 0; p < npeers; ++p) {
-        if (!d_y_peers[p] || !d_state_peers[p]) return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: NULL peer");
-        po.y[p] = d_y_peers[p];
-        po.state[p] = d_state_peers[p];
+        if (!d_y_peers[p]) return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: NULL peer");
+        po.y[p] = static_cast<unsigned long long *>(d_y_peers[p]);
     }
+    po.own_state = d_state;
     po.y_stride = (long long)y_row_stride;
     po.y_half = (long long)y_half;
     po.y_col0 = (long long)y_col0;
     po.npeers = npeers;
-    po.rank = rank;
     const bool fused = w->codebook == EXL3CU_CB_MUL1 && rows >= 1 && rows < gemm_min_rows() &&
                        mul1_supported(w->bits, int(rows < 64 ? rows : 64));
     if (fused) {
-        int rc = validate_mm(w, d_x, x_dtype, rows, x_row_stride, d_y_peers[rank] + y_col0, y_row_stride);
+        // the operator's own y argument is not written on this path: validate shapes against the slice
+        float * y_unused = d_slice;
+        if (!y_unused) y_unused = reinterpret_cast<float *>(po.y[0]);
+        int rc = validate_mm(w, d_x, x_dtype, rows, x_row_stride, y_unused, n_local);
         if (rc) return rc;
         if ((rc = check_device_ptr(d_x, w->device, "x"))) return rc;
-        const MmItem item{w, d_x, x_dtype, rows, x_row_stride, d_y_peers[rank] + y_col0, y_row_stride};
+        const MmItem item{w, d_x, x_dtype, rows, x_row_stride, y_unused, n_local};
         return run_cluster(&item, 1, static_cast<cudaStream_t>(stream), &po);
     }
     if (!d_slice) return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: this operand needs d_slice");
     int rc = exl3cu_mul_mat(w, d_x, x_dtype, rows, x_row_stride, d_slice, slice_stride, stream);
     if (rc) return rc;
     return exl3cu_store_peers(d_slice, rows, n_local, slice_stride, npeers, d_y_peers, y_row_stride, y_half, y_col0,
-                              d_state_peers, rank, stream);
+                              d_state, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -103,6 +103,25 @@ __device__ __forceinline__ void bulk_g2s_hint(void * dst_smem, const void * src_
         : "memory");
 }
 
+// Peer-exchange words: (epoch << 32 | float bits).  Four values go out as two 16-byte stores
+// whose 8-byte elements are each single-copy atomic at system scope, so a reader on any GPU sees
+// a value together with the epoch it was stored under.  `p` is 16-byte aligned.
+__device__ __forceinline__ void store_pairs4(unsigned long long * p, float4 v, unsigned epoch) {
+    const unsigned long long e = (unsigned long long)epoch << 32;
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(e | __float_as_uint(v.x)),
+                 "l"(e | __float_as_uint(v.y))
+                 : "memory");
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p + 2), "l"(e | __float_as_uint(v.z)),
+                 "l"(e | __float_as_uint(v.w))
+                 : "memory");
+}
+
+__device__ __forceinline__ unsigned long long load_pair(const unsigned long long * p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 

@@ -28,9 +28,9 @@
 // The K split runs across a thread-block cluster and is reduced through
 // distributed shared memory by cluster rank 0, which applies H128 and sv.
 // With a peer output (a column split over GPUs) rank 0 of every column block
-// stores its y block into every rank's buffer over NVLink, and the last block
-// to finish publishes the call's epoch to every rank: the GEMV and its
-// all-gather are one kernel.
+// stores its y block into every rank's buffer over NVLink as self-validating
+// (epoch, value) words: the GEMV and its all-gather are one kernel, with no
+// fence and no flag.
 // Programmatic dependent launch: weights stream before griddepcontrol.wait
 // (marked evict-first in L2, so activations stay there); only the activation
 // prologue waits for the previous kernel.  Warp reductions use redux.sync.
@@ -501,7 +501,7 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
         // column split over GPUs: this call's epoch picks the half of every rank's y buffer
         constexpr bool to_peers = PEER;  // a separate build, so the plain kernel carries none of this
         const unsigned epoch =
-            to_peers ? *reinterpret_cast<const volatile unsigned *>(b.peer.state[b.peer.rank] + kPeerEpochWord) + 1u : 0u;
+            to_peers ? *reinterpret_cast<const volatile unsigned *>(b.peer.own_state + kPeerEpochWord) + 1u : 0u;
         for (int r = warp; r < rows; r += kMW) {
             float v[4];
 #pragma unroll
@@ -519,10 +519,10 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
                 o.z += y_prev.z;
                 o.w += y_prev.w;
             }
-            if constexpr (to_peers) {  // NVLink stores into every rank's y (this rank's own buffer included)
+            if constexpr (to_peers) {  // NVLink stores of (epoch, value) words into every rank's y
                 const long long off = ((epoch & 1u) ? b.peer.y_half : 0) + r * b.peer.y_stride + b.peer.y_col0 +
                                       nb * 128 + lane * 4;
-                for (int pi = 0; pi < b.peer.npeers; ++pi) *reinterpret_cast<float4 *>(b.peer.y[pi] + off) = o;
+                for (int pi = 0; pi < b.peer.npeers; ++pi) store_pairs4(b.peer.y[pi] + off, o, epoch);
             } else {
                 *yp = o;
             }
@@ -534,24 +534,6 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
 #pragma unroll
                 for (int sh = 16; sh; sh >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sh);
                 if (lane == 0) P.y_ss[size_t(r) * P.y_ss_stride + nb] = ss;
-            }
-        }
-        if constexpr (to_peers) {
-            // the last column block to finish (ticket) publishes the epoch to every rank; the peers'
-            // wait (exl3cu_wait_peers) then finds this rank's whole slice in place
-            consumer_sync();
-            if (threadIdx.x == 0) {
-                unsigned * own = b.peer.state[b.peer.rank];
-                __threadfence_system();  // this block's stores reach every GPU before its ticket
-                if (atomicAdd(own + kPeerTicketWord, 1u) == gridDim.x / unsigned(S) - 1u) {
-                    own[kPeerTicketWord] = 0u;  // every block has arrived (and read the counter)
-                    own[kPeerEpochWord] = epoch;
-                    __threadfence_system();
-                    for (int pi = 0; pi < b.peer.npeers; ++pi)
-                        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(b.peer.state[pi] + b.peer.rank),
-                                     "r"(epoch)
-                                     : "memory");
-                }
             }
         }
     }

@@ -58,23 +58,22 @@ constexpr int kXPlain = 0, kXGlu = 1, kXRmsNorm = 2;
 
 constexpr int kMaxBatch = 8;  // problems per launch, passed by value in the kernel parameters
 
-// Peer-memory exchange of a column split (exl3cu_peers.cu, and the mul1 GEMV's epilogue): every
-// rank's state words are [0, kMaxPeers) the last epoch each rank published into this rank,
-// [kPeerTicketWord] an arrival ticket of the kernel that stores this rank's slice (reset by its
-// last CTA), [kPeerEpochWord] this rank's epoch counter.
+// Peer-memory exchange of a column split (exl3cu_peers.cu, and the mul1 GEMV's epilogue).  A rank's
+// y buffer holds (epoch << 32 | float bits) words, [2][rows_cap][y_stride]; its state words are
+// [kPeerTicketWord] the wait kernel's arrival ticket and [kPeerEpochWord] the rank's epoch counter.
 constexpr int kMaxPeers = 8;
-constexpr int kPeerTicketWord = kMaxPeers;
-constexpr int kPeerEpochWord = kMaxPeers + 1;
+constexpr int kPeerTicketWord = 8;
+constexpr int kPeerEpochWord = 9;
 
-// Where a launch's output also goes: the E-th call stores its y rows into half (E & 1) of every
-// rank's y buffer, then its last CTA publishes E into every rank's state (st.release.sys).
+// Where a launch's output also goes: the E-th call (E = counter + 1) stores its y rows as
+// (E, value) words into half (E & 1) of every rank's y buffer.
 struct PeerOut {
-    float * y[kMaxPeers];         // every rank's y buffer [2][rows_cap][y_stride] (this rank's included)
-    unsigned * state[kMaxPeers];  // every rank's state words
-    long long y_stride;           // floats between rows of a y buffer
-    long long y_half;             // floats between the two halves
-    long long y_col0;             // this rank's first column in the full row
-    int npeers, rank;
+    unsigned long long * y[kMaxPeers];  // every rank's y buffer (this rank's included)
+    const unsigned * own_state;         // this rank's state words
+    long long y_stride;                 // words between rows of a y buffer
+    long long y_half;                   // words between the two halves
+    long long y_col0;                   // this rank's first column in the full row
+    int npeers;
 };
 
 struct GemvBatch {

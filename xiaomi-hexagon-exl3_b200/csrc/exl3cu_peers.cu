@@ -1,20 +1,25 @@
 // Peer-memory exchange for the column-split operator (BASELINE configs[4] on
 // 2..8 GPUs, one process per GPU).  It replaces the NCCL all-gather of the
 // output slices: every rank stores its slice of y straight into every peer's
-// y buffer over NVLink (CUDA IPC mappings, plain P2P stores), then raises the
-// call's epoch in every peer's flag word; each rank's wait kernel returns once
-// all ranks' flags show the epoch.  No counterpart in the reference, whose
-// operator (src/exl3-ggml.cpp:51-92) splits columns over CPU threads of one
-// process (`for nb = ith; nb < n/128; nb += nth`, src/exl3-ggml.cpp:74).
+// y buffer over NVLink (CUDA IPC mappings, plain P2P stores), and every rank's
+// wait kernel copies the whole row out of its own buffer once every element of
+// this call has arrived.  No counterpart in the reference, whose operator
+// (src/exl3-ggml.cpp:51-92) splits columns over CPU threads of one process
+// (`for nb = ith; nb < n/128; nb += nth`, src/exl3-ggml.cpp:74).
 //
-// Ordering: a rank's store kernel comes after its consumers of the previous
-// output on its stream, and a peer can be at most one call ahead (its next
-// store waits on this rank's flag), so y is double-buffered by epoch parity and
-// flags compare modulo 2^32.  The epoch lives on the device (a counter the
-// store kernel advances), so a call can be captured in a CUDA graph and
-// replayed; the wait kernel copies the finished half into a fixed output.
-// Every wait is bounded: after about a second it sets kStatusWaitTimeout in
-// the device status and returns.  No multicast, no NVLS: P2P stores only.
+// Protocol: self-validating pairs, no fences and no flags.  Every element of
+// a y buffer is one 8-byte word (epoch << 32 | float bits), written with a
+// single-copy-atomic 8-byte store, so a reader that sees a word of epoch E
+// sees that call's value in the same word; the reader polls each element
+// until its epoch is this call's.  (A fence and a flag per call measured
+// several microseconds per launch: a system-scope fence waits for far more
+// than the stores it orders.)  The epoch E = this rank's counter + 1 lives on
+// the device, so calls can be captured in a CUDA graph and replayed; the wait
+// kernel advances the counter.  A rank can be at most one call ahead of
+// another (its next store follows its wait for this call), so y is
+// double-buffered by epoch parity.  Every wait is bounded: after about a
+// second it sets kStatusWaitTimeout in the device status, copies what is
+// there and returns.  No multicast, no NVLS: P2P stores only.
 #include "exl3cu.h"
 #include "exl3cu_async.cuh"
 #include "exl3cu_internal.h"
@@ -25,34 +30,29 @@ namespace exl3cu {
 
 static __device__ unsigned g_peer_status;
 
-constexpr unsigned kPeerWaitRounds = 1u << 20;  // polls of >= ~1 us: about a second
+constexpr unsigned kPeerWaitRounds = 1u << 24;  // polls about 64 ns apart: about a second
 
-// A rank's state words (its IPC-shared flag buffer): [0, 8) every rank's last
-// epoch, [8] the storing kernel's arrival ticket, [9] this rank's epoch counter.
-constexpr int kTicketWord = kPeerTicketWord;
-constexpr int kEpochWord = kPeerEpochWord;
+// A rank's state words (16, zero-initialised): [kPeerTicketWord] the wait kernel's arrival
+// ticket (reset by its last CTA), [kPeerEpochWord] this rank's epoch counter (calls completed).
 
 struct PeerArgs {
-    float * y[kMaxPeers];         // every rank's y buffer [2][rows_cap][...] (this rank's included)
-    unsigned * state[kMaxPeers];  // every rank's state words
-    const float * src;            // this rank's slice [rows][src_stride]
+    unsigned long long * y[kMaxPeers];  // every rank's pair buffer [2][rows_cap][y_stride] (this rank's included)
+    const unsigned * own_state;         // this rank's state words
+    const float * src;                  // this rank's slice [rows][src_stride]
     long long src_stride;
     long long y_stride;
-    long long y_half;             // floats between the two halves of a y buffer
+    long long y_half;                   // pairs between the two halves of a y buffer
     long long y_col0;
     int rows, cols;
-    int npeers, rank;
+    int npeers;
 };
 
-// The call's epoch E = this rank's counter + 1 (on the device, so the call can be replayed from a
-// CUDA graph); float4s of the slice into half (E & 1) of every rank's y; the last CTA to finish
-// (ticket) publishes E in every rank's state and advances the counter.
+// The call's epoch E = this rank's counter + 1; the slice's values, as (E, value) pairs, into half
+// (E & 1) of every rank's y buffer.
 __global__ void __launch_bounds__(256) k_store_peers(const PeerArgs a) {
-    __shared__ int last;
     pdl_trigger();
     pdl_wait_primary();  // the slice is written by the previous kernel
-    unsigned * own = a.state[a.rank];
-    const unsigned E = *reinterpret_cast<volatile unsigned *>(own + kEpochWord) + 1u;
+    const unsigned E = *reinterpret_cast<const volatile unsigned *>(a.own_state + kPeerEpochWord) + 1u;
     const long long half = (E & 1u) ? a.y_half : 0;
     const int c4 = a.cols / 4;
     const long long total = (long long)a.rows * c4;
@@ -61,59 +61,54 @@ __global__ void __launch_bounds__(256) k_store_peers(const PeerArgs a) {
         const int r = int(i / c4);
         const int c = int(i - (long long)r * c4) * 4;
         const float4 v = *reinterpret_cast<const float4 *>(a.src + r * a.src_stride + c);
-        for (int p = 0; p < a.npeers; ++p)
-            *reinterpret_cast<float4 *>(a.y[p] + half + r * a.y_stride + a.y_col0 + c) = v;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();  // this CTA's peer stores are visible to every GPU before its ticket
-        last = atomicAdd(own + kTicketWord, 1u) == gridDim.x - 1;
-    }
-    __syncthreads();
-    if (last && threadIdx.x == 0) {
-        own[kTicketWord] = 0u;   // every CTA has arrived (and read the counter): reset for the next call
-        own[kEpochWord] = E;
-        __threadfence_system();  // every CTA's stores are ordered before the flags
-        for (int p = 0; p < a.npeers; ++p)
-            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.state[p] + a.rank), "r"(E) : "memory");
+        const long long off = half + r * a.y_stride + a.y_col0 + c;
+        for (int p = 0; p < a.npeers; ++p) store_pairs4(a.y[p] + off, v, E);
     }
 }
 
-// Every CTA: thread 0 waits until every rank's flag has reached this rank's epoch (modulo 2^32: a
-// rank may be one call ahead); then the CTA copies its share of the finished half of y into out.
-__global__ void __launch_bounds__(256) k_wait_peers(const unsigned * state, int npeers, const float * y,
+// Every element of the call's half of this rank's y: wait (bounded) until its epoch is this call's,
+// then copy its value into out; the last CTA (ticket) advances this rank's counter.  A thread that
+// gives up once raises the status and stops waiting, so the whole kernel gives up in about a second.
+__global__ void __launch_bounds__(256) k_wait_peers(unsigned * state, const unsigned long long * y,
                                                     long long y_half, long long y_stride, float * out,
                                                     long long out_stride, int rows, int cols) {
-    __shared__ unsigned epoch_s;
+    __shared__ int last;
     pdl_trigger();
     pdl_wait_primary();  // this rank's own storing kernel has finished: only other GPUs are waited for
-    if (threadIdx.x == 0) {
-        const unsigned E = *reinterpret_cast<const volatile unsigned *>(state + kEpochWord);
-        epoch_s = E;
-        for (int p = 0; p < npeers; ++p) {
-            unsigned i = 0;
-            for (; i < kPeerWaitRounds; ++i) {
-                unsigned v;
-                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(state + p) : "memory");
-                if (int(v - E) >= 0) break;
-                __nanosleep(500);
-            }
-            if (i == kPeerWaitRounds) {
-                atomicOr(&g_peer_status, kStatusWaitTimeout);
-                break;
-            }
-        }
-    }
-    __syncthreads();
-    if (!out) return;
-    const float * src = y + ((epoch_s & 1u) ? y_half : 0);
-    const int c4 = cols / 4;
-    const long long total = (long long)rows * c4;
+    const unsigned E = *reinterpret_cast<const volatile unsigned *>(state + kPeerEpochWord) + 1u;
+    const unsigned long long * src = y + ((E & 1u) ? y_half : 0);
+    const long long total = (long long)rows * cols;
+    bool patient = true;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
-        const int r = int(i / c4);
-        const int c = int(i - (long long)r * c4) * 4;
-        *reinterpret_cast<float4 *>(out + r * out_stride + c) = *reinterpret_cast<const float4 *>(src + r * y_stride + c);
+        const int r = int(i / cols);
+        const int c = int(i - (long long)r * cols);
+        const unsigned long long * w = src + r * y_stride + c;
+        unsigned long long v = load_pair(w);
+        if (unsigned(v >> 32) != E && patient) {
+            unsigned n = 0;
+            for (; n < kPeerWaitRounds && unsigned(v >> 32) != E; ++n) {
+                __nanosleep(64);
+                v = load_pair(w);
+            }
+            if (n == kPeerWaitRounds) {
+                atomicOr(&g_peer_status, kStatusWaitTimeout);
+                patient = false;
+            }
+        }
+        if (out) out[r * out_stride + c] = __uint_as_float(unsigned(v));
+    }
+    if (gridDim.x == 1) {
+        __syncthreads();
+        if (threadIdx.x == 0) state[kPeerEpochWord] = E;
+        return;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(state + kPeerTicketWord, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        state[kPeerTicketWord] = 0u;  // every CTA has read the counter: reset for the next call
+        state[kPeerEpochWord] = E;
     }
 }
 
@@ -209,20 +204,21 @@ int exl3cu_ipc_close(int device, void * ptr) {
 }
 
 int exl3cu_store_peers(const float * d_slice, size_t rows, size_t cols, size_t slice_stride, int npeers,
-                       float * const * d_y_peers, size_t y_row_stride, size_t y_half, size_t y_col0,
-                       unsigned * const * d_state_peers, int rank, void * stream) {
-    if (npeers < 1 || npeers > kMaxPeers || rank < 0 || rank >= npeers)
-        return api_fail(EXL3CU_INVALID_ARGUMENT, "store_peers: 1..8 ranks and 0 <= rank < npeers");
-    if (!d_slice || !d_y_peers || !d_state_peers || !rows || !cols)
+                       void * const * d_y_peers, size_t y_row_stride, size_t y_half, size_t y_col0,
+                       const unsigned * d_state, void * stream) {
+    if (npeers < 1 || npeers > kMaxPeers) return api_fail(EXL3CU_INVALID_ARGUMENT, "store_peers: 1..8 ranks");
+    if (!d_slice || !d_y_peers || !d_state || !rows || !cols)
         return api_fail(EXL3CU_INVALID_ARGUMENT, "store_peers: NULL or empty argument");
-    if (cols % 4 || slice_stride % 4 || y_row_stride % 4 || y_half % 4 || y_col0 % 4 || slice_stride < cols)
-        return api_fail(EXL3CU_INVALID_ARGUMENT, "store_peers: columns, strides and offsets must be multiples of 4");
+    if (cols % 4 || slice_stride % 4 || y_row_stride % 4 || y_half % 4 || y_col0 % 4 || slice_stride < cols ||
+        y_row_stride < y_col0 + cols || y_half < rows * y_row_stride)
+        return api_fail(EXL3CU_INVALID_ARGUMENT,
+                        "store_peers: columns, strides and offsets must be multiples of 4 and fit the buffers");
     PeerArgs a{};
     for (int p = 0; p < npeers; ++p) {
-        if (!d_y_peers[p] || !d_state_peers[p]) return api_fail(EXL3CU_INVALID_ARGUMENT, "store_peers: NULL peer");
-        a.y[p] = d_y_peers[p];
-        a.state[p] = d_state_peers[p];
+        if (!d_y_peers[p]) return api_fail(EXL3CU_INVALID_ARGUMENT, "store_peers: NULL peer");
+        a.y[p] = static_cast<unsigned long long *>(d_y_peers[p]);
     }
+    a.own_state = d_state;
     a.src = d_slice;
     a.src_stride = (long long)slice_stride;
     a.y_stride = (long long)y_row_stride;
@@ -231,23 +227,23 @@ int exl3cu_store_peers(const float * d_slice, size_t rows, size_t cols, size_t s
     a.rows = int(rows);
     a.cols = int(cols);
     a.npeers = npeers;
-    a.rank = rank;
     const size_t f4 = rows * cols / 4;
     const unsigned grid = unsigned(f4 < 256 ? 1 : (f4 + 255) / 256 < 296 ? (f4 + 255) / 256 : 296);
     const cudaError_t e = launch_pdl(k_store_peers, grid, static_cast<cudaStream_t>(stream), a);
     return e == cudaSuccess ? EXL3CU_OK : api_cuda_fail(e, "launching the peer stores");
 }
 
-int exl3cu_wait_peers(const unsigned * d_state, int npeers, const float * d_y, size_t y_row_stride, size_t y_half,
-                      float * d_out, size_t out_row_stride, size_t rows, size_t cols, void * stream) {
-    if (!d_state || npeers < 1 || npeers > kMaxPeers) return api_fail(EXL3CU_INVALID_ARGUMENT, "wait_peers: 1..8 ranks");
-    if (d_out && (!d_y || cols % 4 || y_row_stride % 4 || y_half % 4 || out_row_stride % 4))
-        return api_fail(EXL3CU_INVALID_ARGUMENT, "wait_peers: y, strides and columns must be multiples of 4 floats");
-    const size_t f4 = d_out ? rows * cols / 4 : 0;
-    const unsigned grid = unsigned(f4 < 256 ? 1 : (f4 + 255) / 256 < 148 ? (f4 + 255) / 256 : 148);
-    const cudaError_t e = launch_pdl(k_wait_peers, grid, static_cast<cudaStream_t>(stream), d_state, npeers, d_y,
-                                     (long long)y_half, (long long)y_row_stride, d_out, (long long)out_row_stride,
-                                     int(rows), int(cols));
+int exl3cu_wait_peers(unsigned * d_state, const void * d_y, size_t y_row_stride, size_t y_half, float * d_out,
+                      size_t out_row_stride, size_t rows, size_t cols, void * stream) {
+    if (!d_state || !d_y || !rows || !cols) return api_fail(EXL3CU_INVALID_ARGUMENT, "wait_peers: NULL or empty argument");
+    if (y_row_stride < cols || y_half < rows * y_row_stride || (d_out && out_row_stride < cols))
+        return api_fail(EXL3CU_INVALID_ARGUMENT, "wait_peers: the rows do not fit the buffers");
+    const size_t n = rows * cols;
+    const unsigned grid = unsigned(n <= 1024 ? 1 : (n + 1023) / 1024 < 148 ? (n + 1023) / 1024 : 148);
+    const cudaError_t e =
+        launch_pdl(k_wait_peers, grid, static_cast<cudaStream_t>(stream), d_state,
+                   static_cast<const unsigned long long *>(d_y), (long long)y_half, (long long)y_row_stride, d_out,
+                   (long long)out_row_stride, int(rows), int(cols));
     return e == cudaSuccess ? EXL3CU_OK : api_cuda_fail(e, "launching the peer wait");
 }
 

@@ -95,10 +95,9 @@ def _declare(L):
     L.exl3cu_ipc_free.argtypes = [_c.c_int, _vp]
     L.exl3cu_ipc_open.argtypes = [_c.c_int, _vp, _P(_vp)]
     L.exl3cu_ipc_close.argtypes = [_c.c_int, _vp]
-    L.exl3cu_store_peers.argtypes = [_vp, _sz, _sz, _sz, _c.c_int, _vp, _sz, _sz, _sz, _vp, _c.c_int, _vp]
-    L.exl3cu_wait_peers.argtypes = [_vp, _c.c_int, _vp, _sz, _sz, _vp, _sz, _sz, _sz, _vp]
-    L.exl3cu_mul_mat_peers.argtypes = [_vp, _vp, _c.c_int, _sz, _sz, _vp, _sz, _c.c_int, _vp, _sz, _sz, _sz, _vp,
-                                       _c.c_int, _vp]
+    L.exl3cu_store_peers.argtypes = [_vp, _sz, _sz, _sz, _c.c_int, _vp, _sz, _sz, _sz, _vp, _vp]
+    L.exl3cu_wait_peers.argtypes = [_vp, _vp, _sz, _sz, _vp, _sz, _sz, _sz, _vp]
+    L.exl3cu_mul_mat_peers.argtypes = [_vp, _vp, _c.c_int, _sz, _sz, _vp, _sz, _c.c_int, _vp, _sz, _sz, _sz, _vp, _vp]
     L.exl3cu_model_open.argtypes = [_c.c_char_p, _c.c_int, _c.c_uint, _P(_vp)]
     L.exl3cu_model_free.argtypes = [_vp]
     L.exl3cu_model_info.argtypes = [_vp, _P(_sz), _P(_sz), _P(_sz), _P(_sz), _P(_sz), _P(_c.c_double)]

@@ -111,16 +111,15 @@ class ColumnParallelExl3:
 
 
 class PeerColumnParallelExl3:
-    """Column-split EXL3 matrix whose slices meet over NVLink peer memory.
-
-    Every rank holds y twice ([2][max_rows][n] fp32, used by epoch parity: a rank can be one call
-    ahead of another) and 16 state words (every rank's last epoch, an arrival ticket, its epoch
-    counter), in buffers every other rank maps through CUDA IPC.  forward(): the local slice into a
-    staging buffer (the EXL3 operator), then exl3cu_store_peers writes it into every rank's y and
-    publishes the call's epoch in every rank's state, and exl3cu_wait_peers holds the stream until
-    every rank's epoch has arrived and copies the finished y into a fixed output.  The epoch lives
-    on the device, so forward() can be captured in a CUDA graph and replayed.  The returned tensor
-    is a view of the fixed output, valid until the next call."""
+    """configs[4]'s column split with the all-gather done over NVLink peer memory (no collective
+    library on the data path).  Every rank owns a y buffer of (epoch << 32 | float bits) words, two
+    halves of max_rows x n, which every other rank maps through CUDA IPC, and 16 state words (its epoch
+    counter).  forward(): exl3cu_mul_mat_peers computes the rank's slice and stores it as (epoch,
+    value) words into every rank's buffer -- for 1..4 rows inside the GEMV's epilogue, one launch --
+    and exl3cu_wait_peers holds the stream until every word of this call has arrived, copies the row
+    into a fixed output and advances the counter.  The epoch lives on the device, so forward() can be
+    captured in a CUDA graph and replayed.  The returned tensor is a view of the fixed output, valid
+    until the next call."""
 
     def __init__(self, records, k: int, n: int, bits: int, max_rows: int, group=None, device: int | None = None,
                  codebook: int = 2, weight=None):
@@ -144,30 +143,26 @@ class PeerColumnParallelExl3:
         self.weight = weight if weight is not None else Exl3Weight.from_records(
             records, k, n, bits, codebook=codebook, device=self.dev, first_block=first, block_count=count)
         self.k, self.n, self.max_rows = k, n, max_rows
-        self.half = max_rows * n  # floats between the two halves of y
+        self.half = max_rows * n  # words between the two halves of y
         c = ctypes
-        y_ptr, s_ptr = c.c_void_p(), c.c_void_p()
-        y_h, s_h = (c.c_char * 64)(), (c.c_char * 64)()
-        _lib.check(self.L.exl3cu_ipc_alloc(self.dev, 2 * self.half * 4, c.byref(y_ptr), y_h))
-        _lib.check(self.L.exl3cu_ipc_alloc(self.dev, 64, c.byref(s_ptr), s_h))  # 16 state words
-        self.y_own, self.state_own = y_ptr.value, s_ptr.value
+        y_ptr = c.c_void_p()
+        y_h = (c.c_char * 64)()
+        _lib.check(self.L.exl3cu_ipc_alloc(self.dev, 2 * self.half * 8, c.byref(y_ptr), y_h))  # 8-byte words
+        self.y_own = y_ptr.value
+        self.state = torch.zeros(16, dtype=torch.int32, device=f"cuda:{self.dev}")  # read and advanced locally
         handles = [None] * self.world
-        dist.all_gather_object(handles, (bytes(y_h), bytes(s_h)), group=group)
-        self.y_peers, self.s_peers, self.opened = [], [], []
-        for r, (yh, sh) in enumerate(handles):
+        dist.all_gather_object(handles, bytes(y_h), group=group)
+        self.y_peers, self.opened = [], []
+        for r, yh in enumerate(handles):
             if r == self.rank:
                 self.y_peers.append(self.y_own)
-                self.s_peers.append(self.state_own)
                 continue
-            yp, sp = c.c_void_p(), c.c_void_p()
+            yp = c.c_void_p()
             _lib.check(self.L.exl3cu_ipc_open(self.dev, c.create_string_buffer(yh, 64), c.byref(yp)))
-            _lib.check(self.L.exl3cu_ipc_open(self.dev, c.create_string_buffer(sh, 64), c.byref(sp)))
             self.y_peers.append(yp.value)
-            self.s_peers.append(sp.value)
-            self.opened += [yp.value, sp.value]
+            self.opened.append(yp.value)
         dist.barrier(group=group)  # every rank has mapped every buffer before any store
         self._yp = (c.c_void_p * self.world)(*self.y_peers)
-        self._sp = (c.c_void_p * self.world)(*self.s_peers)
         self.slice = torch.empty((max_rows, count * 128), dtype=torch.float32, device=f"cuda:{self.dev}")
         self.out = torch.empty((max_rows, n), dtype=torch.float32, device=f"cuda:{self.dev}")
 
@@ -190,10 +185,10 @@ class PeerColumnParallelExl3:
         # blocks into every rank's buffer), else the operator into self.slice plus the peer stores
         _lib.check(self.L.exl3cu_mul_mat_peers(self.weight.handle, x.data_ptr(), _lib.F32 if x.dtype == torch.float32
                                                else _lib.F16, rows, x.stride(0), self.slice.data_ptr(), cols,
-                                               self.world, self._yp, self.n, self.half, self.first * 128, self._sp,
-                                               self.rank, sh))
-        _lib.check(self.L.exl3cu_wait_peers(ctypes.c_void_p(self.state_own), self.world, ctypes.c_void_p(self.y_own),
-                                            self.n, self.half, self.out.data_ptr(), self.n, rows, self.n, sh))
+                                               self.world, self._yp, self.n, self.half, self.first * 128,
+                                               self.state.data_ptr(), sh))
+        _lib.check(self.L.exl3cu_wait_peers(self.state.data_ptr(), ctypes.c_void_p(self.y_own), self.n, self.half,
+                                            self.out.data_ptr(), self.n, rows, self.n, sh))
         return self.out[:rows]
 
     def free(self):
@@ -203,6 +198,5 @@ class PeerColumnParallelExl3:
             self.L.exl3cu_ipc_close(self.dev, p)
         dist.barrier(group=self.group)
         self.L.exl3cu_ipc_free(self.dev, self.y_own)
-        self.L.exl3cu_ipc_free(self.dev, self.state_own)
         if self.owns_weight:
             self.weight.free()
