@@ -198,6 +198,32 @@ def test_large_matrix_config4(ops, oracle):
     w.free()
 
 
+@pytest.mark.parametrize("bits", (2, 5, 8))
+def test_long_k_wide_build(ops, oracle, bits):
+    """k >= 8192 runs the GEMV's wide build (two CTAs per SM, tile-pair decode): 1..4 rows at the
+    configs[4] depth and several bit widths, against the oracle, and so does the default build
+    forced on the same call (its own cluster split, so not bit for bit the same)."""
+    import os
+
+    from exl3_b200 import synthetic
+
+    k, n = 14336, 512
+    m = synthetic.matrix(k, n, bits, seed=60 + bits)
+    rec = m.records()
+    w = ops.Exl3Weight.from_records(rec, k, n, bits)
+    for rows in (1, 2, 3, 4):
+        x = synthetic.activations(rows, k, seed=61 + rows)
+        ref = oracle.mul_mat(rec, bits, k, n, x, nth=16)
+        assert_close(_mm(ops, w, x), ref, f"wide bits={bits} rows={rows}")
+        os.environ["EXL3CU_MUL1_WIDE"] = "0"
+        try:
+            y_default = _mm(ops, w, x)
+        finally:
+            del os.environ["EXL3CU_MUL1_WIDE"]
+        assert_close(y_default, ref, f"default bits={bits} rows={rows}")
+    w.free()
+
+
 def test_linearity_full_size(ops):
     """Size-independent property at a full BASELINE size: y(a x1 + b x2) = a y(x1) + b y(x2)."""
     from exl3_b200 import synthetic

@@ -95,8 +95,11 @@ __host__ __device__ inline Mul1Layout mul1_layout(int bits, int cps, int rows, i
     return L;
 }
 
-template <int BITS, bool PEER>
-__global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
+// The kernel body.  PEER: the output goes to the peers' buffers (a column split).  WIDE: the build
+// for long K ranges per CTA (two CTAs per SM, 95 registers), whose decode keeps two tiles' products
+// in flight; the default build keeps three CTAs per SM at 72 registers.
+template <int BITS, bool PEER, bool WIDE>
+__device__ __forceinline__ void gemv_mul1_body(const GemvBatch & b) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int CHUNKB = 256 * BITS;
     pdl_trigger();
@@ -432,18 +435,42 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
             if (lane == 0) mbar_arrive(&empty[s]);
             // products of all 8 tiles first, then the 16 IMMAs ordered so that no two
             // consecutive ones share an accumulator
-            uint32_t pr[8][8];
+            if constexpr (WIDE) {
+                // tile pairs: the products of two tiles, then their four IMMAs
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint32_t st[8];
-                tile_states<BITS>(w, c, src, st);
+                for (int c = 0; c < 8; c += 2) {
+                    uint32_t pa[8], pb[8];
+                    {
+                        uint32_t st[8];
+                        tile_states<BITS>(w, c, src, st);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) pr[c][e] = st[e] * C;
+                        for (int e = 0; e < 8; ++e) pa[e] = st[e] * C;
+                    }
+                    {
+                        uint32_t st[8];
+                        tile_states<BITS>(w, c + 1, src, st);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) pb[e] = st[e] * C;
+                    }
+                    imma_u8s8(D[c], pa[0], pa[4], pa[1], pa[5], bq.x, bq.y);
+                    imma_u8s8(D[c + 1], pb[0], pb[4], pb[1], pb[5], bq.x, bq.y);
+                    imma_u8s8(D[c], pa[2], pa[6], pa[3], pa[7], bq.z, bq.w);
+                    imma_u8s8(D[c + 1], pb[2], pb[6], pb[3], pb[7], bq.z, bq.w);
+                }
+            } else {
+                uint32_t pr[8][8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t st[8];
+                    tile_states<BITS>(w, c, src, st);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) pr[c][e] = st[e] * C;
+                }
+#pragma unroll
+                for (int c = 0; c < 8; ++c) imma_u8s8(D[c], pr[c][0], pr[c][4], pr[c][1], pr[c][5], bq.x, bq.y);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) imma_u8s8(D[c], pr[c][2], pr[c][6], pr[c][3], pr[c][7], bq.z, bq.w);
             }
-#pragma unroll
-            for (int c = 0; c < 8; ++c) imma_u8s8(D[c], pr[c][0], pr[c][4], pr[c][1], pr[c][5], bq.x, bq.y);
-#pragma unroll
-            for (int c = 0; c < 8; ++c) imma_u8s8(D[c], pr[c][2], pr[c][6], pr[c][3], pr[c][7], bq.z, bq.w);
             if (++s == NS) {
                 s = 0;
                 ++round;
@@ -539,24 +566,43 @@ __global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
     }
 }
 
+template <int BITS, bool PEER>
+__global__ void __launch_bounds__(kMThreads) k_gemv_mul1(const GemvBatch b) {
+    gemv_mul1_body<BITS, PEER, false>(b);
+}
+
+template <int BITS, bool PEER>
+__global__ void __launch_bounds__(kMThreads, 2) k_gemv_mul1_wide(const GemvBatch b) {
+    gemv_mul1_body<BITS, PEER, true>(b);
+}
+
 // ---------------------------------------------------------------------------
 
 namespace {
 
+// Kernel variants: bit 0 peer output, bit 1 the wide build.
+constexpr int kVarDefault = 0, kVarPeer = 1, kVarWide = 2;
+constexpr int kWideMinChunks = 512;  // k / 16 from which a problem takes the wide build
+
 template <int BITS>
-void * mul1_kernel(bool peer) {
-    return peer ? reinterpret_cast<void *>(k_gemv_mul1<BITS, true>) : reinterpret_cast<void *>(k_gemv_mul1<BITS, false>);
+void * mul1_kernel(int var) {
+    switch (var) {
+        case kVarPeer: return reinterpret_cast<void *>(k_gemv_mul1<BITS, true>);
+        case kVarWide: return reinterpret_cast<void *>(k_gemv_mul1_wide<BITS, false>);
+        case kVarPeer | kVarWide: return reinterpret_cast<void *>(k_gemv_mul1_wide<BITS, true>);
+        default: return reinterpret_cast<void *>(k_gemv_mul1<BITS, false>);
+    }
 }
 
-void * mul1_kernel_for(unsigned bits, bool peer = false) {
+void * mul1_kernel_for(unsigned bits, int var = kVarDefault) {
     switch (bits) {
-        case 2: return mul1_kernel<2>(peer);
-        case 3: return mul1_kernel<3>(peer);
-        case 4: return mul1_kernel<4>(peer);
-        case 5: return mul1_kernel<5>(peer);
-        case 6: return mul1_kernel<6>(peer);
-        case 7: return mul1_kernel<7>(peer);
-        case 8: return mul1_kernel<8>(peer);
+        case 2: return mul1_kernel<2>(var);
+        case 3: return mul1_kernel<3>(var);
+        case 4: return mul1_kernel<4>(var);
+        case 5: return mul1_kernel<5>(var);
+        case 6: return mul1_kernel<6>(var);
+        case 7: return mul1_kernel<7>(var);
+        case 8: return mul1_kernel<8>(var);
         default: return nullptr;
     }
 }
@@ -570,8 +616,8 @@ bool mul1_prepare(int device, unsigned bits) {
     if (device < 0 || device >= 64 || bits > 8) return false;
     std::lock_guard<std::mutex> g(mu);
     if (done[device][bits]) return true;
-    for (const bool peer : {false, true}) {
-        const void * k = mul1_kernel_for(bits, peer);
+    for (const int var : {kVarDefault, kVarPeer, kVarWide, kVarPeer | kVarWide}) {
+        const void * k = mul1_kernel_for(bits, var);
         if (!k) return false;
         if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMul1MaxSmem)) != cudaSuccess)
             return false;
@@ -583,10 +629,10 @@ bool mul1_prepare(int device, unsigned bits) {
 
 // Clusters of `cs` CTAs with `smem` bytes each that the device holds at once
 // (0 when such a cluster cannot be scheduled at all); cached per key.
-int mul1_active_clusters(int device, unsigned bits, int cs, size_t smem, bool peer) {
+int mul1_active_clusters(int device, unsigned bits, int cs, size_t smem, int var) {
     static std::mutex mu;
-    static std::map<std::tuple<int, unsigned, int, size_t, bool>, int> cache;
-    const auto key = std::make_tuple(device, bits, cs, (smem + 1023) / 1024, peer);
+    static std::map<std::tuple<int, unsigned, int, size_t, int>, int> cache;
+    const auto key = std::make_tuple(device, bits, cs, (smem + 1023) / 1024, var);
     {
         std::lock_guard<std::mutex> g(mu);
         auto it = cache.find(key);
@@ -604,7 +650,7 @@ int mul1_active_clusters(int device, unsigned bits, int cs, size_t smem, bool pe
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, mul1_kernel_for(bits, peer), &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, mul1_kernel_for(bits, var), &cfg) != cudaSuccess) {
         (void)cudaGetLastError();
         n = 0;
     }
@@ -641,6 +687,13 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
         max_nchunks = std::max(max_nchunks, b.prob[i].nchunks);
         max_rows = std::max(max_rows, b.prob[i].rows);
     }
+    // Long K (k >= 8192, every problem): many chunks per CTA, where the wide build's decode pays for its
+    // lower occupancy (14336x4096 at 1 row: 21.4 -> 18.2 us); shorter K keeps the default build,
+    // which the wide one slows by up to 20 % on the 2048-wide layer shapes.  EXL3CU_MUL1_WIDE=0/1
+    // forces either (tuning experiments).
+    const char * wenv = std::getenv("EXL3CU_MUL1_WIDE");
+    const bool wide = wenv && wenv[0] ? wenv[0] == '1' : min_nchunks >= kWideMinChunks;
+    const int var = (b.peer_on ? kVarPeer : 0) | (wide ? kVarWide : 0);
     const char * env = std::getenv("EXL3CU_CLUSTER_SPLITS");  // tuning experiments only
     const int NS = mul1_stages(bits);
     int S = 0;
@@ -660,7 +713,7 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
                 const int cps = (max_nchunks + cand - 1) / cand;
                 const Mul1Layout L = mul1_layout(int(bits), cps, max_rows, cand, NS, staged);
                 if (L.bytes > kMul1MaxSmem) break;  // fewer splits only grow the per-CTA range
-                const int fit = std::min(mul1_active_clusters(device, bits, cand, L.bytes, b.peer_on != 0), cap / cand);
+                const int fit = std::min(mul1_active_clusters(device, bits, cand, L.bytes, var), cap / cand);
                 if (fit <= 0) continue;
                 if (!feasible) {
                     feasible = cand;
@@ -705,7 +758,7 @@ cudaError_t launch_gemv_mul1(GemvBatch & b, int nunits, int sms, int device, uns
     cfg.attrs = attrs;
     cfg.numAttrs = pdl ? 2 : 1;
     void * args[] = {&b};
-    return cudaLaunchKernelExC(&cfg, mul1_kernel_for(bits, b.peer_on != 0), args);
+    return cudaLaunchKernelExC(&cfg, mul1_kernel_for(bits, var), args);
 }
 
 cudaError_t mul1_read_status(unsigned * out, bool clear) {
