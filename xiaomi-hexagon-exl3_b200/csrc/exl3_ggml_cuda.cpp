@@ -47,22 +47,23 @@ struct Cached {
 std::mutex g_mu;
 std::map<std::tuple<const void *, int, int64_t, int64_t>, Cached> g_weights;
 
-// FNV-1a over the first and last record and 64 words sampled evenly across the
-// records: cheap next to the per-call copies, and it changes when a different
-// model occupies the same buffer.
-uint64_t records_digest(const void * data, size_t bytes, size_t group_bytes) {
+// A digest of the records, taken on every call: 8-byte words (the first and last 64 of the buffer
+// and 64 sampled evenly across it) folded FNV-style, one multiply per word.  It changes when a
+// different model occupies the same buffer (new weights differ in nearly every word) and costs well
+// under a microsecond; hashing two whole records byte by byte had cost about 25 us per call.
+uint64_t records_digest(const void * data, size_t bytes) {
     const unsigned char * p = static_cast<const unsigned char *>(data);
-    uint64_t h = 1469598103934665603ull;
-    auto mix = [&](const unsigned char * q, size_t len) {
-        for (size_t i = 0; i < len; ++i) {
-            h ^= q[i];
-            h *= 1099511628211ull;
-        }
-    };
-    mix(p, group_bytes);
-    mix(p + bytes - group_bytes, group_bytes);
     const size_t words = bytes / 8;
-    for (size_t i = 0; i < 64 && words; ++i) mix(p + (i * (words - 1) / 63) * 8, 8);
+    uint64_t h = 1469598103934665603ull;
+    auto mix = [&](size_t word) {
+        uint64_t v;
+        std::memcpy(&v, p + word * 8, 8);
+        h = (h ^ v) * 1099511628211ull;
+    };
+    const size_t edge = words < 64 ? words : 64;
+    for (size_t i = 0; i < edge; ++i) mix(i);
+    for (size_t i = 0; i < edge; ++i) mix(words - edge + i);
+    for (size_t i = 0; i < 64 && words; ++i) mix(i * (words - 1) / 63);
     return h;
 }
 
@@ -79,7 +80,7 @@ int target_device() {
 exl3cu_weight * weight_for(const ggml_tensor * w, unsigned bits, size_t k, size_t n) {
     const auto key = std::make_tuple(static_cast<const void *>(w->data), int(w->type), int64_t(k), int64_t(n));
     const size_t bytes = (k / 128) * (n / 128) * exl3_group_bytes(bits);
-    const uint64_t digest = records_digest(w->data, bytes, exl3_group_bytes(bits));
+    const uint64_t digest = records_digest(w->data, bytes);
     std::lock_guard<std::mutex> g(g_mu);
     auto it = g_weights.find(key);
     if (it != g_weights.end()) {

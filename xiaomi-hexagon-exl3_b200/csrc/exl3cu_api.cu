@@ -42,6 +42,11 @@ struct exl3cu_weight {
     float * stage_y;
     size_t stage_y_bytes;
     std::vector<void *> retired;  // outgrown staging, kept until the handle is freed (graphs may hold it)
+    void * pin_x;        // synchronous small host-form calls: mapped pinned host staging the kernels
+    float * pin_y;       // read and write directly (no copy engine round trips)
+    size_t pin_x_bytes, pin_y_bytes;
+    void * pin_x_dev;    // their device addresses
+    float * pin_y_dev;
 };
 
 namespace {
@@ -137,6 +142,8 @@ void release(exl3cu_weight * w) {
     cudaFree(w->stage_x);
     cudaFree(w->stage_y);
     for (void * p : w->retired) cudaFree(p);
+    if (w->pin_x) cudaFreeHost(w->pin_x);
+    if (w->pin_y) cudaFreeHost(w->pin_y);
     delete w;
 }
 
@@ -328,6 +335,27 @@ int grow_stage(exl3cu_weight * w, void ** buf, size_t * bytes, size_t want) {
     *bytes = want;
     return EXL3CU_OK;
 }
+
+// Mapped pinned host staging (zero-copy) for synchronous host-form calls; grown on demand (a grow
+// synchronises the device, which a synchronous call does anyway).
+int grow_pinned(void ** buf, size_t * bytes, size_t want) {
+    if (*bytes >= want) return EXL3CU_OK;
+    if (*buf) {
+        cudaError_t e = cudaFreeHost(*buf);
+        *buf = nullptr;
+        *bytes = 0;
+        if (e != cudaSuccess) return cuda_fail(e, "freeing outgrown pinned staging");
+    }
+    void * p = nullptr;
+    const cudaError_t e = cudaHostAlloc(&p, want, cudaHostAllocMapped | cudaHostAllocPortable);
+    if (e != cudaSuccess) return cuda_fail(e, "allocating pinned host staging");
+    *buf = p;
+    *bytes = want;
+    return EXL3CU_OK;
+}
+
+// Rows at most which a synchronous host-form call runs zero-copy (decode-sized operands).
+constexpr size_t kZeroCopyRows = 8;
 
 // Rows per GEMM launch pair: bounds the scratch (2 KB per row per 1024 of k)
 // and keeps every index of the launch in 32 bits.
@@ -872,6 +900,26 @@ int exl3cu_mul_mat_host(exl3cu_weight * w, const void * h_x, int x_dtype, size_t
     const size_t es = x_dtype == EXL3CU_F32 ? 4 : 2;
     const size_t xb = rows * w->k * es, yb = rows * n_local * sizeof(float);
     int rc;
+    if (synchronize && rows <= kZeroCopyRows) {
+        // Zero-copy: x is packed into mapped pinned memory the kernel reads over the bus, y is written
+        // there by the kernel's epilogue, and the host copies it out after the synchronisation.  Saves
+        // the two staged copies of pageable memory (about 20 us of a decode-sized call).
+        if (w->pin_x_bytes < xb || w->pin_y_bytes < yb) {
+            if ((rc = grow_pinned(&w->pin_x, &w->pin_x_bytes, xb))) return rc;
+            if ((rc = grow_pinned(reinterpret_cast<void **>(&w->pin_y), &w->pin_y_bytes, yb))) return rc;
+            CU_TRY(cudaHostGetDevicePointer(&w->pin_x_dev, w->pin_x, 0), "mapping pinned x");
+            CU_TRY(cudaHostGetDevicePointer(reinterpret_cast<void **>(&w->pin_y_dev), w->pin_y, 0), "mapping pinned y");
+        }
+        for (size_t r = 0; r < rows; ++r)
+            std::memcpy(static_cast<char *>(w->pin_x) + r * w->k * es,
+                        static_cast<const char *>(h_x) + r * x_row_stride * es, w->k * es);
+        const MmItem item{w, w->pin_x_dev, x_dtype, rows, w->k, w->pin_y_dev, n_local};
+        if ((rc = run_cluster(&item, 1, st))) return rc;
+        CU_TRY(cudaStreamSynchronize(st), "synchronising the stream");
+        for (size_t r = 0; r < rows; ++r)
+            std::memcpy(h_y + r * y_row_stride, w->pin_y + r * n_local, n_local * sizeof(float));
+        return EXL3CU_OK;
+    }
     if ((rc = grow_stage(w, &w->stage_x, &w->stage_x_bytes, xb))) return rc;
     if ((rc = grow_stage(w, reinterpret_cast<void **>(&w->stage_y), &w->stage_y_bytes, yb))) return rc;
     CU_TRY(cudaMemcpy2DAsync(w->stage_x, w->k * es, h_x, x_row_stride * es, w->k * es, rows, cudaMemcpyHostToDevice, st),
