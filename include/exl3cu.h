@@ -264,10 +264,10 @@ int exl3cu_mul_mat_noalloc(const exl3cu_weight * w, const void * d_x, int x_dtyp
  *   slice_stride) go as (E, value) words into half (E & 1) of every rank's y
  *   buffer at column y_col0 (row stride y_row_stride).
  * exl3cu_mul_mat_peers: the operator of this rank's slice (handle w) with the
- *   store above.  For 1..4 rows of mul1 weights this is one launch: the
- *   GEMV's epilogue stores its output blocks to the peers over NVLink.
- *   Other operands run the operator into d_slice (row stride slice_stride)
- *   and then exl3cu_store_peers.
+ *   store above, fused for mul1 weights: the GEMV's epilogue (1..4 rows) or
+ *   the tensor-core GEMM's epilogue (5..2048 rows) stores its output blocks
+ *   to the peers over NVLink.  Other operands run the operator into d_slice
+ *   (row stride slice_stride) and then exl3cu_store_peers.
  * exl3cu_wait_peers: on the stream, waits until every word of rows x cols in
  *   half (E & 1) of this rank's y carries epoch E, copies the values into
  *   d_out (row stride out_row_stride; NULL: wait only) and advances the

@@ -7,9 +7,10 @@ and then rank 1's exl3cu_mul_mat_peers run in stream order (each stores its
 slice into both ranks' buffers and publishes its epoch), and only then do the
 two exl3cu_wait_peers run.  Every word they wait for was stored by a kernel
 that already finished, so no kernel waits on another kernel running at the
-same time.  1 and 4 rows take the fused path (the GEMV's epilogue stores to the
-peers); 8 rows take the operator plus exl3cu_store_peers.  Three calls in a
-row use both halves of the double-buffered y.  Each rank's output is checked
+same time.  The calls cover the fused GEMV (1 and 4 rows: its epilogue stores to
+the peers), the fused tensor-core GEMM (8 rows) and the operator followed by
+exl3cu_store_peers (3 rows); consecutive calls use both halves of the
+double-buffered y.  Each rank's output is checked
 bit for bit against the 1-GPU operator on the same slice, and the epoch
 counters and tickets are checked after the calls.
 """
@@ -41,12 +42,17 @@ def test_two_ranks_on_one_gpu_fused_and_fallback(cuda_lib, oracle):
     outs = [torch.empty((max_rows, n), dtype=torch.float32, device="cuda") for _ in range(world)]
     st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     calls = 0
-    for rows in (1, 4, 8, 1):
+    for rows, fused in ((1, True), (4, True), (8, True), (3, False), (1, True)):
         x = torch.from_numpy(synthetic.activations(rows, k, seed=72 + rows)).cuda()
         for r in range(world):
-            _lib.check(L.exl3cu_mul_mat_peers(ws[r].handle, x.data_ptr(), _lib.F16, rows, k, slices[r].data_ptr(),
-                                              count * 128, world, yp, n, half, r * count * 128,
-                                              states[r].data_ptr(), st))
+            if fused:
+                _lib.check(L.exl3cu_mul_mat_peers(ws[r].handle, x.data_ptr(), _lib.F16, rows, k,
+                                                  slices[r].data_ptr(), count * 128, world, yp, n, half,
+                                                  r * count * 128, states[r].data_ptr(), st))
+            else:
+                ws[r].mul_mat(x, out=slices[r][:rows])
+                _lib.check(L.exl3cu_store_peers(slices[r].data_ptr(), rows, count * 128, count * 128, world, yp, n,
+                                                half, r * count * 128, states[r].data_ptr(), st))
         for r in range(world):
             outs[r].fill_(float("nan"))
             _lib.check(L.exl3cu_wait_peers(states[r].data_ptr(), ys[r].data_ptr(), n, half, outs[r].data_ptr(), n,

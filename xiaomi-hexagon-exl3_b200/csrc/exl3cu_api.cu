@@ -364,7 +364,7 @@ constexpr size_t kGemmRowsPerLaunch = 2048;
 // The tensor-core GEMM over `it`'s rows in launch pairs of at most
 // kGemmRowsPerLaunch rows.  With m_dev set, it.rows is the capacity and the
 // live row count is read on the device (ragged batches).
-int run_gemm(const MmItem & it, cudaStream_t st, const int32_t * m_dev = nullptr) {
+int run_gemm(const MmItem & it, cudaStream_t st, const int32_t * m_dev = nullptr, const PeerOut * peer = nullptr) {
     const exl3cu_weight * w = it.w;
     DeviceGuard guard(w->device);
     const size_t es = it.x_dtype == EXL3CU_F32 ? 4 : 2;
@@ -380,7 +380,7 @@ int run_gemm(const MmItem & it, cudaStream_t st, const int32_t * m_dev = nullptr
         if (rc) return rc;
         const cudaError_t e = launch_gemm(p, w->lsc, w->su, w->sv, w->k, w->nblocks, w->bits, w->codebook, w->device,
                                           x, it.x_dtype == EXL3CU_F16, (long long)it.x_stride, rows, m_dev, int(r0),
-                                          y, (long long)it.y_stride, static_cast<__half *>(xt), pdl_enabled(), st);
+                                          y, (long long)it.y_stride, static_cast<__half *>(xt), pdl_enabled(), st, peer);
         if (e != cudaSuccess) return cuda_fail(e, "launching the EXL3 tensor-core GEMM");
     }
     return EXL3CU_OK;
@@ -1039,9 +1039,18 @@ extern "C" int exl3cu_mul_mat_peers(const exl3cu_weight * w, const void * d_x, i
     po.y_half = (long long)y_half;
     po.y_col0 = (long long)y_col0;
     po.npeers = npeers;
-    const bool fused = w->codebook == EXL3CU_CB_MUL1 && rows >= 1 && rows < gemm_min_rows() &&
-                       mul1_supported(w->bits, int(rows < 64 ? rows : 64));
-    if (fused) {
+    const bool gemv = w->codebook == EXL3CU_CB_MUL1 && rows >= 1 && rows < gemm_min_rows() &&
+                      mul1_supported(w->bits, int(rows < 64 ? rows : 64));
+    const bool gemm = w->codebook == EXL3CU_CB_MUL1 && rows >= gemm_min_rows() && rows <= kGemmRowsPerLaunch;
+    if (gemm) {  // one tcgen05 GEMM launch pair whose epilogue stores to the peers
+        float * y_unused = d_slice ? d_slice : reinterpret_cast<float *>(po.y[0]);
+        int rc = validate_mm(w, d_x, x_dtype, rows, x_row_stride, y_unused, n_local);
+        if (rc) return rc;
+        if ((rc = check_device_ptr(d_x, w->device, "x"))) return rc;
+        const MmItem item{w, d_x, x_dtype, rows, x_row_stride, y_unused, n_local};
+        return run_gemm(item, static_cast<cudaStream_t>(stream), nullptr, &po);
+    }
+    if (gemv) {
         // the operator's own y argument is not written on this path: validate shapes against the slice
         float * y_unused = d_slice;
         if (!y_unused) y_unused = reinterpret_cast<float *>(po.y[0]);

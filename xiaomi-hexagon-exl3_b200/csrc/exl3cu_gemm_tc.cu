@@ -109,6 +109,7 @@ constexpr int kACol0 = 256;        // first TMEM column of the A ring (D uses 0.
 __host__ __device__ constexpr int kperm16(int k) { return 4 * ((k & 7) >> 1) + 2 * (k >> 3) + (k & 1); }
 
 struct GemmArgs {
+    PeerOut peer;       // PEER builds: y goes to every rank's buffer as (epoch, value) words
     const uint32_t * lsc;
     const __half * sv;
     const __half * xt;  // [tgroups][k/16][NTOK/8][2][8][8] fp16, K permuted by kperm16
@@ -225,7 +226,7 @@ __device__ __forceinline__ void tmem_st_tile(uint32_t taddr, const uint32_t (&f)
 // one full barrier (4 decode-warp arrivals + the activation copy's arrival and
 // bytes) and one empty barrier (the MMA commit, waited on by both producers).
 // The MMA thread's whole loop is: wait full, 8 MMAs, commit empty.
-template <int BITS, unsigned CB>
+template <int BITS, unsigned CB, bool PEER>
 __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const GemmArgs a) {
     extern __shared__ __align__(1024) unsigned char smem[];
     constexpr int CHUNKB = 256 * BITS;
@@ -415,6 +416,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const GemmArgs a) {
     cluster.sync();
     if (epi) {
         const int per = NT / S;
+        // column split over GPUs: this call's epoch picks the half of every rank's y buffer
+        const unsigned epoch =
+            PEER ? *reinterpret_cast<const volatile unsigned *>(a.peer.own_state + kPeerEpochWord) + 1u : 0u;
         const uint2 sraw = *reinterpret_cast<const uint2 *>(a.sv + nb * 128 + lane * 4);
         const __half2 s01 = bits_half2(sraw.x), s23 = bits_half2(sraw.y);
         for (int t = split * per + warp; t < (split + 1) * per; t += 12) {
@@ -434,7 +438,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const GemmArgs a) {
                 o.y = __fmul_rn(v[1], __high2float(s01));
                 o.z = __fmul_rn(v[2], __low2float(s23));
                 o.w = __fmul_rn(v[3], __high2float(s23));
-                *reinterpret_cast<float4 *>(a.y + size_t(token) * a.y_stride + nb * 128 + lane * 4) = o;
+                if constexpr (PEER) {  // NVLink stores of (epoch, value) words into every rank's y
+                    const long long off = ((epoch & 1u) ? a.peer.y_half : 0) + token * a.peer.y_stride +
+                                          a.peer.y_col0 + nb * 128 + lane * 4;
+                    for (int pi = 0; pi < a.peer.npeers; ++pi) store_pairs4(a.peer.y[pi] + off, o, epoch);
+                } else {
+                    *reinterpret_cast<float4 *>(a.y + size_t(token) * a.y_stride + nb * 128 + lane * 4) = o;
+                }
             }
         }
     }
@@ -451,26 +461,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const GemmArgs a) {
 
 namespace {
 
+// The PEER build (output to the peers' buffers, for the column split) exists for mul1 weights.
 template <int BITS>
-void * gemm_kernel_cb(unsigned cb) {
+void * gemm_kernel_cb(unsigned cb, bool peer) {
+    if (peer) return cb == CB_MUL1 ? reinterpret_cast<void *>(k_gemm<BITS, CB_MUL1, true>) : nullptr;
     switch (cb) {
-        case CB_3INST: return reinterpret_cast<void *>(k_gemm<BITS, CB_3INST>);
-        case CB_MCG: return reinterpret_cast<void *>(k_gemm<BITS, CB_MCG>);
-        case CB_MUL1: return reinterpret_cast<void *>(k_gemm<BITS, CB_MUL1>);
+        case CB_3INST: return reinterpret_cast<void *>(k_gemm<BITS, CB_3INST, false>);
+        case CB_MCG: return reinterpret_cast<void *>(k_gemm<BITS, CB_MCG, false>);
+        case CB_MUL1: return reinterpret_cast<void *>(k_gemm<BITS, CB_MUL1, false>);
         default: return nullptr;
     }
 }
 
-void * gemm_kernel_for(unsigned bits, unsigned cb) {
+void * gemm_kernel_for(unsigned bits, unsigned cb, bool peer = false) {
     switch (bits) {
-        case 1: return gemm_kernel_cb<1>(cb);
-        case 2: return gemm_kernel_cb<2>(cb);
-        case 3: return gemm_kernel_cb<3>(cb);
-        case 4: return gemm_kernel_cb<4>(cb);
-        case 5: return gemm_kernel_cb<5>(cb);
-        case 6: return gemm_kernel_cb<6>(cb);
-        case 7: return gemm_kernel_cb<7>(cb);
-        case 8: return gemm_kernel_cb<8>(cb);
+        case 1: return gemm_kernel_cb<1>(cb, peer);
+        case 2: return gemm_kernel_cb<2>(cb, peer);
+        case 3: return gemm_kernel_cb<3>(cb, peer);
+        case 4: return gemm_kernel_cb<4>(cb, peer);
+        case 5: return gemm_kernel_cb<5>(cb, peer);
+        case 6: return gemm_kernel_cb<6>(cb, peer);
+        case 7: return gemm_kernel_cb<7>(cb, peer);
+        case 8: return gemm_kernel_cb<8>(cb, peer);
         default: return nullptr;
     }
 }
@@ -514,10 +526,13 @@ bool gemm_prepare(int device, unsigned bits, unsigned cb) {
     if (device < 0 || device >= 64 || bits < 1 || bits > 8 || cb > 2) return false;
     std::lock_guard<std::mutex> g(mu);
     if (done[device][bits][cb]) return true;
-    const void * k = gemm_kernel_for(bits, cb);
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmMaxSmem)) != cudaSuccess)
-        return false;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) return false;
+    for (const bool peer : {false, true}) {
+        const void * k = gemm_kernel_for(bits, cb, peer);
+        if (!k) continue;  // no PEER build for this codebook
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmMaxSmem)) != cudaSuccess)
+            return false;
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) return false;
+    }
     done[device][bits][cb] = true;
     return true;
 }
@@ -591,8 +606,9 @@ GemmPlan plan_gemm(int device, int sms, size_t k, size_t nblocks, unsigned bits,
 cudaError_t launch_gemm(const GemmPlan & p, const uint32_t * lsc, const __half * su, const __half * sv, size_t k,
                         size_t nblocks, unsigned bits, unsigned cb, int device, const void * x, int x_f16,
                         long long x_stride, int rows, const int32_t * m_dev, int m_base, float * y, long long y_stride,
-                        __half * xt, bool pdl, cudaStream_t st) {
+                        __half * xt, bool pdl, cudaStream_t st, const PeerOut * peer) {
     if (!gemm_prepare(device, bits, cb)) return cudaErrorInvalidValue;
+    if (peer && cb != CB_MUL1) return cudaErrorInvalidValue;
     const int rows_pad = p.tgroups * p.ntok;
     const long long warps = (long long)rows_pad * (long long)(k / 128);
     {
@@ -609,7 +625,8 @@ cudaError_t launch_gemm(const GemmPlan & p, const uint32_t * lsc, const __half *
                                            rows_pad, xt);
         if (e != cudaSuccess) return e;
     }
-    GemmArgs a;
+    GemmArgs a{};
+    if (peer) a.peer = *peer;
     a.lsc = lsc;
     a.sv = sv;
     a.xt = xt;
@@ -639,7 +656,7 @@ cudaError_t launch_gemm(const GemmPlan & p, const uint32_t * lsc, const __half *
     cfg.attrs = attrs;
     cfg.numAttrs = pdl ? 2 : 1;
     void * args[] = {&a};
-    return cudaLaunchKernelExC(&cfg, gemm_kernel_for(bits, cb), args);
+    return cudaLaunchKernelExC(&cfg, gemm_kernel_for(bits, cb, peer != nullptr), args);
 }
 
 cudaError_t gemm_read_status(unsigned * out, bool clear) {

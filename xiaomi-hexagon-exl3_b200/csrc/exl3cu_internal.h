@@ -116,7 +116,7 @@ GemmPlan plan_gemm(int device, int sms, size_t k, size_t nblocks, unsigned bits,
 cudaError_t launch_gemm(const GemmPlan & p, const uint32_t * lsc, const __half * su, const __half * sv, size_t k,
                         size_t nblocks, unsigned bits, unsigned cb, int device, const void * x, int x_f16,
                         long long x_stride, int rows, const int32_t * m_dev, int m_base, float * y, long long y_stride,
-                        __half * xt, bool pdl, cudaStream_t st);
+                        __half * xt, bool pdl, cudaStream_t st, const PeerOut * peer = nullptr);
 // Ragged batch packer (exl3cu_kernels.cu): grants each sequence min(want, remaining budget) rows in order.
 cudaError_t launch_pack_ragged(int n_seq, const int32_t * want, const int32_t * pos, int32_t max_rows,
                                int32_t * row_offsets, int32_t * row_seq, int32_t * row_pos, cudaStream_t st);
