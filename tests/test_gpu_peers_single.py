@@ -74,3 +74,28 @@ def test_two_ranks_on_one_gpu_fused_and_fallback(cuda_lib, oracle):
     assert status.value == 0
     for w in ws:
         w.free()
+
+
+def test_peer_entries_reject_host_pointers(cuda_lib):
+    """The exchange's entries validate their buffers on the host: a host pointer where device memory
+    belongs is refused with EXL3CU_INVALID_ARGUMENT before anything is launched."""
+    import numpy as np
+
+    from exl3_b200 import _lib
+
+    L = _lib.lib()
+    host_state = np.zeros(16, np.uint32)
+    y = torch.zeros(2 * 8 * 128, dtype=torch.int64, device="cuda")
+    out = torch.zeros((8, 128), dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    rc = L.exl3cu_wait_peers(host_state.ctypes.data, y.data_ptr(), 128, 8 * 128, out.data_ptr(), 128, 1, 128, st)
+    assert rc == _lib.INVALID_ARGUMENT
+    assert b"state" in L.exl3cu_last_error()
+    slice_ = torch.zeros((1, 128), dtype=torch.float32, device="cuda")
+    host_y = np.zeros(2 * 8 * 128, np.int64)
+    yp = (ctypes.c_void_p * 1)(host_y.ctypes.data)
+    state = torch.zeros(16, dtype=torch.int32, device="cuda")
+    rc = L.exl3cu_store_peers(slice_.data_ptr(), 1, 128, 128, 1, yp, 128, 8 * 128, 0, state.data_ptr(), st)
+    assert rc == _lib.INVALID_ARGUMENT
+    assert b"peer" in L.exl3cu_last_error()
+    torch.cuda.synchronize()

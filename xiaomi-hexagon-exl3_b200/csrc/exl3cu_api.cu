@@ -1023,6 +1023,10 @@ extern "C" int exl3cu_mul_mat_peers(const exl3cu_weight * w, const void * d_x, i
                                     const unsigned * d_state, void * stream) {
     if (npeers < 1 || npeers > kMaxPeers) return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: 1..%d ranks", kMaxPeers);
     if (!d_y_peers || !d_state) return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: NULL peer arrays or state");
+    {
+        const int rc = check_device_ptr(d_state, -1, "state");
+        if (rc) return rc;
+    }
     if (y_row_stride % 4 || y_half % 4 || y_col0 % 4)
         return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: y strides and offsets must be multiples of 4 words");
     if (!w) return fail(EXL3CU_INVALID_ARGUMENT, "weight handle is NULL");
@@ -1031,7 +1035,8 @@ extern "C" int exl3cu_mul_mat_peers(const exl3cu_weight * w, const void * d_x, i
         return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: the slice does not fit the peers' y buffers");
     PeerOut po{};
     for (int p = 0; p < npeers; ++p) {
-        if (!d_y_peers[p]) return fail(EXL3CU_INVALID_ARGUMENT, "mul_mat_peers: NULL peer");
+        const int rc = check_device_ptr(d_y_peers[p], -1, "a peer's y buffer");  // IPC mappings: any device
+        if (rc) return rc;
         po.y[p] = static_cast<unsigned long long *>(d_y_peers[p]);
     }
     po.own_state = d_state;
@@ -1076,6 +1081,8 @@ bool pdl_launch_enabled() { return pdl_enabled(); }
 int api_fail(int status, const char * message) { return fail(status, "%s", message); }
 
 int api_cuda_fail(cudaError_t e, const char * what) { return cuda_fail(e, what); }
+
+int api_check_device_ptr(const void * p, int device, const char * name) { return check_device_ptr(p, device, name); }
 
 void weight_set_model_owned(::exl3cu_weight * w) { w->model_owned = true; }
 

@@ -148,6 +148,9 @@ cudaError_t launch_get_rows(const uint32_t * lsc, const uint16_t * suh, const ui
                             size_t out_stride, bool out_f16, cudaStream_t st);
 cudaError_t rows_read_status(unsigned * out, bool clear);
 cudaError_t peer_read_status(unsigned * out, bool clear);
+// 0 when p is device (or managed) memory of `device` (-1: any device), else a failure status with the
+// thread's error text set (exl3cu_api.cu).
+int api_check_device_ptr(const void * p, int device, const char * name);
 cudaError_t launch_reconstruct_blocks(uint16_t * io, size_t k, size_t column_count, size_t first_column,
                                       const uint16_t * suh, const uint16_t * svh, cudaStream_t st);
 

@@ -213,9 +213,12 @@ int exl3cu_store_peers(const float * d_slice, size_t rows, size_t cols, size_t s
         y_row_stride < y_col0 + cols || y_half < rows * y_row_stride)
         return api_fail(EXL3CU_INVALID_ARGUMENT,
                         "store_peers: columns, strides and offsets must be multiples of 4 and fit the buffers");
+    int rc = api_check_device_ptr(d_slice, -1, "slice");
+    if (!rc) rc = api_check_device_ptr(d_state, -1, "state");
+    if (rc) return rc;
     PeerArgs a{};
     for (int p = 0; p < npeers; ++p) {
-        if (!d_y_peers[p]) return api_fail(EXL3CU_INVALID_ARGUMENT, "store_peers: NULL peer");
+        if ((rc = api_check_device_ptr(d_y_peers[p], -1, "a peer's y buffer"))) return rc;  // IPC mappings: any device
         a.y[p] = static_cast<unsigned long long *>(d_y_peers[p]);
     }
     a.own_state = d_state;
@@ -238,6 +241,10 @@ int exl3cu_wait_peers(unsigned * d_state, const void * d_y, size_t y_row_stride,
     if (!d_state || !d_y || !rows || !cols) return api_fail(EXL3CU_INVALID_ARGUMENT, "wait_peers: NULL or empty argument");
     if (y_row_stride < cols || y_half < rows * y_row_stride || (d_out && out_row_stride < cols))
         return api_fail(EXL3CU_INVALID_ARGUMENT, "wait_peers: the rows do not fit the buffers");
+    int rc = api_check_device_ptr(d_state, -1, "state");
+    if (!rc) rc = api_check_device_ptr(d_y, -1, "y");
+    if (!rc && d_out) rc = api_check_device_ptr(d_out, -1, "out");
+    if (rc) return rc;
     const size_t n = rows * cols;
     const unsigned grid = unsigned(n <= 1024 ? 1 : (n + 1023) / 1024 < 148 ? (n + 1023) / 1024 : 148);
     const cudaError_t e =
