@@ -19,9 +19,10 @@ Each pattern's step is captured once in a CUDA graph and replayed; launches
 chain with programmatic dependent launch.
 
   value   algorithmic bytes of K steps / device time of K replays (decoder)
-  e2e     the same metric from host memory: per step one pinned host->device
-          copy of every matrix's fp16 x, the decoder pattern's C-ABI calls,
-          one device->host copy of every f32 y, all inside the timed region
+  e2e     the same metric from host memory: per step every matrix's fp16 x
+          copied from pinned host memory and every f32 y copied back, pipelined
+          by layer on two copy streams around the decoder pattern's C-ABI calls,
+          all inside the timed region
   --impl reference   the reference's own CPU operator (ggml_exl3_mul_mat from
           oracle/_ref, built from the reference's sources) on all host cores
 
@@ -246,26 +247,60 @@ def time_pattern(torch, dist, ops, stack, pattern, steps, warmup, world):
 
 
 def time_e2e(torch, ops, stack, steps):
-    """End to end from host memory: per step, one pinned host->device copy of every matrix's fp16 x,
-    the decoder pattern's 112 C-ABI launches (a CUDA graph of exl3cu_mul_mat_batch calls), one
-    device->host copy of every f32 y into pinned memory, and a stream synchronisation."""
-    stream = torch.cuda.Stream()
-    run, _ = step_launcher(ops, stack, "decoder", stream)
+    """End to end from host memory, per step: every matrix's fp16 x copied from pinned host memory, the
+    decoder pattern's 112 C-ABI launches, every f32 y copied back into pinned memory, and a stream
+    synchronisation.  The copies are pipelined by layer: a copy stream moves layer l's x while earlier
+    layers compute, layer l's launches wait only for their own x, and a second copy stream returns
+    layer l's y while later layers compute.  The whole step (copies, launches, the streams' events)
+    is one CUDA graph, replayed.  Returns (ms for `steps` steps, H2D bytes and D2H bytes per step)."""
+    stream, cin, cout = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
     x_host = stack.x_all.cpu().pin_memory()
     y_host = torch.empty(stack.y_all.shape, dtype=torch.float32).pin_memory()
+    layers = []
+    for mats in stack:  # each layer's x and y are contiguous ranges of x_all / y_all
+        xs = [m["x"] for m in mats.values()]
+        ys = [m["y"] for m in mats.values()]
+        x0 = min(x.storage_offset() for x in xs)
+        x1 = max(x.storage_offset() + x.numel() for x in xs)
+        y0 = min(y.storage_offset() for y in ys)
+        y1 = max(y.storage_offset() + y.numel() for y in ys)
+        groups = [[mats[name] for name in grp] for grp in DECODER_GROUPS]
+        packed = [([m["w"] for m in g], [m["x"] for m in g], [m["y"] for m in g]) for g in groups]
+        layers.append((x0, x1, y0, y1, packed))
+    ev_in = [torch.cuda.Event() for _ in layers]
+    ev_out = [torch.cuda.Event() for _ in layers]
+
+    def body():
+        cin.wait_stream(stream)
+        cout.wait_stream(stream)
+        with torch.cuda.stream(cin):
+            for li, (x0, x1, _, _, _) in enumerate(layers):
+                stack.x_all[x0:x1].copy_(x_host[x0:x1], non_blocking=True)
+                ev_in[li].record(cin)
+        with torch.cuda.stream(stream):
+            for li, (_, _, _, _, packed) in enumerate(layers):
+                stream.wait_event(ev_in[li])
+                for ws, xs, ys in packed:
+                    ops.mul_mat_batch(ws, xs, ys, stream=stream)
+                ev_out[li].record(stream)
+        with torch.cuda.stream(cout):
+            for li, (_, _, y0, y1, _) in enumerate(layers):
+                cout.wait_event(ev_out[li])
+                y_host[y0:y1].copy_(stack.y_all[y0:y1], non_blocking=True)
+        stream.wait_stream(cin)
+        stream.wait_stream(cout)
+
     with torch.cuda.stream(stream):
         for _ in range(3):
-            run()
+            body()
     stream.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream, capture_error_mode="relaxed"):
-        run()
+        body()
 
     def step():
         with torch.cuda.stream(stream):
-            stack.x_all.copy_(x_host, non_blocking=True)
             graph.replay()
-            y_host.copy_(stack.y_all, non_blocking=True)
         stream.synchronize()
 
     for _ in range(3):
@@ -1049,8 +1084,9 @@ def main(argv=None):
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "api": "one pinned H2D of all x, the decoder pattern's exl3cu_mul_mat_batch calls (CUDA graph), "
-                           "one D2H of all y into pinned memory, stream synchronise",
+                    "api": "per step: every x copied from pinned host memory and every y back, pipelined by "
+                           "layer on two copy streams around the decoder pattern's exl3cu_mul_mat_batch calls "
+                           "(one CUDA graph per step), stream synchronise",
                     "ms_per_step": round(e2e_ms / args.e2e_steps, 4),
                     "per_call_ggml": {
                         "value": round(step_bytes * world / (ggml_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
