@@ -419,8 +419,9 @@ def run_model_measure(torch, dist, local, rank, world, new_tokens=256, single_pr
 
     single: one request, 512-token prompt prefilled, then `new_tokens` greedy steps replayed from one
             captured step with device-side token feedback (CUDA events around the replays);
-    single_e2e: the same request served step by step through the engine API: pinned H2D of the step
-            metadata, the captured step, D2H of the next token, host loop (events around the loop);
+    single_e2e: the same request served step by step through the engine API: per token the host fills
+            the step metadata, one captured graph copies it in, runs the step and copies the token
+            out (pinned buffers), and the host synchronises; events around the loop;
     ragged8: 8 requests, prompts U[32,1024] seeded, `new_tokens` greedy tokens each, continuous
             admission (decode rows of running requests + 512-row prefill chunks of the next one per
             step), host scheduler in the loop; runs of pure decode steps with nothing to admit go
@@ -479,16 +480,13 @@ def run_model_measure(torch, dist, local, rank, world, new_tokens=256, single_pr
     pos = n + 1
     tok = int(eng.out_tokens[0].item())
     e2e_steps = min(new_tokens, 128)
-    out_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
     s_ev.record(stream)
     for _ in range(e2e_steps):
         eng.meta.fill([tok], [0], [pos], [0, 1], [1], [0])
         with torch.cuda.stream(stream):
-            eng.meta.upload(stream)
-            sg.replay()
-            out_host.copy_(eng.out_tokens[:1], non_blocking=True)
+            sg.replay()  # the captured step copies the metadata in and the token out itself
         stream.synchronize()
-        tok = int(out_host[0])
+        tok = int(sg.out_host[0])
         pos += 1
     e_ev.record(stream)
     e_ev.synchronize()
@@ -543,7 +541,8 @@ def run_model_measure(torch, dist, local, rank, world, new_tokens=256, single_pr
         "single_ms_per_token": round(single_ms / new_tokens, 4),
         "single_timing": "one captured decode step replayed with device-side token feedback; CUDA events",
         "single_e2e_tok_s": round(world * e2e_steps / (e2e_ms * 1e-3), 1),
-        "single_e2e_api": "per token: pinned H2D of the step metadata (92 B), captured step, D2H of the token",
+        "single_e2e_api": "per token: one captured graph copies the step metadata in from pinned memory "
+                          "(6.2 KB), runs the step and copies the token out; host synchronise",
         "ragged8_tok_s": round(gen_total / (ragged_ms_max * 1e-3), 1),
         "ragged8": {"requests_per_gpu": 8, "prompt_tokens": [int(x) for x in lens], "new_tokens": new_tokens,
                     "steps": steps, "rows": rows, "ms": round(ragged_ms_max, 1), "runs_ms": runs_ms,

@@ -596,14 +596,16 @@ def run_requests(engine: HybridEngine, requests, chunk: int = 512, stream=None, 
         engine.meta.fill(tokens, row_seq, row_pos, offsets, slots_, logit_rows)
         n = len(tokens)
         pure_decode = n == len(seqs) == len(logit_rows)
+        g = graphs.get(n) if pure_decode else None
         with torch.cuda.stream(stream):
-            engine.meta.upload(stream)
-            g = graphs.get(n) if pure_decode else None
-            if g is not None:
+            if g is not None:  # metadata in, step, tokens out: one captured graph
                 g.replay()
+                stream.synchronize()
+                out = g.out_host[:len(logit_rows)]
             else:
+                engine.meta.upload(stream)
                 engine.forward(n, len(seqs), len(logit_rows), stream)
-            out = engine.out_tokens[:len(logit_rows)].to("cpu", non_blocking=False)
+                out = engine.out_tokens[:len(logit_rows)].to("cpu", non_blocking=False)
         if pure_decode and n not in graphs:
             if n in seen:
                 graphs[n] = _StepGraph(engine, n, stream)
@@ -628,13 +630,19 @@ def run_requests(engine: HybridEngine, requests, chunk: int = 512, stream=None, 
 
 
 class _StepGraph:
-    """A captured pure decode step of n sequences (metadata read from the device buffer as it is)."""
+    """A captured pure decode step of n sequences, its host I/O included: the step metadata is copied
+    in from the engine's pinned host buffer and the n next tokens out into `out_host` (pinned), so a
+    host-scheduled step is one graph launch and one synchronisation.  Fill engine.meta on the host,
+    replay(), synchronise the stream, read out_host[:n]."""
 
     def __init__(self, engine, n, stream):
         torch = engine.torch
+        self.out_host = torch.zeros(8, dtype=torch.int32, pin_memory=True)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=stream):
+            engine.meta.upload(stream)
             engine.forward(n, n, n, stream)
+            self.out_host[:n].copy_(engine.out_tokens[:n], non_blocking=True)
 
     def replay(self):
         self.graph.replay()
